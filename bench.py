@@ -1,0 +1,638 @@
+#!/usr/bin/env python
+"""Benchmark of the fused-op hot path on B200 (one JSON line on rank 0).
+
+Metric: fwd+bwd tokens/s per fused op at Qwen3-VL shapes, with
+the fraction of the HBM / tensor-core roofline.  The default workload is
+BASELINE configs[1] — SwiGLU (gate/up [8,2048,6144] bf16) plus RoPE (q
+[8,16,2048,128], k [8,8,2048,128] bf16, positions 0..2047, theta 5e6, cos/sin
+recomputed in-kernel), forward + backward — one "step" = one fwd+bwd pass of
+both ops over the 16,384 tokens.  Other configs are selectable with
+``--workload`` (they are parity-test cases; the default line is configs[1]).
+
+  value    device-timed tokens/s, inputs resident in HBM, CUDA events on the
+           launching stream, max over ranks (weak scaling: every rank runs
+           the full per-GPU workload, no collective on the data path);
+  e2e      the same metric through the public autograd API with HOST
+           (pinned) buffers: per step H2D of all inputs and D2H of all
+           outputs inside the timed region;
+  roofline the dominant kernel's algorithmic bytes (or FLOPs) per launch over
+           its event-timed average duration, against MEASURED_PEAKS.json;
+  cpu_baseline  the CPU oracle (a restatement of the reference's torch ops)
+           on the host cores over a bounded sample (rank 0, N=1 only).
+
+``--impl reference`` times that CPU implementation alone (the reference arm).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+       torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
+
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic(workload: str, kernel: str):
+    """DRAM bytes per launch of `kernel` from a committed ncu summary, or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        d = json.loads(p.read_text())
+        return d.get(workload, {}).get(kernel)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Polls NVML (SM clock, throttle reasons) from a thread during the timed region."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples = []
+        self.reasons = 0
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thr = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            # NVML enumerates physical GPUs; map through CUDA_VISIBLE_DEVICES.
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = device_index
+            if vis:
+                ids = [v.strip() for v in vis.split(",") if v.strip()]
+                if device_index < len(ids) and ids[device_index].isdigit():
+                    idx = int(ids[device_index])
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thr = threading.Thread(target=self._run, daemon=True)
+            self._thr.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml_unavailable"]}
+        names = [n for bit, n in self.REASONS.items() if self.reasons & bit]
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": names,
+            "samples": len(self.samples),
+        }
+
+
+class KernelTimer:
+    """CUDA-event brackets around named launches on the current stream."""
+
+    def __init__(self):
+        self.marks = []
+
+    def __call__(self, name, fn, *args):
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = fn(*args)
+        e.record()
+        self.marks.append((name, s, e))
+        return out
+
+    def averages_ms(self):
+        acc = {}
+        for name, s, e in self.marks:
+            acc.setdefault(name, []).append(s.elapsed_time(e))
+        return {k: sum(v) / len(v) for k, v in acc.items()}
+
+
+def plain(name, fn, *args):
+    return fn(*args)
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+class SwigluRope:
+    """SwiGLU + RoPE fwd+bwd, bf16, Qwen3-VL-2B layer shape."""
+
+    name = "swiglu_rope"
+    bound = "hbm"
+    dtype = "bf16"
+    B, S, I = 8, 2048, 6144
+    HQ, HK, D = 16, 8, 128
+    THETA = 5e6
+    dominant = "swiglu_backward"
+
+    def __init__(self):
+        self.tokens = self.B * self.S
+        n = self.tokens * self.I
+        rq = self.B * self.HQ * self.S * self.D
+        rk = self.B * self.HK * self.S * self.D
+        # algorithmic bytes per launch (bf16 = 2 B): every tensor read/written once
+        self.bytes = {
+            "swiglu_forward": 3 * n * 2,
+            "swiglu_backward": 5 * n * 2,
+            "rope_forward": 2 * (rq + rk) * 2,
+            "rope_backward": 2 * (rq + rk) * 2,
+        }
+        self.launches_per_step = 4
+
+    def config(self):
+        return {
+            "workload": "swiglu_rope_bf16 (BASELINE configs[1]): SwiGLU gate/up [8,2048,6144] + "
+                        "RoPE q [8,16,2048,128], k [8,8,2048,128], positions 0..2047, "
+                        "theta 5e6, cos/sin recomputed in-kernel; fwd+bwd",
+            "tokens_per_step": self.tokens,
+            "global_batch": self.B,
+            "seq_len": self.S,
+            "intermediate": self.I,
+            "parallelism": "replicas (token rows; no collective)",
+            "l2": "inputs larger than L2 (every tensor >= 67 MB; 2.0 GB touched per step)",
+        }
+
+    def make_inputs(self, device, seed=1235):
+        g = torch.Generator(device=device).manual_seed(seed)
+        shp = (self.B, self.S, self.I)
+        t = {
+            "gate": torch.randn(shp, generator=g, device=device).bfloat16(),
+            "up": torch.randn(shp, generator=g, device=device).bfloat16(),
+            "dout": torch.randn(shp, generator=g, device=device).bfloat16(),
+            "q": torch.randn(self.B, self.HQ, self.S, self.D, generator=g,
+                             device=device).bfloat16(),
+            "k": torch.randn(self.B, self.HK, self.S, self.D, generator=g,
+                             device=device).bfloat16(),
+            "dq": torch.randn(self.B, self.HQ, self.S, self.D, generator=g,
+                              device=device).bfloat16(),
+            "dk": torch.randn(self.B, self.HK, self.S, self.D, generator=g,
+                              device=device).bfloat16(),
+        }
+        t["pos"] = torch.arange(self.S, device=device).expand(self.B, self.S).contiguous()
+        from metal_liger_b200.ops.fused_rope import rope_inv_freq
+
+        t["inv_freq"] = rope_inv_freq(self.D, self.THETA, device=device)
+        return t
+
+    def step(self, t, timer=plain):
+        ops = torch.ops.metal_liger
+        timer("swiglu_forward", ops.swiglu_forward, t["gate"], t["up"], "")
+        timer("swiglu_backward", ops.swiglu_backward, t["gate"], t["up"], t["dout"], "")
+        timer("rope_forward", ops.rope_apply_qk_pos, t["q"], t["k"], t["pos"], t["inv_freq"],
+              1.0, 1)
+        timer("rope_backward", ops.rope_apply_qk_pos, t["dq"], t["dk"], t["pos"], t["inv_freq"],
+              1.0, -1)
+
+    # ---- end to end through the public API with host buffers ----
+    def e2e_setup(self, device):
+        t = self.make_inputs(device, seed=77)
+        host = {k: v.cpu().pin_memory() for k, v in t.items() if k not in ("pos", "inv_freq")}
+        dev = {k: torch.empty_like(v) for k, v in t.items() if k not in ("pos", "inv_freq")}
+        outs_shapes = {"out": t["gate"], "dgate": t["gate"], "dup": t["up"], "q_rot": t["q"],
+                       "k_rot": t["k"], "dq_in": t["q"], "dk_in": t["k"]}
+        host_out = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True)
+                    for k, v in outs_shapes.items()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        return {"host": host, "dev": dev, "host_out": host_out, "pos": t["pos"],
+                "inv_freq": t["inv_freq"], "h2d": h2d, "d2h": d2h}
+
+    def e2e_step(self, s):
+        from metal_liger_b200.ops.fused_swiglu import fused_swiglu
+        from metal_liger_b200.ops.fused_rope import apply_fused_rotary_from_positions
+
+        d, h, ho = s["dev"], s["host"], s["host_out"]
+        for k in d:
+            d[k].copy_(h[k], non_blocking=True)
+        gate = d["gate"].detach().requires_grad_(True)
+        up = d["up"].detach().requires_grad_(True)
+        out = fused_swiglu(gate, up)
+        out.backward(d["dout"])
+        q = d["q"].detach().requires_grad_(True)
+        k = d["k"].detach().requires_grad_(True)
+        qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"], inv_freq=s["inv_freq"])
+        torch.autograd.backward([qr, kr], [d["dq"], d["dk"]])
+        for name, src in (("out", out), ("dgate", gate.grad), ("dup", up.grad), ("q_rot", qr),
+                          ("k_rot", kr), ("dq_in", q.grad), ("dk_in", k.grad)):
+            ho[name].copy_(src.detach(), non_blocking=True)
+
+    # ---- CPU oracle on a bounded sample ----
+    def cpu_inputs(self, tokens, seed=5):
+        g = torch.Generator().manual_seed(seed)
+        return {
+            "gate": torch.randn(tokens, self.I, generator=g).bfloat16(),
+            "up": torch.randn(tokens, self.I, generator=g).bfloat16(),
+            "dout": torch.randn(tokens, self.I, generator=g).bfloat16(),
+            "q": torch.randn(1, self.HQ, tokens, self.D, generator=g).bfloat16(),
+            "k": torch.randn(1, self.HK, tokens, self.D, generator=g).bfloat16(),
+            "dq": torch.randn(1, self.HQ, tokens, self.D, generator=g).bfloat16(),
+            "dk": torch.randn(1, self.HK, tokens, self.D, generator=g).bfloat16(),
+            "pos": torch.arange(tokens)[None],
+        }
+
+    def cpu_step(self, c):
+        from oracle import ops as O
+
+        O.swiglu_forward(c["gate"], c["up"])
+        O.swiglu_backward(c["gate"], c["up"], c["dout"])
+        cos, sin = O.rope_cos_sin(c["pos"], O.rope_inv_freq(self.D, self.THETA))
+        cos, sin = cos[:, None], sin[:, None]
+        for x in (c["q"], c["k"]):
+            O.rope_apply(x, cos, sin).to(torch.bfloat16)
+        for gx in (c["dq"], c["dk"]):
+            O.rope_backward(gx, cos, sin).to(torch.bfloat16)
+
+
+class RmsNorm:
+    """RMSNorm fwd+bwd fp32, x [8,1024,2048]."""
+
+    name = "rmsnorm"
+    bound = "hbm"
+    dtype = "f32"
+    B, S, H = 8, 1024, 2048
+    dominant = "rms_norm_backward"
+
+    def __init__(self):
+        self.tokens = self.B * self.S
+        n = self.tokens * self.H
+        self.bytes = {"rms_norm_forward": 2 * n * 4 + self.tokens * 4,
+                      "rms_norm_backward": 3 * n * 4 + self.tokens * 4}
+        self.launches_per_step = 3  # fwd, bwd, dweight reduce
+
+    def config(self):
+        return {"workload": "rmsnorm_f32 (BASELINE configs[0]): x [8,1024,2048], eps 1e-6; "
+                            "fwd+bwd (y, dX, dW)",
+                "tokens_per_step": self.tokens, "global_batch": self.B, "seq_len": self.S,
+                "hidden": self.H, "parallelism": "replicas (token rows; no collective)",
+                "l2": "inputs larger than L2 is false (67 MB); L2 flushed between steps"}
+
+    def make_inputs(self, device, seed=1234):
+        g = torch.Generator(device=device).manual_seed(seed)
+        x = torch.randn(self.B, self.S, self.H, generator=g, device=device)
+        w = 1.0 + 0.1 * torch.randn(self.H, generator=g, device=device)
+        dy = torch.randn(self.B, self.S, self.H, generator=g, device=device)
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+        return {"x": x, "w": w, "dy": dy, "flush": flush}
+
+    def step(self, t, timer=plain):
+        ops = torch.ops.metal_liger
+        t["flush"].fill_(0.0)  # evict L2 (256 MB > 126 MB) so inputs come from HBM
+        y, rrms = timer("rms_norm_forward", ops.rms_norm_forward, t["x"], t["w"], 1e-6, "")
+        timer("rms_norm_backward", ops.rms_norm_backward, t["x"], t["w"], t["dy"], 1e-6, "",
+              rrms)
+
+    def e2e_setup(self, device):
+        t = self.make_inputs(device, seed=78)
+        host = {k: t[k].cpu().pin_memory() for k in ("x", "w", "dy")}
+        dev = {k: torch.empty_like(t[k]) for k in ("x", "w", "dy")}
+        host_out = {"y": torch.empty_like(host["x"]).pin_memory(),
+                    "dx": torch.empty_like(host["x"]).pin_memory(),
+                    "dw": torch.empty_like(host["w"]).pin_memory()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h}
+
+    def e2e_step(self, s):
+        from metal_liger_b200.ops.fused_rms_norm import _FusedRMSNormFunction
+
+        d, h, ho = s["dev"], s["host"], s["host_out"]
+        for k in d:
+            d[k].copy_(h[k], non_blocking=True)
+        x = d["x"].detach().requires_grad_(True)
+        w = d["w"].detach().requires_grad_(True)
+        y = _FusedRMSNormFunction.apply(x, w, 1e-6)
+        y.backward(d["dy"])
+        ho["y"].copy_(y.detach(), non_blocking=True)
+        ho["dx"].copy_(x.grad, non_blocking=True)
+        ho["dw"].copy_(w.grad, non_blocking=True)
+
+    def cpu_inputs(self, tokens, seed=6):
+        g = torch.Generator().manual_seed(seed)
+        return {"x": torch.randn(tokens, self.H, generator=g),
+                "w": 1 + 0.1 * torch.randn(self.H, generator=g),
+                "dy": torch.randn(tokens, self.H, generator=g)}
+
+    def cpu_step(self, c):
+        from oracle import ops as O
+
+        _, rr = O.rms_norm_forward(c["x"], c["w"], 1e-6)
+        O.rms_norm_backward(c["x"], c["w"], rr, c["dy"])
+
+
+WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm}
+
+
+def _register_optional_workloads():
+    """FLCE / LoRA workloads live beside their ops (imported when present)."""
+    try:
+        from metal_liger_b200 import bench_workloads  # noqa: F401
+    except ImportError:
+        return
+    WORKLOADS.update(bench_workloads.WORKLOADS)
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+def cpu_measure(wl, budget_s: float, max_steps: int | None = None):
+    """Time the CPU oracle on a bounded sample: returns (tokens/s, tokens, steps, cores)."""
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    tokens = 64
+    c = wl.cpu_inputs(tokens)
+    t0 = time.perf_counter()
+    wl.cpu_step(c)
+    dt = max(time.perf_counter() - t0, 1e-4)
+    per_tok = dt / tokens
+    steps = max_steps or 3
+    tokens = int(max(16, min(wl.tokens, budget_s / steps / per_tok)))
+    c = wl.cpu_inputs(tokens)
+    wl.cpu_step(c)  # warm
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        wl.cpu_step(c)
+    el = time.perf_counter() - t0
+    return tokens * steps / el, tokens, steps, torch.get_num_threads()
+
+
+def run_reference_arm(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    budget = float(os.environ.get("BENCH_CPU_BUDGET_S", "60"))
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    per_step_budget = budget / max(1, args.steps + args.warmup)
+    # calibrate the sample size so the whole run stays within the budget
+    c = wl.cpu_inputs(64)
+    t0 = time.perf_counter()
+    wl.cpu_step(c)
+    per_tok = max(time.perf_counter() - t0, 1e-4) / 64
+    tokens = int(max(16, min(wl.tokens, per_step_budget / per_tok)))
+    c = wl.cpu_inputs(tokens)
+    for _ in range(args.warmup):
+        wl.cpu_step(c)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        wl.cpu_step(c)
+    el = time.perf_counter() - t0
+    value = tokens * args.steps / el
+    sample = (f"{tokens} of {wl.tokens} tokens per step (same shapes per token), "
+              f"torch CPU fp32 oracle restating the reference ops, TORCHDYNAMO_DISABLE=1")
+    line = {
+        "impl": "reference",
+        "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
+        "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps * wl.tokens / tokens,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
+        "data": "synthetic", "config": wl.config(),
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu_arm(args, wl):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}), flush=True)
+        return 1
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist_mod
+
+        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=device)
+        dist = dist_mod
+
+    import metal_liger_b200  # noqa: F401  (registers ops, loads the library on first call)
+    from metal_liger_b200 import _C
+
+    _C.load()
+    peaks, peaks_kind = load_peaks()
+
+    t = wl.make_inputs(device)
+    for _ in range(args.warmup):
+        wl.step(t)
+    torch.cuda.synchronize()
+
+    # ---- timed region ----
+    timer = KernelTimer()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record()
+        for _ in range(args.steps):
+            wl.step(t, timer)
+        end.record()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    if dist:
+        el = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        elapsed_ms = el.item()
+    kernel_ms = timer.averages_ms()
+    value = world * wl.tokens * args.steps / (elapsed_ms / 1e3)
+
+    # ---- end to end through the public API with host buffers ----
+    del t
+    torch.cuda.empty_cache()
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    s = wl.e2e_setup(device)
+    for _ in range(2):
+        wl.e2e_step(s)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        wl.e2e_step(s)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        el = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(el, op=dist.ReduceOp.MAX)
+        e2e_ms = el.item()
+    e2e_value = world * wl.tokens * e2e_steps / (e2e_ms / 1e3)
+    h2d, d2h = s["h2d"], s["d2h"]
+    del s
+    torch.cuda.empty_cache()
+
+    # ---- roofline of the dominant kernel ----
+    dom = wl.dominant
+    dom_ms = kernel_ms.get(dom)
+    if wl.bound == "hbm":
+        peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+        achieved = wl.bytes[dom] / (dom_ms / 1e3) / 1e9
+        unit = "GB/s"
+    else:
+        key = "bf16_tflops_sustained" if args.sustained else "bf16_tflops"
+        peak = float(peaks.get(key, FALLBACK_PEAKS[key]))
+        achieved = wl.flops[dom] / (dom_ms / 1e3) / 1e12
+        unit = "TFLOP/s"
+    traffic = load_traffic(wl.name, dom)
+    per_kernel = {}
+    for k, ms in kernel_ms.items():
+        entry = {"avg_ms": ms}
+        if wl.bound == "hbm" and k in wl.bytes:
+            gbs = wl.bytes[k] / (ms / 1e3) / 1e9
+            entry.update({"algorithmic_bytes": wl.bytes[k], "GB/s": gbs,
+                          "frac_of_measured_hbm": gbs / float(peaks.get("hbm_gbs", 1))})
+        if getattr(wl, "flops", None) and k in wl.flops:
+            tf = wl.flops[k] / (ms / 1e3) / 1e12
+            entry.update({"algorithmic_flops": wl.flops[k], "TFLOP/s": tf,
+                          "frac_of_measured_bf16": tf / float(peaks.get("bf16_tflops", 1))})
+        per_kernel[k] = entry
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            v, tok, st, cores = cpu_measure(wl, budget_s=args.cpu_budget)
+            cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                   "sample": f"{tok} of {wl.tokens} tokens x {st} steps through the CPU oracle "
+                             f"(torch fp32 restatement of the reference ops), "
+                             f"{cores} threads"}
+        line = {
+            "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": wl.dtype,
+            "data": "synthetic (seeded normal inputs of the BASELINE shapes)",
+            "config": wl.config(),
+            "roofline": {
+                "kernel": dom,
+                "bound": wl.bound,
+                "achieved": achieved,
+                "peak": peak,
+                "peak_source": f"{peaks_kind} ({'MEASURED_PEAKS.json' if peaks_kind == 'measured' else 'profiling-recipe fallback'})",
+                "unit": unit,
+                "frac": achieved / peak,
+                "traffic": traffic,
+            },
+            "per_kernel": per_kernel,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                    "api": "public autograd Functions (metal_liger_b200.ops.*), pinned host "
+                           "buffers, H2D inputs + D2H all outputs per step"},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    _register_optional_workloads()
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu_rope")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of CPU-oracle work for cpu_baseline")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+    ap.add_argument("--sustained", action="store_true",
+                    help="use the sustained bf16 peak for tensor-bound rooflines")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        args.warmup = 3  # timing rule: at least 3 warm-up steps
+    wl = WORKLOADS[args.workload]()
+    if args.impl == "reference":
+        return run_reference_arm(args, wl)
+    return run_gpu_arm(args, wl)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

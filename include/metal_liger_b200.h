@@ -1,0 +1,160 @@
+/*
+ * metal_liger_b200 — C ABI of the B200 (sm_100a) fused-op library.
+ *
+ * This is the drop-in boundary that replaces the reference's native layer:
+ * the Objective-C++/Metal functions declared in csrc/metal_liger_ops.h and
+ * bound by csrc/bindings.mm, plus the pure-ATen hot paths of ops/*.py that
+ * never had a native kernel (RoPE, chunked fused linear cross-entropy, fused
+ * LoRA).  Each entry point cites the reference interface it replaces.
+ *
+ * Conventions (all entry points):
+ *   - pointers are DEVICE pointers owned by the caller (inputs borrowed,
+ *     outputs written in place); nothing here allocates device memory unless
+ *     the comment says so;
+ *   - sizes are element counts; strides are in elements;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream); work is only enqueued, never synchronised;
+ *   - the return value is ML_OK (0) or an ML_ERR_* code; the message of the
+ *     last failure on the calling host thread is returned by ml_last_error().
+ *     Argument errors are detected on the host before anything is enqueued.
+ */
+#ifndef METAL_LIGER_B200_H_
+#define METAL_LIGER_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ML_API __attribute__((visibility("default")))
+#else
+#define ML_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types accepted by the dtype arguments. */
+enum {
+  ML_DTYPE_F32 = 0,
+  ML_DTYPE_BF16 = 1,
+  ML_DTYPE_F16 = 2
+};
+
+/* Status codes. */
+enum {
+  ML_OK = 0,
+  ML_ERR_INVALID_ARG = 1, /* bad shape / dtype / alignment / null pointer */
+  ML_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed */
+  ML_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+  ML_ERR_TIMEOUT = 4      /* a bounded device-side wait gave up */
+};
+
+/* Library version as 10000*major + 100*minor + patch. */
+ML_API int ml_version(void);
+
+/* Message describing the last failure on this host thread ("" if none). */
+ML_API const char* ml_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * RMSNorm
+ * ------------------------------------------------------------------------ */
+
+/*
+ * y = (x * rsqrt(mean(x^2, -1) + eps) * weight).to(x dtype), computed in fp32,
+ * and rrms[row] = rsqrt(mean(x^2) + eps) in fp32.
+ * x, y: [rows, hidden] contiguous, dtype x_dtype; weight: [hidden], w_dtype.
+ * rrms: [rows] fp32 (may be NULL when not needed).
+ * Replaces metal_rms_norm_forward (reference csrc/metal_liger_ops.h:14-18,
+ * csrc/rms_norm_metal.mm:110-160) and the math of
+ * _FusedRMSNormFunction.forward (ops/fused_rms_norm.py:30-41).
+ */
+ML_API int ml_rms_norm_forward(const void* x, int x_dtype, const void* weight, int w_dtype,
+                        void* y, float* rrms, int64_t rows, int64_t hidden, float eps,
+                        void* stream);
+
+/* Bytes of device scratch ml_rms_norm_backward needs for these sizes. */
+ML_API size_t ml_rms_norm_backward_workspace_bytes(int64_t rows, int64_t hidden);
+
+/*
+ * dx = g*w*r - x*mean(g*w*x)*r^3 (per row, to x dtype) and
+ * dweight = sum_rows(g * x * r) (to w dtype), all arithmetic in fp32, where
+ * r = rrms[row] if rrms != NULL else rsqrt(mean(x^2)+eps) recomputed from x.
+ * dy has x_dtype.  dweight is reduced deterministically in two stages
+ * through `workspace` (>= ml_rms_norm_backward_workspace_bytes bytes, 16-byte
+ * aligned); no [rows, hidden] per-row buffer is formed.
+ * Replaces metal_rms_norm_backward (reference csrc/metal_liger_ops.h:20-25,
+ * csrc/rms_norm_metal.mm:164-213) and _FusedRMSNormFunction.backward
+ * (ops/fused_rms_norm.py:43-60).
+ */
+ML_API int ml_rms_norm_backward(const void* x, int x_dtype, const void* weight, int w_dtype,
+                         const float* rrms, const void* dy, void* dx, void* dweight,
+                         float eps, void* workspace, size_t workspace_bytes,
+                         int64_t rows, int64_t hidden, void* stream);
+
+/* ------------------------------------------------------------------------
+ * SwiGLU
+ * ------------------------------------------------------------------------ */
+
+/*
+ * out = (silu(gate) * up).to(dtype), fp32 arithmetic; n elements, all three
+ * buffers contiguous with the same dtype.
+ * Replaces metal_swiglu_forward (reference csrc/metal_liger_ops.h:28-31,
+ * csrc/swiglu_metal.mm:66-105) and _FusedSwiGLUFunction.forward
+ * (ops/fused_swiglu.py:26-35).
+ */
+ML_API int ml_swiglu_forward(const void* gate, const void* up, void* out, int64_t n, int dtype,
+                      void* stream);
+
+/*
+ * dgate = dout*up*s*(1 + gate*(1-s)), dup = dout*gate*s with s = sigmoid(gate)
+ * recomputed in fp32 (nothing beyond gate/up is saved by the forward).
+ * Replaces metal_swiglu_backward (reference csrc/metal_liger_ops.h:33-36,
+ * csrc/swiglu_metal.mm:109-143) and _FusedSwiGLUFunction.backward
+ * (ops/fused_swiglu.py:37-50).
+ */
+ML_API int ml_swiglu_backward(const void* gate, const void* up, const void* dout, void* dgate,
+                       void* dup, int64_t n, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * RoPE (rotate-half convention)
+ * ------------------------------------------------------------------------ */
+
+/* One [batch, heads, seq, head_dim] view to rotate (strides in elements; the
+ * head_dim stride must be 1, the others are free, e.g. a transpose view). */
+typedef struct ml_rope_tensor {
+  const void* in;
+  void* out;
+  int64_t heads;
+  int64_t in_strides[4];  /* batch, head, seq, dim */
+  int64_t out_strides[4]; /* batch, head, seq, dim */
+} ml_rope_tensor;
+
+/*
+ * out = in*cos + rotate_half(in)*(sin_sign*sin) for q and (optionally) k in
+ * one launch; rotate_half([a, b]) = [-b, a].  sin_sign = +1 is the forward
+ * rotation, -1 the reference's backward (inverse) rotation.
+ * Angles come from one of two sources:
+ *   table mode  (cos != NULL): cos/sin element (b, s, d) is read at
+ *     b*cs_strides[0] + s*cs_strides[1] + d*cs_strides[2] (use stride 0 to
+ *     broadcast, e.g. a [seq, head_dim] table), dtype cs_dtype;
+ *   recompute mode (cos == NULL): angle = float(pos) * inv_freq[d mod D/2],
+ *     pos = positions[b*pos_stride_batch + s] (or s when positions == NULL),
+ *     cos/sin evaluated in fp32 in-kernel and multiplied by `scaling`.
+ * in_dtype / out_dtype may differ (torch type promotion of the reference's
+ * x*cos expression).  All arithmetic is fp32.
+ * Replaces _FusedRoPEFunction.forward/backward and _apply_rotary_fused
+ * (reference ops/fused_rope.py:22-57, :67-75) and apply_fused_rotary
+ * (ops/fused_rope.py:110-127); the reference has no native RoPE.
+ */
+ML_API int ml_rope(const ml_rope_tensor* q, const ml_rope_tensor* k, int in_dtype, int out_dtype,
+            int64_t batch, int64_t seq, int64_t head_dim,
+            const void* cos, const void* sin, int cs_dtype, const int64_t* cs_strides,
+            const int64_t* positions, int64_t pos_stride_batch, const float* inv_freq,
+            float scaling, int sin_sign, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* METAL_LIGER_B200_H_ */

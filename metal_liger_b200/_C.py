@@ -1,0 +1,141 @@
+"""ctypes binding of the C ABI in ``include/metal_liger_b200.h``.
+
+The shared library is built in-tree by ``metal_liger_b200._build`` (nvcc,
+sm_100a only).  There is no fallback: if the library is missing or a call
+fails, a ``RuntimeError`` is raised with the library's own message.  This
+module replaces the reference's pybind module ``metal_liger_ext``
+(csrc/bindings.mm:10-33); the tensor-level API lives in
+``metal_liger_b200.metal_liger_ext`` and ``metal_liger_b200._torch_library``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmetal_liger_b200.so"
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+ML_OK = 0
+ML_ERR_TIMEOUT = 4
+
+c_void_p = ctypes.c_void_p
+c_int = ctypes.c_int
+c_int64 = ctypes.c_int64
+c_float = ctypes.c_float
+c_size_t = ctypes.c_size_t
+
+
+class RopeTensor(ctypes.Structure):
+    """Mirror of ``ml_rope_tensor``."""
+
+    _fields_ = [
+        ("inp", c_void_p),
+        ("out", c_void_p),
+        ("heads", c_int64),
+        ("in_strides", c_int64 * 4),
+        ("out_strides", c_int64 * 4),
+    ]
+
+
+# name -> (restype, argtypes).  Kept in the same order as the header.
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "ml_version": (c_int, []),
+    "ml_last_error": (ctypes.c_char_p, []),
+    "ml_rms_norm_forward": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                    c_int64, c_int64, c_float, c_void_p]),
+    "ml_rms_norm_backward_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ml_rms_norm_backward": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_int64,
+                                     c_int64, c_void_p]),
+    "ml_swiglu_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "ml_swiglu_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                   c_int, c_void_p]),
+    "ml_rope": (c_int, [ctypes.POINTER(RopeTensor), ctypes.POINTER(RopeTensor), c_int, c_int,
+                        c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int,
+                        ctypes.POINTER(c_int64), c_void_p, c_int64, c_void_p, c_float, c_int,
+                        c_void_p]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load the CUDA library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"metal_liger_b200: CUDA library not found at {LIB_PATH}. Build it with "
+                "`python -m metal_liger_b200._build` (nvcc, sm_100a). There is no CPU fallback.")
+        lib = ctypes.CDLL(str(LIB_PATH), mode=os.RTLD_NOW | getattr(os, "RTLD_LOCAL", 0))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().ml_last_error()
+    return msg.decode(errors="replace") if msg else ""
+
+
+def check(status: int, what: str) -> None:
+    if status != ML_OK:
+        raise RuntimeError(f"metal_liger_b200 {what} failed (status {status}): {last_error()}")
+
+
+def call(name: str, *args) -> int:
+    """Invoke an entry point and raise on a non-zero status."""
+    fn = getattr(load(), name)
+    status = fn(*args)
+    check(status, name)
+    return status
+
+
+def dtype_code(t: torch.Tensor | torch.dtype) -> int:
+    dt = t if isinstance(t, torch.dtype) else t.dtype
+    try:
+        return DTYPE_CODES[dt]
+    except KeyError:
+        raise RuntimeError(f"metal_liger_b200: unsupported dtype {dt}") from None
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    """Raw cudaStream_t of torch's current stream on ``t``'s device."""
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(name: str, *tensors: torch.Tensor | None) -> None:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise RuntimeError(
+                f"metal_liger_b200 {name}: tensors must be on a CUDA device, got {t.device} "
+                "(there is no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"metal_liger_b200 {name}: tensors on different devices")
+
+
+def exported_symbols() -> list[str]:
+    return list(SIGNATURES)

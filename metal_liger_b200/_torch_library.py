@@ -1,0 +1,363 @@
+"""``metal_liger::`` custom operators backed by the sm_100a CUDA library.
+
+Mirrors the reference's torch.library registration (_torch_library.py:26-86)
+with two deliberate differences:
+
+* the ``torch.library.Library`` object is held at module scope.  The
+  reference builds it as a temporary inside ``torch.library.define(...,
+  lib=torch.library.Library(...))`` (_torch_library.py:47,66), so its ops
+  vanish again and a second registration raises; here registration happens
+  once at import and ``register_metal_liger_ops()`` is idempotent;
+* kernels are registered for the ``CUDA`` dispatch key (the reference used
+  ``mps``, _torch_library.py:50,69).  No CPU kernel is registered: calling an
+  op with CPU tensors raises, there is no fallback.
+
+The reference schemas ``rms_norm_forward(Tensor x, Tensor weight, float eps,
+str kernel_dir) -> (Tensor, Tensor)`` and ``swiglu_forward(Tensor gate, Tensor
+up, str kernel_dir) -> Tensor`` are kept verbatim; ``kernel_dir`` is accepted
+and ignored (kernels are compiled ahead of time).  The other ops extend the
+surface to the rest of the hot path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import logging
+
+import torch
+from torch import Tensor
+
+from metal_liger_b200 import _C
+
+logger = logging.getLogger(__name__)
+
+NAMESPACE = "metal_liger"
+_LIB = torch.library.Library(NAMESPACE, "DEF")  # module scope: keeps the ops alive
+_REGISTERED = False
+
+
+def _contig(t: Tensor) -> Tensor:
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# RMSNorm
+# ---------------------------------------------------------------------------
+
+def rms_norm_forward_cuda(x: Tensor, weight: Tensor, eps: float, kernel_dir: str = ""):
+    """(y, rrms) with y = x*rsqrt(mean(x^2)+eps)*w in fp32, rrms of shape x.shape[:-1]."""
+    _C.require_cuda("rms_norm_forward", x, weight)
+    if x.dim() < 1 or weight.dim() != 1 or weight.shape[0] != x.shape[-1]:
+        raise RuntimeError(
+            f"rms_norm_forward: weight {tuple(weight.shape)} does not match x {tuple(x.shape)}")
+    x = _contig(x)
+    weight = _contig(weight)
+    hidden = x.shape[-1]
+    rows = x.numel() // hidden if hidden else 0
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    rrms = torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device)
+    _C.call("ml_rms_norm_forward", _C.ptr(x), _C.dtype_code(x), _C.ptr(weight),
+            _C.dtype_code(weight), _C.ptr(y), _C.ptr(rrms), rows, hidden, float(eps),
+            _C.stream_of(x))
+    return y, rrms
+
+
+def rms_norm_backward_cuda(x: Tensor, weight: Tensor, grad_out: Tensor, eps: float,
+                           kernel_dir: str = "", rrms: Tensor | None = None):
+    """(dx, dweight); uses the saved fp32 ``rrms`` when given, else recomputes it."""
+    _C.require_cuda("rms_norm_backward", x, weight, grad_out, rrms)
+    if grad_out.shape != x.shape:
+        raise RuntimeError("rms_norm_backward: grad_out shape differs from x")
+    x = _contig(x)
+    weight = _contig(weight)
+    grad_out = _contig(grad_out.to(x.dtype))
+    hidden = x.shape[-1]
+    rows = x.numel() // hidden if hidden else 0
+    if rrms is not None:
+        rrms = _contig(rrms.to(torch.float32))
+        if rrms.numel() != rows:
+            raise RuntimeError("rms_norm_backward: rrms has the wrong number of rows")
+    dx = torch.empty_like(x, memory_format=torch.contiguous_format)
+    dw = torch.empty_like(weight, memory_format=torch.contiguous_format)
+    lib = _C.load()
+    ws_bytes = int(lib.ml_rms_norm_backward_workspace_bytes(rows, hidden))
+    ws = torch.empty(max(ws_bytes // 4, 4), dtype=torch.float32, device=x.device)
+    _C.call("ml_rms_norm_backward", _C.ptr(x), _C.dtype_code(x), _C.ptr(weight),
+            _C.dtype_code(weight), _C.ptr(rrms), _C.ptr(grad_out), _C.ptr(dx), _C.ptr(dw),
+            float(eps), _C.ptr(ws), ws.numel() * 4, rows, hidden, _C.stream_of(x))
+    return dx, dw
+
+
+# ---------------------------------------------------------------------------
+# SwiGLU
+# ---------------------------------------------------------------------------
+
+def swiglu_forward_cuda(gate: Tensor, up: Tensor, kernel_dir: str = "") -> Tensor:
+    _C.require_cuda("swiglu_forward", gate, up)
+    if gate.shape != up.shape:
+        raise RuntimeError("MetalLiger SwiGLU: gate and up must match")
+    gate = _contig(gate)
+    up = _contig(up.to(gate.dtype))
+    out = torch.empty_like(gate, memory_format=torch.contiguous_format)
+    _C.call("ml_swiglu_forward", _C.ptr(gate), _C.ptr(up), _C.ptr(out), gate.numel(),
+            _C.dtype_code(gate), _C.stream_of(gate))
+    return out
+
+
+def swiglu_backward_cuda(gate: Tensor, up: Tensor, grad_out: Tensor, kernel_dir: str = ""):
+    _C.require_cuda("swiglu_backward", gate, up, grad_out)
+    if gate.shape != up.shape or grad_out.shape != gate.shape:
+        raise RuntimeError("MetalLiger SwiGLU backward: gate, up and grad_out must match")
+    up_dtype = up.dtype
+    gate = _contig(gate)
+    up = _contig(up.to(gate.dtype))
+    grad_out = _contig(grad_out.to(gate.dtype))
+    dgate = torch.empty_like(gate, memory_format=torch.contiguous_format)
+    dup = torch.empty_like(gate, memory_format=torch.contiguous_format)
+    _C.call("ml_swiglu_backward", _C.ptr(gate), _C.ptr(up), _C.ptr(grad_out), _C.ptr(dgate),
+            _C.ptr(dup), gate.numel(), _C.dtype_code(gate), _C.stream_of(gate))
+    return dgate, dup.to(up_dtype)
+
+
+# ---------------------------------------------------------------------------
+# RoPE
+# ---------------------------------------------------------------------------
+
+def _as_bhsd(x: Tensor, name: str) -> Tensor:
+    if x.dim() == 4:
+        return x
+    if x.dim() == 3:
+        return x.unsqueeze(0)
+    raise RuntimeError(f"{name}: expected a [batch, heads, seq, head_dim] tensor, got {x.dim()}-D")
+
+
+def _rope_view(x: Tensor, out: Tensor) -> _C.RopeTensor:
+    v = _C.RopeTensor()
+    v.inp = x.data_ptr()
+    v.out = out.data_ptr()
+    v.heads = x.shape[1]
+    for i in range(4):
+        v.in_strides[i] = x.stride(i)
+        v.out_strides[i] = out.stride(i)
+    return v
+
+
+def _prep_rope_input(x: Tensor, name: str) -> Tensor:
+    x = _as_bhsd(x, name)
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def _cs_strides(cos: Tensor, sin: Tensor, shape: torch.Size):
+    """Broadcast cos/sin to ``shape`` ([B,H,S,D]); returns (cos, sin, strides[b,s,d])."""
+    ce = cos.expand(shape) if cos.dim() <= 4 else None
+    se = sin.expand(shape) if sin.dim() <= 4 else None
+    if ce is None or se is None:
+        raise RuntimeError("rope: cos/sin must broadcast to x")
+    if ce.stride(1) != 0 or se.stride(1) != 0:
+        # Tables that vary per head cannot share the per-position cache.
+        if torch.equal(ce[:, :1].expand(shape), ce) and torch.equal(se[:, :1].expand(shape), se):
+            ce = ce[:, :1].contiguous().expand(shape)
+            se = se[:, :1].contiguous().expand(shape)
+        else:
+            raise RuntimeError("rope: cos/sin that vary across heads are not supported")
+    if (ce.stride(0), ce.stride(2), ce.stride(3)) != (se.stride(0), se.stride(2), se.stride(3)):
+        ce = ce[:, :1].contiguous().expand(shape)
+        se = se[:, :1].contiguous().expand(shape)
+    if se.dtype != ce.dtype:
+        se = se.to(ce.dtype)
+        se = se[:, :1].contiguous().expand(shape)
+        ce = ce[:, :1].contiguous().expand(shape)
+    strides = (ctypes.c_int64 * 3)(ce.stride(0), ce.stride(2), ce.stride(3))
+    return ce, se, strides
+
+
+def _rope_launch(tensors, cos, sin, sign, positions=None, inv_freq=None, scaling=1.0,
+                 out_dtype=None):
+    first = tensors[0]
+    B, _, S, D = first.shape
+    for t in tensors[1:]:
+        if t.shape[0] != B or t.shape[2] != S or t.shape[3] != D:
+            raise RuntimeError("rope: q and k must agree on batch, seq and head_dim")
+        if t.dtype != first.dtype:
+            raise RuntimeError("rope: q and k must have the same dtype")
+    in_dtype = first.dtype
+    if out_dtype is None:
+        out_dtype = in_dtype
+    outs = [torch.empty(t.shape, dtype=out_dtype, device=t.device) for t in tensors]
+    views = [_rope_view(t, o) for t, o in zip(tensors, outs)]
+    qv = ctypes.pointer(views[0])
+    kv = ctypes.pointer(views[1]) if len(views) > 1 else None
+    if cos is not None:
+        ce, se, strides = _cs_strides(cos, sin, first.shape)
+        _C.call("ml_rope", qv, kv, _C.dtype_code(in_dtype), _C.dtype_code(out_dtype), B, S, D,
+                ce.data_ptr(), se.data_ptr(), _C.dtype_code(ce), strides, None, 0, None, 1.0,
+                int(sign), _C.stream_of(first))
+    else:
+        pos_ptr, pos_sb = None, 0
+        if positions is not None:
+            positions = positions.to(device=first.device, dtype=torch.int64)
+            if positions.dim() == 1:
+                positions = positions.unsqueeze(0)
+            if positions.shape[-1] != S or positions.shape[0] not in (1, B):
+                raise RuntimeError("rope: position_ids must be [batch, seq] or [seq]")
+            positions = positions.contiguous()
+            pos_sb = 0 if positions.shape[0] == 1 else positions.stride(0)
+            pos_ptr = positions.data_ptr()
+        inv = inv_freq.to(device=first.device, dtype=torch.float32).contiguous()
+        if inv.numel() != D // 2:
+            raise RuntimeError(f"rope: inv_freq must have head_dim/2 = {D // 2} entries")
+        _C.call("ml_rope", qv, kv, _C.dtype_code(in_dtype), _C.dtype_code(out_dtype), B, S, D,
+                None, None, 0, None, pos_ptr, pos_sb, inv.data_ptr(), float(scaling), int(sign),
+                _C.stream_of(first))
+        # keep temporaries alive until the launch is enqueued (it is, by now)
+        del positions, inv
+    return outs
+
+
+def rope_apply_cuda(x: Tensor, cos: Tensor, sin: Tensor, sin_sign: int) -> Tensor:
+    _C.require_cuda("rope_apply", x, cos, sin)
+    orig_dim = x.dim()
+    xv = _prep_rope_input(x, "rope_apply")
+    out_dtype = torch.promote_types(torch.promote_types(x.dtype, cos.dtype), sin.dtype)
+    (y,) = _rope_launch([xv], cos, sin, sin_sign, out_dtype=out_dtype)
+    return y if orig_dim == 4 else y.squeeze(0)
+
+
+def rope_apply_qk_cuda(q: Tensor, k: Tensor, cos: Tensor, sin: Tensor, sin_sign: int):
+    _C.require_cuda("rope_apply_qk", q, k, cos, sin)
+    qv = _prep_rope_input(q, "rope_apply_qk")
+    kv = _prep_rope_input(k, "rope_apply_qk")
+    out_dtype = torch.promote_types(torch.promote_types(q.dtype, cos.dtype), sin.dtype)
+    yq, yk = _rope_launch([qv, kv], cos, sin, sin_sign, out_dtype=out_dtype)
+    if q.dim() == 3:
+        yq, yk = yq.squeeze(0), yk.squeeze(0)
+    return yq, yk
+
+
+def rope_apply_pos_cuda(x: Tensor, position_ids: Tensor | None, inv_freq: Tensor,
+                        scaling: float, sin_sign: int) -> Tensor:
+    _C.require_cuda("rope_apply_pos", x, position_ids, inv_freq)
+    orig_dim = x.dim()
+    xv = _prep_rope_input(x, "rope_apply_pos")
+    (y,) = _rope_launch([xv], None, None, sin_sign, positions=position_ids, inv_freq=inv_freq,
+                        scaling=scaling)
+    return y if orig_dim == 4 else y.squeeze(0)
+
+
+def rope_apply_qk_pos_cuda(q: Tensor, k: Tensor, position_ids: Tensor | None, inv_freq: Tensor,
+                           scaling: float, sin_sign: int):
+    _C.require_cuda("rope_apply_qk_pos", q, k, position_ids, inv_freq)
+    qv = _prep_rope_input(q, "rope_apply_qk_pos")
+    kv = _prep_rope_input(k, "rope_apply_qk_pos")
+    yq, yk = _rope_launch([qv, kv], None, None, sin_sign, positions=position_ids,
+                          inv_freq=inv_freq, scaling=scaling)
+    if q.dim() == 3:
+        yq, yk = yq.squeeze(0), yk.squeeze(0)
+    return yq, yk
+
+
+# ---------------------------------------------------------------------------
+# Registration
+# ---------------------------------------------------------------------------
+
+_SCHEMAS = {
+    "rms_norm_forward": "rms_norm_forward(Tensor x, Tensor weight, float eps, str kernel_dir) "
+                        "-> (Tensor, Tensor)",
+    "rms_norm_backward": "rms_norm_backward(Tensor x, Tensor weight, Tensor grad_out, float eps, "
+                         "str kernel_dir, Tensor? rrms=None) -> (Tensor, Tensor)",
+    "swiglu_forward": "swiglu_forward(Tensor gate, Tensor up, str kernel_dir) -> Tensor",
+    "swiglu_backward": "swiglu_backward(Tensor gate, Tensor up, Tensor grad_out, str kernel_dir) "
+                       "-> (Tensor, Tensor)",
+    "rope_apply": "rope_apply(Tensor x, Tensor cos, Tensor sin, int sin_sign) -> Tensor",
+    "rope_apply_qk": "rope_apply_qk(Tensor q, Tensor k, Tensor cos, Tensor sin, int sin_sign) "
+                     "-> (Tensor, Tensor)",
+    "rope_apply_pos": "rope_apply_pos(Tensor x, Tensor? position_ids, Tensor inv_freq, "
+                      "float scaling, int sin_sign) -> Tensor",
+    "rope_apply_qk_pos": "rope_apply_qk_pos(Tensor q, Tensor k, Tensor? position_ids, "
+                         "Tensor inv_freq, float scaling, int sin_sign) -> (Tensor, Tensor)",
+}
+
+_CUDA_IMPLS = {
+    "rms_norm_forward": rms_norm_forward_cuda,
+    "rms_norm_backward": rms_norm_backward_cuda,
+    "swiglu_forward": swiglu_forward_cuda,
+    "swiglu_backward": swiglu_backward_cuda,
+    "rope_apply": rope_apply_cuda,
+    "rope_apply_qk": rope_apply_qk_cuda,
+    "rope_apply_pos": rope_apply_pos_cuda,
+    "rope_apply_qk_pos": rope_apply_qk_pos_cuda,
+}
+
+
+def _promote3(a, b, c):
+    return torch.promote_types(torch.promote_types(a.dtype, b.dtype), c.dtype)
+
+
+def _fake_impls():
+    def rms_fwd(x, weight, eps, kernel_dir):
+        return (torch.empty_like(x),
+                torch.empty(x.shape[:-1], dtype=torch.float32, device=x.device))
+
+    def rms_bwd(x, weight, grad_out, eps, kernel_dir, rrms=None):
+        return torch.empty_like(x), torch.empty_like(weight)
+
+    def swi_fwd(gate, up, kernel_dir):
+        return torch.empty_like(gate)
+
+    def swi_bwd(gate, up, grad_out, kernel_dir):
+        return torch.empty_like(gate), torch.empty_like(up)
+
+    def rope(x, cos, sin, sin_sign):
+        return torch.empty(x.shape, dtype=_promote3(x, cos, sin), device=x.device)
+
+    def rope_qk(q, k, cos, sin, sin_sign):
+        dt = _promote3(q, cos, sin)
+        return (torch.empty(q.shape, dtype=dt, device=q.device),
+                torch.empty(k.shape, dtype=dt, device=k.device))
+
+    def rope_pos(x, position_ids, inv_freq, scaling, sin_sign):
+        return torch.empty(x.shape, dtype=x.dtype, device=x.device)
+
+    def rope_qk_pos(q, k, position_ids, inv_freq, scaling, sin_sign):
+        return (torch.empty(q.shape, dtype=q.dtype, device=q.device),
+                torch.empty(k.shape, dtype=k.dtype, device=k.device))
+
+    return {
+        "rms_norm_forward": rms_fwd,
+        "rms_norm_backward": rms_bwd,
+        "swiglu_forward": swi_fwd,
+        "swiglu_backward": swi_bwd,
+        "rope_apply": rope,
+        "rope_apply_qk": rope_qk,
+        "rope_apply_pos": rope_pos,
+        "rope_apply_qk_pos": rope_qk_pos,
+    }
+
+
+def _register_all() -> None:
+    fakes = _fake_impls()
+    for name, schema in _SCHEMAS.items():
+        _LIB.define(schema)
+        _LIB.impl(name, _CUDA_IMPLS[name], "CUDA")
+        torch.library.register_fake(f"{NAMESPACE}::{name}", fakes[name], lib=_LIB)
+
+
+def register_metal_liger_ops() -> bool:
+    """Register the ``metal_liger::`` ops (idempotent).  Returns True when registered.
+
+    Mirrors reference _torch_library.py:26-86.  Registration does not load the
+    CUDA library; the first op call does, and raises if it is missing.
+    """
+    global _REGISTERED
+    if _REGISTERED:
+        return True
+    _register_all()
+    _REGISTERED = True
+    logger.debug("metal_liger_b200: registered %d metal_liger:: ops", len(_SCHEMAS))
+    return True
+
+
+def registered_op_names() -> list[str]:
+    return list(_SCHEMAS)

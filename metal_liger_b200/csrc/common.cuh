@@ -1,0 +1,135 @@
+// Shared device/host helpers for the metal_liger_b200 CUDA library.
+//
+// Every kernel in this library is compiled for sm_100a only.  Host launchers
+// are plain `extern "C"` functions (see include/metal_liger_b200.h) that take
+// raw device pointers, sizes and a cudaStream_t, and return an int status
+// (0 = ok).  The last error message is kept per host thread and can be read
+// with ml_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdarg.h>
+
+#include "../../include/metal_liger_b200.h"
+
+namespace ml {
+
+// ---------------------------------------------------------------------------
+// Error reporting (host)
+// ---------------------------------------------------------------------------
+void set_error(const char* fmt, ...);
+
+#define ML_CHECK_ARG(cond, ...)                                              \
+  do {                                                                       \
+    if (!(cond)) {                                                           \
+      ::ml::set_error(__VA_ARGS__);                                          \
+      return ML_ERR_INVALID_ARG;                                             \
+    }                                                                        \
+  } while (0)
+
+#define ML_CHECK_LAUNCH(what)                                                \
+  do {                                                                       \
+    cudaError_t _e = cudaGetLastError();                                     \
+    if (_e != cudaSuccess) {                                                 \
+      ::ml::set_error("%s: CUDA launch failed: %s", what,                    \
+                      cudaGetErrorString(_e));                               \
+      return ML_ERR_CUDA;                                                    \
+    }                                                                        \
+  } while (0)
+
+#define ML_CHECK_CUDA(call, what)                                            \
+  do {                                                                       \
+    cudaError_t _e = (call);                                                 \
+    if (_e != cudaSuccess) {                                                 \
+      ::ml::set_error("%s: %s", what, cudaGetErrorString(_e));               \
+      return ML_ERR_CUDA;                                                    \
+    }                                                                        \
+  } while (0)
+
+int num_sms();  // SM count of the current device (cached per device)
+
+inline bool aligned16(const void* p) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---------------------------------------------------------------------------
+// Element access (device): load/store one element of a runtime dtype as fp32.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) {
+  return __float2half_rn(v);
+}
+
+__device__ __forceinline__ float load_as_f32(const void* p, int64_t i, int dtype) {
+  switch (dtype) {
+    case ML_DTYPE_F32: return static_cast<const float*>(p)[i];
+    case ML_DTYPE_BF16: return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+    default: return __half2float(static_cast<const __half*>(p)[i]);
+  }
+}
+
+__device__ __forceinline__ void store_from_f32(void* p, int64_t i, int dtype, float v) {
+  switch (dtype) {
+    case ML_DTYPE_F32: static_cast<float*>(p)[i] = v; break;
+    case ML_DTYPE_BF16: static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v); break;
+    default: static_cast<__half*>(p)[i] = __float2half_rn(v); break;
+  }
+}
+
+// 16-byte vector of T: VEC = 16 / sizeof(T) elements.
+template <typename T>
+struct alignas(16) Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_vec(const T* p) {
+  Vec16<T> r;
+  *reinterpret_cast<int4*>(&r) = __ldg(reinterpret_cast<const int4*>(p));
+  return r;
+}
+
+// Streaming load: data read exactly once (evict-first in L1/L2).
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_vec_stream(const T* p) {
+  Vec16<T> r;
+  *reinterpret_cast<int4*>(&r) = __ldcs(reinterpret_cast<const int4*>(p));
+  return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_vec(T* p, const Vec16<T>& v) {
+  *reinterpret_cast<int4*>(p) = *reinterpret_cast<const int4*>(&v);
+}
+
+template <typename T>
+__device__ __forceinline__ void st_vec_stream(T* p, const Vec16<T>& v) {
+  __stcs(reinterpret_cast<int4*>(p), *reinterpret_cast<const int4*>(&v));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+}  // namespace ml

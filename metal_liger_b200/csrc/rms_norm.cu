@@ -1,0 +1,485 @@
+// RMSNorm forward/backward for sm_100a.
+//
+// Follows the math of the reference's _FusedRMSNormFunction
+// (ops/fused_rms_norm.py:30-60) and the Metal kernels it was meant to drive
+// (kernels/rms_norm.metal:22-200): fp32 accumulation, rrms saved per row,
+// analytic VJP with no recompute of x_norm.
+//
+// Launch shape (B200-first): the row is held in registers, read once with
+// 16-byte vector loads.  A CTA holds G row-groups of TPR threads; each group
+// owns one row per iteration and reduces it with warp shuffles plus one
+// shared-memory exchange.  The grid is persistent (a multiple of the SM
+// count), so the backward's dweight partials are one fp32 row per CTA,
+// reduced deterministically by a second small kernel — never a [rows, hidden]
+// per-row buffer like the reference's Metal host code (csrc/rms_norm_metal.mm:182,211).
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace ml {
+namespace {
+
+constexpr int kMaxThreads = 1024;
+
+struct RowCfg {
+  int nv = 0;       // 16-byte vectors per thread per row
+  int tpr = 0;      // threads per row
+  int groups = 0;   // rows in flight per CTA
+  bool vec = false; // false -> generic scalar kernels
+};
+
+template <typename TX>
+RowCfg pick_cfg(int64_t hidden, const void* a, const void* b, const void* c, const void* d) {
+  RowCfg cfg;
+  constexpr int VEC = 16 / sizeof(TX);
+  if (hidden % VEC != 0 || !aligned16(a) || !aligned16(b) || !aligned16(c) || !aligned16(d))
+    return cfg;
+  int64_t nvec = hidden / VEC;
+  int nv = 1;
+  while ((nvec + nv - 1) / nv > 256 && nv < 8) nv *= 2;
+  int64_t tpr = ((nvec + nv - 1) / nv + 31) / 32 * 32;
+  if (tpr > kMaxThreads) return cfg;
+  cfg.nv = nv;
+  cfg.tpr = static_cast<int>(tpr);
+  cfg.groups = std::max(1, std::min(8, kMaxThreads / cfg.tpr));
+  cfg.vec = true;
+  return cfg;
+}
+
+// Reduce `v` (and optionally `v2`) over the TPR threads of this thread's row
+// group.  `red` is a [2][32][2] shared array double-buffered by `buf` so one
+// __syncthreads per row suffices.
+__device__ __forceinline__ float2 group_sum2(float v, float v2, float (*red)[32][2], int buf,
+                                            int tpr) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  v2 = warp_sum(v2);
+  if (lane == 0) {
+    red[buf][warp][0] = v;
+    red[buf][warp][1] = v2;
+  }
+  __syncthreads();
+  const int wpg = tpr >> 5;                 // warps per group
+  const int first = (warp / wpg) * wpg;     // first warp of my group
+  float s = 0.f, s2 = 0.f;
+  for (int i = 0; i < wpg; ++i) {           // fixed order: deterministic
+    s += red[buf][first + i][0];
+    s2 += red[buf][first + i][1];
+  }
+  return make_float2(s, s2);
+}
+
+template <typename TW, int VEC>
+__device__ __forceinline__ void load_weight(const TW* w, int64_t col, int64_t hidden, float* out) {
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) out[j] = (col + j < hidden) ? to_f32(w[col + j]) : 0.f;
+}
+
+// ------------------------------- forward ----------------------------------
+template <typename TX, typename TW, int NV>
+__global__ void __launch_bounds__(kMaxThreads)
+rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
+            float* __restrict__ rrms, int64_t rows, int64_t hidden, float eps, int tpr,
+            int groups) {
+  constexpr int VEC = 16 / sizeof(TX);
+  __shared__ float red[2][32][2];
+  const int g = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const bool in_group = g < groups;
+  float wr[NV][VEC];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) load_weight<TW, VEC>(w, (int64_t)(i * tpr + t) * VEC, hidden, wr[i]);
+
+  const int64_t row_stride = (int64_t)gridDim.x * groups;
+  const int64_t niter = (rows + row_stride - 1) / row_stride;
+  const float inv_h = 1.f / (float)hidden;
+  int buf = 0;
+  for (int64_t it = 0; it < niter; ++it) {
+    const int64_t row = it * row_stride + (int64_t)blockIdx.x * groups + g;
+    const bool active = in_group && row < rows;
+    Vec16<TX> xv[NV];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (active && col < hidden) {
+        xv[i] = ld_vec_stream(x + row * hidden + col);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float f = to_f32(xv[i].v[j]);
+          ss = fmaf(f, f, ss);
+        }
+      }
+    }
+    const float tot = group_sum2(ss, 0.f, red, buf, tpr).x;
+    buf ^= 1;
+    if (!active) continue;
+    const float r = rsqrtf(tot * inv_h + eps);
+    if (t == 0 && rrms != nullptr) rrms[row] = r;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (col < hidden) {
+        Vec16<TX> o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) o.v[j] = from_f32<TX>((to_f32(xv[i].v[j]) * r) * wr[i][j]);
+        st_vec_stream(y + row * hidden + col, o);
+      }
+    }
+  }
+}
+
+// Generic path: any hidden size / alignment.  One CTA per row (grid-stride),
+// two passes over the row (the second hits L1/L2).
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(256)
+rms_fwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
+                float* __restrict__ rrms, int64_t rows, int64_t hidden, float eps) {
+  __shared__ float red[2][32][2];
+  int buf = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const TX* xr = x + row * hidden;
+    float ss = 0.f;
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      const float f = to_f32(xr[c]);
+      ss = fmaf(f, f, ss);
+    }
+    const float tot = group_sum2(ss, 0.f, red, buf, blockDim.x).x;
+    buf ^= 1;
+    const float r = rsqrtf(tot / (float)hidden + eps);
+    if (threadIdx.x == 0 && rrms != nullptr) rrms[row] = r;
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x)
+      y[row * hidden + c] = from_f32<TX>((to_f32(xr[c]) * r) * to_f32(w[c]));
+  }
+}
+
+// ------------------------------- backward ---------------------------------
+// Writes dx and one fp32 dweight partial row per CTA into `partial`
+// ([gridDim.x, hidden]).  Row groups of a CTA fold their partials together
+// through shared memory (fixed order) before the single store.
+template <typename TX, typename TW, int NV>
+__global__ void __launch_bounds__(kMaxThreads)
+rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
+            const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
+            int64_t rows, int64_t hidden, float eps, int tpr, int groups) {
+  constexpr int VEC = 16 / sizeof(TX);
+  __shared__ float red[2][32][2];
+  extern __shared__ float fold[];  // [groups][hidden] when groups > 1
+  const int g = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const bool in_group = g < groups;
+  float wr[NV][VEC];
+  float acc[NV][VEC];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    load_weight<TW, VEC>(w, (int64_t)(i * tpr + t) * VEC, hidden, wr[i]);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[i][j] = 0.f;
+  }
+  const int64_t row_stride = (int64_t)gridDim.x * groups;
+  const int64_t niter = (rows + row_stride - 1) / row_stride;
+  const float inv_h = 1.f / (float)hidden;
+  int buf = 0;
+  for (int64_t it = 0; it < niter; ++it) {
+    const int64_t row = it * row_stride + (int64_t)blockIdx.x * groups + g;
+    const bool active = in_group && row < rows;
+    Vec16<TX> xv[NV], gv[NV];
+    float ss = 0.f, gwx = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (active && col < hidden) {
+        xv[i] = ld_vec_stream(x + row * hidden + col);
+        gv[i] = ld_vec_stream(dy + row * hidden + col);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = to_f32(xv[i].v[j]);
+          ss = fmaf(xf, xf, ss);
+          gwx = fmaf(to_f32(gv[i].v[j]) * wr[i][j], xf, gwx);
+        }
+      }
+    }
+    const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
+    buf ^= 1;
+    if (!active) continue;
+    const float r = rrms != nullptr ? rrms[row] : rsqrtf(sums.x * inv_h + eps);
+    const float c = (sums.y * inv_h) * (r * r * r);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (col < hidden) {
+        Vec16<TX> o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = to_f32(xv[i].v[j]);
+          const float gf = to_f32(gv[i].v[j]);
+          o.v[j] = from_f32<TX>((gf * wr[i][j]) * r - xf * c);
+          acc[i][j] = fmaf(gf, xf * r, acc[i][j]);
+        }
+        st_vec_stream(dx + row * hidden + col, o);
+      }
+    }
+  }
+  // Fold the row groups' partials (fixed order) and store one row per CTA.
+  if (groups > 1) {
+    if (in_group) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t col = (int64_t)(i * tpr + t) * VEC;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          if (col + j < hidden) fold[(int64_t)g * hidden + col + j] = acc[i][j];
+      }
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      float s = 0.f;
+      for (int k = 0; k < groups; ++k) s += fold[(int64_t)k * hidden + c];
+      partial[(int64_t)blockIdx.x * hidden + c] = s;
+    }
+  } else if (in_group) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        if (col + j < hidden) partial[(int64_t)blockIdx.x * hidden + col + j] = acc[i][j];
+    }
+  }
+}
+
+template <typename TX, typename TW>
+__global__ void __launch_bounds__(256)
+rms_bwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
+                const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
+                int64_t rows, int64_t hidden, float eps) {
+  __shared__ float red[2][32][2];
+  // Per-CTA dweight partial lives directly in `partial` (this CTA's row):
+  // each column is owned by exactly one thread, so no races.
+  float* prow = partial + (int64_t)blockIdx.x * hidden;
+  for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) prow[c] = 0.f;
+  int buf = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const TX* xr = x + row * hidden;
+    const TX* gr = dy + row * hidden;
+    float ss = 0.f, gwx = 0.f;
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      const float xf = to_f32(xr[c]);
+      ss = fmaf(xf, xf, ss);
+      gwx = fmaf(to_f32(gr[c]) * to_f32(w[c]), xf, gwx);
+    }
+    const float2 sums = group_sum2(ss, gwx, red, buf, blockDim.x);
+    buf ^= 1;
+    const float r = rrms != nullptr ? rrms[row] : rsqrtf(sums.x / (float)hidden + eps);
+    const float cc = (sums.y / (float)hidden) * (r * r * r);
+    for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
+      const float xf = to_f32(xr[c]);
+      const float gf = to_f32(gr[c]);
+      dx[row * hidden + c] = from_f32<TX>((gf * to_f32(w[c])) * r - xf * cc);
+      prow[c] = fmaf(gf, xf * r, prow[c]);
+    }
+  }
+}
+
+// Second stage: dweight[c] = sum_p partial[p][c], fixed summation order.
+// Block (32 columns x 8 part-lanes); each lane strides over the parts, then
+// the 8 lane sums are added in order through shared memory.
+template <typename TW>
+__global__ void __launch_bounds__(256)
+rms_dw_reduce(const float* __restrict__ partial, int parts, int64_t hidden, TW* __restrict__ dw) {
+  __shared__ float s[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + tx;
+  float acc = 0.f;
+  if (c < hidden) {
+#pragma unroll 4
+    for (int p = ty; p < parts; p += 8) acc += partial[(int64_t)p * hidden + c];
+  }
+  s[ty][tx] = acc;
+  __syncthreads();
+  if (ty == 0 && c < hidden) {
+    float tot = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) tot += s[k][tx];
+    dw[c] = from_f32<TW>(tot);
+  }
+}
+
+int occupancy_grid(const void* kernel, int threads, size_t smem, int64_t work_ctas) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem) != cudaSuccess ||
+      per_sm <= 0)
+    per_sm = 1;
+  int64_t grid = (int64_t)num_sms() * per_sm;
+  if (work_ctas < grid) grid = work_ctas;
+  return static_cast<int>(std::max<int64_t>(grid, 1));
+}
+
+// Grid used by the backward; the workspace size is derived from it, so the
+// two must agree.  It depends only on sizes and the device's SM count.
+constexpr int kBwdCtasPerSm = 2;
+constexpr int kGenericGrid = 4;  // CTAs per SM for the generic kernels
+
+int64_t bwd_grid_upper_bound(int64_t rows) {
+  int64_t g = (int64_t)num_sms() * std::max(kBwdCtasPerSm, kGenericGrid);
+  return std::max<int64_t>(1, std::min<int64_t>(g, rows));
+}
+
+template <typename TX, typename TW>
+int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows, int64_t hidden,
+               float eps, cudaStream_t st) {
+  const TX* xp = static_cast<const TX*>(x);
+  const TW* wp = static_cast<const TW*>(w);
+  TX* yp = static_cast<TX*>(y);
+  RowCfg cfg = pick_cfg<TX>(hidden, x, y, x, y);
+  if (cfg.vec) {
+    const int threads = cfg.tpr * cfg.groups;
+    const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
+#define ML_FWD_CASE(NV_)                                                                   \
+  case NV_: {                                                                              \
+    auto k = rms_fwd_vec<TX, TW, NV_>;                                                     \
+    int grid = occupancy_grid((const void*)k, threads, 0, work);                           \
+    k<<<grid, threads, 0, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups); \
+    break;                                                                                 \
+  }
+    switch (cfg.nv) {
+      ML_FWD_CASE(1)
+      ML_FWD_CASE(2)
+      ML_FWD_CASE(4)
+      ML_FWD_CASE(8)
+      default: set_error("rms_norm_forward: bad config"); return ML_ERR_INVALID_ARG;
+    }
+#undef ML_FWD_CASE
+  } else {
+    int grid = static_cast<int>(std::min<int64_t>(rows, (int64_t)num_sms() * kGenericGrid));
+    rms_fwd_generic<TX, TW><<<std::max(grid, 1), 256, 0, st>>>(xp, wp, yp, rrms, rows, hidden, eps);
+  }
+  ML_CHECK_LAUNCH("rms_norm_forward");
+  return ML_OK;
+}
+
+template <typename TX, typename TW>
+int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, void* dx, void* dw,
+               float eps, float* partial, size_t partial_bytes, int64_t rows, int64_t hidden,
+               cudaStream_t st) {
+  const TX* xp = static_cast<const TX*>(x);
+  const TW* wp = static_cast<const TW*>(w);
+  const TX* gp = static_cast<const TX*>(dy);
+  TX* dxp = static_cast<TX*>(dx);
+  RowCfg cfg = pick_cfg<TX>(hidden, x, dy, dx, x);
+  int grid = 0;
+  const int64_t max_parts = static_cast<int64_t>(partial_bytes / (sizeof(float) * (size_t)hidden));
+  if (cfg.vec) {
+    const int threads = cfg.tpr * cfg.groups;
+    size_t smem = cfg.groups > 1 ? (size_t)cfg.groups * hidden * sizeof(float) : 0;
+    if (smem > 96 * 1024) {  // fold buffer too large: one row group per CTA
+      cfg.groups = 1;
+      smem = 0;
+    }
+    const int threads_eff = cfg.tpr * cfg.groups;
+    (void)threads;
+    const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
+    grid = static_cast<int>(std::min<int64_t>(
+        std::min<int64_t>(work, (int64_t)num_sms() * kBwdCtasPerSm), max_parts));
+    grid = std::max(grid, 1);
+#define ML_BWD_CASE(NV_)                                                                     \
+  case NV_: {                                                                                \
+    auto k = rms_bwd_vec<TX, TW, NV_>;                                                       \
+    if (smem > 48 * 1024)                                                                    \
+      ML_CHECK_CUDA(cudaFuncSetAttribute((const void*)k,                                     \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                                         (int)smem),                                         \
+                    "rms_norm_backward: smem attribute");                                    \
+    k<<<grid, threads_eff, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps,    \
+                                       cfg.tpr, cfg.groups);                                 \
+    break;                                                                                   \
+  }
+    switch (cfg.nv) {
+      ML_BWD_CASE(1)
+      ML_BWD_CASE(2)
+      ML_BWD_CASE(4)
+      ML_BWD_CASE(8)
+      default: set_error("rms_norm_backward: bad config"); return ML_ERR_INVALID_ARG;
+    }
+#undef ML_BWD_CASE
+  } else {
+    grid = static_cast<int>(std::min<int64_t>(
+        std::min<int64_t>(rows, (int64_t)num_sms() * kGenericGrid), max_parts));
+    grid = std::max(grid, 1);
+    rms_bwd_generic<TX, TW><<<grid, 256, 0, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps);
+  }
+  ML_CHECK_LAUNCH("rms_norm_backward");
+  const int rblocks = static_cast<int>((hidden + 31) / 32);
+  rms_dw_reduce<TW><<<rblocks, 256, 0, st>>>(partial, grid, hidden, static_cast<TW*>(dw));
+  ML_CHECK_LAUNCH("rms_norm_backward(dweight reduce)");
+  return ML_OK;
+}
+
+#define ML_DISPATCH_XW(XD, WD, FN, ...)                                             \
+  [&]() -> int {                                                                    \
+    switch ((XD) * 3 + (WD)) {                                                      \
+      case ML_DTYPE_F32 * 3 + ML_DTYPE_F32: return FN<float, float>(__VA_ARGS__);   \
+      case ML_DTYPE_F32 * 3 + ML_DTYPE_BF16: return FN<float, __nv_bfloat16>(__VA_ARGS__); \
+      case ML_DTYPE_F32 * 3 + ML_DTYPE_F16: return FN<float, __half>(__VA_ARGS__);  \
+      case ML_DTYPE_BF16 * 3 + ML_DTYPE_F32: return FN<__nv_bfloat16, float>(__VA_ARGS__); \
+      case ML_DTYPE_BF16 * 3 + ML_DTYPE_BF16:                                       \
+        return FN<__nv_bfloat16, __nv_bfloat16>(__VA_ARGS__);                       \
+      case ML_DTYPE_BF16 * 3 + ML_DTYPE_F16: return FN<__nv_bfloat16, __half>(__VA_ARGS__); \
+      case ML_DTYPE_F16 * 3 + ML_DTYPE_F32: return FN<__half, float>(__VA_ARGS__);  \
+      case ML_DTYPE_F16 * 3 + ML_DTYPE_BF16: return FN<__half, __nv_bfloat16>(__VA_ARGS__); \
+      case ML_DTYPE_F16 * 3 + ML_DTYPE_F16: return FN<__half, __half>(__VA_ARGS__); \
+    }                                                                               \
+    set_error("unsupported dtype pair (%d, %d)", (int)(XD), (int)(WD));             \
+    return ML_ERR_INVALID_ARG;                                                      \
+  }()
+
+bool valid_dtype(int d) { return d == ML_DTYPE_F32 || d == ML_DTYPE_BF16 || d == ML_DTYPE_F16; }
+
+}  // namespace
+}  // namespace ml
+
+using namespace ml;
+
+extern "C" int ml_rms_norm_forward(const void* x, int x_dtype, const void* weight, int w_dtype,
+                                   void* y, float* rrms, int64_t rows, int64_t hidden, float eps,
+                                   void* stream) {
+  ML_CHECK_ARG(valid_dtype(x_dtype) && valid_dtype(w_dtype),
+               "rms_norm_forward: bad dtype codes (%d, %d)", x_dtype, w_dtype);
+  ML_CHECK_ARG(rows >= 0 && hidden > 0, "rms_norm_forward: bad sizes rows=%lld hidden=%lld",
+               (long long)rows, (long long)hidden);
+  if (rows == 0) return ML_OK;
+  ML_CHECK_ARG(x && weight && y, "rms_norm_forward: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return ML_DISPATCH_XW(x_dtype, w_dtype, launch_fwd, x, weight, y, rrms, rows, hidden, eps, st);
+}
+
+extern "C" size_t ml_rms_norm_backward_workspace_bytes(int64_t rows, int64_t hidden) {
+  if (rows <= 0 || hidden <= 0) return 0;
+  return (size_t)bwd_grid_upper_bound(rows) * (size_t)hidden * sizeof(float);
+}
+
+extern "C" int ml_rms_norm_backward(const void* x, int x_dtype, const void* weight, int w_dtype,
+                                    const float* rrms, const void* dy, void* dx, void* dweight,
+                                    float eps, void* workspace, size_t workspace_bytes,
+                                    int64_t rows, int64_t hidden, void* stream) {
+  ML_CHECK_ARG(valid_dtype(x_dtype) && valid_dtype(w_dtype),
+               "rms_norm_backward: bad dtype codes (%d, %d)", x_dtype, w_dtype);
+  ML_CHECK_ARG(rows >= 0 && hidden > 0, "rms_norm_backward: bad sizes rows=%lld hidden=%lld",
+               (long long)rows, (long long)hidden);
+  ML_CHECK_ARG(weight && dweight, "rms_norm_backward: null weight/dweight");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    // Empty input: dweight is an empty sum.
+    const size_t wbytes = (size_t)hidden * (w_dtype == ML_DTYPE_F32 ? 4 : 2);
+    ML_CHECK_CUDA(cudaMemsetAsync(dweight, 0, wbytes, st), "rms_norm_backward: memset");
+    return ML_OK;
+  }
+  ML_CHECK_ARG(x && dy && dx, "rms_norm_backward: null pointer");
+  ML_CHECK_ARG(workspace != nullptr && aligned16(workspace),
+               "rms_norm_backward: workspace must be a non-null 16-byte aligned pointer");
+  ML_CHECK_ARG(workspace_bytes >= (size_t)hidden * sizeof(float),
+               "rms_norm_backward: workspace too small (%zu bytes)", workspace_bytes);
+  return ML_DISPATCH_XW(x_dtype, w_dtype, launch_bwd, x, weight, rrms, dy, dx, dweight, eps,
+                        static_cast<float*>(workspace), workspace_bytes, rows, hidden, st);
+}

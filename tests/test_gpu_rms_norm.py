@@ -1,0 +1,130 @@
+"""RMSNorm CUDA parity: reference fixtures, reference-test shapes, BASELINE config 0."""
+
+import pytest
+import torch
+
+from conftest import golden_names, load_golden
+from oracle import ops as O
+from tolerances import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def run_fused(x, w, eps, dy):
+    from metal_liger_b200.ops.fused_rms_norm import _FusedRMSNormFunction
+    xl = x.detach().clone().to(DEV).requires_grad_(True)
+    wl = w.detach().clone().to(DEV).requires_grad_(True)
+    y = _FusedRMSNormFunction.apply(xl, wl, eps)
+    y.backward(dy.to(DEV))
+    torch.cuda.synchronize()
+    return y.detach().cpu(), xl.grad.cpu(), wl.grad.cpu()
+
+
+@pytest.mark.parametrize("name", golden_names("rms_"))
+def test_against_reference_fixture(name):
+    d = load_golden(name)
+    y, dx, dw = run_fused(d["x"], d["w"], float(d["eps"]), d["dy"])
+    assert y.dtype == d["y"].dtype and dw.dtype == d["dw"].dtype
+    if d["x"].dtype == torch.float32:
+        assert_close(y, d["y"], rtol=1e-5, atol=1e-6, what="y")
+        assert_close(dx, d["dx"], rtol=1e-5, atol=1e-5, what="dx")
+    else:
+        assert_close(y, d["y"].float(), dtype=torch.bfloat16, what="y")
+        assert_close(dx, d["dx"].float(), dtype=torch.bfloat16, what="dx")
+    scale = d["dw"].float().abs().max().item()
+    assert_close(dw, d["dw"], rtol=1e-5 if dw.dtype == torch.float32 else 2e-2,
+                 atol=1e-5 * scale if dw.dtype == torch.float32 else 1e-2,
+                 norm_rtol=1e-5 if dw.dtype == torch.float32 else 1e-2, what="dw")
+
+
+def test_reference_test_shapes():
+    """tests/test_fused_ops.py:37-84 shapes: fwd [2,128,2048], bwd [2,16,256]."""
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(2, 128, 2048, generator=g)
+    w = torch.randn(2048, generator=g)
+    dy = torch.ones_like(x)
+    y, _, _ = run_fused(x, w, 1e-6, dy)
+    ref = O.rms_norm_forward(x, w, 1e-6)[0]
+    assert torch.allclose(ref, y, atol=1e-5, rtol=1e-4)
+    x = torch.randn(2, 16, 256, generator=g)
+    w = torch.randn(256, generator=g)
+    dy = torch.ones_like(x)  # out.sum().backward()
+    _, dx, dw = run_fused(x, w, 1e-6, dy)
+    _, rrms = O.rms_norm_forward(x, w, 1e-6)
+    rdx, rdw = O.rms_norm_backward(x, w, rrms, dy)
+    assert torch.allclose(rdx, dx, atol=1e-4, rtol=1e-3)
+    assert torch.allclose(rdw, dw, atol=1e-4, rtol=1e-3)
+
+
+def test_baseline_config_c1_full_size():
+    """x [8,1024,2048] fp32, w = 1+0.1N, eps 1e-6, dY ~ N(0,1)."""
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(8, 1024, 2048, generator=g)
+    w = 1.0 + 0.1 * torch.randn(2048, generator=g)
+    dy = torch.randn(8, 1024, 2048, generator=g)
+    y, dx, dw = run_fused(x, w, 1e-6, dy)
+    ry, rrms = O.rms_norm_forward(x, w, 1e-6)
+    rdx, rdw = O.rms_norm_backward(x, w, rrms, dy)
+    assert_close(y, ry, rtol=1e-5, atol=1e-6, what="y")
+    assert_close(dx, rdx, rtol=1e-5, atol=1e-5, what="dx")
+    assert_close(dw, rdw, rtol=1e-5, atol=1e-5 * rdw.abs().max().item(), norm_rtol=1e-6,
+                 what="dw")
+
+
+@pytest.mark.parametrize("shape,xd,wd", [
+    ((1, 1), torch.float32, torch.float32),
+    ((5, 3), torch.float32, torch.float32),
+    ((7, 4100), torch.float32, torch.float32),        # > vector-path width for fp32 NV
+    ((3, 40000), torch.float32, torch.float32),       # generic path (too wide for registers)
+    ((9, 1000), torch.bfloat16, torch.float32),
+    ((9, 1000), torch.float16, torch.float16),
+    ((33, 4096), torch.bfloat16, torch.bfloat16),     # Qwen3-VL-8B hidden
+    ((2, 3, 128), torch.bfloat16, torch.bfloat16),    # per-head q_norm/k_norm shape
+])
+def test_edge_shapes(shape, xd, wd):
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(*shape, generator=g).to(xd)
+    w = (1 + 0.1 * torch.randn(shape[-1], generator=g)).to(wd)
+    dy = torch.randn(*shape, generator=g).to(xd)
+    y, dx, dw = run_fused(x, w, 1e-6, dy)
+    ry, rrms = O.rms_norm_forward(x, w, 1e-6)
+    rdx, rdw = O.rms_norm_backward(x, w, rrms, dy)
+    low = xd != torch.float32
+    assert_close(y, ry.float(), dtype=xd, rtol=None if low else 1e-5, what="y")
+    assert_close(dx, rdx.float(), dtype=xd, rtol=None if low else 1e-5,
+                 atol=None if low else 1e-5, what="dx")
+    scale = max(rdw.float().abs().max().item(), 1.0)
+    if wd == torch.float32 and not low:
+        assert_close(dw, rdw, rtol=1e-5, atol=1e-5 * scale, what="dw")
+    else:
+        assert_close(dw, rdw.float(), rtol=2e-2, atol=1e-2 * scale, norm_rtol=1e-2, what="dw")
+
+
+def test_noncontiguous_input_and_empty():
+    from metal_liger_b200.ops.fused_rms_norm import _FusedRMSNormFunction
+    x = torch.randn(64, 32, device=DEV).t()  # non-contiguous view
+    w = torch.ones(64, device=DEV)
+    y = _FusedRMSNormFunction.apply(x, w, 1e-6)
+    ref = O.rms_norm_forward(x.cpu(), w.cpu(), 1e-6)[0]
+    assert_close(y.cpu(), ref, rtol=1e-5, atol=1e-6, what="y")
+    e = torch.empty(0, 16, device=DEV, requires_grad=True)
+    we = torch.ones(16, device=DEV, requires_grad=True)
+    out = _FusedRMSNormFunction.apply(e, we, 1e-6)
+    out.sum().backward()
+    assert out.shape == (0, 16) and we.grad.abs().sum().item() == 0
+
+
+def test_metal_liger_ext_mirror():
+    from metal_liger_b200 import metal_liger_ext as ext
+    x = torch.randn(4, 256, device=DEV)
+    w = torch.randn(256, device=DEV)
+    g = torch.randn(4, 256, device=DEV)
+    y, rc = ext.rms_norm_forward(x, w, 1e-6, "kernels")
+    dx, dw = ext.rms_norm_backward(x, w, g, 1e-6, "kernels")
+    ry, rr = O.rms_norm_forward(x.cpu(), w.cpu(), 1e-6)
+    rdx, rdw = O.rms_norm_backward(x.cpu(), w.cpu(), rr, g.cpu())
+    assert_close(y.cpu(), ry, rtol=1e-5, atol=1e-6, what="ext y")
+    assert_close(rc.cpu(), rr, rtol=1e-5, atol=1e-6, what="ext rrms")
+    assert_close(dx.cpu(), rdx, rtol=1e-5, atol=1e-5, what="ext dx")
+    assert_close(dw.cpu(), rdw, rtol=1e-5, atol=1e-5, what="ext dw")

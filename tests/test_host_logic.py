@@ -1,0 +1,61 @@
+"""Host-side logic that needs no GPU: op registration, fake kernels, no-fallback policy."""
+
+import sys
+
+import pytest
+import torch
+
+import metal_liger_b200 as ml
+from metal_liger_b200 import _torch_library as tl
+
+
+def test_registration_is_idempotent():
+    assert ml.register_metal_liger_ops() is True
+    assert ml.register_metal_liger_ops() is True
+    for name in tl.registered_op_names():
+        assert hasattr(torch.ops.metal_liger, name)
+
+
+def test_reference_schemas_kept():
+    s = str(torch.ops.metal_liger.rms_norm_forward.default._schema)
+    assert "Tensor x, Tensor weight, float eps, str kernel_dir" in s
+    s = str(torch.ops.metal_liger.swiglu_forward.default._schema)
+    assert "Tensor gate, Tensor up, str kernel_dir" in s
+
+
+def test_fake_shapes_on_meta():
+    x = torch.empty(3, 5, 16, device="meta", dtype=torch.bfloat16)
+    w = torch.empty(16, device="meta")
+    y, rrms = torch.ops.metal_liger.rms_norm_forward(x, w, 1e-6, "")
+    assert y.shape == x.shape and y.dtype == x.dtype
+    assert rrms.shape == (3, 5) and rrms.dtype == torch.float32
+    q = torch.empty(2, 4, 8, 32, device="meta", dtype=torch.bfloat16)
+    cos = torch.empty(8, 32, device="meta", dtype=torch.float32)
+    out = torch.ops.metal_liger.rope_apply(q, cos, cos, 1)
+    assert out.dtype == torch.float32  # torch promotion of x*cos, as in the reference
+
+
+@pytest.mark.parametrize("call", [
+    lambda: torch.ops.metal_liger.rms_norm_forward(torch.randn(2, 8), torch.ones(8), 1e-6, ""),
+    lambda: torch.ops.metal_liger.swiglu_forward(torch.randn(8), torch.randn(8), ""),
+    lambda: ml.ops.fused_swiglu.fused_swiglu(torch.randn(8), torch.randn(8)),
+])
+def test_cpu_tensors_fail_loudly(call):
+    with pytest.raises((NotImplementedError, RuntimeError)):
+        call()
+
+
+def test_install_alias():
+    ml.install_as_metal_liger()
+    import metal_liger  # noqa: F401
+    assert sys.modules["metal_liger"] is ml
+    from metal_liger.ops.fused_rms_norm import MetalLigerRMSNorm
+    assert MetalLigerRMSNorm is ml.MetalLigerRMSNorm
+    for k in [k for k in sys.modules if k == "metal_liger" or k.startswith("metal_liger.")]:
+        del sys.modules[k]
+
+
+def test_rms_module_repr_and_params():
+    m = ml.MetalLigerRMSNorm(16, eps=1e-5)
+    assert m.weight.shape == (16,)
+    assert "hidden_size=16" in repr(m)
