@@ -153,6 +153,50 @@ ML_API int ml_rope(const ml_rope_tensor* q, const ml_rope_tensor* k, int in_dtyp
             const int64_t* positions, int64_t pos_stride_batch, const float* inv_freq,
             float scaling, int sin_sign, void* stream);
 
+
+/* ------------------------------------------------------------------------
+ * Dense bf16 GEMM on the tcgen05 tensor cores (the building block of the
+ * FLCE and LoRA paths; the reference uses ATen matmul/addmm there,
+ * ops/fused_lora.py:69-82,142-165 and ops/fused_linear_cross_entropy.py:44,78-79)
+ * ------------------------------------------------------------------------ */
+
+/* A row-major bf16 operand.  For A (logical [M, K]): mn_major = 0 means it is
+ * stored as [M, K] (K contiguous), 1 means stored as [K, M].  For B (logical
+ * [N, K]): 0 = stored [N, K], 1 = stored [K, N].  ld = row pitch in elements
+ * (multiple of 8); ptr must be 16-byte aligned. */
+typedef struct ml_gemm_operand {
+  const void* ptr;
+  int64_t ld;
+  int mn_major;
+} ml_gemm_operand;
+
+/* One K-segment: the segments' products are summed into one accumulator. */
+typedef struct ml_gemm_segment {
+  ml_gemm_operand a;
+  ml_gemm_operand b;
+  int64_t k;
+} ml_gemm_segment;
+
+/* Scratch bytes ml_gemm_bf16 can use for split-K partials (0 = none needed). */
+ML_API size_t ml_gemm_bf16_workspace_bytes(int64_t m, int64_t n, int64_t k_total);
+
+/*
+ * D[m, n] = alpha * sum_s A_s[m, k_s] * B_s[n, k_s]^T  (+ D if beta == 1),
+ * bf16 operands, fp32 accumulation, D fp32 or bf16 (beta = 1 needs fp32 D)
+ * with row pitch ldd.  1 <= nseg <= 4; all segments share operand majorness.
+ * Uses split-K (deterministic, fixed-order reduction) when the workspace
+ * allows and the tile count is small.
+ */
+ML_API int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int nseg, void* d,
+                        int d_dtype, int64_t ldd, float alpha, float beta, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, then returns and clears the device error word set
+ * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
+ * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the
+ * synchronisation itself fails. */
+ML_API int ml_device_error(void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

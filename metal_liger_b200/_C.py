@@ -43,6 +43,18 @@ class RopeTensor(ctypes.Structure):
     ]
 
 
+class GemmOperand(ctypes.Structure):
+    """Mirror of ``ml_gemm_operand``."""
+
+    _fields_ = [("ptr", c_void_p), ("ld", c_int64), ("mn_major", c_int)]
+
+
+class GemmSegment(ctypes.Structure):
+    """Mirror of ``ml_gemm_segment``."""
+
+    _fields_ = [("a", GemmOperand), ("b", GemmOperand), ("k", c_int64)]
+
+
 # name -> (restype, argtypes).  Kept in the same order as the header.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_version": (c_int, []),
@@ -60,6 +72,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                         c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int,
                         ctypes.POINTER(c_int64), c_void_p, c_int64, c_void_p, c_float, c_int,
                         c_void_p]),
+    "ml_gemm_bf16_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "ml_gemm_bf16": (c_int, [c_int64, c_int64, ctypes.POINTER(GemmSegment), c_int, c_void_p, c_int,
+                             c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "ml_device_error": (c_int, [c_void_p]),
 }
 
 _lib = None

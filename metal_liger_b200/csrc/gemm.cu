@@ -1,0 +1,337 @@
+// Host side of the tcgen05 GEMM: tensor-map encoding, tile-width choice,
+// kernel instantiations, split-K reduction and the generic C-ABI GEMM entry.
+#include "gemm.cuh"
+
+#include <algorithm>
+#include <mutex>
+
+namespace ml {
+namespace gemm {
+
+// Device-wide error word written by bounded waits that gave up (0 = none).
+__device__ int g_device_error = 0;
+
+int* device_error_word() {
+  static std::mutex mu;
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major matrix: inner extent `inner`
+// (contiguous), outer extent `outer`, row pitch `ld` elements; box
+// {64, box_outer} with 128-byte swizzle; out-of-range elements read as zero.
+int make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld,
+             int box_outer, const char* what) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) {
+    set_error("%s: cuTensorMapEncodeTiled unavailable from the driver", what);
+    return ML_ERR_CUDA;
+  }
+  if (ptr == nullptr || !aligned16(ptr)) {
+    set_error("%s: operand pointer must be non-null and 16-byte aligned", what);
+    return ML_ERR_INVALID_ARG;
+  }
+  if (inner <= 0 || outer <= 0 || ld < inner || (ld * 2) % 16 != 0) {
+    set_error("%s: bad operand shape (inner=%lld outer=%lld ld=%lld; ld must be a multiple of 8)",
+              what, (long long)inner, (long long)outer, (long long)ld);
+    return ML_ERR_INVALID_ARG;
+  }
+  cuuint64_t gdim[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t gstride[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_outer};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), gdim, gstride,
+                   box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+    return ML_ERR_CUDA;
+  }
+  return ML_OK;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_t(const Params& prm, int grid, cudaStream_t st) {
+  auto k = gemm_kernel<BN, A_MN, B_MN>;
+  const size_t smem = Cfg<BN>::SMEM;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem);
+  });
+  if (attr_err != cudaSuccess) {
+    set_error("gemm: cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err));
+    return ML_ERR_CUDA;
+  }
+  k<<<grid, kThreads, smem, st>>>(prm);
+  ML_CHECK_LAUNCH("gemm_kernel");
+  return ML_OK;
+}
+
+template <int BN>
+int launch_bn(const Params& prm, bool a_mn, bool b_mn, int grid, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_t<BN, false, false>(prm, grid, st);
+  if (!a_mn && b_mn) return launch_t<BN, false, true>(prm, grid, st);
+  if (a_mn && !b_mn) return launch_t<BN, true, false>(prm, grid, st);
+  return launch_t<BN, true, true>(prm, grid, st);
+}
+
+}  // namespace
+
+int pick_bn(int64_t N) {
+  if (N > 128) return 256;
+  if (N > 64) return 128;
+  return 64;
+}
+
+int launch(const Problem& pr, cudaStream_t st) {
+  if (pr.M <= 0 || pr.N <= 0 || pr.nseg <= 0 || pr.nseg > kMaxSeg) {
+    set_error("gemm: bad problem (M=%lld N=%lld nseg=%d)", (long long)pr.M, (long long)pr.N,
+              pr.nseg);
+    return ML_ERR_INVALID_ARG;
+  }
+  const int bn = pr.bn ? pr.bn : pick_bn(pr.N);
+  if (bn != 64 && bn != 128 && bn != 256) {
+    set_error("gemm: bad tile width %d", bn);
+    return ML_ERR_INVALID_ARG;
+  }
+  if (pr.epi == EPI_FLCE && bn != 256) {
+    set_error("gemm: the FLCE epilogue needs 256-wide tiles");
+    return ML_ERR_INVALID_ARG;
+  }
+  Params prm;
+  memset(&prm, 0, sizeof(prm));
+  int kb_total = 0;
+  for (int s = 0; s < pr.nseg; ++s) {
+    const Seg& g = pr.seg[s];
+    if (g.K <= 0) {
+      set_error("gemm: segment %d has K=%lld", s, (long long)g.K);
+      return ML_ERR_INVALID_ARG;
+    }
+    int rc;
+    // A: logical [M, K]
+    if (!pr.a_mn)
+      rc = make_map(&prm.tma_a[s], g.a.ptr, g.K, pr.M, g.a.ld, BM, "gemm A (K-major)");
+    else
+      rc = make_map(&prm.tma_a[s], g.a.ptr, pr.M, g.K, g.a.ld, BK, "gemm A (M-major)");
+    if (rc) return rc;
+    // B: logical [N, K]
+    if (!pr.b_mn)
+      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, bn, "gemm B (K-major)");
+    else
+      rc = make_map(&prm.tma_b[s], g.b.ptr, pr.N, g.K, g.b.ld, BK, "gemm B (N-major)");
+    if (rc) return rc;
+    prm.seg_kb[s] = (int)((g.K + BK - 1) / BK);
+    kb_total += prm.seg_kb[s];
+  }
+  prm.nseg = pr.nseg;
+  prm.M = (int)pr.M;
+  prm.N = (int)pr.N;
+  prm.m_tiles = (int)((pr.M + BM - 1) / BM);
+  prm.n_tiles = (int)((pr.N + bn - 1) / bn);
+  int splits = std::max(1, std::min(pr.splits, kb_total));
+  const int kb_per = (kb_total + splits - 1) / splits;
+  splits = (kb_total + kb_per - 1) / kb_per;
+  if (pr.epi != EPI_PARTIAL && splits != 1) {
+    set_error("gemm: split-K needs the partial epilogue");
+    return ML_ERR_INVALID_ARG;
+  }
+  prm.splits = splits;
+  prm.kb_per_split = kb_per;
+  prm.kb_total = kb_total;
+  prm.raster = pr.raster;
+  prm.group_m = pr.group_m;
+  prm.epi = pr.epi;
+  prm.d_f32 = pr.d_f32 ? 1 : 0;
+  prm.D = pr.D;
+  prm.ldd = pr.ldd;
+  prm.alpha = pr.alpha;
+  prm.beta = pr.beta;
+  const int elt = (pr.epi == EPI_STORE && !pr.d_f32) || pr.epi == EPI_FLCE ? 2 : 4;
+  prm.vec_ok = aligned16(pr.D) && ((pr.ldd * elt) % 16 == 0);
+  prm.labels = pr.labels;
+  prm.ignore_index = pr.ignore_index;
+  prm.part_m = pr.part_m;
+  prm.part_s = pr.part_s;
+  prm.tgt = pr.tgt;
+  prm.vocab = pr.N;
+  prm.err = device_error_word();
+  const int64_t units = (int64_t)prm.m_tiles * prm.n_tiles * prm.splits;
+  if (units > 0x7fffffff) {
+    set_error("gemm: problem too large");
+    return ML_ERR_INVALID_ARG;
+  }
+  int grid = (int)std::min<int64_t>(units, pr.max_ctas > 0 ? pr.max_ctas : num_sms());
+  grid = std::max(grid, 1);
+  switch (bn) {
+    case 64: return launch_bn<64>(prm, pr.a_mn, pr.b_mn, grid, st);
+    case 128: return launch_bn<128>(prm, pr.a_mn, pr.b_mn, grid, st);
+    default: return launch_bn<256>(prm, pr.a_mn, pr.b_mn, grid, st);
+  }
+}
+
+}  // namespace gemm
+
+namespace {
+
+// D[m, n] = sum_s partial[s][m][n] (+ beta * D), fixed summation order.
+__global__ void splitk_reduce(const float* __restrict__ part, int splits, int64_t M, int64_t N,
+                              int64_t ldp, void* __restrict__ D, int64_t ldd, int d_f32,
+                              float beta) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - (i / N) * N;
+    float s = 0.f;
+    for (int k = 0; k < splits; ++k) s += part[((int64_t)k * M + m) * ldp + n];
+    if (d_f32) {
+      float* d = static_cast<float*>(D) + m * ldd + n;
+      *d = s + (beta != 0.f ? *d : 0.f);
+    } else {
+      __nv_bfloat16* d = static_cast<__nv_bfloat16*>(D) + m * ldd + n;
+      *d = __float2bfloat16_rn(s + (beta != 0.f ? __bfloat162float(*d) : 0.f));
+    }
+  }
+}
+
+int choose_splits(int64_t m, int64_t n, int64_t k_total, int bn) {
+  const int64_t tiles = ((m + gemm::BM - 1) / gemm::BM) * ((n + bn - 1) / bn);
+  const int64_t kb = (k_total + gemm::BK - 1) / gemm::BK;
+  const int sms = num_sms();
+  if (tiles * 2 > sms || kb < 16) return 1;
+  int64_t s = std::min<int64_t>((sms + tiles - 1) / tiles, kb / 8);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(s, 16));
+}
+
+}  // namespace
+}  // namespace ml
+
+using namespace ml;
+
+extern "C" int ml_device_error(void* stream) {
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  ML_CHECK_CUDA(cudaStreamSynchronize(st), "device_error: sync");
+  ML_CHECK_CUDA(cudaMemcpyFromSymbol(&h, gemm::g_device_error, sizeof(int)), "device_error: read");
+  if (h != 0) {
+    const int zero = 0;
+    ML_CHECK_CUDA(cudaMemcpyToSymbol(gemm::g_device_error, &zero, sizeof(int)),
+                  "device_error: clear");
+  }
+  return h;
+}
+
+extern "C" size_t ml_gemm_bf16_workspace_bytes(int64_t m, int64_t n, int64_t k_total) {
+  if (m <= 0 || n <= 0 || k_total <= 0) return 0;
+  const int s = choose_splits(m, n, k_total, gemm::pick_bn(n));
+  return s > 1 ? (size_t)s * (size_t)m * (size_t)n * sizeof(float) : 0;
+}
+
+extern "C" int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int nseg, void* d,
+                            int d_dtype, int64_t ldd, float alpha, float beta, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  ML_CHECK_ARG(m >= 0 && n >= 0, "gemm: negative sizes");
+  ML_CHECK_ARG(nseg >= 1 && nseg <= gemm::kMaxSeg, "gemm: nseg must be in [1, %d]",
+               gemm::kMaxSeg);
+  ML_CHECK_ARG(segs != nullptr, "gemm: null segment list");
+  ML_CHECK_ARG(d_dtype == ML_DTYPE_F32 || d_dtype == ML_DTYPE_BF16,
+               "gemm: output dtype must be f32 or bf16");
+  ML_CHECK_ARG(beta == 0.f || beta == 1.f, "gemm: beta must be 0 or 1");
+  ML_CHECK_ARG(ldd >= n, "gemm: ldd < n");
+  if (m == 0 || n == 0) return ML_OK;
+  ML_CHECK_ARG(d != nullptr, "gemm: null output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  gemm::Problem pr;
+  pr.M = m;
+  pr.N = n;
+  pr.nseg = nseg;
+  pr.a_mn = segs[0].a.mn_major != 0;
+  pr.b_mn = segs[0].b.mn_major != 0;
+  int64_t k_total = 0;
+  for (int s = 0; s < nseg; ++s) {
+    ML_CHECK_ARG((segs[s].a.mn_major != 0) == pr.a_mn && (segs[s].b.mn_major != 0) == pr.b_mn,
+                 "gemm: all segments must share operand majorness");
+    ML_CHECK_ARG(segs[s].k >= 0, "gemm: negative k");
+    pr.seg[s].a.ptr = segs[s].a.ptr;
+    pr.seg[s].a.ld = segs[s].a.ld;
+    pr.seg[s].b.ptr = segs[s].b.ptr;
+    pr.seg[s].b.ld = segs[s].b.ld;
+    pr.seg[s].K = segs[s].k;
+    k_total += segs[s].k;
+  }
+  if (k_total == 0 || std::all_of(segs, segs + nseg, [](const ml_gemm_segment& g) {
+        return g.k == 0;
+      })) {
+    set_error("gemm: K == 0 is not supported (scale or clear D instead)");
+    return ML_ERR_INVALID_ARG;
+  }
+  // drop empty segments
+  int w = 0;
+  for (int s = 0; s < nseg; ++s)
+    if (pr.seg[s].K > 0) pr.seg[w++] = pr.seg[s];
+  pr.nseg = w;
+  pr.d_f32 = d_dtype == ML_DTYPE_F32;
+  pr.D = d;
+  pr.ldd = ldd;
+  pr.alpha = alpha;
+  pr.beta = beta;
+  const int bn = gemm::pick_bn(n);
+  int splits = choose_splits(m, n, k_total, bn);
+  if (splits > 1 &&
+      (workspace == nullptr || !aligned16(workspace) ||
+       workspace_bytes < (size_t)splits * (size_t)m * (size_t)n * sizeof(float)))
+    splits = 1;
+  if (splits == 1) {
+    pr.epi = gemm::EPI_STORE;
+    if (!pr.d_f32 && beta != 0.f) {
+      set_error("gemm: beta=1 needs an fp32 output");
+      return ML_ERR_INVALID_ARG;
+    }
+    return gemm::launch(pr, st);
+  }
+  pr.epi = gemm::EPI_PARTIAL;
+  pr.splits = splits;
+  pr.D = workspace;
+  pr.ldd = n;
+  pr.d_f32 = true;
+  pr.beta = 0.f;
+  int rc = gemm::launch(pr, st);
+  if (rc) return rc;
+  const int64_t total = m * n;
+  int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+  splitk_reduce<<<std::max(grid, 1), 256, 0, st>>>(static_cast<const float*>(workspace), splits, m,
+                                                    n, n, d, ldd, d_dtype == ML_DTYPE_F32,
+                                                    beta);
+  ML_CHECK_LAUNCH("gemm split-K reduce");
+  return ML_OK;
+}

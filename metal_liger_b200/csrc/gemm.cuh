@@ -1,0 +1,496 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a (bf16 in, fp32 accumulate).
+//
+//   D[M, N] = alpha * sum_seg A_seg[M, K_seg] * B_seg[N, K_seg]^T  (+ epilogue)
+//
+// Each operand is given as a row-major bf16 matrix that is either "K-major"
+// (K contiguous: A as [M, K], B as [N, K]) or "MN-major" (M or N contiguous:
+// A as [K, M], B as [K, N]); both layouts are fed to the tensor core directly
+// through 128-byte-swizzled TMA tiles, so no operand is ever transposed in
+// memory.  Up to kMaxSeg K-segments (each with its own A/B tensors) are
+// accumulated into one accumulator — this is how LoRA's rank-r term joins the
+// base-weight product in the same TMEM tile, and how dQ*Wq + dK*Wk + dV*Wv
+// becomes one GEMM.
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory
+// ring, warp 1 allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from
+// one thread, warps 2-5 drain the fp32 accumulator (tcgen05.ld) and run the
+// epilogue.  The accumulator is double-buffered in TMEM (2*BN columns) so the
+// epilogue of tile i overlaps the MMAs of tile i+1.  The grid is persistent
+// (<= one CTA per SM) and walks tiles in an L2-friendly raster.
+//
+// Every mbarrier wait is bounded (see sm100::mbar_wait_bounded): on timeout
+// the CTA records an error in the library's device error word, all roles drain and the
+// kernel frees its TMEM and returns.  No TMA multicast is used.
+#pragma once
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace ml {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;       // one 128-byte swizzle row of bf16
+constexpr int kMaxSeg = 4;
+constexpr int kThreads = 192;
+
+enum Epi : int {
+  EPI_STORE = 0,        // D = alpha*acc (+ beta*D), D bf16 or fp32
+  EPI_PARTIAL = 1,      // split-K: fp32 partial [split][M][ldd] = alpha*acc
+  EPI_FLCE = 2,         // fused linear-cross-entropy logits epilogue (BN = 256)
+};
+
+// Wait sites recorded in the device error word.
+enum Site : int { SITE_PROD_EMPTY = 1, SITE_MMA_TEMPTY = 2, SITE_MMA_FULL = 3, SITE_EPI = 4,
+                  SITE_DRAIN = 5 };
+
+struct alignas(64) Params {
+  CUtensorMap tma_a[kMaxSeg];
+  CUtensorMap tma_b[kMaxSeg];
+  int seg_kb[kMaxSeg];     // k-blocks (of BK) per segment
+  int nseg;
+  int M, N;
+  int m_tiles, n_tiles, splits, kb_per_split, kb_total;
+  int raster;              // 0: M-tiles fastest, 1: N-tiles fastest
+  int group_m;             // raster 0 only: N-tile groups of this many M-tiles (0 = all)
+  int epi;
+  int d_f32;               // EPI_STORE: 1 = fp32 output, 0 = bf16 output
+  int vec_ok;              // output pointer/ld allow 16-byte stores
+  void* D;
+  int64_t ldd;
+  float alpha;
+  float beta;              // EPI_STORE with fp32 D: D = alpha*acc + beta*D (beta in {0,1})
+  // EPI_FLCE
+  const int64_t* labels;   // labels for rows [0, M) (already offset to the chunk)
+  int64_t ignore_index;
+  float* part_m;           // [n_tiles][M] tile max of the logits row
+  float* part_s;           // [n_tiles][M] sum exp(logit - tile max)
+  float* tgt;              // [M] target logit
+  int64_t vocab;           // valid logit columns (= N)
+  int* err;                // device error word (bounded-wait timeouts)
+};
+
+__device__ __forceinline__ void decode_unit(const Params& p, int unit, int& mt, int& nt, int& sp) {
+  const int tiles = p.m_tiles * p.n_tiles;
+  sp = unit / tiles;
+  int t = unit - sp * tiles;
+  if (p.raster == 1) {
+    mt = t / p.n_tiles;
+    nt = t - mt * p.n_tiles;
+  } else if (p.group_m > 0 && p.group_m < p.m_tiles) {
+    // groups of group_m M-tiles sweep all N-tiles before moving on
+    const int per_group = p.group_m * p.n_tiles;
+    const int g = t / per_group;
+    const int r = t - g * per_group;
+    const int gm0 = g * p.group_m;
+    const int gsize = min(p.group_m, p.m_tiles - gm0);
+    nt = r / gsize;
+    mt = gm0 + (r - nt * gsize);
+  } else {
+    nt = t / p.m_tiles;
+    mt = t - nt * p.m_tiles;
+  }
+}
+
+__device__ __forceinline__ void locate_kb(const Params& p, int kb, int& seg, int& kl) {
+  seg = 0;
+  kl = kb;
+#pragma unroll
+  for (int s = 0; s < kMaxSeg - 1; ++s) {
+    if (seg < p.nseg - 1 && kl >= p.seg_kb[seg]) {
+      kl -= p.seg_kb[seg];
+      ++seg;
+    }
+  }
+}
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  static constexpr uint32_t A_BYTES = BM * BK * 2;
+  static constexpr uint32_t B_BYTES = BN * BK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr size_t SMEM = 1024 /*align slack*/ + (size_t)STAGES * STAGE_BYTES + 256;
+};
+
+// ---------------------------------------------------------------------------
+// epilogue helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Store 32 consecutive columns [col0, col0+32) of one output row.
+__device__ __forceinline__ void store_row32(const Params& p, float (&v)[32], int64_t row,
+                                            int col0, float* __restrict__ partial_base) {
+  const int N = p.N;
+  if (p.epi == EPI_PARTIAL) {
+    float* dst = partial_base + row * p.ldd + col0;
+    if (p.vec_ok && col0 + 32 <= N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(dst + j) =
+            make_float4(v[j] * p.alpha, v[j + 1] * p.alpha, v[j + 2] * p.alpha, v[j + 3] * p.alpha);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = v[j] * p.alpha;
+    }
+    return;
+  }
+  if (p.d_f32) {
+    float* dst = static_cast<float*>(p.D) + row * p.ldd + col0;
+    if (p.vec_ok && col0 + 32 <= N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 o = make_float4(v[j] * p.alpha, v[j + 1] * p.alpha, v[j + 2] * p.alpha,
+                               v[j + 3] * p.alpha);
+        if (p.beta != 0.f) {
+          const float4 old = *reinterpret_cast<const float4*>(dst + j);
+          o.x += old.x;
+          o.y += old.y;
+          o.z += old.z;
+          o.w += old.w;
+        }
+        *reinterpret_cast<float4*>(dst + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = v[j] * p.alpha + (p.beta != 0.f ? dst[j] : 0.f);
+    }
+  } else {
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+    if (p.vec_ok && col0 + 32 <= N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 o;
+        o.x = pack_bf16x2(v[j] * p.alpha, v[j + 1] * p.alpha);
+        o.y = pack_bf16x2(v[j + 2] * p.alpha, v[j + 3] * p.alpha);
+        o.z = pack_bf16x2(v[j + 4] * p.alpha, v[j + 5] * p.alpha);
+        o.w = pack_bf16x2(v[j + 6] * p.alpha, v[j + 7] * p.alpha);
+        *reinterpret_cast<uint4*>(dst + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = __float2bfloat16_rn(v[j] * p.alpha);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the kernel
+// ---------------------------------------------------------------------------
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ Params p) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  constexpr uint32_t IDESC = sm100::idesc_bf16_f32(BM, BN, A_MN, B_MN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < p.nseg; ++s) {
+      sm100::tma_prefetch_desc(&p.tma_a[s]);
+      sm100::tma_prefetch_desc(&p.tma_b[s]);
+    }
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    sm100::tmem_relinquish();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_units = p.m_tiles * p.n_tiles * p.splits;
+
+  if (warp == 0) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int inflight = 0;  // stages issued but not yet known to be consumed
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        int mt, nt, sp;
+        decode_unit(p, unit, mt, nt, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, p.err, SITE_PROD_EMPTY)) {
+            ok = false;
+            break;
+          }
+          inflight = min(inflight + 1, STAGES);
+          int seg, kl;
+          locate_kb(p, kb, seg, kl);
+          const int kx = kl * BK;
+          uint64_t* bar = &full[stage];
+          sm100::mbar_arrive_expect_tx(bar, C::STAGE_BYTES);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
+          if constexpr (!A_MN) {
+            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, kx, mt * BM);
+          } else {
+            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, mt * BM, kx);
+            sm100::tma_load_2d(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, mt * BM + 64, kx);
+          }
+          if constexpr (!B_MN) {
+            sm100::tma_load_2d(b_dst, &p.tma_b[seg], bar, kx, nt * BN);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              sm100::tma_load_2d(b_dst + c * 64 * BK * 2, &p.tma_b[seg], bar, nt * BN + c * 64,
+                                 kx);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: let every issued copy land before the CTA exits (bounded).
+        int s = stage, ph = phase;
+        for (int i = 0; i < inflight; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          const uint64_t t0 = sm100::globaltimer_ns();
+          while (!sm100::mbar_try_wait(&full[s], ph) &&
+                 sm100::globaltimer_ns() - t0 < 1000000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer -----------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        int mt, nt, sp;
+        decode_unit(p, unit, mt, nt, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        if (!sm100::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err, SITE_MMA_TEMPTY)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!sm100::mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = sm100::smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sm100::sdesc_sw128(a_base + k * 2048, 64 * BK * 2, 1024)
+                                     : sm100::sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::sdesc_sw128(b_base + k * 2048, 64 * BK * 2, 1024)
+                                     : sm100::sdesc_sw128(b_base + k * 32, 16, 1024);
+            sm100::umma_bf16(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          sm100::umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        sm100::umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // ------------------------------ epilogue -------------------------------
+    const int ew = warp & 3;                 // TMEM sub-partition of this warp
+    const int rloc = ew * 32 + lane;         // row within the tile
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      int mt, nt, sp;
+      decode_unit(p, unit, mt, nt, sp);
+      bool ok = sm100::mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err, SITE_EPI);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      sm100::tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t row = (int64_t)mt * BM + rloc;
+      const bool row_ok = row < p.M;
+      if (p.epi == EPI_FLCE) {
+        if constexpr (BN == 256) {
+          constexpr float kLog2e = 1.4426950408889634f;
+          const int col_base = nt * BN;
+          const int64_t label = row_ok ? p.labels[row] : p.ignore_index;
+          const int64_t lrel = label - col_base;
+          float m = -INFINITY;
+          float tgt = 0.f;
+          bool has_tgt = false;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int col = col_base + c * 32 + j;
+              if (col < p.vocab) m = fmaxf(m, v[j]);
+              if (lrel == (int64_t)(c * 32 + j)) {
+                tgt = v[j];
+                has_tgt = true;
+              }
+            }
+          }
+          const float mb = m * kLog2e;
+          float s = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+            const int col0 = col_base + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float e = (col0 + j < p.vocab) ? sm100::fast_exp2(fmaf(v[j], kLog2e, -mb)) : 0.f;
+              s += e;
+              v[j] = e;
+            }
+            if (row_ok) {
+              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+              if (p.vec_ok && col0 + 32 <= p.vocab) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 8) {
+                  uint4 o;
+                  o.x = pack_bf16x2(v[j], v[j + 1]);
+                  o.y = pack_bf16x2(v[j + 2], v[j + 3]);
+                  o.z = pack_bf16x2(v[j + 4], v[j + 5]);
+                  o.w = pack_bf16x2(v[j + 6], v[j + 7]);
+                  *reinterpret_cast<uint4*>(dst + j) = o;
+                }
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.vocab) dst[j] = __float2bfloat16_rn(v[j]);
+              }
+            }
+          }
+          if (row_ok) {
+            p.part_m[(int64_t)nt * p.M + row] = m;
+            p.part_s[(int64_t)nt * p.M + row] = s;
+            if (has_tgt) p.tgt[row] = tgt;
+          }
+        }
+      } else {
+        float* partial_base = nullptr;
+        if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.M * p.ldd;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+          const int col0 = nt * BN + c * 32;
+          if (row_ok && col0 < p.N) store_row32(p, v, row, col0, partial_base);
+        }
+      }
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  if (warp == 1) sm100::tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+// Row-major bf16 matrix [rows, cols] with leading dimension `ld` (elements).
+struct Mat {
+  const void* ptr = nullptr;
+  int64_t rows = 0, cols = 0, ld = 0;
+};
+
+// One K-segment: logical A [M, K], logical B [N, K].
+//   a_mn = false: A stored as [M, K] (K contiguous); true: stored as [K, M].
+//   b_mn = false: B stored as [N, K];                true: stored as [K, N].
+struct Seg {
+  Mat a, b;
+  int64_t K = 0;
+};
+
+struct Problem {
+  int64_t M = 0, N = 0;
+  Seg seg[kMaxSeg];
+  int nseg = 0;
+  bool a_mn = false, b_mn = false;
+  int epi = EPI_STORE;
+  bool d_f32 = false;
+  void* D = nullptr;
+  int64_t ldd = 0;
+  float alpha = 1.f, beta = 0.f;
+  int splits = 1;      // EPI_PARTIAL only
+  int raster = 0;
+  int group_m = 0;
+  int bn = 0;          // 0 = choose
+  int max_ctas = 0;    // 0 = SM count
+  // FLCE
+  const int64_t* labels = nullptr;
+  int64_t ignore_index = -100;
+  float* part_m = nullptr;
+  float* part_s = nullptr;
+  float* tgt = nullptr;
+};
+
+// Builds tensor maps, picks the tile width and launches.  Returns ML_OK or an
+// error code (message via set_error).
+int launch(const Problem& pr, cudaStream_t stream);
+
+// Tile width the launcher would use for N (64, 128 or 256).
+int pick_bn(int64_t N);
+
+// Device address of the library's error word on the current device.
+int* device_error_word();
+
+}  // namespace gemm
+}  // namespace ml
