@@ -92,6 +92,28 @@ ML_API int ml_rms_norm_backward(const void* x, int x_dtype, const void* weight, 
                          float eps, void* workspace, size_t workspace_bytes,
                          int64_t rows, int64_t hidden, void* stream);
 
+/*
+ * Allocation-free ml_rms_norm_backward: same arguments and results, minus the
+ * workspace.  It has no counterpart in the reference; it exists for callers
+ * that cannot allocate device memory at call time -- hosts whose memory
+ * planner owns all device memory after start-up (fixed arenas), and hot loops
+ * that must not pay the implicit device synchronisation cudaMalloc/cudaFree
+ * can cause.  The dweight partials live in a static device array of 4 MiB
+ * (1,048,576 floats) that every GPU which loads this library keeps until the
+ * process exits; hidden must be <= 1,048,576 (larger returns
+ * ML_ERR_INVALID_ARG), rows are unlimited.  The first call on each device
+ * looks up the array's device address with that device current; make that
+ * first call before any stream capture.  All calls share the one array, so
+ * calls whose work overlaps on the GPU (other streams, other host threads on
+ * the same device) race and must be serialised by the caller.  Each call
+ * writes every scratch element it reads, so nothing needs clearing between
+ * calls.  Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+ML_API int ml_rms_norm_backward_noalloc(const void* x, int x_dtype, const void* weight,
+                                        int w_dtype, const float* rrms, const void* dy, void* dx,
+                                        void* dweight, float eps, int64_t rows, int64_t hidden,
+                                        void* stream);
+
 /* ------------------------------------------------------------------------
  * SwiGLU
  * ------------------------------------------------------------------------ */

@@ -65,6 +65,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_rms_norm_backward": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p, c_void_p,
                                      c_void_p, c_void_p, c_float, c_void_p, c_size_t, c_int64,
                                      c_int64, c_void_p]),
+    "ml_rms_norm_backward_noalloc": (c_int, [c_void_p, c_int, c_void_p, c_int, c_void_p,
+                                             c_void_p, c_void_p, c_void_p, c_float, c_int64,
+                                             c_int64, c_void_p]),
     "ml_swiglu_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "ml_swiglu_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                    c_int, c_void_p]),

@@ -15,6 +15,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <mutex>
 
 namespace ml {
 namespace {
@@ -436,6 +437,39 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
 
 bool valid_dtype(int d) { return d == ML_DTYPE_F32 || d == ML_DTYPE_BF16 || d == ML_DTYPE_F16; }
 
+// ---------------------------------------------------------------------------
+// Scratch for ml_rms_norm_backward_noalloc: a file-scope device array, so the
+// entry point never allocates.  Every GPU that loads this library holds it
+// (4 MiB) until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;
+static __device__ __align__(256) float g_rms_bwd_scratch[kNoAllocScratchFloats];
+
+// Device address of g_rms_bwd_scratch on the current device.  Looked up once
+// per device (with that device current) and cached; host code must never pass
+// the symbol itself to a kernel, since on the host it only names a stand-in.
+float* noalloc_scratch() {
+  static std::mutex mu;
+  static float* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("rms_norm_backward_noalloc: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_rms_bwd_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("rms_norm_backward_noalloc: cudaGetSymbolAddress failed: %s",
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    cache[dev] = static_cast<float*>(p);
+  }
+  return cache[dev];
+}
+
 }  // namespace
 }  // namespace ml
 
@@ -482,4 +516,33 @@ extern "C" int ml_rms_norm_backward(const void* x, int x_dtype, const void* weig
                "rms_norm_backward: workspace too small (%zu bytes)", workspace_bytes);
   return ML_DISPATCH_XW(x_dtype, w_dtype, launch_bwd, x, weight, rrms, dy, dx, dweight, eps,
                         static_cast<float*>(workspace), workspace_bytes, rows, hidden, st);
+}
+
+extern "C" int ml_rms_norm_backward_noalloc(const void* x, int x_dtype, const void* weight,
+                                            int w_dtype, const float* rrms, const void* dy,
+                                            void* dx, void* dweight, float eps, int64_t rows,
+                                            int64_t hidden, void* stream) {
+  ML_CHECK_ARG(valid_dtype(x_dtype) && valid_dtype(w_dtype),
+               "rms_norm_backward_noalloc: bad dtype codes (%d, %d)", x_dtype, w_dtype);
+  ML_CHECK_ARG(rows >= 0 && hidden > 0,
+               "rms_norm_backward_noalloc: bad sizes rows=%lld hidden=%lld", (long long)rows,
+               (long long)hidden);
+  ML_CHECK_ARG((size_t)hidden <= kNoAllocScratchFloats,
+               "rms_norm_backward_noalloc: hidden=%lld exceeds the static scratch limit of %zu "
+               "columns; use ml_rms_norm_backward with a workspace",
+               (long long)hidden, kNoAllocScratchFloats);
+  ML_CHECK_ARG(weight && dweight, "rms_norm_backward_noalloc: null weight/dweight");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    const size_t wbytes = (size_t)hidden * (w_dtype == ML_DTYPE_F32 ? 4 : 2);
+    ML_CHECK_CUDA(cudaMemsetAsync(dweight, 0, wbytes, st), "rms_norm_backward_noalloc: memset");
+    return ML_OK;
+  }
+  ML_CHECK_ARG(x && dy && dx, "rms_norm_backward_noalloc: null pointer");
+  float* scratch = noalloc_scratch();
+  if (scratch == nullptr) return ML_ERR_CUDA;
+  // Every partial row the reduction reads is written earlier in this same
+  // call, so the scratch needs no clearing between calls.
+  return ML_DISPATCH_XW(x_dtype, w_dtype, launch_bwd, x, weight, rrms, dy, dx, dweight, eps,
+                        scratch, kNoAllocScratchFloats * sizeof(float), rows, hidden, st);
 }
