@@ -379,16 +379,94 @@ class RmsNorm:
         O.rms_norm_backward(c["x"], c["w"], rr, c["dy"])
 
 
-WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm}
+class Flce:
+    """chunked fused linear cross-entropy, bf16, N 16384, H 2048, V 151936."""
+
+    name = "flce"
+    bound = "tensor"
+    dtype = "bf16"
+    N, H, V, CHUNK = 16384, 2048, 151936, 8192
+    dominant = "flce_forward"
+
+    def __init__(self):
+        self.tokens = self.N
+        f = 6.0 * self.N * self.H * self.V  # logits, dX and dW GEMMs once each
+        self.flops = {"flce_forward": f}
+        self.bytes = {}
+        # count, (logits GEMM, lse, transform, dX GEMM, dW GEMM, memset) per chunk, loss;
+        # backward: two scale-casts
+        self.launches_per_step = 1 + 5 * (self.N // self.CHUNK) + 1 + 2
+
+    def config(self):
+        return {"workload": "flce_bf16 (BASELINE configs[2]): hidden [16384,2048] ~N(0,1), "
+                            "lm_head W [151936,2048] ~N(0,0.02), 10% labels = -100, token "
+                            "chunk 8192, mean over non-ignored; loss + dX + dW",
+                "tokens_per_step": self.N, "hidden": self.H, "vocab": self.V,
+                "chunk_tokens": self.CHUNK, "parallelism": "single GPU (vocab-parallel is a "
+                "separate path)", "l2": "inputs larger than L2 (W 622 MB)"}
+
+    def make_inputs(self, device, seed=1236):
+        g = torch.Generator(device=device).manual_seed(seed)
+        h = torch.randn(self.N, self.H, generator=g, device=device).bfloat16()
+        w = (0.02 * torch.randn(self.V, self.H, generator=g, device=device)).bfloat16()
+        lab = torch.randint(0, self.V, (self.N,), generator=g, device=device)
+        lab[torch.randperm(self.N, generator=g, device=device)[: self.N // 10]] = -100
+        go = torch.ones((), device=device)
+        return {"h": h, "w": w, "lab": lab, "go": go}
+
+    def step(self, t, timer=plain):
+        ops = torch.ops.metal_liger
+        loss, dx, dw = timer("flce_forward", ops.flce_forward, t["h"], t["w"], t["lab"], None,
+                             -100, self.CHUNK, True, True)
+        timer("flce_backward", ops.flce_backward, t["go"], dx, dw, 1, 1)
+
+    def e2e_setup(self, device):
+        t = self.make_inputs(device, seed=79)
+        host = {k: t[k].cpu().pin_memory() for k in ("h", "w", "lab")}
+        dev = {k: torch.empty_like(t[k]) for k in ("h", "w", "lab")}
+        host_out = {"loss": torch.empty((), pin_memory=True),
+                    "dh": torch.empty_like(host["h"]).pin_memory(),
+                    "dw": torch.empty_like(host["w"]).pin_memory()}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h}
+
+    def e2e_step(self, s):
+        from metal_liger_b200.ops.fused_linear_cross_entropy import \
+            _FusedLinearCrossEntropyFunction
+
+        d, h, ho = s["dev"], s["host"], s["host_out"]
+        for k in d:
+            d[k].copy_(h[k], non_blocking=True)
+        hid = d["h"].detach().requires_grad_(True)
+        w = d["w"].detach().requires_grad_(True)
+        loss = _FusedLinearCrossEntropyFunction.apply(hid, w, d["lab"], None, -100, self.CHUNK)
+        loss.backward()
+        ho["loss"].copy_(loss.detach(), non_blocking=True)
+        ho["dh"].copy_(hid.grad, non_blocking=True)
+        ho["dw"].copy_(w.grad, non_blocking=True)
+
+    def cpu_inputs(self, tokens, seed=7):
+        g = torch.Generator().manual_seed(seed)
+        if not hasattr(self, "_cpu_w"):
+            self._cpu_w = (0.02 * torch.randn(self.V, self.H, generator=g)).bfloat16()
+        h = torch.randn(tokens, self.H, generator=g).bfloat16()
+        lab = torch.randint(0, self.V, (tokens,), generator=g)
+        lab[: tokens // 10] = -100
+        return {"h": h, "w": self._cpu_w, "lab": lab}
+
+    def cpu_step(self, c):
+        from oracle import ops as O
+
+        loss, lse, mask = O.flce_forward(c["h"], c["w"], c["lab"], None, -100, 8192)
+        O.flce_backward(c["h"], c["w"], c["lab"], lse, mask, 1.0, None, 8192)
+
+
+WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce}
 
 
 def _register_optional_workloads():
-    """FLCE / LoRA workloads live beside their ops (imported when present)."""
-    try:
-        from metal_liger_b200 import bench_workloads  # noqa: F401
-    except ImportError:
-        return
-    WORKLOADS.update(bench_workloads.WORKLOADS)
+    return
 
 
 # ---------------------------------------------------------------------------

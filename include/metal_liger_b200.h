@@ -213,6 +213,49 @@ ML_API int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int n
                         int d_dtype, int64_t ldd, float alpha, float beta, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Fused linear cross-entropy
+ * ------------------------------------------------------------------------ */
+
+/* Number of fp32 [n, h] slabs ml_flce_forward writes for dhidden (split-K). */
+ML_API int ml_flce_dx_slabs(int64_t n, int64_t h, int64_t v, int64_t chunk_tokens);
+
+/* Device scratch bytes ml_flce_forward needs (256-byte aligned buffer). */
+ML_API size_t ml_flce_workspace_bytes(int64_t n, int64_t h, int64_t v, int64_t chunk_tokens);
+
+/*
+ * Mean cross-entropy of logits = hidden @ weight^T (+ bias) over rows whose
+ * label != ignore_index, without materialising the [n, v] logits:
+ *   loss[0] = sum_r (lse_r - logit_r[label_r]) / max(#valid, 1)
+ * hidden [n, h] and weight [v, h] are bf16 row-major (h a multiple of 8);
+ * bias [v] (optional, bias_dtype) gets no gradient; labels int64 [n].
+ * When dx_slabs / dw_acc are non-NULL the gradients for grad_output = 1 are
+ * produced in the same pass (each logit is computed once):
+ *   dx_slabs: ml_flce_dx_slabs(...) fp32 slabs of [n, h] that sum to dhidden;
+ *   dw_acc:   fp32 [v, h] dweight.
+ * lse (optional) receives the per-row log-sum-exp.  Tokens are processed in
+ * chunks of chunk_tokens rows (<= 0: all rows); the result does not depend
+ * on it.  workspace: >= ml_flce_workspace_bytes(...), 256-byte aligned.
+ * Replaces _FusedLinearCrossEntropyFunction.forward/backward
+ * (reference ops/fused_linear_cross_entropy.py:39-185), which has no native
+ * kernel in the reference.
+ */
+ML_API int ml_flce_forward(const void* hidden, const void* weight, const void* bias,
+                           int bias_dtype, const int64_t* labels, int64_t n, int64_t h, int64_t v,
+                           int64_t ignore_index, int64_t chunk_tokens, float* loss, float* lse,
+                           float* dx_slabs, float* dw_acc, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of ml_flce_forward: dhidden = grad_output[0] * sum(dx_slabs) cast to
+ * dh_dtype, dweight = grad_output[0] * dw_acc cast to dw_dtype (either output
+ * may be NULL).  grad_output is a device fp32 scalar.
+ */
+ML_API int ml_flce_backward(const float* grad_output, const float* dx_slabs, int slabs,
+                            void* dhidden, int dh_dtype, int64_t n, int64_t h,
+                            const float* dw_acc, void* dweight, int dw_dtype, int64_t v,
+                            void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

@@ -78,6 +78,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemm_bf16_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "ml_gemm_bf16": (c_int, [c_int64, c_int64, ctypes.POINTER(GemmSegment), c_int, c_void_p, c_int,
                              c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "ml_flce_dx_slabs": (c_int, [c_int64, c_int64, c_int64, c_int64]),
+    "ml_flce_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "ml_flce_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int64,
+                                c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_size_t, c_void_p]),
+    "ml_flce_backward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64,
+                                 c_void_p, c_void_p, c_int, c_int64, c_void_p]),
     "ml_device_error": (c_int, [c_void_p]),
 }
 

@@ -259,6 +259,82 @@ def rope_apply_qk_pos_cuda(q: Tensor, k: Tensor, position_ids: Tensor | None, in
 
 
 # ---------------------------------------------------------------------------
+# Fused linear cross-entropy
+# ---------------------------------------------------------------------------
+
+def _bf16_2d(t: Tensor, cols: int) -> Tensor:
+    t = t.reshape(-1, cols)
+    if t.dtype != torch.bfloat16:
+        t = t.to(torch.bfloat16)
+    return _contig(t)
+
+
+def flce_forward_cuda(hidden: Tensor, weight: Tensor, labels: Tensor, bias: Tensor | None,
+                      ignore_index: int, chunk_size: int, need_dx: bool, need_dw: bool):
+    """(loss, dx_slabs, dw_acc): loss and, when requested, the fp32 gradients at
+    grad_output = 1 (dx as split-K slabs [s, N, H], dw [V, H]).
+
+    Operands enter the tensor cores as bf16 (inputs of other dtypes are cast).
+    """
+    _C.require_cuda("flce_forward", hidden, weight, labels, bias)
+    H = hidden.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != H:
+        raise RuntimeError(f"flce_forward: weight {tuple(weight.shape)} does not match hidden {H}")
+    h2 = _bf16_2d(hidden, H)
+    w2 = _bf16_2d(weight, H)
+    lab = _contig(labels.reshape(-1).to(torch.int64))
+    N, V = h2.shape[0], w2.shape[0]
+    if lab.numel() != N:
+        raise RuntimeError(f"flce_forward: {lab.numel()} labels for {N} rows")
+    b = None
+    if bias is not None:
+        b = _contig(bias.reshape(-1))
+        if b.numel() != V:
+            raise RuntimeError("flce_forward: bias must have vocab entries")
+    lib = _C.load()
+    chunk = int(chunk_size) if chunk_size and chunk_size > 0 else N
+    slabs = int(lib.ml_flce_dx_slabs(N, H, V, chunk))
+    dev = hidden.device
+    loss = torch.empty((), dtype=torch.float32, device=dev)
+    dx = torch.empty((slabs, N, H) if need_dx else (0,), dtype=torch.float32, device=dev)
+    dw = torch.empty((V, H) if need_dw else (0,), dtype=torch.float32, device=dev)
+    ws_bytes = int(lib.ml_flce_workspace_bytes(N, H, V, chunk))
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_flce_forward", _C.ptr(h2), _C.ptr(w2), _C.ptr(b),
+            _C.dtype_code(b) if b is not None else 0, _C.ptr(lab), N, H, V, int(ignore_index),
+            chunk, _C.ptr(loss), None, _C.ptr(dx) if need_dx else None,
+            _C.ptr(dw) if need_dw else None, _C.ptr(ws), ws_bytes, _C.stream_of(hidden))
+    return loss, dx, dw
+
+
+_CODE_TO_DTYPE = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}
+
+
+def flce_backward_cuda(grad_output: Tensor, dx_slabs: Tensor, dw_acc: Tensor, dh_dtype: int,
+                       dw_dtype: int):
+    """(dhidden [N, H], dweight [V, H]) = grad_output * saved gradients, cast."""
+    _C.require_cuda("flce_backward", grad_output, dx_slabs, dw_acc)
+    g = _contig(grad_output.reshape(1).to(torch.float32))
+    dev = grad_output.device
+    dh = torch.empty(0, device=dev)
+    dwt = torch.empty(0, device=dev)
+    n = h = v = 0
+    slabs = 1
+    if dx_slabs.numel():
+        slabs, n, h = dx_slabs.shape
+        dh = torch.empty((n, h), dtype=_CODE_TO_DTYPE[dh_dtype], device=dev)
+    if dw_acc.numel():
+        v, h = dw_acc.shape
+        dwt = torch.empty((v, h), dtype=_CODE_TO_DTYPE[dw_dtype], device=dev)
+    if dx_slabs.numel() or dw_acc.numel():
+        _C.call("ml_flce_backward", _C.ptr(g), _C.ptr(dx_slabs) if dx_slabs.numel() else None,
+                slabs, _C.ptr(dh) if dh.numel() else None, dh_dtype, n, max(h, 1),
+                _C.ptr(dw_acc) if dw_acc.numel() else None, _C.ptr(dwt) if dwt.numel() else None,
+                dw_dtype, v, _C.stream_of(grad_output))
+    return dh, dwt
+
+
+# ---------------------------------------------------------------------------
 # Registration
 # ---------------------------------------------------------------------------
 
@@ -277,6 +353,11 @@ _SCHEMAS = {
                       "float scaling, int sin_sign) -> Tensor",
     "rope_apply_qk_pos": "rope_apply_qk_pos(Tensor q, Tensor k, Tensor? position_ids, "
                          "Tensor inv_freq, float scaling, int sin_sign) -> (Tensor, Tensor)",
+    "flce_forward": "flce_forward(Tensor hidden, Tensor weight, Tensor labels, Tensor? bias, "
+                    "int ignore_index, int chunk_size, bool need_dx, bool need_dw) "
+                    "-> (Tensor, Tensor, Tensor)",
+    "flce_backward": "flce_backward(Tensor grad_output, Tensor dx_slabs, Tensor dw_acc, "
+                     "int dh_dtype, int dw_dtype) -> (Tensor, Tensor)",
 }
 
 _CUDA_IMPLS = {
@@ -288,6 +369,8 @@ _CUDA_IMPLS = {
     "rope_apply_qk": rope_apply_qk_cuda,
     "rope_apply_pos": rope_apply_pos_cuda,
     "rope_apply_qk_pos": rope_apply_qk_pos_cuda,
+    "flce_forward": flce_forward_cuda,
+    "flce_backward": flce_backward_cuda,
 }
 
 
@@ -324,7 +407,27 @@ def _fake_impls():
         return (torch.empty(q.shape, dtype=q.dtype, device=q.device),
                 torch.empty(k.shape, dtype=k.dtype, device=k.device))
 
+    def flce_fwd(hidden, weight, labels, bias, ignore_index, chunk_size, need_dx, need_dw):
+        H = hidden.shape[-1]
+        N = hidden.numel() // H
+        V = weight.shape[0]
+        dev = hidden.device
+        slabs = 1  # shape-only estimate for tracing
+        return (torch.empty((), dtype=torch.float32, device=dev),
+                torch.empty((slabs, N, H) if need_dx else (0,), dtype=torch.float32, device=dev),
+                torch.empty((V, H) if need_dw else (0,), dtype=torch.float32, device=dev))
+
+    def flce_bwd(grad_output, dx_slabs, dw_acc, dh_dtype, dw_dtype):
+        dev = grad_output.device
+        dh = (torch.empty(dx_slabs.shape[1:], dtype=_CODE_TO_DTYPE[dh_dtype], device=dev)
+              if dx_slabs.dim() == 3 else torch.empty(0, device=dev))
+        dw = (torch.empty(dw_acc.shape, dtype=_CODE_TO_DTYPE[dw_dtype], device=dev)
+              if dw_acc.dim() == 2 else torch.empty(0, device=dev))
+        return dh, dw
+
     return {
+        "flce_forward": flce_fwd,
+        "flce_backward": flce_bwd,
         "rms_norm_forward": rms_fwd,
         "rms_norm_backward": rms_bwd,
         "swiglu_forward": swi_fwd,

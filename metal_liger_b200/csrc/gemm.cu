@@ -185,6 +185,9 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.part_s = pr.part_s;
   prm.tgt = pr.tgt;
   prm.vocab = pr.N;
+  prm.bias = pr.bias;
+  prm.bias_dtype = pr.bias_dtype;
+  prm.split_stride = pr.split_stride ? pr.split_stride : pr.M * pr.ldd;
   prm.err = device_error_word();
   const int64_t units = (int64_t)prm.m_tiles * prm.n_tiles * prm.splits;
   if (units > 0x7fffffff) {

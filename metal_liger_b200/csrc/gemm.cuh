@@ -58,6 +58,7 @@ struct alignas(64) Params {
   int vec_ok;              // output pointer/ld allow 16-byte stores
   void* D;
   int64_t ldd;
+  int64_t split_stride;    // EPI_PARTIAL: elements between split slabs
   float alpha;
   float beta;              // EPI_STORE with fp32 D: D = alpha*acc + beta*D (beta in {0,1})
   // EPI_FLCE
@@ -67,6 +68,8 @@ struct alignas(64) Params {
   float* part_s;           // [n_tiles][M] sum exp(logit - tile max)
   float* tgt;              // [M] target logit
   int64_t vocab;           // valid logit columns (= N)
+  const void* bias;        // optional [vocab] logit bias (EPI_FLCE)
+  int bias_dtype;
   int* err;                // device error word (bounded-wait timeouts)
 };
 
@@ -178,6 +181,14 @@ __device__ __forceinline__ void store_row32(const Params& p, float (&v)[32], int
       for (int j = 0; j < 32; ++j)
         if (col0 + j < N) dst[j] = __float2bfloat16_rn(v[j] * p.alpha);
     }
+  }
+}
+
+__device__ __forceinline__ void add_bias32(const Params& p, float (&v)[32], int col0) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int col = col0 + j;
+    if (col < p.vocab) v[j] += load_as_f32(p.bias, col, p.bias_dtype);
   }
 }
 
@@ -369,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           for (int c = 0; c < BN / 32; ++c) {
             float v[32];
             sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+            if (p.bias != nullptr) add_bias32(p, v, col_base + c * 32);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const int col = col_base + c * 32 + j;
@@ -386,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             float v[32];
             sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
             const int col0 = col_base + c * 32;
+            if (p.bias != nullptr) add_bias32(p, v, col0);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               const float e = (col0 + j < p.vocab) ? sm100::fast_exp2(fmaf(v[j], kLog2e, -mb)) : 0.f;
@@ -418,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         }
       } else {
         float* partial_base = nullptr;
-        if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.M * p.ldd;
+        if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.split_stride;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           float v[32];
@@ -480,6 +493,9 @@ struct Problem {
   float* part_m = nullptr;
   float* part_s = nullptr;
   float* tgt = nullptr;
+  const void* bias = nullptr;
+  int bias_dtype = 0;
+  int64_t split_stride = 0;   // EPI_PARTIAL; 0 = M * ldd
 };
 
 // Builds tensor maps, picks the tile width and launches.  Returns ML_OK or an
