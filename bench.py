@@ -462,7 +462,142 @@ class Flce:
         O.flce_backward(c["h"], c["w"], c["lab"], lse, mask, 1.0, None, 8192)
 
 
-WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce}
+class Lora:
+    """fused LoRA QKV + MLP fwd+bwd, bf16, X [8,2048,4096], r=16, alpha=32."""
+
+    name = "lora"
+    bound = "tensor"
+    dtype = "bf16"
+    T, H, I, R, S = 8 * 2048, 4096, 12288, 16, 2.0
+    QO, KVO = 4096, 1024
+    dominant = "lora_mlp_backward"
+
+    def __init__(self):
+        T, H, I, r = self.T, self.H, self.I, self.R
+        self.tokens = T
+        qkv_o = self.QO + 2 * self.KVO
+        lora_f = lambda i, o: 2 * r * (i + o)  # noqa: E731  x A^T and U B^T
+        self.flops = {
+            "lora_qkv_forward": T * (2 * H * qkv_o + sum(lora_f(H, o) for o in
+                                                         (self.QO, self.KVO, self.KVO))),
+            "lora_qkv_backward": T * (2 * H * qkv_o + sum(2 * r * (2 * o + 2 * H) for o in
+                                                          (self.QO, self.KVO, self.KVO))),
+            "lora_mlp_forward": T * (3 * 2 * H * I + 2 * lora_f(H, I) + lora_f(I, H)),
+            "lora_mlp_backward": T * (3 * 2 * H * I + 2 * 2 * r * (2 * I + 2 * H) +
+                                      2 * r * (2 * H + 2 * I)),
+        }
+        self.bytes = {}
+        # GEMM + pack launches per op (counted from csrc/lora.cu)
+        self.launches_per_step = (4 + 4) + (1 + 3 * 2 + 2 + 2 + 3 * 2 + 3) + \
+            (6 + 4 + 1 + 1) + (5 + 6 + 2 + 1 + 1 + 4 + 2 + 4)
+
+    def config(self):
+        return {"workload": "lora_bf16 (BASELINE configs[3]): X [8,2048,4096]; Wq [4096,4096], "
+                            "Wk/Wv [1024,4096], Wgate/Wup [12288,4096], Wdown [4096,12288] "
+                            "~N(0,0.02); r=16, alpha=32; QKV + MLP forward and backward "
+                            "(dX, dA, dB of all 6 adapters)",
+                "tokens_per_step": self.T, "hidden": self.H, "intermediate": self.I,
+                "rank": self.R, "parallelism": "replicas (token rows; no collective)",
+                "l2": "inputs larger than L2 (X 128 MB, Wgate/Wup/Wdown 100 MB each)"}
+
+    def _proj(self, g, o, i, device):
+        w = (0.02 * torch.randn(o, i, generator=g, device=device)).bfloat16()
+        a = (0.01 * torch.randn(self.R, i, generator=g, device=device)).bfloat16()
+        b = (0.01 * torch.randn(o, self.R, generator=g, device=device)).bfloat16()
+        return w, a, b
+
+    def make_inputs(self, device, seed=1237):
+        g = torch.Generator(device=device).manual_seed(seed)
+        T, H, I = self.T, self.H, self.I
+        t = {"x": torch.randn(T, H, generator=g, device=device).bfloat16()}
+        t["q"], t["k"], t["v"] = (self._proj(g, o, H, device) for o in (self.QO, self.KVO,
+                                                                          self.KVO))
+        t["g"], t["u"] = self._proj(g, I, H, device), self._proj(g, I, H, device)
+        t["d"] = self._proj(g, H, I, device)
+        for name, o in (("dq", self.QO), ("dk", self.KVO), ("dv", self.KVO), ("dy", H)):
+            t[name] = torch.randn(T, o, generator=g, device=device).bfloat16()
+        return t
+
+    def step(self, t, timer=plain):
+        ops = torch.ops.metal_liger
+        s3 = [self.S] * 3
+        qkv = (*t["q"], *t["k"], *t["v"])
+        Q, K, V, U = timer("lora_qkv_forward", ops.lora_qkv_forward, t["x"], *qkv, s3)
+        timer("lora_qkv_backward", ops.lora_qkv_backward, t["x"], U, *qkv, s3, t["dq"], t["dk"],
+              t["dv"])
+        mlp = (*t["g"], *t["u"], *t["d"])
+        out, gate, up, h, u1, u2 = timer("lora_mlp_forward", ops.lora_mlp_forward, t["x"], *mlp,
+                                         s3)
+        timer("lora_mlp_backward", ops.lora_mlp_backward, t["x"], gate, up, h, u1, u2, *mlp, s3,
+              t["dy"])
+
+    def e2e_setup(self, device):
+        t = self.make_inputs(device, seed=80)
+        names = ("x", "dq", "dk", "dv", "dy")
+        host = {k: t[k].cpu().pin_memory() for k in names}
+        dev = {k: torch.empty_like(t[k]) for k in names}
+        T, H = self.T, self.H
+        outs = {"Q": (T, self.QO), "K": (T, self.KVO), "V": (T, self.KVO), "out": (T, H),
+                "dx_qkv": (T, H), "dx_mlp": (T, H)}
+        host_out = {k: torch.empty(s, dtype=torch.bfloat16, pin_memory=True)
+                    for k, s in outs.items()}
+        for i, (o, fin) in enumerate(((self.QO, H), (self.KVO, H), (self.KVO, H), (self.I, H),
+                                      (self.I, H), (H, self.I))):
+            host_out[f"dA{i}"] = torch.empty((self.R, fin), pin_memory=True)
+            host_out[f"dB{i}"] = torch.empty((o, self.R), pin_memory=True)
+        params = {k: t[k] for k in ("q", "k", "v", "g", "u", "d")}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        return {"host": host, "dev": dev, "host_out": host_out, "params": params, "h2d": h2d,
+                "d2h": d2h}
+
+    def e2e_step(self, s):
+        from metal_liger_b200.ops.fused_lora import _LoRA_MLP, _LoRA_QKV
+
+        d, h, ho, P = s["dev"], s["host"], s["host_out"], s["params"]
+        for k in d:
+            d[k].copy_(h[k], non_blocking=True)
+        leaves = {}
+        for k in ("q", "k", "v", "g", "u", "d"):
+            w, a, b = P[k]
+            leaves[k] = (w, a.detach().requires_grad_(True), b.detach().requires_grad_(True),
+                         self.S)
+        x = d["x"].detach().requires_grad_(True)
+        Q, K, V = _LoRA_QKV.apply(x, *leaves["q"], *leaves["k"], *leaves["v"])
+        torch.autograd.backward([Q, K, V], [d["dq"], d["dk"], d["dv"]])
+        x2 = d["x"].detach().requires_grad_(True)
+        out = _LoRA_MLP.apply(x2, *leaves["g"], *leaves["u"], *leaves["d"])
+        out.backward(d["dy"])
+        for name, src in (("Q", Q), ("K", K), ("V", V), ("out", out), ("dx_qkv", x.grad),
+                          ("dx_mlp", x2.grad)):
+            ho[name].copy_(src.detach(), non_blocking=True)
+        for i, k in enumerate(("q", "k", "v", "g", "u", "d")):
+            ho[f"dA{i}"].copy_(leaves[k][1].grad.float(), non_blocking=True)
+            ho[f"dB{i}"].copy_(leaves[k][2].grad.float(), non_blocking=True)
+
+    def cpu_inputs(self, tokens, seed=8):
+        g = torch.Generator().manual_seed(seed)
+        if not hasattr(self, "_cpu_p"):
+            self._cpu_p = {k: (*self._proj(g, o, i, "cpu"), self.S) for k, o, i in
+                           (("q", self.QO, self.H), ("k", self.KVO, self.H),
+                            ("v", self.KVO, self.H), ("g", self.I, self.H), ("u", self.I, self.H),
+                            ("d", self.H, self.I))}
+        c = {"x": torch.randn(tokens, self.H, generator=g).bfloat16()}
+        for name, o in (("dq", self.QO), ("dk", self.KVO), ("dv", self.KVO), ("dy", self.H)):
+            c[name] = torch.randn(tokens, o, generator=g).bfloat16()
+        return c
+
+    def cpu_step(self, c):
+        from oracle import ops as O
+
+        P = self._cpu_p
+        O.lora_qkv_forward(c["x"], P["q"], P["k"], P["v"])
+        O.lora_qkv_backward(c["x"], P["q"], P["k"], P["v"], c["dq"], c["dk"], c["dv"])
+        O.lora_mlp_forward(c["x"], P["g"], P["u"], P["d"])
+        O.lora_mlp_backward(c["x"], P["g"], P["u"], P["d"], c["dy"])
+
+
+WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce, "lora": Lora}
 
 
 def _register_optional_workloads():

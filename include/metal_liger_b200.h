@@ -256,6 +256,76 @@ ML_API int ml_flce_backward(const float* grad_output, const float* dx_slabs, int
                             const float* dw_acc, void* dweight, int dw_dtype, int64_t v,
                             void* stream);
 
+/* ------------------------------------------------------------------------
+ * Fused LoRA QKV / MLP
+ * ------------------------------------------------------------------------ */
+
+/* One LoRA-adapted projection y = x W^T + scaling * (x A^T) B^T. */
+typedef struct ml_lora_proj {
+  const void* w;         /* frozen base weight [out_features, in_features], bf16 */
+  const void* a;         /* lora_A [rank, in_features], dtype a_dtype */
+  const void* b;         /* lora_B [out_features, rank], dtype b_dtype */
+  int a_dtype;
+  int b_dtype;
+  int64_t out_features;
+  float scaling;
+} ml_lora_proj;
+
+/* Workspace bytes (256-byte aligned buffer) for ml_lora_qkv_forward
+ * (backward = 0) or ml_lora_qkv_backward (backward = 1). */
+ML_API size_t ml_lora_qkv_workspace_bytes(int64_t tokens, int64_t in_features,
+                                          const ml_lora_proj* proj, int backward);
+
+/*
+ * Q, K, V for proj[0..2] sharing one input x [tokens, in_features] (bf16):
+ * out[i] [tokens, out_i] bf16.  Also writes u [tokens, 64] bf16, the stacked
+ * x A_i^T (adapter i in columns [i*rank, (i+1)*rank)) that the backward
+ * reuses.  rank <= 21.  Replaces _LoRA_QKV.forward (reference
+ * ops/fused_lora.py:96-119) and _lora_linear (:69-82).
+ */
+ML_API int ml_lora_qkv_forward(const void* x, int64_t tokens, int64_t in_features, int64_t rank,
+                               const ml_lora_proj* proj, void* const* out, void* u,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of ml_lora_qkv_forward for upstream dy[0..2] (bf16): dx [tokens,
+ * in] bf16 = sum_i dy_i W_i + s_i (dy_i B_i) A_i (one GEMM), and per adapter
+ * da[i] [rank, in] = s_i (dy_i B_i)^T x, db[i] [out_i, rank] = s_i dy_i^T u_i,
+ * both fp32.  W gets no gradient.  Replaces _LoRA_QKV.backward (reference
+ * ops/fused_lora.py:121-171).
+ */
+ML_API int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens, int64_t in_features,
+                                int64_t rank, const ml_lora_proj* proj, const void* const* dy,
+                                void* dx, float* const* da, float* const* db, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* Workspace bytes for the MLP entry points (backward = 0 or 1). */
+ML_API size_t ml_lora_mlp_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
+                                          int backward);
+
+/*
+ * LoRA SwiGLU MLP, proj = {gate [inter x hidden], up [inter x hidden],
+ * down [hidden x inter]}: gate, up [tokens, inter]; h = silu(gate) * up (fp32
+ * math, bf16 out); out [tokens, hidden] = down(h).  u1 / u2 [tokens, 64]
+ * receive x [Ag;Au]^T and h Ad^T for the backward.  rank <= 32.  Replaces
+ * _LoRA_MLP.forward (reference ops/fused_lora.py:182-207).
+ */
+ML_API int ml_lora_mlp_forward(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
+                               int64_t rank, const ml_lora_proj* proj, void* gate, void* up,
+                               void* h, void* out, void* u1, void* u2, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Backward of ml_lora_mlp_forward: dx [tokens, hidden] bf16 and fp32 da[i]
+ * [rank, in_i], db[i] [out_i, rank] for gate, up, down.  Replaces
+ * _LoRA_MLP.backward (reference ops/fused_lora.py:209-266).
+ */
+ML_API int ml_lora_mlp_backward(const void* x, const void* gate, const void* up, const void* h,
+                                const void* u1, const void* u2, int64_t tokens, int64_t hidden,
+                                int64_t inter, int64_t rank, const ml_lora_proj* proj,
+                                const void* dy, void* dx, float* const* da, float* const* db,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

@@ -55,6 +55,13 @@ class GemmSegment(ctypes.Structure):
     _fields_ = [("a", GemmOperand), ("b", GemmOperand), ("k", c_int64)]
 
 
+class LoraProj(ctypes.Structure):
+    """Mirror of ``ml_lora_proj``."""
+
+    _fields_ = [("w", c_void_p), ("a", c_void_p), ("b", c_void_p), ("a_dtype", c_int),
+                ("b_dtype", c_int), ("out_features", c_int64), ("scaling", c_float)]
+
+
 # name -> (restype, argtypes).  Kept in the same order as the header.
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_version": (c_int, []),
@@ -85,6 +92,22 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 c_void_p, c_size_t, c_void_p]),
     "ml_flce_backward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64,
                                  c_void_p, c_void_p, c_int, c_int64, c_void_p]),
+    "ml_lora_qkv_workspace_bytes": (c_size_t, [c_int64, c_int64, ctypes.POINTER(LoraProj), c_int]),
+    "ml_lora_qkv_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, ctypes.POINTER(LoraProj),
+                                    ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_size_t,
+                                    c_void_p]),
+    "ml_lora_qkv_backward": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                     ctypes.POINTER(LoraProj), ctypes.POINTER(c_void_p), c_void_p,
+                                     ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_void_p,
+                                     c_size_t, c_void_p]),
+    "ml_lora_mlp_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
+    "ml_lora_mlp_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64,
+                                    ctypes.POINTER(LoraProj), c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ml_lora_mlp_backward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_int64, c_int64, c_int64, c_int64, ctypes.POINTER(LoraProj),
+                                     c_void_p, c_void_p, ctypes.POINTER(c_void_p),
+                                     ctypes.POINTER(c_void_p), c_void_p, c_size_t, c_void_p]),
     "ml_device_error": (c_int, [c_void_p]),
 }
 

@@ -25,12 +25,26 @@ register_metal_liger_ops()
 from metal_liger_b200.ops.fused_rms_norm import MetalLigerRMSNorm  # noqa: E402
 from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU  # noqa: E402
 from metal_liger_b200.ops.fused_rope import MetalLigerRoPE  # noqa: E402
+from metal_liger_b200.ops.fused_linear_cross_entropy import (  # noqa: E402
+    MetalLigerFusedLinearCrossEntropy,
+)
+from metal_liger_b200.ops.fused_lora import (  # noqa: E402
+    apply_fused_lora_qkv,
+    apply_fused_lora_mlp,
+    patch_fused_lora,
+)
+from metal_liger_b200.patch import apply_metal_liger_to_qwen3vl  # noqa: E402
 from metal_liger_b200._compile import apply_compile  # noqa: E402
 
 __all__ = [
     "MetalLigerRMSNorm",
     "MetalLigerSwiGLU",
     "MetalLigerRoPE",
+    "MetalLigerFusedLinearCrossEntropy",
+    "apply_metal_liger_to_qwen3vl",
+    "apply_fused_lora_qkv",
+    "apply_fused_lora_mlp",
+    "patch_fused_lora",
     "apply_compile",
     "register_metal_liger_ops",
     "install_as_metal_liger",

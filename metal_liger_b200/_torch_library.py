@@ -335,6 +335,144 @@ def flce_backward_cuda(grad_output: Tensor, dx_slabs: Tensor, dw_acc: Tensor, dh
 
 
 # ---------------------------------------------------------------------------
+# Fused LoRA
+# ---------------------------------------------------------------------------
+
+def _lora_proj(w: Tensor, a: Tensor, b: Tensor, scaling: float, keep: list) -> _C.LoraProj:
+    w = _contig(w if w.dtype == torch.bfloat16 else w.to(torch.bfloat16))
+    a = _contig(a)
+    b = _contig(b)
+    keep += [w, a, b]
+    p = _C.LoraProj()
+    p.w, p.a, p.b = w.data_ptr(), a.data_ptr(), b.data_ptr()
+    p.a_dtype, p.b_dtype = _C.dtype_code(a), _C.dtype_code(b)
+    p.out_features = w.shape[0]
+    p.scaling = float(scaling)
+    return p
+
+
+def _ptr_array(tensors):
+    arr = (ctypes.c_void_p * len(tensors))()
+    for i, t in enumerate(tensors):
+        arr[i] = t.data_ptr()
+    return arr
+
+
+def _check_rank(a_list, b_list, in_list):
+    r = a_list[0].shape[0]
+    for a, b, fin in zip(a_list, b_list, in_list):
+        if a.dim() != 2 or b.dim() != 2 or a.shape[0] != r or b.shape[1] != r or a.shape[1] != fin:
+            raise RuntimeError("lora: A must be [rank, in] and B [out, rank] with one shared rank")
+    return r
+
+
+def lora_qkv_forward_cuda(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
+    _C.require_cuda("lora_qkv_forward", x, qw, qa, qb, kw, ka, kb, vw, va, vb)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    keep: list = []
+    projs = (_C.LoraProj * 3)()
+    ws_ = (qw, kw, vw)
+    r = _check_rank((qa, ka, va), (qb, kb, vb), (H, H, H))
+    for i, (w, a, b) in enumerate(((qw, qa, qb), (kw, ka, kb), (vw, va, vb))):
+        if w.shape[1] != H:
+            raise RuntimeError("lora_qkv_forward: weight in_features differ from x")
+        projs[i] = _lora_proj(w, a, b, scaling[i], keep)
+    dev = x.device
+    outs = [torch.empty((T, w.shape[0]), dtype=torch.bfloat16, device=dev) for w in ws_]
+    u = torch.empty((T, 64), dtype=torch.bfloat16, device=dev)
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_qkv_workspace_bytes(T, H, projs, 0))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_qkv_forward", _C.ptr(x2), T, H, r, projs, _ptr_array(outs), _C.ptr(u),
+            _C.ptr(ws), nbytes, _C.stream_of(x))
+    outs = [o.to(x.dtype) for o in outs]
+    return outs[0], outs[1], outs[2], u
+
+
+def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq, dk, dv):
+    _C.require_cuda("lora_qkv_backward", x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, dq, dk, dv)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    keep: list = []
+    projs = (_C.LoraProj * 3)()
+    r = _check_rank((qa, ka, va), (qb, kb, vb), (H, H, H))
+    for i, (w, a, b) in enumerate(((qw, qa, qb), (kw, ka, kb), (vw, va, vb))):
+        projs[i] = _lora_proj(w, a, b, scaling[i], keep)
+    dys = [_bf16_2d(d, w.shape[0]) for d, w in ((dq, qw), (dk, kw), (dv, vw))]
+    dev = x.device
+    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    das = [torch.empty((r, H), dtype=torch.float32, device=dev) for _ in range(3)]
+    dbs = [torch.empty((w.shape[0], r), dtype=torch.float32, device=dev) for w in (qw, kw, vw)]
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_qkv_workspace_bytes(T, H, projs, 1))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_qkv_backward", _C.ptr(x2), _C.ptr(_contig(u)), T, H, r, projs,
+            _ptr_array(dys), _C.ptr(dx), _ptr_array(das), _ptr_array(dbs), _C.ptr(ws), nbytes,
+            _C.stream_of(x))
+    return (dx.to(x.dtype).view(x.shape), das[0], dbs[0], das[1], dbs[1], das[2], dbs[2])
+
+
+def lora_mlp_forward_cuda(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
+    _C.require_cuda("lora_mlp_forward", x, gw, ga, gb, uw, ua, ub, dw, da, db)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    inter = gw.shape[0]
+    if uw.shape[0] != inter or dw.shape != (H, inter) or gw.shape[1] != H or uw.shape[1] != H:
+        raise RuntimeError("lora_mlp_forward: gate/up must be [inter, hidden], down [hidden, inter]")
+    r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
+    keep: list = []
+    projs = (_C.LoraProj * 3)()
+    for i, (w, a, b) in enumerate(((gw, ga, gb), (uw, ua, ub), (dw, da, db))):
+        projs[i] = _lora_proj(w, a, b, scaling[i], keep)
+    dev = x.device
+    bf = torch.bfloat16
+    gate = torch.empty((T, inter), dtype=bf, device=dev)
+    up = torch.empty((T, inter), dtype=bf, device=dev)
+    h = torch.empty((T, inter), dtype=bf, device=dev)
+    out = torch.empty((T, H), dtype=bf, device=dev)
+    u1 = torch.empty((T, 64), dtype=bf, device=dev)
+    u2 = torch.empty((T, 64), dtype=bf, device=dev)
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_mlp_workspace_bytes(T, H, inter, 0))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_mlp_forward", _C.ptr(x2), T, H, inter, r, projs, _C.ptr(gate), _C.ptr(up),
+            _C.ptr(h), _C.ptr(out), _C.ptr(u1), _C.ptr(u2), _C.ptr(ws), nbytes, _C.stream_of(x))
+    return out.to(x.dtype).view(x.shape), gate, up, h, u1, u2
+
+
+def lora_mlp_backward_cuda(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, da, db, scaling,
+                           dy):
+    _C.require_cuda("lora_mlp_backward", x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, da,
+                    db, dy)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    inter = gw.shape[0]
+    r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
+    keep: list = []
+    projs = (_C.LoraProj * 3)()
+    for i, (w, a, b) in enumerate(((gw, ga, gb), (uw, ua, ub), (dw, da, db))):
+        projs[i] = _lora_proj(w, a, b, scaling[i], keep)
+    dy2 = _bf16_2d(dy, H)
+    dev = x.device
+    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    das = [torch.empty((r, fin), dtype=torch.float32, device=dev) for fin in (H, H, inter)]
+    dbs = [torch.empty((fo, r), dtype=torch.float32, device=dev) for fo in (inter, inter, H)]
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_mlp_workspace_bytes(T, H, inter, 1))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_mlp_backward", _C.ptr(x2), _C.ptr(_contig(gate)), _C.ptr(_contig(up)),
+            _C.ptr(_contig(h)), _C.ptr(_contig(u1)), _C.ptr(_contig(u2)), T, H, inter, r, projs,
+            _C.ptr(dy2), _C.ptr(dx), _ptr_array(das), _ptr_array(dbs), _C.ptr(ws), nbytes,
+            _C.stream_of(x))
+    return (dx.to(x.dtype).view(x.shape), das[0], dbs[0], das[1], dbs[1], das[2], dbs[2])
+
+
+# ---------------------------------------------------------------------------
 # Registration
 # ---------------------------------------------------------------------------
 
@@ -358,6 +496,20 @@ _SCHEMAS = {
                     "-> (Tensor, Tensor, Tensor)",
     "flce_backward": "flce_backward(Tensor grad_output, Tensor dx_slabs, Tensor dw_acc, "
                      "int dh_dtype, int dw_dtype) -> (Tensor, Tensor)",
+    "lora_qkv_forward": "lora_qkv_forward(Tensor x, Tensor qw, Tensor qa, Tensor qb, Tensor kw, "
+                        "Tensor ka, Tensor kb, Tensor vw, Tensor va, Tensor vb, float[] scaling) "
+                        "-> (Tensor, Tensor, Tensor, Tensor)",
+    "lora_qkv_backward": "lora_qkv_backward(Tensor x, Tensor u, Tensor qw, Tensor qa, Tensor qb, "
+                         "Tensor kw, Tensor ka, Tensor kb, Tensor vw, Tensor va, Tensor vb, "
+                         "float[] scaling, Tensor dq, Tensor dk, Tensor dv) -> (Tensor, Tensor, "
+                         "Tensor, Tensor, Tensor, Tensor, Tensor)",
+    "lora_mlp_forward": "lora_mlp_forward(Tensor x, Tensor gw, Tensor ga, Tensor gb, Tensor uw, "
+                        "Tensor ua, Tensor ub, Tensor dw, Tensor da, Tensor db, float[] scaling) "
+                        "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)",
+    "lora_mlp_backward": "lora_mlp_backward(Tensor x, Tensor gate, Tensor up, Tensor h, Tensor u1, "
+                         "Tensor u2, Tensor gw, Tensor ga, Tensor gb, Tensor uw, Tensor ua, "
+                         "Tensor ub, Tensor dw, Tensor da, Tensor db, float[] scaling, Tensor dy) "
+                         "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)",
 }
 
 _CUDA_IMPLS = {
@@ -371,6 +523,10 @@ _CUDA_IMPLS = {
     "rope_apply_qk_pos": rope_apply_qk_pos_cuda,
     "flce_forward": flce_forward_cuda,
     "flce_backward": flce_backward_cuda,
+    "lora_qkv_forward": lora_qkv_forward_cuda,
+    "lora_qkv_backward": lora_qkv_backward_cuda,
+    "lora_mlp_forward": lora_mlp_forward_cuda,
+    "lora_mlp_backward": lora_mlp_backward_cuda,
 }
 
 
@@ -425,7 +581,36 @@ def _fake_impls():
               if dw_acc.dim() == 2 else torch.empty(0, device=dev))
         return dh, dw
 
+    def lqkv_fwd(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
+        T = x.numel() // x.shape[-1]
+        mk = lambda w: torch.empty((T, w.shape[0]), dtype=x.dtype, device=x.device)  # noqa: E731
+        return mk(qw), mk(kw), mk(vw), torch.empty((T, 64), dtype=torch.bfloat16, device=x.device)
+
+    def lqkv_bwd(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq, dk, dv):
+        f = lambda *s: torch.empty(s, dtype=torch.float32, device=x.device)  # noqa: E731
+        r, H = qa.shape
+        return (torch.empty_like(x), f(r, H), f(qw.shape[0], r), f(r, H), f(kw.shape[0], r),
+                f(r, H), f(vw.shape[0], r))
+
+    def lmlp_fwd(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
+        T = x.numel() // x.shape[-1]
+        inter = gw.shape[0]
+        bf = lambda *s: torch.empty(s, dtype=torch.bfloat16, device=x.device)  # noqa: E731
+        return (torch.empty_like(x), bf(T, inter), bf(T, inter), bf(T, inter), bf(T, 64),
+                bf(T, 64))
+
+    def lmlp_bwd(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, da, db, scaling, dy):
+        f = lambda *s: torch.empty(s, dtype=torch.float32, device=x.device)  # noqa: E731
+        r, H = ga.shape
+        inter = gw.shape[0]
+        return (torch.empty_like(x), f(r, H), f(inter, r), f(r, H), f(inter, r), f(r, inter),
+                f(H, r))
+
     return {
+        "lora_qkv_forward": lqkv_fwd,
+        "lora_qkv_backward": lqkv_bwd,
+        "lora_mlp_forward": lmlp_fwd,
+        "lora_mlp_backward": lmlp_bwd,
         "flce_forward": flce_fwd,
         "flce_backward": flce_bwd,
         "rms_norm_forward": rms_fwd,

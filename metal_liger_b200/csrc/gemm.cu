@@ -227,6 +227,57 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int64_
   }
 }
 
+}  // namespace
+
+namespace gemm {
+
+int auto_splits(int64_t M, int64_t N, int64_t K) {
+  const int bn = pick_bn(N);
+  const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+  const int64_t kb = (K + BK - 1) / BK;
+  const int sms = num_sms();
+  if (tiles >= sms || kb < 8) return 1;
+  int64_t s = std::min<int64_t>((2 * (int64_t)sms + tiles - 1) / tiles, kb / 4);
+  s = std::max<int64_t>(1, std::min<int64_t>(s, 16));
+  const int64_t per = (kb + s - 1) / s;
+  return (int)((kb + per - 1) / per);
+}
+
+int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partial,
+                  size_t partial_bytes, cudaStream_t st) {
+  if (splits <= 1) {
+    pr.epi = EPI_STORE;
+    pr.d_f32 = true;
+    pr.D = out;
+    pr.ldd = ldo;
+    pr.splits = 1;
+    return launch(pr, st);
+  }
+  if (partial == nullptr ||
+      partial_bytes < (size_t)splits * (size_t)pr.M * (size_t)pr.N * sizeof(float)) {
+    set_error("gemm split-K: partial buffer too small");
+    return ML_ERR_INVALID_ARG;
+  }
+  pr.epi = EPI_PARTIAL;
+  pr.splits = splits;
+  pr.D = partial;
+  pr.ldd = pr.N;
+  pr.split_stride = pr.M * pr.N;
+  pr.d_f32 = true;
+  int rc = launch(pr, st);
+  if (rc) return rc;
+  const int64_t total = pr.M * pr.N;
+  int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+  splitk_reduce<<<std::max(grid, 1), 256, 0, st>>>(partial, splits, pr.M, pr.N, pr.N, out, ldo, 1,
+                                                    0.f);
+  ML_CHECK_LAUNCH("gemm split-K reduce");
+  return ML_OK;
+}
+
+}  // namespace gemm
+
+namespace {
+
 int choose_splits(int64_t m, int64_t n, int64_t k_total, int bn) {
   const int64_t tiles = ((m + gemm::BM - 1) / gemm::BM) * ((n + bn - 1) / bn);
   const int64_t kb = (k_total + gemm::BK - 1) / gemm::BK;

@@ -508,5 +508,14 @@ int pick_bn(int64_t N);
 // Device address of the library's error word on the current device.
 int* device_error_word();
 
+// Split-K helper: out[M, N] (fp32, row pitch ldo) = alpha * A B^T via
+// `splits` fp32 partial slabs in `partial` (>= splits*M*N floats) and a
+// fixed-order reduction.  pr.epi / pr.D / pr.splits are filled in here.
+int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partial,
+                  size_t partial_bytes, cudaStream_t stream);
+
+// Split count launch_splitk would pick to fill the GPU for these sizes.
+int auto_splits(int64_t M, int64_t N, int64_t K);
+
 }  // namespace gemm
 }  // namespace ml

@@ -1,0 +1,530 @@
+// Fused LoRA QKV and LoRA MLP (forward + backward) on sm_100a.
+//
+// Same results as the reference's _LoRA_QKV / _LoRA_MLP (ops/fused_lora.py:85-266):
+//   y_i   = X W_i^T + s_i (X A_i^T) B_i^T
+//   dA_i  = s_i (dY_i B_i)^T X,  dB_i = s_i dY_i^T (X A_i^T)   (fp32 results)
+//   dX    = sum_i dY_i W_i + s_i (dY_i B_i) A_i                (frozen W: no dW)
+// and for the MLP the SwiGLU in between (h = silu(gate) * up in fp32).
+//
+// Every product runs on the tcgen05 GEMM.  The rank-r terms never get their
+// own pass over the big tensors: the adapters' A matrices are stacked into
+// one [64, in] operand so a single skinny GEMM yields U = X [A_q;A_k;A_v]^T
+// for all of them, and the low-rank update is folded into the base GEMM as
+// one extra 64-wide K-segment ([X | U] [W | s B_pad]^T), accumulating in the
+// same TMEM tile.  In the backward, dX = dQ Wq + dK Wk + dV Wv + G (s A) is a
+// single 4-segment GEMM with G = [dQ Bq | dK Bk | dV Bv] (one 3-segment GEMM),
+// and the dA/dB products are split-K GEMMs over the token dimension reading
+// X / dY in their stored layout (MN-major operands, no transposes).
+// Small pack kernels build the padded, scaled rank operands (<= 64 x out).
+#include "gemm.cuh"
+
+#include <algorithm>
+
+extern "C" int ml_swiglu_forward(const void* gate, const void* up, void* out, int64_t n, int dtype,
+                                 void* stream);
+extern "C" int ml_swiglu_backward(const void* gate, const void* up, const void* dout, void* dgate,
+                                  void* dup, int64_t n, int dtype, void* stream);
+
+namespace ml {
+namespace lora {
+namespace {
+
+constexpr int kSlot = 64;  // padded rank width shared by the adapters of one call
+using bf16 = __nv_bfloat16;
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Carves 256-byte-aligned buffers out of the caller's workspace; in dry mode
+// it only measures, so sizing and use share one code path.
+struct Arena {
+  uint8_t* base = nullptr;
+  size_t off = 0;
+  bool dry = true;
+  template <typename T>
+  T* take(size_t count) {
+    off = align256(off);
+    T* p = dry ? nullptr : reinterpret_cast<T*>(base + off);
+    off += count * sizeof(T);
+    return p;
+  }
+};
+
+// ------------------------------ pack kernels -------------------------------
+// dst[(row0 + i) * ld + c] = scale * src[i * cols + c]     (i < rows, c < cols)
+__global__ void pack_rows_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t rows,
+                            int64_t cols, int64_t row0, float scale) {
+  const int64_t n = rows * cols;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / cols, c = e - (e / cols) * cols;
+    dst[(row0 + i) * ld + c] = __float2bfloat16_rn(scale * load_as_f32(src, e, dt));
+  }
+}
+
+// dst[i * ld + col0 + j] = scale * src[i * r + j]           (i < rows, j < r)
+__global__ void pack_cols_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t rows, int64_t r,
+                            int64_t col0, float scale) {
+  const int64_t n = rows * r;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / r, j = e - (e / r) * r;
+    dst[i * ld + col0 + j] = __float2bfloat16_rn(scale * load_as_f32(src, e, dt));
+  }
+}
+
+// dst[(row0 + j) * ld + i] = scale * src[i * r + j]         (transpose of [out, r])
+__global__ void pack_t_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t out, int64_t r,
+                         int64_t row0, float scale) {
+  const int64_t n = out * r;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = e / out, i = e - (e / out) * out;  // coalesced writes along i
+    dst[(row0 + j) * ld + i] = __float2bfloat16_rn(scale * load_as_f32(src, i * r + j, dt));
+  }
+}
+
+// dst[j * cols + c] = scale * src[c * 64 + col0 + j]        (dA from X^T G)
+__global__ void unpack_t_k(float* dst, const float* src, int64_t cols, int64_t r, int64_t col0,
+                           float scale) {
+  const int64_t n = r * cols;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = e / cols, c = e - (e / cols) * cols;
+    dst[e] = scale * src[c * kSlot + col0 + j];
+  }
+}
+
+// dst[i * r + j] = scale * src[i * 64 + col0 + j]           (dB from dY^T U)
+__global__ void unpack_cols_k(float* dst, const float* src, int64_t rows, int64_t r, int64_t col0,
+                              float scale) {
+  const int64_t n = rows * r;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / r, j = e - (e / r) * r;
+    dst[e] = scale * src[i * kSlot + col0 + j];
+  }
+}
+
+inline int egrid(int64_t n) {
+  return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8));
+}
+
+#define LORA_LAUNCH(kernel, n, ...)                                        \
+  do {                                                                     \
+    if ((n) > 0) {                                                         \
+      kernel<<<egrid(n), 256, 0, st>>>(__VA_ARGS__);                       \
+      ML_CHECK_LAUNCH(#kernel);                                            \
+    }                                                                      \
+  } while (0)
+
+#define LORA_TRY(call)          \
+  do {                                \
+    int _rc = (call);                 \
+    if (_rc != ML_OK) return _rc;     \
+  } while (0)
+
+int zero(void* p, size_t bytes, cudaStream_t st) {
+  ML_CHECK_CUDA(cudaMemsetAsync(p, 0, bytes, st), "lora: memset");
+  return ML_OK;
+}
+
+// One K-segment: A [M, K] / B [N, K] logical views.
+gemm::Seg seg(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t k) {
+  gemm::Seg s;
+  s.a.ptr = a;
+  s.a.ld = lda;
+  s.b.ptr = b;
+  s.b.ld = ldb;
+  s.K = k;
+  return s;
+}
+
+// D[M, N] (bf16, pitch ldd) = sum of segments.
+int gemm_bf16(int64_t M, int64_t N, std::initializer_list<gemm::Seg> segs, bool a_mn, bool b_mn,
+              void* D, int64_t ldd, cudaStream_t st) {
+  gemm::Problem p;
+  p.M = M;
+  p.N = N;
+  p.nseg = 0;
+  for (const auto& s : segs) p.seg[p.nseg++] = s;
+  p.a_mn = a_mn;
+  p.b_mn = b_mn;
+  p.epi = gemm::EPI_STORE;
+  p.d_f32 = false;
+  p.D = D;
+  p.ldd = ldd;
+  return gemm::launch(p, st);
+}
+
+// out[M, 64] fp32 = A^T-style skinny product over the token dimension, split-K.
+int gemm_skinny_f32(int64_t M, const gemm::Seg& s, float* out, float* partial,
+                    size_t partial_bytes, cudaStream_t st) {
+  gemm::Problem p;
+  p.M = M;
+  p.N = kSlot;
+  p.nseg = 1;
+  p.seg[0] = s;
+  p.a_mn = true;
+  p.b_mn = true;
+  const int splits = gemm::auto_splits(M, kSlot, s.K);
+  return gemm::launch_splitk(p, splits, out, kSlot, partial, partial_bytes, st);
+}
+
+size_t skinny_partial_floats(int64_t M, int64_t K) {
+  return (size_t)gemm::auto_splits(M, kSlot, K) * (size_t)M * kSlot;
+}
+
+bool valid_proj(const ml_lora_proj& p) {
+  return p.w && p.a && p.b && p.out_features > 0 && p.a_dtype >= 0 && p.a_dtype <= 2 &&
+         p.b_dtype >= 0 && p.b_dtype <= 2;
+}
+
+// ------------------------------- QKV --------------------------------------
+int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, const ml_lora_proj* pj,
+                void* const* out, bf16* u, Arena& ar, cudaStream_t st) {
+  bf16* acat = ar.take<bf16>((size_t)kSlot * H);
+  bf16* bpad[3];
+  for (int i = 0; i < 3; ++i) bpad[i] = ar.take<bf16>((size_t)pj[i].out_features * kSlot);
+  if (ar.dry) return ML_OK;
+  LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
+  for (int i = 0; i < 3; ++i) {
+    const int64_t o = pj[i].out_features;
+    LORA_TRY(zero(bpad[i], (size_t)o * kSlot * 2, st));
+    LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[i].a, pj[i].a_dtype, r, H, i * r, 1.f);
+    LORA_LAUNCH(pack_cols_k, o * r, bpad[i], kSlot, pj[i].b, pj[i].b_dtype, o, r, i * r,
+                pj[i].scaling);
+  }
+  // U = X [A_q; A_k; A_v]^T   [T, 64]
+  LORA_TRY(gemm_bf16(T, kSlot, {seg(x, H, acat, H, H)}, false, false, u, kSlot, st));
+  // y_i = [X | U] [W_i | s_i B_i (in its slot)]^T
+  for (int i = 0; i < 3; ++i) {
+    const int64_t o = pj[i].out_features;
+    LORA_TRY(gemm_bf16(T, o, {seg(x, H, pj[i].w, H, H), seg(u, kSlot, bpad[i], kSlot, kSlot)},
+                       false, false, out[i], o, st));
+  }
+  return ML_OK;
+}
+
+int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r,
+                 const ml_lora_proj* pj, const void* const* dy, bf16* dx, float* const* da,
+                 float* const* db, Arena& ar, cudaStream_t st) {
+  int64_t omax = 0;
+  for (int i = 0; i < 3; ++i) omax = std::max(omax, pj[i].out_features);
+  bf16* bt[3];
+  for (int i = 0; i < 3; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
+  bf16* acat_s = ar.take<bf16>((size_t)kSlot * H);
+  bf16* G = ar.take<bf16>((size_t)T * kSlot);
+  float* dAT = ar.take<float>((size_t)H * kSlot);
+  float* dBt = ar.take<float>((size_t)omax * kSlot);
+  const size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(omax, T));
+  float* part = ar.take<float>(pf);
+  if (ar.dry) return ML_OK;
+  LORA_TRY(zero(acat_s, (size_t)kSlot * H * 2, st));
+  for (int i = 0; i < 3; ++i) {
+    const int64_t o = pj[i].out_features;
+    LORA_TRY(zero(bt[i], (size_t)kSlot * o * 2, st));
+    LORA_LAUNCH(pack_t_k, o * r, bt[i], o, pj[i].b, pj[i].b_dtype, o, r, i * r, 1.f);
+    LORA_LAUNCH(pack_rows_k, r * H, acat_s, H, pj[i].a, pj[i].a_dtype, r, H, i * r,
+                pj[i].scaling);
+  }
+  const int64_t o0 = pj[0].out_features, o1 = pj[1].out_features, o2 = pj[2].out_features;
+  // G = [dQ Bq | dK Bk | dV Bv]   [T, 64]
+  LORA_TRY(gemm_bf16(T, kSlot,
+                     {seg(dy[0], o0, bt[0], o0, o0), seg(dy[1], o1, bt[1], o1, o1),
+                      seg(dy[2], o2, bt[2], o2, o2)},
+                     false, false, G, kSlot, st));
+  // dX = dQ Wq + dK Wk + dV Wv + G (s A)   — one accumulator, W read in place (N-major)
+  LORA_TRY(gemm_bf16(T, H,
+                     {seg(dy[0], o0, pj[0].w, H, o0), seg(dy[1], o1, pj[1].w, H, o1),
+                      seg(dy[2], o2, pj[2].w, H, o2), seg(G, kSlot, acat_s, H, kSlot)},
+                     false, true, dx, H, st));
+  // dA_i = s_i (X^T G)[:, slot_i]^T
+  LORA_TRY(gemm_skinny_f32(H, seg(x, H, G, kSlot, T), dAT, part, pf * 4, st));
+  for (int i = 0; i < 3; ++i)
+    LORA_LAUNCH(unpack_t_k, r * H, da[i], dAT, H, r, i * r, pj[i].scaling);
+  // dB_i = s_i dY_i^T U[:, slot_i]
+  for (int i = 0; i < 3; ++i) {
+    const int64_t o = pj[i].out_features;
+    LORA_TRY(gemm_skinny_f32(o, seg(dy[i], o, u, kSlot, T), dBt, part, pf * 4, st));
+    LORA_LAUNCH(unpack_cols_k, o * r, db[i], dBt, o, r, i * r, pj[i].scaling);
+  }
+  return ML_OK;
+}
+
+// ------------------------------- MLP --------------------------------------
+// pj[0] = gate (I x H), pj[1] = up (I x H), pj[2] = down (H x I).
+int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
+                const ml_lora_proj* pj, bf16* gate, bf16* up, bf16* h, bf16* out, bf16* u1,
+                bf16* u2, Arena& ar, cudaStream_t st) {
+  bf16* acat = ar.take<bf16>((size_t)kSlot * H);   // rows [0,r) = Ag, [r,2r) = Au
+  bf16* bgp = ar.take<bf16>((size_t)I * kSlot);     // cols [0,r) = s_g Bg
+  bf16* bup = ar.take<bf16>((size_t)I * kSlot);     // cols [r,2r) = s_u Bu
+  bf16* ad = ar.take<bf16>((size_t)kSlot * I);      // rows [0,r) = Ad
+  bf16* bdp = ar.take<bf16>((size_t)H * kSlot);     // cols [0,r) = s_d Bd
+  if (ar.dry) return ML_OK;
+  LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
+  LORA_TRY(zero(bgp, (size_t)I * kSlot * 2, st));
+  LORA_TRY(zero(bup, (size_t)I * kSlot * 2, st));
+  LORA_TRY(zero(ad, (size_t)kSlot * I * 2, st));
+  LORA_TRY(zero(bdp, (size_t)H * kSlot * 2, st));
+  LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[0].a, pj[0].a_dtype, r, H, 0, 1.f);
+  LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[1].a, pj[1].a_dtype, r, H, r, 1.f);
+  LORA_LAUNCH(pack_cols_k, I * r, bgp, kSlot, pj[0].b, pj[0].b_dtype, I, r, 0, pj[0].scaling);
+  LORA_LAUNCH(pack_cols_k, I * r, bup, kSlot, pj[1].b, pj[1].b_dtype, I, r, r, pj[1].scaling);
+  LORA_LAUNCH(pack_rows_k, r * I, ad, I, pj[2].a, pj[2].a_dtype, r, I, 0, 1.f);
+  LORA_LAUNCH(pack_cols_k, H * r, bdp, kSlot, pj[2].b, pj[2].b_dtype, H, r, 0, pj[2].scaling);
+  // U1 = X [Ag; Au]^T
+  LORA_TRY(gemm_bf16(T, kSlot, {seg(x, H, acat, H, H)}, false, false, u1, kSlot, st));
+  // gate / up = [X | U1] [W | s B]^T
+  LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[0].w, H, H), seg(u1, kSlot, bgp, kSlot, kSlot)}, false,
+                     false, gate, I, st));
+  LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[1].w, H, H), seg(u1, kSlot, bup, kSlot, kSlot)}, false,
+                     false, up, I, st));
+  // h = silu(gate) * up (fp32 math)
+  LORA_TRY(ml_swiglu_forward(gate, up, h, T * I, ML_DTYPE_BF16, st));
+  // U2 = h Ad^T ; out = [h | U2] [Wd | s Bd]^T
+  LORA_TRY(gemm_bf16(T, kSlot, {seg(h, I, ad, I, I)}, false, false, u2, kSlot, st));
+  LORA_TRY(gemm_bf16(T, H, {seg(h, I, pj[2].w, I, I), seg(u2, kSlot, bdp, kSlot, kSlot)}, false,
+                     false, out, H, st));
+  return ML_OK;
+}
+
+int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h, const bf16* u1,
+                 const bf16* u2, int64_t T, int64_t H, int64_t I, int64_t r,
+                 const ml_lora_proj* pj, const bf16* dy, bf16* dx, float* const* da,
+                 float* const* db, Arena& ar, cudaStream_t st) {
+  bf16* bdT = ar.take<bf16>((size_t)kSlot * H);     // rows [0,r) = Bd^T
+  bf16* ads = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = s_d Ad
+  bf16* bgT = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = Bg^T
+  bf16* buT = ar.take<bf16>((size_t)kSlot * I);     // rows [r,2r) = Bu^T
+  bf16* acs = ar.take<bf16>((size_t)kSlot * H);     // rows [0,r) = s_g Ag, [r,2r) = s_u Au
+  bf16* Gd = ar.take<bf16>((size_t)T * kSlot);
+  bf16* Ggu = ar.take<bf16>((size_t)T * kSlot);
+  bf16* dH = ar.take<bf16>((size_t)T * I);
+  bf16* dgate = ar.take<bf16>((size_t)T * I);
+  bf16* dup = ar.take<bf16>((size_t)T * I);
+  const int64_t mmax = std::max(H, I);
+  float* dAT = ar.take<float>((size_t)mmax * kSlot);
+  float* dBt = ar.take<float>((size_t)mmax * kSlot);
+  const size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(I, T));
+  float* part = ar.take<float>(pf);
+  if (ar.dry) return ML_OK;
+  LORA_TRY(zero(bdT, (size_t)kSlot * H * 2, st));
+  LORA_TRY(zero(ads, (size_t)kSlot * I * 2, st));
+  LORA_TRY(zero(bgT, (size_t)kSlot * I * 2, st));
+  LORA_TRY(zero(buT, (size_t)kSlot * I * 2, st));
+  LORA_TRY(zero(acs, (size_t)kSlot * H * 2, st));
+  LORA_LAUNCH(pack_t_k, H * r, bdT, H, pj[2].b, pj[2].b_dtype, H, r, 0, 1.f);
+  LORA_LAUNCH(pack_rows_k, r * I, ads, I, pj[2].a, pj[2].a_dtype, r, I, 0, pj[2].scaling);
+  LORA_LAUNCH(pack_t_k, I * r, bgT, I, pj[0].b, pj[0].b_dtype, I, r, 0, 1.f);
+  LORA_LAUNCH(pack_t_k, I * r, buT, I, pj[1].b, pj[1].b_dtype, I, r, r, 1.f);
+  LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[0].a, pj[0].a_dtype, r, H, 0, pj[0].scaling);
+  LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[1].a, pj[1].a_dtype, r, H, r, pj[1].scaling);
+  // G_d = dY Bd ; dH = dY Wd + G_d (s_d Ad)      (Wd stored [H, I]: N-major)
+  LORA_TRY(gemm_bf16(T, kSlot, {seg(dy, H, bdT, H, H)}, false, false, Gd, kSlot, st));
+  LORA_TRY(gemm_bf16(T, I, {seg(dy, H, pj[2].w, I, H), seg(Gd, kSlot, ads, I, kSlot)}, false,
+                     true, dH, I, st));
+  // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
+  LORA_TRY(gemm_skinny_f32(I, seg(h, I, Gd, kSlot, T), dAT, part, pf * 4, st));
+  LORA_LAUNCH(unpack_t_k, r * I, da[2], dAT, I, r, 0, pj[2].scaling);
+  LORA_TRY(gemm_skinny_f32(H, seg(dy, H, u2, kSlot, T), dBt, part, pf * 4, st));
+  LORA_LAUNCH(unpack_cols_k, H * r, db[2], dBt, H, r, 0, pj[2].scaling);
+  // SwiGLU backward (sigmoid recomputed)
+  LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
+  // G_gu = [d_gate Bg | d_up Bu]
+  LORA_TRY(gemm_bf16(T, kSlot, {seg(dgate, I, bgT, I, I), seg(dup, I, buT, I, I)}, false, false,
+                     Ggu, kSlot, st));
+  // dX = d_gate Wg + d_up Wu + G_gu (s A)        (Wg/Wu stored [I, H]: N-major)
+  LORA_TRY(gemm_bf16(T, H,
+                     {seg(dgate, I, pj[0].w, H, I), seg(dup, I, pj[1].w, H, I),
+                      seg(Ggu, kSlot, acs, H, kSlot)},
+                     false, true, dx, H, st));
+  // gate/up adapter grads
+  LORA_TRY(gemm_skinny_f32(H, seg(x, H, Ggu, kSlot, T), dAT, part, pf * 4, st));
+  LORA_LAUNCH(unpack_t_k, r * H, da[0], dAT, H, r, 0, pj[0].scaling);
+  LORA_LAUNCH(unpack_t_k, r * H, da[1], dAT, H, r, r, pj[1].scaling);
+  LORA_TRY(gemm_skinny_f32(I, seg(dgate, I, u1, kSlot, T), dBt, part, pf * 4, st));
+  LORA_LAUNCH(unpack_cols_k, I * r, db[0], dBt, I, r, 0, pj[0].scaling);
+  LORA_TRY(gemm_skinny_f32(I, seg(dup, I, u1, kSlot, T), dBt, part, pf * 4, st));
+  LORA_LAUNCH(unpack_cols_k, I * r, db[1], dBt, I, r, r, pj[1].scaling);
+  return ML_OK;
+}
+
+int check_ws(const Arena& need, size_t have, void* ws, const char* what) {
+  if (ws == nullptr || ((uintptr_t)ws & 255) != 0) {
+    set_error("%s: workspace must be a non-null 256-byte aligned pointer", what);
+    return ML_ERR_INVALID_ARG;
+  }
+  if (have < need.off) {
+    set_error("%s: workspace too small (%zu < %zu bytes)", what, have, need.off);
+    return ML_ERR_INVALID_ARG;
+  }
+  return ML_OK;
+}
+
+}  // namespace
+}  // namespace lora
+}  // namespace ml
+
+using namespace ml;
+using lora::Arena;
+
+#define LORA_ARGCHECK_COMMON(what)                                                           \
+  ML_CHECK_ARG(tokens >= 0 && in_features > 0 && rank > 0, what ": bad sizes");              \
+  ML_CHECK_ARG(in_features % 8 == 0, what ": in_features must be a multiple of 8");          \
+  ML_CHECK_ARG(proj != nullptr, what ": null projections");                                   \
+  for (int _i = 0; _i < 3; ++_i)                                                              \
+    ML_CHECK_ARG(lora::valid_proj(proj[_i]) && proj[_i].out_features % 8 == 0,                \
+                 what ": projection %d is invalid (null pointer, bad dtype, or out_features " \
+                 "not a multiple of 8)", _i);
+
+extern "C" size_t ml_lora_qkv_workspace_bytes(int64_t tokens, int64_t in_features,
+                                              const ml_lora_proj* proj, int backward) {
+  if (tokens <= 0 || in_features <= 0 || proj == nullptr) return 256;
+  Arena ar;
+  const int64_t r = 1;
+  if (backward)
+    lora::qkv_backward(nullptr, nullptr, tokens, in_features, r, proj, nullptr, nullptr, nullptr,
+                       nullptr, ar, nullptr);
+  else
+    lora::qkv_forward(nullptr, tokens, in_features, r, proj, nullptr, nullptr, ar, nullptr);
+  return std::max<size_t>(ar.off, 256);
+}
+
+extern "C" int ml_lora_qkv_forward(const void* x, int64_t tokens, int64_t in_features,
+                                   int64_t rank, const ml_lora_proj* proj, void* const* out,
+                                   void* u, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+  LORA_ARGCHECK_COMMON("lora_qkv_forward")
+  ML_CHECK_ARG(3 * rank <= lora::kSlot, "lora_qkv_forward: rank %lld > 21 is not supported",
+               (long long)rank);
+  if (tokens == 0) return ML_OK;
+  ML_CHECK_ARG(x && out && out[0] && out[1] && out[2] && u, "lora_qkv_forward: null pointer");
+  Arena need;
+  lora::qkv_forward(nullptr, tokens, in_features, rank, proj, nullptr, nullptr, need, nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_qkv_forward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  return lora::qkv_forward(static_cast<const __nv_bfloat16*>(x), tokens, in_features, rank, proj,
+                           out, static_cast<__nv_bfloat16*>(u), ar,
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens,
+                                    int64_t in_features, int64_t rank, const ml_lora_proj* proj,
+                                    const void* const* dy, void* dx, float* const* da,
+                                    float* const* db, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  LORA_ARGCHECK_COMMON("lora_qkv_backward")
+  ML_CHECK_ARG(3 * rank <= lora::kSlot, "lora_qkv_backward: rank %lld > 21 is not supported",
+               (long long)rank);
+  ML_CHECK_ARG(dy && da && db, "lora_qkv_backward: null pointer arrays");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tokens == 0) {
+    for (int i = 0; i < 3; ++i) {
+      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_features * 4, st), "memset dA");
+      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
+                    "memset dB");
+    }
+    return ML_OK;
+  }
+  ML_CHECK_ARG(x && u && dx && dy[0] && dy[1] && dy[2], "lora_qkv_backward: null pointer");
+  Arena need;
+  lora::qkv_backward(nullptr, nullptr, tokens, in_features, rank, proj, nullptr, nullptr, nullptr,
+                     nullptr, need, nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_qkv_backward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  return lora::qkv_backward(static_cast<const __nv_bfloat16*>(x),
+                            static_cast<const __nv_bfloat16*>(u), tokens, in_features, rank, proj,
+                            dy, static_cast<__nv_bfloat16*>(dx), da, db, ar, st);
+}
+
+#define LORA_MLP_CHECK(what)                                                                   \
+  ML_CHECK_ARG(tokens >= 0 && hidden > 0 && inter > 0 && rank > 0, what ": bad sizes");        \
+  ML_CHECK_ARG(hidden % 8 == 0 && inter % 8 == 0, what ": sizes must be multiples of 8");      \
+  ML_CHECK_ARG(2 * rank <= lora::kSlot, what ": rank %lld > 32 is not supported",              \
+               (long long)rank);                                                                \
+  ML_CHECK_ARG(proj != nullptr && lora::valid_proj(proj[0]) && lora::valid_proj(proj[1]) &&    \
+                   lora::valid_proj(proj[2]),                                                  \
+               what ": invalid projections");                                                  \
+  ML_CHECK_ARG(proj[0].out_features == inter && proj[1].out_features == inter &&               \
+                   proj[2].out_features == hidden,                                             \
+               what ": projection shapes do not match hidden/intermediate");
+
+extern "C" size_t ml_lora_mlp_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
+                                              int backward) {
+  if (tokens <= 0 || hidden <= 0 || inter <= 0) return 256;
+  Arena ar;
+  ml_lora_proj dummy[3] = {};
+  if (backward)
+    lora::mlp_backward(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, tokens, hidden,
+                       inter, 1, dummy, nullptr, nullptr, nullptr, nullptr, ar, nullptr);
+  else
+    lora::mlp_forward(nullptr, tokens, hidden, inter, 1, dummy, nullptr, nullptr, nullptr,
+                      nullptr, nullptr, nullptr, ar, nullptr);
+  return std::max<size_t>(ar.off, 256);
+}
+
+extern "C" int ml_lora_mlp_forward(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
+                                   int64_t rank, const ml_lora_proj* proj, void* gate, void* up,
+                                   void* h, void* out, void* u1, void* u2, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  LORA_MLP_CHECK("lora_mlp_forward")
+  if (tokens == 0) return ML_OK;
+  ML_CHECK_ARG(x && gate && up && h && out && u1 && u2, "lora_mlp_forward: null pointer");
+  Arena need;
+  ml_lora_proj dummy[3] = {};
+  lora::mlp_forward(nullptr, tokens, hidden, inter, 1, dummy, nullptr, nullptr, nullptr, nullptr,
+                    nullptr, nullptr, need, nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_mlp_forward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  using b = __nv_bfloat16;
+  return lora::mlp_forward(static_cast<const b*>(x), tokens, hidden, inter, rank, proj,
+                           static_cast<b*>(gate), static_cast<b*>(up), static_cast<b*>(h),
+                           static_cast<b*>(out), static_cast<b*>(u1), static_cast<b*>(u2), ar,
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ml_lora_mlp_backward(const void* x, const void* gate, const void* up,
+                                    const void* h, const void* u1, const void* u2, int64_t tokens,
+                                    int64_t hidden, int64_t inter, int64_t rank,
+                                    const ml_lora_proj* proj, const void* dy, void* dx,
+                                    float* const* da, float* const* db, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  LORA_MLP_CHECK("lora_mlp_backward")
+  ML_CHECK_ARG(da && db, "lora_mlp_backward: null pointer arrays");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tokens == 0) {
+    const int64_t in_f[3] = {hidden, hidden, inter};
+    for (int i = 0; i < 3; ++i) {
+      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_f[i] * 4, st), "memset dA");
+      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
+                    "memset dB");
+    }
+    return ML_OK;
+  }
+  ML_CHECK_ARG(x && gate && up && h && u1 && u2 && dy && dx, "lora_mlp_backward: null pointer");
+  Arena need;
+  ml_lora_proj dummy[3] = {};
+  lora::mlp_backward(nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, tokens, hidden, inter,
+                     1, dummy, nullptr, nullptr, nullptr, nullptr, need, nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_mlp_backward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  using b = __nv_bfloat16;
+  return lora::mlp_backward(static_cast<const b*>(x), static_cast<const b*>(gate),
+                            static_cast<const b*>(up), static_cast<const b*>(h),
+                            static_cast<const b*>(u1), static_cast<const b*>(u2), tokens, hidden,
+                            inter, rank, proj, static_cast<const b*>(dy), static_cast<b*>(dx), da,
+                            db, ar, st);
+}

@@ -1,0 +1,151 @@
+"""Model patching for HuggingFace Qwen3-VL-style models — drop-in for patch.py.
+
+``apply_metal_liger_to_qwen3vl(model, fuse_rms_norm=True, fuse_swiglu=True,
+fuse_rope=False, fuse_cross_entropy=False, fuse_lora=True,
+use_optimized_generator=False)`` keeps the reference's signature, flags and
+behaviour (reference patch.py:181-240):
+
+* every decoder layer's ``input_layernorm`` / ``post_attention_layernorm`` and
+  the final norm become ``MetalLigerRMSNorm`` sharing the original weight
+  storage (so ``state_dict`` keys and values are unchanged);
+* every MLP with a ``gate_proj`` is wrapped in ``MetalLigerSwiGLU``;
+* PEFT LoRA projections are routed through the fused LoRA Functions by
+  ``patch_fused_lora`` (which never touches ``_modules``);
+* ``fuse_rope`` / ``fuse_cross_entropy`` only log that the fused functions are
+  available (``apply_fused_rotary*``, ``MetalLigerFusedLinearCrossEntropy``),
+  exactly as the reference does.
+
+Layers are located through the same PEFT / VL nesting paths the reference
+tries (patch.py:27-89).
+"""
+
+import logging
+
+import torch.nn as nn
+
+from metal_liger_b200.generation import patch_generator
+from metal_liger_b200.ops.fused_lora import patch_fused_lora
+from metal_liger_b200.ops.fused_rms_norm import MetalLigerRMSNorm
+from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU
+
+logger = logging.getLogger(__name__)
+
+
+def _walk(obj, path):
+    for name in path:
+        obj = getattr(obj, name, None)
+        if obj is None:
+            return None
+    return obj
+
+
+# Attribute paths to the decoder layer list, most specific first
+# (reference patch.py:36-54).
+_LAYER_PATHS = (
+    ("base_model", "model", "model", "language_model", "layers"),
+    ("base_model", "model", "model", "layers"),
+    ("model", "language_model", "layers"),
+    ("model", "layers"),
+    ("layers",),
+    ("module", "model", "layers"),
+)
+
+# Parents of the final norm (reference patch.py:69-81 and :146-154).
+_NORM_PARENTS = (
+    ("base_model", "model", "model", "language_model"),
+    ("model", "language_model"),
+    ("base_model", "model", "model"),
+    ("model",),
+)
+
+
+def _find_layers(model: nn.Module):
+    for path in _LAYER_PATHS:
+        try:
+            layers = _walk(model, path)
+            if layers is not None and len(layers) > 0:
+                return layers
+        except (AttributeError, TypeError):
+            continue
+    return None
+
+
+def _find_final_norm(model: nn.Module):
+    """(parent, norm) of the final RMSNorm, or (None, None)."""
+    for path in _NORM_PARENTS:
+        parent = _walk(model, path)
+        norm = getattr(parent, "norm", None) if parent is not None else None
+        if norm is not None and hasattr(norm, "weight"):
+            return parent, norm
+    return None, None
+
+
+def _fused_norm_like(old: nn.Module) -> MetalLigerRMSNorm:
+    eps = getattr(old, "variance_epsilon", getattr(old, "eps", 1e-6))
+    return MetalLigerRMSNorm(hidden_size=old.weight.shape[0], eps=eps, weight=old.weight.data)
+
+
+def _replace_rms_norms(model: nn.Module) -> int:
+    layers = _find_layers(model)
+    if layers is None:
+        logger.warning("MetalLiger: could not find transformer layers for RMSNorm patching")
+        return 0
+    count = 0
+    for layer in layers:
+        for attr in ("input_layernorm", "post_attention_layernorm"):
+            if hasattr(layer, attr):
+                setattr(layer, attr, _fused_norm_like(getattr(layer, attr)))
+                count += 1
+    parent, norm = _find_final_norm(model)
+    if parent is not None:
+        parent.norm = _fused_norm_like(norm)
+        count += 1
+    return count
+
+
+def _replace_mlps(model: nn.Module) -> int:
+    layers = _find_layers(model)
+    if layers is None:
+        return 0
+    count = 0
+    for layer in layers:
+        if hasattr(layer, "mlp") and hasattr(layer.mlp, "gate_proj"):
+            layer.mlp = MetalLigerSwiGLU(layer.mlp)
+            count += 1
+    return count
+
+
+def apply_metal_liger_to_qwen3vl(
+    model: nn.Module,
+    fuse_rms_norm: bool = True,
+    fuse_swiglu: bool = True,
+    fuse_rope: bool = False,
+    fuse_cross_entropy: bool = False,
+    fuse_lora: bool = True,
+    use_optimized_generator: bool = False,
+) -> nn.Module:
+    """Apply the fused B200 ops to a Qwen3-VL (or similar) model in place; returns it."""
+    stats = {}
+    if fuse_rms_norm:
+        stats["rms_norm"] = _replace_rms_norms(model)
+        logger.info("MetalLiger: replaced %d RMSNorm layers with fused versions",
+                    stats["rms_norm"])
+    if fuse_swiglu:
+        stats["swiglu"] = _replace_mlps(model)
+        logger.info("MetalLiger: replaced %d MLP layers with fused SwiGLU", stats["swiglu"])
+    if fuse_lora:
+        stats["fused_lora"] = patch_fused_lora(model)
+        logger.info("MetalLiger: fused LoRA QKV+MLP on %d modules", stats["fused_lora"])
+    if use_optimized_generator:
+        patch_generator(model)
+        stats["generator"] = "optimized"
+    if fuse_rope:
+        logger.info("MetalLiger: fused RoPE — use apply_fused_rotary() / "
+                    "apply_fused_rotary_from_positions()")
+        stats["rope"] = "available"
+    if fuse_cross_entropy:
+        logger.info("MetalLiger: fused CE — use MetalLigerFusedLinearCrossEntropy in the trainer")
+        stats["cross_entropy"] = "available"
+    total = sum(v for v in stats.values() if isinstance(v, int))
+    logger.info("MetalLiger: %d total layers patched. Details: %s", total, stats)
+    return model

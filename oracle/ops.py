@@ -189,41 +189,58 @@ def flce_backward(hidden, weight, labels, lse, mask, grad_output=1.0, bias=None,
 # Fused LoRA — reference ops/fused_lora.py:69-266
 # ---------------------------------------------------------------------------
 
-def lora_linear(x, w, a, b, s):
-    """ops/fused_lora.py:69-82: x W^T + s (x A^T) B^T, in x's dtype."""
+def _store(t, store_dtype):
+    """Round ``t`` to the dtype the reference stores that intermediate in (no-op
+    when ``store_dtype`` is None)."""
+    return t if store_dtype is None else t.to(store_dtype).to(t.dtype)
+
+
+def lora_linear(x, w, a, b, s, store_dtype=None):
+    """ops/fused_lora.py:69-82: x W^T + s (x A^T) B^T, in x's dtype.
+
+    ``store_dtype`` rounds the rank projection x A^T where the reference holds it
+    as a tensor of the input dtype."""
     dt = x.dtype
     out = x @ w.t()
     if a is not None and b is not None:
-        out = out + (x @ a.to(dt).t()) @ b.to(dt).t() * s
+        out = out + _store(x @ a.to(dt).t(), store_dtype) @ b.to(dt).t() * s
     return out
 
 
-def _lora_grads(dy, x, a, b, s):
+def _lora_grads(dy, x, a, b, s, store_dtype=None):
     """ops/fused_lora.py:142-149: dA = s (dY B)^T X ; dB = s dY^T (X A^T), as fp32."""
     dt = dy.dtype
     ac, bc = a.to(dt), b.to(dt)
-    da = ((dy @ bc).t() @ x * s).float()
-    db = (dy.t() @ (x @ ac.t()) * s).float()
+    da = (_store(dy @ bc, store_dtype).t() @ x * s).float()
+    db = (dy.t() @ _store(x @ ac.t(), store_dtype) * s).float()
     return da, db
 
 
-def _lora_dx(dy, w, a, b, s):
+def _lora_dx(dy, w, a, b, s, store_dtype=None):
     """ops/fused_lora.py:155-161: dY W + s (dY B) A."""
     dt = dy.dtype
-    return dy @ w + (dy @ b.to(dt)) @ a.to(dt) * s
+    return dy @ w + _store(dy @ b.to(dt), store_dtype) @ a.to(dt) * s
 
 
-def lora_qkv_forward(x, q, k, v, dtype=None):
+# The reference evaluates in the input dtype.  Tests evaluate the same
+# algorithm with fp32 products (``dtype=torch.float32``); ``store_dtype``
+# then rounds every intermediate the reference keeps as a tensor of the input
+# dtype -- x A^T, dY B, gate, up, h, dH, d_gate, d_up -- so the comparison
+# measures accumulation differences, not the reference's own storage
+# quantisation.
+
+def lora_qkv_forward(x, q, k, v, dtype=None, store_dtype=None):
     """ops/fused_lora.py:96-119.  q/k/v are (W, A, B, s) tuples.  Returns Q, K, V."""
     cast = (lambda t: t) if dtype is None else (lambda t: t.to(dtype))
     xf = cast(x).reshape(-1, x.shape[-1])
     outs = []
     for (w, a, b, s) in (q, k, v):
-        outs.append(lora_linear(xf, cast(w), cast(a), cast(b), s).view(*x.shape[:-1], -1))
+        outs.append(lora_linear(xf, cast(w), cast(a), cast(b), s, store_dtype)
+                    .view(*x.shape[:-1], -1))
     return tuple(outs)
 
 
-def lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=None):
+def lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=None, store_dtype=None):
     """ops/fused_lora.py:121-171.  Returns (dX, [(dA, dB) for q, k, v])."""
     cast = (lambda t: t) if dtype is None else (lambda t: t.to(dtype))
     xf = cast(x).reshape(-1, x.shape[-1])
@@ -231,13 +248,13 @@ def lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=None):
     grads = []
     for (w, a, b, s), dy in zip((q, k, v), (dq, dk, dv)):
         dyf = cast(dy).reshape(-1, dy.shape[-1])
-        grads.append(_lora_grads(dyf, xf, cast(a), cast(b), s))
-        term = _lora_dx(dyf, cast(w), cast(a), cast(b), s)
+        grads.append(_lora_grads(dyf, xf, cast(a), cast(b), s, store_dtype))
+        term = _lora_dx(dyf, cast(w), cast(a), cast(b), s, store_dtype)
         dx = term if dx is None else dx + term
     return dx.view(*x.shape), grads
 
 
-def lora_mlp_forward(x, g, u, d, dtype=None):
+def lora_mlp_forward(x, g, u, d, dtype=None, store_dtype=None):
     """ops/fused_lora.py:182-207: gate/up LoRA linears, h = silu(gate)*up (fp32 math,
     cast to x dtype), down LoRA linear.  Returns (out, gate, up, h)."""
     cast = (lambda t: t) if dtype is None else (lambda t: t.to(dtype))
@@ -245,34 +262,35 @@ def lora_mlp_forward(x, g, u, d, dtype=None):
     gw, ga, gb, gs = g
     uw, ua, ub, us = u
     dw, da, db, ds = d
-    gate = lora_linear(xf, cast(gw), cast(ga), cast(gb), gs)
-    up = lora_linear(xf, cast(uw), cast(ua), cast(ub), us)
+    gate = _store(lora_linear(xf, cast(gw), cast(ga), cast(gb), gs, store_dtype), store_dtype)
+    up = _store(lora_linear(xf, cast(uw), cast(ua), cast(ub), us, store_dtype), store_dtype)
     gf = gate.float()
-    h = (gf * torch.sigmoid(gf) * up.float()).to(xf.dtype)
-    out = lora_linear(h, cast(dw), cast(da), cast(db), ds)
+    h = _store((gf * torch.sigmoid(gf) * up.float()).to(xf.dtype), store_dtype)
+    out = lora_linear(h, cast(dw), cast(da), cast(db), ds, store_dtype)
     return out.view(*x.shape[:-1], -1), gate, up, h
 
 
-def lora_mlp_backward(x, g, u, d, dy, dtype=None):
+def lora_mlp_backward(x, g, u, d, dy, dtype=None, store_dtype=None):
     """ops/fused_lora.py:209-266.  Returns (dX, [(dA, dB) for gate, up, down])."""
     cast = (lambda t: t) if dtype is None else (lambda t: t.to(dtype))
-    _, gate, up, h = lora_mlp_forward(x, g, u, d, dtype)
+    _, gate, up, h = lora_mlp_forward(x, g, u, d, dtype, store_dtype)
     xf = cast(x).reshape(-1, x.shape[-1])
     dyf = cast(dy).reshape(-1, dy.shape[-1])
     gw, ga, gb, gs = (cast(t) if torch.is_tensor(t) else t for t in g)
     uw, ua, ub, us = (cast(t) if torch.is_tensor(t) else t for t in u)
     dw, da, db, ds = (cast(t) if torch.is_tensor(t) else t for t in d)
     dt = dyf.dtype
-    d_da, d_db = _lora_grads(dyf, h, da, db, ds)
-    dh = dyf @ dw + (dyf @ db.to(dt)) @ da.to(dt) * ds
+    d_da, d_db = _lora_grads(dyf, h, da, db, ds, store_dtype)
+    dh = _store(dyf @ dw + _store(dyf @ db.to(dt), store_dtype) @ da.to(dt) * ds, store_dtype)
     gf, uf = gate.float(), up.float()
     sg = torch.sigmoid(gf)
     dhf = dh.float()
-    d_gate = (dhf * uf * sg * (1.0 + gf * (1.0 - sg))).to(dt)
-    d_up = (dhf * (gf * sg)).to(dt)
-    g_grads = _lora_grads(d_gate, xf, ga, gb, gs)
-    u_grads = _lora_grads(d_up, xf, ua, ub, us)
-    dx = _lora_dx(d_gate, gw, ga, gb, gs) + _lora_dx(d_up, uw, ua, ub, us)
+    d_gate = _store((dhf * uf * sg * (1.0 + gf * (1.0 - sg))).to(dt), store_dtype)
+    d_up = _store((dhf * (gf * sg)).to(dt), store_dtype)
+    g_grads = _lora_grads(d_gate, xf, ga, gb, gs, store_dtype)
+    u_grads = _lora_grads(d_up, xf, ua, ub, us, store_dtype)
+    dx = _lora_dx(d_gate, gw, ga, gb, gs, store_dtype) + \
+        _lora_dx(d_up, uw, ua, ub, us, store_dtype)
     return dx.view(*x.shape), [g_grads, u_grads, (d_da, d_db)]
 
 

@@ -1,0 +1,234 @@
+"""Fused LoRA QKV / MLP CUDA parity and the patched model end to end.
+
+The products run on bf16 tensor cores with fp32 accumulation, so comparisons
+are at the bf16 tolerance (2e-2 relative / 1e-2 absolute element-wise) against
+an fp32 evaluation of the oracle on the same inputs, plus a relative Frobenius
+bound.  A/B gradients come back in fp32 as in the reference.
+"""
+
+import copy
+
+import pytest
+import torch
+
+from conftest import golden_names, load_golden
+from oracle import ops as O
+from tolerances import assert_close
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+F32 = torch.float32
+BF = torch.bfloat16  # storage dtype of the reference's intermediates for bf16 inputs
+
+
+def _tuple(d, n):
+    return (d[f"{n}_w"], d[f"{n}_a"], d[f"{n}_b"], float(d["s"]))
+
+
+def _leaf(t):
+    return t.detach().clone().to(DEV).requires_grad_(True)
+
+
+def run_qkv(x, q, k, v, dq, dk, dv):
+    from metal_liger_b200.ops.fused_lora import _LoRA_QKV
+    xl = _leaf(x)
+    params = []
+    for (w, a, b, s) in (q, k, v):
+        params.append((w.to(DEV), _leaf(a), _leaf(b), s))
+    flat = [t for p in params for t in p]
+    Q, K, V = _LoRA_QKV.apply(xl, *flat)
+    torch.autograd.backward([Q, K, V], [dq.to(DEV), dk.to(DEV), dv.to(DEV)])
+    torch.cuda.synchronize()
+    grads = [(p[1].grad, p[2].grad) for p in params]
+    return (Q.detach(), K.detach(), V.detach()), xl.grad, grads
+
+
+def run_mlp(x, g, u, d, dy):
+    from metal_liger_b200.ops.fused_lora import _LoRA_MLP
+    xl = _leaf(x)
+    params = []
+    for (w, a, b, s) in (g, u, d):
+        params.append((w.to(DEV), _leaf(a), _leaf(b), s))
+    flat = [t for p in params for t in p]
+    out = _LoRA_MLP.apply(xl, *flat)
+    out.backward(dy.to(DEV))
+    torch.cuda.synchronize()
+    grads = [(p[1].grad, p[2].grad) for p in params]
+    return out.detach(), xl.grad, grads
+
+
+def close(got, exp, what, norm=2e-2):
+    assert_close(got.float().cpu(), exp.float().cpu(), dtype=torch.bfloat16, norm_rtol=norm,
+                 what=what)
+
+
+def close_reduction(got, exp, what, norm=1e-2):
+    """dA / dB are sums over every token of products of bf16 operands (and are
+    cast to the bf16 parameter dtype by autograd, as in the reference), so their
+    absolute error scales with the tensor's RMS, not with each element:
+    |got - exp| <= 2e-2 * max(|exp|, rms(exp)) + 1e-2, plus a Frobenius bound."""
+    g = got.float().cpu()
+    e = exp.float().cpu()
+    rms = e.pow(2).mean().sqrt().item()
+    bad = (g - e).abs() > 2e-2 * torch.clamp(e.abs(), min=rms) + 1e-2
+    assert not bad.any(), f"{what}: {int(bad.sum())} / {bad.numel()} elements out of tolerance"
+    rel = ((g - e).norm() / e.norm().clamp(min=1e-30)).item()
+    assert rel <= norm, f"{what}: relative Frobenius error {rel:.3e} > {norm}"
+
+
+def close_fp32_inputs(got, exp, what):
+    """fp32 inputs enter the tensor cores rounded to bf16, so the element-wise
+    absolute floor scales with the tensor's magnitude; the Frobenius bound is
+    the bf16 one."""
+    scale = max(1.0, exp.float().abs().max().item())
+    assert_close(got.float().cpu(), exp.float().cpu(), rtol=2e-2, atol=1e-2 * scale,
+                 norm_rtol=2e-2, what=what)
+
+
+@pytest.mark.parametrize("name", golden_names("lora_qkv"))
+def test_qkv_against_reference_fixture(name):
+    d = load_golden(name)
+    q, k, v = (_tuple(d, n) for n in ("q", "k", "v"))
+    outs, dx, grads = run_qkv(d["x"], q, k, v, d["dq"], d["dk"], d["dv"])
+    for got, key in zip(outs, ("Q", "K", "V")):
+        assert got.dtype == d[key].dtype
+        close_fp32_inputs(got, d[key], f"{name} {key}")
+    close_fp32_inputs(dx, d["dx"], f"{name} dX")
+    for (da, db), n in zip(grads, ("q", "k", "v")):
+        close_fp32_inputs(da, d[f"{n}_da"], f"{name} d{n}A")
+        close_fp32_inputs(db, d[f"{n}_db"], f"{name} d{n}B")
+
+
+def test_mlp_against_reference_fixture():
+    d = load_golden("lora_mlp_f32")
+    g, u, dn = (_tuple(d, n) for n in ("gate", "up", "down"))
+    out, dx, grads = run_mlp(d["x"], g, u, dn, d["dy"])
+    close_fp32_inputs(out, d["out"], "out")
+    close_fp32_inputs(dx, d["dx"], "dX")
+    for (da, db), n in zip(grads, ("gate", "up", "down")):
+        close_fp32_inputs(da, d[f"{n}_da"], f"d{n}A")
+        close_fp32_inputs(db, d[f"{n}_db"], f"d{n}B")
+
+
+def _proj(gen, out_f, in_f, r, s, dev="cpu", wstd=0.02, astd=0.05):
+    w = (wstd * torch.randn(out_f, in_f, generator=gen, device=dev)).bfloat16()
+    a = (astd * torch.randn(r, in_f, generator=gen, device=dev)).bfloat16()
+    b = (astd * torch.randn(out_f, r, generator=gen, device=dev)).bfloat16()
+    return (w, a, b, s)
+
+
+@pytest.mark.parametrize("T,H,qo,kvo,r", [(400, 512, 512, 128, 16), (130, 256, 256, 64, 8),
+                                          (64, 128, 128, 128, 21)])
+def test_qkv_bf16_against_oracle(T, H, qo, kvo, r):
+    gen = torch.Generator().manual_seed(T + H)
+    x = torch.randn(2, T // 2, H, generator=gen).bfloat16()
+    q, k, v = _proj(gen, qo, H, r, 2.0), _proj(gen, kvo, H, r, 1.5), _proj(gen, kvo, H, r, 0.5)
+    dq = torch.randn(2, T // 2, qo, generator=gen).bfloat16()
+    dk = torch.randn(2, T // 2, kvo, generator=gen).bfloat16()
+    dv = torch.randn(2, T // 2, kvo, generator=gen).bfloat16()
+    outs, dx, grads = run_qkv(x, q, k, v, dq, dk, dv)
+    rq, rk, rv = O.lora_qkv_forward(x, q, k, v, dtype=F32, store_dtype=BF)
+    rdx, rgrads = O.lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=F32, store_dtype=BF)
+    for got, exp, n in zip(outs, (rq, rk, rv), "QKV"):
+        assert got.dtype == torch.bfloat16
+        close(got, exp, n)
+    close(dx, rdx, "dX")
+    for (da, db), (rda, rdb), n in zip(grads, rgrads, "qkv"):
+        assert da.dtype == torch.bfloat16 and da.shape == (r, H)
+        close_reduction(da, rda, f"d{n}A")
+        close_reduction(db, rdb, f"d{n}B")
+
+
+@pytest.mark.parametrize("T,H,I,r", [(300, 256, 768, 16), (128, 128, 384, 32)])
+def test_mlp_bf16_against_oracle(T, H, I, r):
+    gen = torch.Generator().manual_seed(T + I)
+    x = torch.randn(T, H, generator=gen).bfloat16()
+    g, u, d = _proj(gen, I, H, r, 2.0), _proj(gen, I, H, r, 2.0), _proj(gen, H, I, r, 2.0)
+    dy = torch.randn(T, H, generator=gen).bfloat16()
+    out, dx, grads = run_mlp(x, g, u, d, dy)
+    rout, _, _, _ = O.lora_mlp_forward(x, g, u, d, dtype=F32, store_dtype=BF)
+    rdx, rgrads = O.lora_mlp_backward(x, g, u, d, dy, dtype=F32, store_dtype=BF)
+    close(out, rout, "out")
+    close(dx, rdx, "dX")
+    for (da, db), (rda, rdb), n in zip(grads, rgrads, ("gate", "up", "down")):
+        close_reduction(da, rda, f"d{n}A")
+        close_reduction(db, rdb, f"d{n}B")
+
+
+def test_reference_test_case():
+    """tests/test_fused_ops.py:198-240 (seed 42, X [2,16,128], W 128x128, r=8, s=2),
+    checked against autograd of the plain expression in fp32."""
+    torch.manual_seed(42)
+    X = torch.randn(2, 16, 128)
+    mk = lambda: (torch.randn(128, 128), torch.randn(8, 128), torch.randn(128, 8), 2.0)  # noqa
+    q, k, v = mk(), mk(), mk()
+    ones = [torch.ones(2, 16, 128)] * 3
+    outs, dx, grads = run_qkv(X, q, k, v, *ones)
+    rq, rk, rv = O.lora_qkv_forward(X, q, k, v)
+    rdx, rgrads = O.lora_qkv_backward(X, q, k, v, *ones)
+    for got, exp, n in zip(outs, (rq, rk, rv), "QKV"):
+        close_fp32_inputs(got, exp, n)
+    close_fp32_inputs(dx, rdx, "dX")
+    close_fp32_inputs(grads[0][0], rgrads[0][0], "dQA")
+    close_fp32_inputs(grads[0][1], rgrads[0][1], "dQB")
+
+
+def test_baseline_config_c4_full_size():
+    """X [8,2048,4096]; Wq [4096,4096], Wk/Wv [1024,4096],
+    Wgate/Wup [12288,4096], Wdown [4096,12288] ~N(0,0.02); r=16, alpha=32 (s=2),
+    A, B ~N(0,0.01); upstream grads ~N(0,1).  fp32 reference on the GPU."""
+    torch.backends.cuda.matmul.allow_tf32 = False
+    gen = torch.Generator(device=DEV).manual_seed(1237)
+    T, H, I, r, s = 8 * 2048, 4096, 12288, 16, 2.0
+    x = torch.randn(8, 2048, H, generator=gen, device=DEV).bfloat16()
+    P = lambda o, i: _proj(gen, o, i, r, s, dev=DEV, wstd=0.02, astd=0.01)  # noqa: E731
+    q, k, v = P(4096, H), P(1024, H), P(1024, H)
+    dq = torch.randn(8, 2048, 4096, generator=gen, device=DEV).bfloat16()
+    dk = torch.randn(8, 2048, 1024, generator=gen, device=DEV).bfloat16()
+    dv = torch.randn(8, 2048, 1024, generator=gen, device=DEV).bfloat16()
+    outs, dx, grads = run_qkv(x, q, k, v, dq, dk, dv)
+    rq, rk, rv = O.lora_qkv_forward(x, q, k, v, dtype=F32, store_dtype=BF)
+    for got, exp, n in zip(outs, (rq, rk, rv), "QKV"):
+        close(got, exp, f"C4 {n}", norm=1e-2)
+    del rq, rk, rv
+    rdx, rgrads = O.lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=F32, store_dtype=BF)
+    close(dx, rdx, "C4 QKV dX", norm=1e-2)
+    for (da, db), (rda, rdb), n in zip(grads, rgrads, "qkv"):
+        close_reduction(da, rda, f"C4 d{n}A")
+        close_reduction(db, rdb, f"C4 d{n}B")
+    del outs, dx, grads, rdx, rgrads, dq, dk, dv
+    torch.cuda.empty_cache()
+    g, u, d = P(I, H), P(I, H), P(H, I)
+    dy = torch.randn(8, 2048, H, generator=gen, device=DEV).bfloat16()
+    out, dx, grads = run_mlp(x, g, u, d, dy)
+    # fp32 products, bf16 storage of gate/up/h/dH/d_gate/d_up as in the reference
+    rout, _, _, _ = O.lora_mlp_forward(x, g, u, d, dtype=F32, store_dtype=BF)
+    close(out, rout, "C4 MLP out", norm=1e-2)
+    del rout
+    rdx, rgrads = O.lora_mlp_backward(x, g, u, d, dy, dtype=F32, store_dtype=BF)
+    close(dx, rdx, "C4 MLP dX", norm=1e-2)
+    for (da, db), (rda, rdb), n in zip(grads, rgrads, ("gate", "up", "down")):
+        close_reduction(da, rda, f"C4 d{n}A")
+        close_reduction(db, rdb, f"C4 d{n}B")
+    torch.cuda.empty_cache()
+
+
+def test_patched_model_matches_unpatched():
+    from metal_liger_b200 import apply_metal_liger_to_qwen3vl
+    from peft_stub import make_model
+    ref = make_model(n_layers=2, h=128, q_out=128, kv_out=32, inter=256, r=8).to(DEV).bfloat16()
+    fused = copy.deepcopy(ref)
+    apply_metal_liger_to_qwen3vl(fused)
+    x = torch.randn(2, 24, 128, device=DEV).bfloat16()
+    outs, grads = [], []
+    for m in (ref, fused):
+        xi = x.clone().requires_grad_(True)
+        y = m(xi)
+        (y.float() ** 2).mean().backward()
+        outs.append((y.detach(), xi.grad))
+        grads.append({n: p.grad for n, p in m.named_parameters() if p.grad is not None})
+    close(outs[1][0], outs[0][0], "patched output", norm=2e-2)
+    close(outs[1][1], outs[0][1], "patched dX", norm=3e-2)
+    assert set(grads[0]) == set(grads[1])
+    for n in grads[0]:
+        close_reduction(grads[1][n], grads[0][n], f"grad {n}", norm=3e-2)
