@@ -171,6 +171,19 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.kb_total = kb_total;
   prm.raster = pr.raster;
   prm.group_m = pr.group_m;
+  if (pr.raster == 0 && pr.group_m == 0 && prm.n_tiles > 1) {
+    // M-fastest raster re-reads all of A once per N-tile column.  When A does
+    // not fit comfortably in L2, sweep the N-tiles in groups of M-tiles whose
+    // A rows (~16 MB) stay resident, so A is read from HBM about once and B
+    // once per group.
+    int64_t k_total = 0;
+    for (int s = 0; s < pr.nseg; ++s) k_total += pr.seg[s].K;
+    const int64_t a_bytes_per_mtile = (int64_t)BM * k_total * 2;
+    if ((int64_t)prm.m_tiles * a_bytes_per_mtile > ((int64_t)48 << 20)) {
+      const int64_t g = std::max<int64_t>(1, ((int64_t)16 << 20) / a_bytes_per_mtile);
+      prm.group_m = (int)std::min<int64_t>(g, prm.m_tiles);
+    }
+  }
   prm.epi = pr.epi;
   prm.d_f32 = pr.d_f32 ? 1 : 0;
   prm.D = pr.D;

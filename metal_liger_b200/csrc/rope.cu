@@ -7,12 +7,12 @@
 // d + D/2 uses cos[d+D/2]/sin[d+D/2], exactly as the broadcast expression
 // does, so tables whose halves differ give the reference's answer too.
 //
-// Launch shape: one CTA per (batch, tile of kPos positions).  The CTA first
-// materialises cos/sin for its positions in shared memory (in recompute mode
-// from fp32 pos*inv_freq, so HBM never sees a table), then streams every
-// head row of q and k for those positions: each row is split into
-// 16-byte vectors of the first and second half, so one thread holds the
-// (d, d+D/2) pairs it rotates.  Reads/writes are fully coalesced per row.
+// Launch shape: work units of (batch, 16 positions, 8 heads of q|k), taken in
+// contiguous ranges by a grid of ~4 waves.  Each thread owns one position and
+// 16 bytes of each half of the head dim, keeps that position's cos/sin for
+// its frequencies in registers (recompute mode: fp32 pos*inv_freq, sincosf,
+// so HBM never sees a table) and rotates 4 head rows per step with all loads
+// in flight together.  Each row half is a coalesced 16-byte-per-thread access.
 #include "common.cuh"
 
 #include <algorithm>
@@ -20,9 +20,11 @@
 namespace ml {
 namespace {
 
-constexpr int kPos = 8;        // positions per CTA
-constexpr int kThreads = 256;
-constexpr int kMaxHeadDim = 512;  // 2*kPos*512*4 B = 32 KB of shared memory
+constexpr int kPos = 16;       // positions per work unit (one per thread group)
+constexpr int kHeads = 8;      // heads per work unit
+constexpr int kBatch = 4;      // rows per thread with loads in flight together
+constexpr int kThreads = 256;  // upper bound; positions per unit shrink for wide rows
+constexpr int kMaxHeadDim = 512;
 
 struct RopeView {
   const void* in;
@@ -80,100 +82,138 @@ __device__ __forceinline__ void store_n(T* p, const float* f) {
   }
 }
 
-// VEC = elements of each half handled per thread (16 bytes of Tin, or 1 for
-// the scalar path).
+// Work unit = (batch, block of kPos positions, block of kHeads heads of the
+// concatenated [q heads..., k heads...] list).  A CTA of kPos*TPH threads owns
+// one position per thread group; each thread owns VEC frequencies, so it
+// evaluates its 2*VEC cos/sin values once per position block (in registers,
+// no shared memory, no barrier) and applies them to every head row of the
+// unit.  CTAs take contiguous ranges of units (head blocks fastest), so cos/sin
+// are recomputed only when the position block changes.
 template <typename Tin, typename Tout, int VEC>
-__global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a) {
-  extern __shared__ float smem_cs[];  // [2][kPos][head_dim]
+__global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_t units_per_cta,
+                                                        int npos) {
   const int64_t D = a.head_dim;
-  float* cs_base = smem_cs;
-  float* sn_base = smem_cs + kPos * D;
-#define cs_s(p, d) cs_base[(p) * D + (d)]
-#define sn_s(p, d) sn_base[(p) * D + (d)]
   const int64_t half = D >> 1;
-  const int64_t tiles = (a.seq + kPos - 1) / kPos;
-  const int64_t b = blockIdx.x / tiles;
-  const int64_t s0 = (blockIdx.x % tiles) * kPos;
-  const int np = (int)(a.seq - s0 < kPos ? a.seq - s0 : kPos);
-
-  // 1) cos/sin for this CTA's positions.
-  if (a.cos != nullptr) {
-    for (int idx = threadIdx.x; idx < np * D; idx += blockDim.x) {
-      const int p = idx / (int)D;
-      const int64_t d = idx % D;
-      const int64_t off = b * a.cs[0] + (s0 + p) * a.cs[1] + d * a.cs[2];
-      cs_s(p, d) = load_as_f32(a.cos, off, a.cs_dtype);
-      sn_s(p, d) = load_as_f32(a.sin, off, a.cs_dtype);
-    }
-  } else {
-    for (int idx = threadIdx.x; idx < np * half; idx += blockDim.x) {
-      const int p = idx / (int)half;
-      const int64_t i = idx % half;
-      const int64_t s = s0 + p;
-      const int64_t pos = a.positions != nullptr ? a.positions[b * a.pos_sb + s] : s;
-      const float ang = (float)pos * a.inv_freq[i];
-      float sv, cv;
-      sincosf(ang, &sv, &cv);
-      cv *= a.scaling;
-      sv *= a.scaling;
-      cs_s(p, i) = cv;
-      cs_s(p, i + half) = cv;
-      sn_s(p, i) = sv;
-      sn_s(p, i + half) = sv;
-    }
-  }
-  __syncthreads();
-
-  // 2) rotate every (tensor, head, position) row.
-  const int tph = (int)(half / VEC);  // threads per row
-  const int slots = blockDim.x / tph; // rows in flight per CTA step
-  const int slot = threadIdx.x / tph;
+  const int tph = (int)(half / VEC);           // threads per row
+  const int pgrp = threadIdx.x / tph;          // position within the block
   const int lane = threadIdx.x % tph;
-  if (slot >= slots) return;
+  if (pgrp >= npos) return;
   const int64_t d0 = (int64_t)lane * VEC;
+  const int64_t heads_total = a.t[0].heads + (a.ntensors > 1 ? a.t[1].heads : 0);
+  const int64_t hblocks = (heads_total + kHeads - 1) / kHeads;
+  const int64_t pblocks = (a.seq + npos - 1) / npos;
+  const int64_t units = a.batch * pblocks * hblocks;
+  const int64_t u0 = (int64_t)blockIdx.x * units_per_cta;
+  const int64_t u1 = u0 + units_per_cta < units ? u0 + units_per_cta : units;
   const float sign = a.sign;
-  for (int ti = 0; ti < a.ntensors; ++ti) {
-    const RopeView& v = a.t[ti];
-    const int64_t nrows = v.heads * np;
-    const Tin* in = static_cast<const Tin*>(v.in);
-    Tout* out = static_cast<Tout*>(v.out);
-    for (int64_t r = slot; r < nrows; r += slots) {
-      const int64_t h = r / np;
-      const int p = (int)(r % np);
-      const int64_t s = s0 + p;
-      const Tin* xr = in + b * v.is[0] + h * v.is[1] + s * v.is[2];
-      Tout* yr = out + b * v.os[0] + h * v.os[1] + s * v.os[2];
-      float x1[VEC], x2[VEC], y1[VEC], y2[VEC];
-      load_n<Tin, VEC>(xr + d0, x1);
-      load_n<Tin, VEC>(xr + half + d0, x2);
+  float c1[VEC], c2[VEC], s1[VEC], s2[VEC];
+  int64_t cached = -1;
+  for (int64_t u = u0; u < u1; ++u) {
+    const int64_t bp = u / hblocks;            // (batch, position block)
+    const int64_t hb = u - bp * hblocks;
+    const int64_t b = bp / pblocks;
+    const int64_t s = (bp - b * pblocks) * npos + pgrp;
+    const bool pos_ok = s < a.seq;
+    if (bp != cached) {
+      cached = bp;
+      if (pos_ok) {
+        if (a.cos != nullptr) {
+          const int64_t base = b * a.cs[0] + s * a.cs[1];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const int64_t d = d0 + j;
-        y1[j] = x1[j] * cs_s(p, d) - x2[j] * (sign * sn_s(p, d));
-        y2[j] = x2[j] * cs_s(p, d + half) + x1[j] * (sign * sn_s(p, d + half));
+          for (int j = 0; j < VEC; ++j) {
+            c1[j] = load_as_f32(a.cos, base + (d0 + j) * a.cs[2], a.cs_dtype);
+            c2[j] = load_as_f32(a.cos, base + (d0 + j + half) * a.cs[2], a.cs_dtype);
+            s1[j] = load_as_f32(a.sin, base + (d0 + j) * a.cs[2], a.cs_dtype);
+            s2[j] = load_as_f32(a.sin, base + (d0 + j + half) * a.cs[2], a.cs_dtype);
+          }
+        } else {
+          const int64_t pos = a.positions != nullptr ? a.positions[b * a.pos_sb + s] : s;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            float sv, cv;
+            sincosf((float)pos * a.inv_freq[d0 + j], &sv, &cv);
+            c1[j] = c2[j] = cv * a.scaling;
+            s1[j] = s2[j] = sv * a.scaling;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          s1[j] *= sign;
+          s2[j] *= sign;
+        }
       }
-      store_n<Tout, VEC>(yr + d0, y1);
-      store_n<Tout, VEC>(yr + half + d0, y2);
+    }
+    if (!pos_ok) continue;
+    // rows of this unit: heads [hb*kHeads, ...) of the concatenated list
+    const int64_t h_begin = hb * kHeads;
+    const int64_t h_end = h_begin + kHeads < heads_total ? h_begin + kHeads : heads_total;
+#pragma unroll 1
+    for (int64_t h0 = h_begin; h0 < h_end; h0 += kBatch) {
+      float x1[kBatch][VEC], x2[kBatch][VEC];
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        const int64_t hh = h0 + q;
+        if (hh < h_end) {
+          const int ti = hh < a.t[0].heads ? 0 : 1;
+          const RopeView& v = a.t[ti];
+          const int64_t h = ti == 0 ? hh : hh - a.t[0].heads;
+          const Tin* xr = static_cast<const Tin*>(v.in) + b * v.is[0] + h * v.is[1] + s * v.is[2];
+          load_n<Tin, VEC>(xr + d0, x1[q]);
+          load_n<Tin, VEC>(xr + half + d0, x2[q]);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kBatch; ++q) {
+        const int64_t hh = h0 + q;
+        if (hh < h_end) {
+          const int ti = hh < a.t[0].heads ? 0 : 1;
+          const RopeView& v = a.t[ti];
+          const int64_t h = ti == 0 ? hh : hh - a.t[0].heads;
+          float y1[VEC], y2[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            y1[j] = x1[q][j] * c1[j] - x2[q][j] * s1[j];
+            y2[j] = x2[q][j] * c2[j] + x1[q][j] * s2[j];
+          }
+          Tout* yr = static_cast<Tout*>(v.out) + b * v.os[0] + h * v.os[1] + s * v.os[2];
+          store_n<Tout, VEC>(yr + d0, y1);
+          store_n<Tout, VEC>(yr + half + d0, y2);
+        }
+      }
     }
   }
-#undef cs_s
-#undef sn_s
 }
 
 template <typename Tin, typename Tout>
 int launch(const RopeArgs& a, bool vec_ok, cudaStream_t st) {
-  const int64_t tiles = (a.seq + kPos - 1) / kPos;
-  const int64_t grid = a.batch * tiles;
-  if (grid > 0x7fffffff) {
-    set_error("rope: grid too large");
-    return ML_ERR_INVALID_ARG;
-  }
   constexpr int V = 16 / sizeof(Tin);
-  const size_t smem = 2 * kPos * (size_t)a.head_dim * sizeof(float);
+  const int vec = vec_ok ? V : 1;
+  const int64_t half = a.head_dim / 2;
+  const int tph = (int)(half / vec);
+  if (tph > kThreads) {
+    set_error("rope: head_dim too large for the launch shape");
+    return ML_ERR_UNSUPPORTED;
+  }
+  const int npos = std::max(1, std::min(kPos, kThreads / tph));
+  const int threads = std::max(32, (tph * npos + 31) / 32 * 32);
+  const int64_t heads_total = a.t[0].heads + (a.ntensors > 1 ? a.t[1].heads : 0);
+  const int64_t units = a.batch * ((a.seq + npos - 1) / npos) * ((heads_total + kHeads - 1) / kHeads);
+  int per_sm = 0;
+  auto kv = rope_kernel<Tin, Tout, V>;
+  auto k1 = rope_kernel<Tin, Tout, 1>;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, vec_ok ? (const void*)kv : (const void*)k1,
+                                                threads, 0);
+  per_sm = std::max(per_sm, 1);
+  // one unit per CTA while that keeps the grid under ~8 waves (small tail);
+  // beyond that, contiguous unit ranges amortise the cos/sin evaluation
+  int64_t ctas = std::min<int64_t>(units, (int64_t)num_sms() * per_sm * 8);
+  ctas = std::max<int64_t>(ctas, 1);
+  const int64_t per_cta = (units + ctas - 1) / ctas;
+  ctas = (units + per_cta - 1) / per_cta;
   if (vec_ok)
-    rope_kernel<Tin, Tout, V><<<(unsigned)grid, kThreads, smem, st>>>(a);
+    kv<<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
   else
-    rope_kernel<Tin, Tout, 1><<<(unsigned)grid, kThreads, smem, st>>>(a);
+    k1<<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
   ML_CHECK_LAUNCH("rope");
   return ML_OK;
 }
