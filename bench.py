@@ -390,34 +390,60 @@ class Flce:
 
     def __init__(self):
         self.tokens = self.N
-        f = 6.0 * self.N * self.H * self.V  # logits, dX and dW GEMMs once each
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        # vocabulary shard of this rank (the whole vocabulary on one GPU)
+        base, rem = divmod(self.V, self.world)
+        self.v_local = base + (1 if self.rank < rem else 0)
+        f = 6.0 * self.N * self.H * self.v_local  # logits, dX and dW GEMMs once each
         self.flops = {"flce_forward": f}
         self.bytes = {}
+        if self.world > 1:
+            self.scaling = "strong"
+            self.per_rank_tokens = False
         # count, (logits GEMM, lse, transform, dX GEMM, dW GEMM, memset) per chunk, loss;
         # backward: two scale-casts
         self.launches_per_step = 1 + 5 * (self.N // self.CHUNK) + 1 + 2
 
     def config(self):
+        par = ("single GPU" if self.world == 1 else
+               f"vocab-parallel over {self.world} GPUs (lm_head rows sharded; per-chunk NCCL "
+               f"all-reduce of row max / sum-exp / target logit and of partial dX)")
         return {"workload": "flce_bf16 (BASELINE configs[2]): hidden [16384,2048] ~N(0,1), "
                             "lm_head W [151936,2048] ~N(0,0.02), 10% labels = -100, token "
                             "chunk 8192, mean over non-ignored; loss + dX + dW",
                 "tokens_per_step": self.N, "hidden": self.H, "vocab": self.V,
-                "chunk_tokens": self.CHUNK, "parallelism": "single GPU (vocab-parallel is a "
-                "separate path)", "l2": "inputs larger than L2 (W 622 MB)"}
+                "vocab_per_rank": self.v_local, "chunk_tokens": self.CHUNK,
+                "parallelism": par, "l2": "inputs larger than L2 (W 622 MB)"}
 
     def make_inputs(self, device, seed=1236):
+        from metal_liger_b200.ops.fused_linear_cross_entropy import shard_lm_head
+
         g = torch.Generator(device=device).manual_seed(seed)
         h = torch.randn(self.N, self.H, generator=g, device=device).bfloat16()
         w = (0.02 * torch.randn(self.V, self.H, generator=g, device=device)).bfloat16()
         lab = torch.randint(0, self.V, (self.N,), generator=g, device=device)
         lab[torch.randperm(self.N, generator=g, device=device)[: self.N // 10]] = -100
         go = torch.ones((), device=device)
-        return {"h": h, "w": w, "lab": lab, "go": go}
+        ws, off = shard_lm_head(w, self.rank, self.world)
+        ws = ws.contiguous()
+        del w
+        return {"h": h, "w": ws, "off": off, "lab": lab, "go": go}
+
+    def _vp(self, t):
+        from metal_liger_b200.ops.fused_linear_cross_entropy import vocab_parallel_flce
+
+        loss, dx, dw = vocab_parallel_flce(t["h"], t["w"], t["lab"], t["off"],
+                                           chunk_size=self.CHUNK)
+        return loss, dx.unsqueeze(0), dw
 
     def step(self, t, timer=plain):
         ops = torch.ops.metal_liger
-        loss, dx, dw = timer("flce_forward", ops.flce_forward, t["h"], t["w"], t["lab"], None,
-                             -100, self.CHUNK, True, True)
+        if self.world == 1:
+            loss, dx, dw = timer("flce_forward", ops.flce_forward, t["h"], t["w"], t["lab"], None,
+                                 -100, self.CHUNK, True, True)
+        else:
+            loss, dx, dw = timer("flce_forward", self._vp, t)
         timer("flce_backward", ops.flce_backward, t["go"], dx, dw, 1, 1)
 
     def e2e_setup(self, device):
@@ -429,7 +455,8 @@ class Flce:
                     "dw": torch.empty_like(host["w"]).pin_memory()}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
-        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h}
+        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h,
+                "off": t["off"]}
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_linear_cross_entropy import \
@@ -440,7 +467,14 @@ class Flce:
             d[k].copy_(h[k], non_blocking=True)
         hid = d["h"].detach().requires_grad_(True)
         w = d["w"].detach().requires_grad_(True)
-        loss = _FusedLinearCrossEntropyFunction.apply(hid, w, d["lab"], None, -100, self.CHUNK)
+        if self.world == 1:
+            loss = _FusedLinearCrossEntropyFunction.apply(hid, w, d["lab"], None, -100,
+                                                          self.CHUNK)
+        else:
+            from metal_liger_b200.ops.fused_linear_cross_entropy import \
+                _VocabParallelFLCEFunction
+            loss = _VocabParallelFLCEFunction.apply(hid, w, d["lab"], None, s["off"], -100,
+                                                    self.CHUNK, None)
         loss.backward()
         ho["loss"].copy_(loss.detach(), non_blocking=True)
         ho["dh"].copy_(hid.grad, non_blocking=True)
@@ -720,7 +754,9 @@ def run_gpu_arm(args, wl):
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         elapsed_ms = el.item()
     kernel_ms = timer.averages_ms()
-    value = world * wl.tokens * args.steps / (elapsed_ms / 1e3)
+    # weak scaling: every rank processes wl.tokens; strong: the job processes wl.tokens
+    job_tokens = wl.tokens * (world if getattr(wl, "scaling", "weak") == "weak" else 1)
+    value = job_tokens * args.steps / (elapsed_ms / 1e3)
 
     # ---- end to end through the public API with host buffers ----
     del t
@@ -744,7 +780,7 @@ def run_gpu_arm(args, wl):
         el = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         e2e_ms = el.item()
-    e2e_value = world * wl.tokens * e2e_steps / (e2e_ms / 1e3)
+    e2e_value = job_tokens * e2e_steps / (e2e_ms / 1e3)
     h2d, d2h = s["h2d"], s["d2h"]
     del s
     torch.cuda.empty_cache()
@@ -798,7 +834,7 @@ def run_gpu_arm(args, wl):
             "warmup": args.warmup,
             "ms_per_step": elapsed_ms / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None,
             "dtype": wl.dtype,
             "data": "synthetic (seeded normal inputs of the BASELINE shapes)",

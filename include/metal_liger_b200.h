@@ -256,6 +256,45 @@ ML_API int ml_flce_backward(const float* grad_output, const float* dx_slabs, int
                             const float* dw_acc, void* dweight, int dw_dtype, int64_t v,
                             void* stream);
 
+/* --- vocabulary-parallel FLCE (weight sharded by vocabulary rows) -------- */
+
+/* out[0] = #(labels != ignore_index), out[1] = 1 / max(out[0], 1) (fp32, device). */
+ML_API int ml_flce_count_valid(const int64_t* labels, int64_t n, int64_t ignore_index, float* out,
+                               void* stream);
+
+/* Workspace bytes shared by ml_flce_shard_stats / _grads for one token chunk. */
+ML_API size_t ml_flce_shard_workspace_bytes(int64_t rows, int64_t v_local);
+
+/*
+ * Phase 1 for one token chunk on one vocabulary shard (weight rows
+ * [vocab_offset, vocab_offset + v_local) of the full lm_head): per row the
+ * shard's logit max, sum exp(logit - max) and the target logit (0 when the
+ * label lies outside the shard).  The shard's exp(logit - tile max) values
+ * stay in `workspace` for phase 2.  The caller merges the three [rows]
+ * vectors across ranks (max, then rescaled sum; target by sum) into the
+ * global log-sum-exp.  Same math as _chunked_forward_pass
+ * (reference ops/fused_linear_cross_entropy.py:39-55), split by vocabulary.
+ */
+ML_API int ml_flce_shard_stats(const void* hidden, const void* weight, const void* bias,
+                               int bias_dtype, const int64_t* labels, int64_t rows, int64_t h,
+                               int64_t v_local, int64_t vocab_offset, int64_t ignore_index,
+                               float* row_max, float* row_sum, float* row_tgt, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/*
+ * Phase 2: with the GLOBAL per-row log-sum-exp `lse` and `scale` (device
+ * scalar, 1/max(#valid,1)), form this shard's (softmax - onehot) * scale and
+ * write dx [rows, h] fp32 (this shard's partial dhidden, to be summed across
+ * ranks) and dw [v_local, h] fp32 (this shard's dweight; accumulated when
+ * dw_accumulate != 0).  Either output may be NULL.  Same math as
+ * _chunked_backward_pass (reference ops/fused_linear_cross_entropy.py:57-80).
+ */
+ML_API int ml_flce_shard_grads(const void* hidden, const void* weight, const int64_t* labels,
+                               int64_t rows, int64_t h, int64_t v_local, int64_t vocab_offset,
+                               int64_t ignore_index, const float* lse, const float* scale,
+                               float* dx, float* dw, int dw_accumulate, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Fused LoRA QKV / MLP
  * ------------------------------------------------------------------------ */

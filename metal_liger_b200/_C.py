@@ -92,6 +92,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                 c_void_p, c_size_t, c_void_p]),
     "ml_flce_backward": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int64, c_int64,
                                  c_void_p, c_void_p, c_int, c_int64, c_void_p]),
+    "ml_flce_count_valid": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    "ml_flce_shard_workspace_bytes": (c_size_t, [c_int64, c_int64]),
+    "ml_flce_shard_stats": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int64,
+                                    c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_size_t, c_void_p]),
+    "ml_flce_shard_grads": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                    c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_int, c_void_p, c_size_t, c_void_p]),
     "ml_lora_qkv_workspace_bytes": (c_size_t, [c_int64, c_int64, ctypes.POINTER(LoraProj), c_int]),
     "ml_lora_qkv_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, ctypes.POINTER(LoraProj),
                                     ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_size_t,

@@ -153,21 +153,23 @@ flce_lse(float* __restrict__ part_m, const float* __restrict__ part_s,
 }
 
 // P = E * f[tile][row] - onehot(label) * scale, in place, 8 bf16 per step.
+// Column c of E holds vocabulary id label_base + c.
 __global__ void __launch_bounds__(256)
 flce_transform(__nv_bfloat16* __restrict__ E, int64_t ldE, int64_t rows, int64_t vocab,
                const float* __restrict__ f, const int64_t* __restrict__ labels, int64_t ignore,
-               const float* __restrict__ cnt) {
+               const float* __restrict__ scale_ptr, int64_t label_base) {
   const int64_t vpr = (vocab + 7) / 8;  // vectors per row
   const int64_t total = rows * vpr;
-  const float scale = cnt[1];
+  const float scale = scale_ptr[0];
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / vpr;
     const int64_t c0 = (i - r * vpr) * 8;
     const int64_t t = c0 / kTileV;
     const float fr = f[t * rows + r];
-    const int64_t lab = labels[r];
-    const float sub = lab != ignore ? scale : 0.f;
+    const int64_t lab0 = labels[r];
+    const float sub = lab0 != ignore ? scale : 0.f;
+    const int64_t lab = lab0 != ignore ? lab0 - label_base : (int64_t)-1;
     __nv_bfloat16* p = E + r * ldE + c0;
     if (c0 + 8 <= vocab) {
       Vec16<__nv_bfloat16> v = *reinterpret_cast<Vec16<__nv_bfloat16>*>(p);
@@ -185,6 +187,64 @@ flce_transform(__nv_bfloat16* __restrict__ E, int64_t ldE, int64_t rows, int64_t
         p[j] = __float2bfloat16_rn(x);
       }
     }
+  }
+}
+
+// Vocabulary-sharded path, phase 1: merge this shard's tile partials into a
+// per-row (max, sum exp(logit - max)).  Block = 32 rows x 8 tile-lanes.
+__global__ void __launch_bounds__(256)
+flce_merge_tiles(const float* __restrict__ part_m, const float* __restrict__ part_s,
+                 int64_t rows, int64_t n_tiles, float* __restrict__ row_m,
+                 float* __restrict__ row_s) {
+  __shared__ float sm[8][33], ss[8][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t r = (int64_t)blockIdx.x * 32 + tx;
+  float M = -INFINITY, S = 0.f;
+  if (r < rows) {
+    for (int64_t t = ty; t < n_tiles; t += 8) {
+      const float m = part_m[t * rows + r];
+      const float s = part_s[t * rows + r];
+      if (m > M) {
+        S = S * __expf(M - m) + s;
+        M = m;
+      } else {
+        S += s * __expf(m - M);
+      }
+    }
+  }
+  sm[ty][tx] = M;
+  ss[ty][tx] = S;
+  __syncthreads();
+  if (ty == 0 && r < rows) {
+    float MM = -INFINITY, SS = 0.f;
+    for (int k = 0; k < 8; ++k) {
+      const float m = sm[k][tx], s = ss[k][tx];
+      if (s == 0.f) continue;
+      if (m > MM) {
+        SS = SS * __expf(MM - m) + s;
+        MM = m;
+      } else {
+        SS += s * __expf(m - MM);
+      }
+    }
+    row_m[r] = MM;
+    row_s[r] = SS;
+  }
+}
+
+// Vocabulary-sharded path, phase 2: f[t][r] = exp(m_t - lse_r) * mask * scale,
+// written over part_m, from the GLOBAL per-row log-sum-exp.
+__global__ void __launch_bounds__(256)
+flce_factors(float* __restrict__ part_m, int64_t rows, int64_t n_tiles,
+             const float* __restrict__ lse, const int64_t* __restrict__ labels, int64_t ignore,
+             const float* __restrict__ scale_ptr) {
+  const int64_t total = rows * n_tiles;
+  const float scale = scale_ptr[0];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i % rows;
+    const float sc = labels[r] != ignore ? scale : 0.f;
+    part_m[i] = __expf(part_m[i] - lse[r]) * sc;
   }
 }
 
@@ -358,7 +418,7 @@ extern "C" int ml_flce_forward(const void* hidden, const void* weight, const voi
       const int64_t total = rows * ((v + 7) / 8);
       const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
       flce::flce_transform<<<grid, 256, 0, st>>>(E, L.ldE, rows, v, pm, labels + r0,
-                                                 ignore_index, cnt);
+                                                 ignore_index, cnt + 1, 0);
       ML_CHECK_LAUNCH("flce_transform");
     }
     // 4a. dX slabs = P W  (A = P [rows, V] K-major, B = W stored [V, H]: N-major)
@@ -422,6 +482,136 @@ extern "C" int ml_flce_backward(const float* grad_output, const float* dx_slabs,
   if (dweight != nullptr) {
     ML_CHECK_ARG(dw_acc != nullptr, "flce_backward: dweight requested without dw_acc");
     int rc = flce::launch_scale_cast(dw_acc, 1, 0, v * h, grad_output, dweight, dw_dtype, st);
+    if (rc) return rc;
+  }
+  return ML_OK;
+}
+
+extern "C" int ml_flce_count_valid(const int64_t* labels, int64_t n, int64_t ignore_index,
+                                   float* out, void* stream) {
+  ML_CHECK_ARG(n >= 0 && out != nullptr && (n == 0 || labels != nullptr),
+               "flce_count_valid: bad arguments");
+  flce::flce_count<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(labels, n, ignore_index,
+                                                                      out);
+  ML_CHECK_LAUNCH("flce_count_valid");
+  return ML_OK;
+}
+
+extern "C" size_t ml_flce_shard_workspace_bytes(int64_t rows, int64_t v_local) {
+  if (rows <= 0 || v_local <= 0) return 256;
+  return flce::layout(rows, v_local, rows).total;
+}
+
+extern "C" int ml_flce_shard_stats(const void* hidden, const void* weight, const void* bias,
+                                   int bias_dtype, const int64_t* labels, int64_t rows, int64_t h,
+                                   int64_t v_local, int64_t vocab_offset, int64_t ignore_index,
+                                   float* row_max, float* row_sum, float* row_tgt,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  ML_CHECK_ARG(rows > 0 && h > 0 && v_local > 0 && vocab_offset >= 0,
+               "flce_shard_stats: bad sizes");
+  ML_CHECK_ARG(h % 8 == 0, "flce_shard_stats: hidden size must be a multiple of 8");
+  ML_CHECK_ARG(hidden && weight && labels && row_max && row_sum && row_tgt,
+               "flce_shard_stats: null pointer");
+  const flce::Layout L = flce::layout(rows, v_local, rows);
+  ML_CHECK_ARG(workspace != nullptr && ((uintptr_t)workspace & 255) == 0 &&
+                   workspace_bytes >= L.total,
+               "flce_shard_stats: workspace must be 256-byte aligned and >= %zu bytes", L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  float* pm = reinterpret_cast<float*>(ws + L.off_pm);
+  float* ps = reinterpret_cast<float*>(ws + L.off_ps);
+  ML_CHECK_CUDA(cudaMemsetAsync(row_tgt, 0, (size_t)rows * 4, st), "flce_shard_stats: memset");
+  gemm::Problem g1;
+  g1.M = rows;
+  g1.N = v_local;
+  g1.nseg = 1;
+  g1.seg[0].a = {hidden, rows, h, h};
+  g1.seg[0].b = {weight, v_local, h, h};
+  g1.seg[0].K = h;
+  g1.epi = gemm::EPI_FLCE;
+  g1.bn = 256;
+  g1.D = ws + L.off_E;
+  g1.ldd = L.ldE;
+  g1.labels = labels;
+  g1.label_base = vocab_offset;
+  g1.ignore_index = ignore_index;
+  g1.part_m = pm;
+  g1.part_s = ps;
+  g1.tgt = row_tgt;
+  g1.bias = bias;
+  g1.bias_dtype = bias_dtype;
+  int rc = gemm::launch(g1, st);
+  if (rc) return rc;
+  flce::flce_merge_tiles<<<(unsigned)((rows + 31) / 32), 256, 0, st>>>(pm, ps, rows, L.n_tiles,
+                                                                       row_max, row_sum);
+  ML_CHECK_LAUNCH("flce_merge_tiles");
+  return ML_OK;
+}
+
+extern "C" int ml_flce_shard_grads(const void* hidden, const void* weight, const int64_t* labels,
+                                   int64_t rows, int64_t h, int64_t v_local, int64_t vocab_offset,
+                                   int64_t ignore_index, const float* lse, const float* scale,
+                                   float* dx, float* dw, int dw_accumulate, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  ML_CHECK_ARG(rows > 0 && h > 0 && v_local > 0 && vocab_offset >= 0,
+               "flce_shard_grads: bad sizes");
+  ML_CHECK_ARG(hidden && weight && labels && lse && scale, "flce_shard_grads: null pointer");
+  const flce::Layout L = flce::layout(rows, v_local, rows);
+  ML_CHECK_ARG(workspace != nullptr && ((uintptr_t)workspace & 255) == 0 &&
+                   workspace_bytes >= L.total,
+               "flce_shard_grads: workspace must be 256-byte aligned and >= %zu bytes", L.total);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  __nv_bfloat16* E = reinterpret_cast<__nv_bfloat16*>(ws + L.off_E);
+  float* pm = reinterpret_cast<float*>(ws + L.off_pm);
+  {
+    const int64_t total = rows * L.n_tiles;
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
+    flce::flce_factors<<<grid, 256, 0, st>>>(pm, rows, L.n_tiles, lse, labels, ignore_index,
+                                             scale);
+    ML_CHECK_LAUNCH("flce_factors");
+  }
+  {
+    const int64_t total = rows * ((v_local + 7) / 8);
+    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+    flce::flce_transform<<<grid, 256, 0, st>>>(E, L.ldE, rows, v_local, pm, labels, ignore_index,
+                                               scale, vocab_offset);
+    ML_CHECK_LAUNCH("flce_transform");
+  }
+  if (dx != nullptr) {
+    gemm::Problem g2;
+    g2.M = rows;
+    g2.N = h;
+    g2.nseg = 1;
+    g2.seg[0].a = {E, rows, v_local, L.ldE};
+    g2.seg[0].b = {weight, v_local, h, h};
+    g2.seg[0].K = v_local;
+    g2.b_mn = true;
+    g2.epi = gemm::EPI_STORE;
+    g2.d_f32 = true;
+    g2.D = dx;
+    g2.ldd = h;
+    g2.raster = 1;
+    int rc = gemm::launch(g2, st);
+    if (rc) return rc;
+  }
+  if (dw != nullptr) {
+    gemm::Problem g3;
+    g3.M = v_local;
+    g3.N = h;
+    g3.nseg = 1;
+    g3.seg[0].a = {E, rows, v_local, L.ldE};
+    g3.seg[0].b = {hidden, rows, h, h};
+    g3.seg[0].K = rows;
+    g3.a_mn = true;
+    g3.b_mn = true;
+    g3.epi = gemm::EPI_STORE;
+    g3.d_f32 = true;
+    g3.D = dw;
+    g3.ldd = h;
+    g3.beta = dw_accumulate ? 1.f : 0.f;
+    g3.raster = 1;
+    int rc = gemm::launch(g3, st);
     if (rc) return rc;
   }
   return ML_OK;

@@ -193,6 +193,7 @@ int launch(const Problem& pr, cudaStream_t st) {
   const int elt = (pr.epi == EPI_STORE && !pr.d_f32) || pr.epi == EPI_FLCE ? 2 : 4;
   prm.vec_ok = aligned16(pr.D) && ((pr.ldd * elt) % 16 == 0);
   prm.labels = pr.labels;
+  prm.label_base = pr.label_base;
   prm.ignore_index = pr.ignore_index;
   prm.part_m = pr.part_m;
   prm.part_s = pr.part_s;

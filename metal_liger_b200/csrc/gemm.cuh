@@ -63,6 +63,7 @@ struct alignas(64) Params {
   float beta;              // EPI_STORE with fp32 D: D = alpha*acc + beta*D (beta in {0,1})
   // EPI_FLCE
   const int64_t* labels;   // labels for rows [0, M) (already offset to the chunk)
+  int64_t label_base;      // vocabulary id of logit column 0 (vocab-sharded logits)
   int64_t ignore_index;
   float* part_m;           // [n_tiles][M] tile max of the logits row
   float* part_s;           // [n_tiles][M] sum exp(logit - tile max)
@@ -372,7 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           constexpr float kLog2e = 1.4426950408889634f;
           const int col_base = nt * BN;
           const int64_t label = row_ok ? p.labels[row] : p.ignore_index;
-          const int64_t lrel = label - col_base;
+          const int64_t lrel =
+              label == p.ignore_index ? (int64_t)-1 : label - p.label_base - col_base;
           float m = -INFINITY;
           float tgt = 0.f;
           bool has_tgt = false;
@@ -489,6 +491,7 @@ struct Problem {
   int max_ctas = 0;    // 0 = SM count
   // FLCE
   const int64_t* labels = nullptr;
+  int64_t label_base = 0;
   int64_t ignore_index = -100;
   float* part_m = nullptr;
   float* part_s = nullptr;

@@ -76,3 +76,165 @@ class MetalLigerFusedLinearCrossEntropy(nn.Module):
         labels_flat = labels.reshape(-1)
         return _FusedLinearCrossEntropyFunction.apply(
             hidden_flat, self.weight, labels_flat, self.bias, self.ignore_index, self.chunk_size)
+
+
+# ---------------------------------------------------------------------------
+# Vocabulary-parallel FLCE (lm_head sharded by vocabulary rows across ranks)
+# ---------------------------------------------------------------------------
+
+def shard_lm_head(weight: torch.Tensor, rank: int, world: int):
+    """(weight[v0:v1], v0): this rank's contiguous vocabulary shard (row split as even as
+    possible; earlier ranks get the remainder)."""
+    v = weight.shape[0]
+    base, rem = divmod(v, world)
+    v0 = rank * base + min(rank, rem)
+    v1 = v0 + base + (1 if rank < rem else 0)
+    return weight[v0:v1], v0
+
+
+class CudaShardPhases:
+    """The two per-chunk phases on this GPU (ml_flce_shard_stats / _grads)."""
+
+    def count(self, labels, ignore_index):
+        from metal_liger_b200 import _C
+        out = torch.empty(2, dtype=torch.float32, device=labels.device)
+        _C.call("ml_flce_count_valid", labels.data_ptr(), labels.numel(), int(ignore_index),
+                out.data_ptr(), _C.stream_of(labels))
+        return out
+
+    def stats(self, hidden, weight, bias, labels, vocab_offset, ignore_index):
+        from metal_liger_b200 import _C
+        rows, h = hidden.shape
+        v_local = weight.shape[0]
+        lib = _C.load()
+        nbytes = int(lib.ml_flce_shard_workspace_bytes(rows, v_local))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=hidden.device)
+        m = torch.empty(rows, dtype=torch.float32, device=hidden.device)
+        s = torch.empty_like(m)
+        t = torch.empty_like(m)
+        _C.call("ml_flce_shard_stats", hidden.data_ptr(), weight.data_ptr(),
+                bias.data_ptr() if bias is not None else None,
+                _C.dtype_code(bias) if bias is not None else 0, labels.data_ptr(), rows, h,
+                v_local, int(vocab_offset), int(ignore_index), m.data_ptr(), s.data_ptr(),
+                t.data_ptr(), ws.data_ptr(), nbytes, _C.stream_of(hidden))
+        return m, s, t, ws
+
+    def grads(self, state, hidden, weight, labels, vocab_offset, ignore_index, lse, scale,
+              dx_out, dw_out, dw_accumulate):
+        from metal_liger_b200 import _C
+        rows, h = hidden.shape
+        _C.call("ml_flce_shard_grads", hidden.data_ptr(), weight.data_ptr(), labels.data_ptr(),
+                rows, h, weight.shape[0], int(vocab_offset), int(ignore_index), lse.data_ptr(),
+                scale.data_ptr(), dx_out.data_ptr() if dx_out is not None else None,
+                dw_out.data_ptr() if dw_out is not None else None, int(dw_accumulate),
+                state.data_ptr(), state.numel(), _C.stream_of(hidden))
+
+
+def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=None,
+                        ignore_index=-100, chunk_size=8192, group=None, phases=None,
+                        need_dx=True, need_dw=True):
+    """Vocabulary-parallel fused linear cross-entropy; every rank calls it with the
+    same hidden/labels and its own contiguous vocabulary shard of the lm_head.
+
+    Per token chunk: each rank computes its shard's per-row (max, sum-exp,
+    target logit); two all-reduces (MAX of the maxima, then SUM of the
+    rescaled sums and target logits) give the global log-sum-exp; each rank
+    then forms its shard's (softmax - onehot)/n_valid and produces its partial
+    dX (summed across ranks with an all-reduce that overlaps the next chunk)
+    and its own dW shard, which never leaves the rank.
+
+    Returns (loss, dx [N, H] fp32 or None, dw_shard [V_local, H] fp32 or None),
+    the gradients at grad_output = 1.
+    """
+    import torch.distributed as dist
+
+    phases = phases or CudaShardPhases()
+    hidden = hidden.reshape(-1, hidden.shape[-1])
+    if hidden.dtype != torch.bfloat16 and isinstance(phases, CudaShardPhases):
+        hidden = hidden.to(torch.bfloat16)
+    if weight_shard.dtype != torch.bfloat16 and isinstance(phases, CudaShardPhases):
+        weight_shard = weight_shard.to(torch.bfloat16)
+    hidden = hidden.contiguous()
+    weight_shard = weight_shard.contiguous()
+    labels = labels.reshape(-1).to(torch.int64).contiguous()
+    n, h = hidden.shape
+    dev = hidden.device
+    cnt = phases.count(labels, ignore_index)
+    row_loss = torch.zeros(n, dtype=torch.float32, device=dev)
+    dx = torch.zeros((n, h), dtype=torch.float32, device=dev) if need_dx else None
+    dw = (torch.zeros((weight_shard.shape[0], h), dtype=torch.float32, device=dev)
+          if need_dw else None)
+    chunk = int(chunk_size) if chunk_size and chunk_size > 0 else n
+    pending = []
+    for r0 in range(0, n, chunk):
+        r1 = min(n, r0 + chunk)
+        hc, lc = hidden[r0:r1], labels[r0:r1]
+        m, s, t, state = phases.stats(hc, weight_shard, bias_shard, lc, vocab_offset,
+                                      ignore_index)
+        mg = m.clone()
+        dist.all_reduce(mg, op=dist.ReduceOp.MAX, group=group)
+        st = torch.stack([s * torch.exp(m - mg), t])
+        dist.all_reduce(st, op=dist.ReduceOp.SUM, group=group)
+        lse = mg + torch.log(st[0])
+        mask = (lc != ignore_index).to(torch.float32)
+        row_loss[r0:r1] = (lse - st[1]) * mask
+        phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index, lse.contiguous(),
+                     cnt[1:2], dx[r0:r1] if need_dx else None, dw, r0 > 0)
+        if need_dx:
+            pending.append(dist.all_reduce(dx[r0:r1], op=dist.ReduceOp.SUM, group=group,
+                                           async_op=True))
+    for work in pending:
+        work.wait()
+    loss = row_loss.sum() * cnt[1]
+    return loss, dx, dw
+
+
+class _VocabParallelFLCEFunction(torch.autograd.Function):
+    """Autograd wrapper of vocab_parallel_flce (gradients formed in forward)."""
+
+    @staticmethod
+    def forward(ctx, hidden, weight_shard, labels, bias_shard, vocab_offset, ignore_index,
+                chunk_size, group):
+        need_dx = bool(ctx.needs_input_grad[0])
+        need_dw = bool(ctx.needs_input_grad[1])
+        loss, dx, dw = vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset,
+                                           bias_shard, ignore_index, chunk_size, group,
+                                           need_dx=need_dx, need_dw=need_dw)
+        empty = torch.empty(0, device=hidden.device)
+        ctx.save_for_backward(dx.unsqueeze(0) if dx is not None else empty,
+                              dw if dw is not None else empty)
+        ctx.hidden_shape = hidden.shape
+        ctx.codes = (DTYPE_CODES.get(hidden.dtype, 0), DTYPE_CODES.get(weight_shard.dtype, 0))
+        return loss
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        dx, dw = ctx.saved_tensors
+        gh, gw = torch.ops.metal_liger.flce_backward(grad_output, dx, dw, ctx.codes[0],
+                                                     ctx.codes[1])
+        grad_hidden = gh.view(ctx.hidden_shape) if ctx.needs_input_grad[0] else None
+        grad_weight = gw if ctx.needs_input_grad[1] else None
+        return grad_hidden, grad_weight, None, None, None, None, None, None
+
+
+class VocabParallelFusedLinearCrossEntropy(nn.Module):
+    """lm_head + cross-entropy with the lm_head split by vocabulary across a process
+    group: holds this rank's shard (``weight_shard`` = rows [vocab_offset,
+    vocab_offset + V_local) of the full head).  The loss is the full-vocabulary
+    mean cross-entropy, identical on every rank."""
+
+    def __init__(self, weight_shard: nn.Parameter, vocab_offset: int, bias_shard=None,
+                 ignore_index: int = -100, chunk_size: int = 8192, group=None):
+        super().__init__()
+        self.weight = weight_shard
+        self.bias = bias_shard
+        self.vocab_offset = vocab_offset
+        self.ignore_index = ignore_index
+        self.chunk_size = chunk_size
+        self.group = group
+
+    def forward(self, hidden_states: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        hidden_flat = hidden_states.reshape(-1, hidden_states.shape[-1])
+        return _VocabParallelFLCEFunction.apply(hidden_flat, self.weight, labels.reshape(-1),
+                                                self.bias, self.vocab_offset, self.ignore_index,
+                                                self.chunk_size, self.group)
