@@ -20,7 +20,7 @@
 namespace ml {
 namespace {
 
-constexpr int kMaxThreads = 1024;
+constexpr int kMaxThreads = 256;  // vector path: per-thread registers hold 2 rows (prefetch)
 
 struct RowCfg {
   int nv = 0;       // 16-byte vectors per thread per row
@@ -49,7 +49,17 @@ RowCfg pick_cfg(int64_t hidden, const void* a, const void* b, const void* c, con
 
 // Reduce `v` (and optionally `v2`) over the TPR threads of this thread's row
 // group.  `red` is a [2][32][2] shared array double-buffered by `buf` so one
-// __syncthreads per row suffices.
+// barrier per row suffices.  Each row group synchronises on its own named
+// barrier (id 1 + group), so groups never wait for one another.
+__device__ __forceinline__ void group_barrier(int tpr) {
+  if (tpr == (int)blockDim.x) {
+    __syncthreads();
+  } else {
+    const int id = 1 + (int)threadIdx.x / tpr;
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(tpr) : "memory");
+  }
+}
+
 __device__ __forceinline__ float2 group_sum2(float v, float v2, float (*red)[32][2], int buf,
                                             int tpr) {
   const int lane = threadIdx.x & 31;
@@ -60,7 +70,7 @@ __device__ __forceinline__ float2 group_sum2(float v, float v2, float (*red)[32]
     red[buf][warp][0] = v;
     red[buf][warp][1] = v2;
   }
-  __syncthreads();
+  group_barrier(tpr);
   const int wpg = tpr >> 5;                 // warps per group
   const int first = (warp / wpg) * wpg;     // first warp of my group
   float s = 0.f, s2 = 0.f;
@@ -87,7 +97,6 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
   __shared__ float red[2][32][2];
   const int g = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
-  const bool in_group = g < groups;
   float wr[NV][VEC];
 #pragma unroll
   for (int i = 0; i < NV; ++i) load_weight<TW, VEC>(w, (int64_t)(i * tpr + t) * VEC, hidden, wr[i]);
@@ -95,17 +104,29 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
   const int64_t row_stride = (int64_t)gridDim.x * groups;
   const int64_t niter = (rows + row_stride - 1) / row_stride;
   const float inv_h = 1.f / (float)hidden;
+  int64_t row = (int64_t)blockIdx.x * groups + g;
+  // Software pipeline: the next row's loads are in flight while this row is
+  // reduced and written.
+  Vec16<TX> xv[NV], xn[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t col = (int64_t)(i * tpr + t) * VEC;
+    if (row < rows && col < hidden) xv[i] = ld_vec_stream(x + row * hidden + col);
+  }
   int buf = 0;
-  for (int64_t it = 0; it < niter; ++it) {
-    const int64_t row = it * row_stride + (int64_t)blockIdx.x * groups + g;
-    const bool active = in_group && row < rows;
-    Vec16<TX> xv[NV];
+  for (int64_t it = 0; it < niter; ++it, row += row_stride) {
+    const bool active = row < rows;
+    const int64_t nrow = row + row_stride;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (nrow < rows && col < hidden) xn[i] = ld_vec_stream(x + nrow * hidden + col);
+    }
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = (int64_t)(i * tpr + t) * VEC;
       if (active && col < hidden) {
-        xv[i] = ld_vec_stream(x + row * hidden + col);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
           const float f = to_f32(xv[i].v[j]);
@@ -115,19 +136,23 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
     }
     const float tot = group_sum2(ss, 0.f, red, buf, tpr).x;
     buf ^= 1;
-    if (!active) continue;
-    const float r = rsqrtf(tot * inv_h + eps);
-    if (t == 0 && rrms != nullptr) rrms[row] = r;
+    if (active) {
+      const float r = rsqrtf(tot * inv_h + eps);
+      if (t == 0 && rrms != nullptr) rrms[row] = r;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int64_t col = (int64_t)(i * tpr + t) * VEC;
-      if (col < hidden) {
-        Vec16<TX> o;
+      for (int i = 0; i < NV; ++i) {
+        const int64_t col = (int64_t)(i * tpr + t) * VEC;
+        if (col < hidden) {
+          Vec16<TX> o;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) o.v[j] = from_f32<TX>((to_f32(xv[i].v[j]) * r) * wr[i][j]);
-        st_vec_stream(y + row * hidden + col, o);
+          for (int j = 0; j < VEC; ++j)
+            o.v[j] = from_f32<TX>((to_f32(xv[i].v[j]) * r) * wr[i][j]);
+          st_vec_stream(y + row * hidden + col, o);
+        }
       }
     }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) xv[i] = xn[i];
   }
 }
 
@@ -169,7 +194,6 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   extern __shared__ float fold[];  // [groups][hidden] when groups > 1
   const int g = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
-  const bool in_group = g < groups;
   float wr[NV][VEC];
   float acc[NV][VEC];
 #pragma unroll
@@ -181,18 +205,33 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   const int64_t row_stride = (int64_t)gridDim.x * groups;
   const int64_t niter = (rows + row_stride - 1) / row_stride;
   const float inv_h = 1.f / (float)hidden;
+  int64_t row = (int64_t)blockIdx.x * groups + g;
+  Vec16<TX> xv[NV], gv[NV], xn[NV], gn[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t col = (int64_t)(i * tpr + t) * VEC;
+    if (row < rows && col < hidden) {
+      xv[i] = ld_vec_stream(x + row * hidden + col);
+      gv[i] = ld_vec_stream(dy + row * hidden + col);
+    }
+  }
   int buf = 0;
-  for (int64_t it = 0; it < niter; ++it) {
-    const int64_t row = it * row_stride + (int64_t)blockIdx.x * groups + g;
-    const bool active = in_group && row < rows;
-    Vec16<TX> xv[NV], gv[NV];
+  for (int64_t it = 0; it < niter; ++it, row += row_stride) {
+    const bool active = row < rows;
+    const int64_t nrow = row + row_stride;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
+      if (nrow < rows && col < hidden) {
+        xn[i] = ld_vec_stream(x + nrow * hidden + col);
+        gn[i] = ld_vec_stream(dy + nrow * hidden + col);
+      }
+    }
     float ss = 0.f, gwx = 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = (int64_t)(i * tpr + t) * VEC;
       if (active && col < hidden) {
-        xv[i] = ld_vec_stream(x + row * hidden + col);
-        gv[i] = ld_vec_stream(dy + row * hidden + col);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
           const float xf = to_f32(xv[i].v[j]);
@@ -203,35 +242,39 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
     }
     const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
     buf ^= 1;
-    if (!active) continue;
-    const float r = rrms != nullptr ? rrms[row] : rsqrtf(sums.x * inv_h + eps);
-    const float c = (sums.y * inv_h) * (r * r * r);
+    if (active) {
+      const float r = rrms != nullptr ? rrms[row] : rsqrtf(sums.x * inv_h + eps);
+      const float c = (sums.y * inv_h) * (r * r * r);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t col = (int64_t)(i * tpr + t) * VEC;
+        if (col < hidden) {
+          Vec16<TX> o;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float xf = to_f32(xv[i].v[j]);
+            const float gf = to_f32(gv[i].v[j]);
+            o.v[j] = from_f32<TX>((gf * wr[i][j]) * r - xf * c);
+            acc[i][j] = fmaf(gf, xf * r, acc[i][j]);
+          }
+          st_vec_stream(dx + row * hidden + col, o);
+        }
+      }
+    }
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int64_t col = (int64_t)(i * tpr + t) * VEC;
-      if (col < hidden) {
-        Vec16<TX> o;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          const float xf = to_f32(xv[i].v[j]);
-          const float gf = to_f32(gv[i].v[j]);
-          o.v[j] = from_f32<TX>((gf * wr[i][j]) * r - xf * c);
-          acc[i][j] = fmaf(gf, xf * r, acc[i][j]);
-        }
-        st_vec_stream(dx + row * hidden + col, o);
-      }
+      xv[i] = xn[i];
+      gv[i] = gn[i];
     }
   }
   // Fold the row groups' partials (fixed order) and store one row per CTA.
   if (groups > 1) {
-    if (in_group) {
 #pragma unroll
-      for (int i = 0; i < NV; ++i) {
-        const int64_t col = (int64_t)(i * tpr + t) * VEC;
+    for (int i = 0; i < NV; ++i) {
+      const int64_t col = (int64_t)(i * tpr + t) * VEC;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-          if (col + j < hidden) fold[(int64_t)g * hidden + col + j] = acc[i][j];
-      }
+      for (int j = 0; j < VEC; ++j)
+        if (col + j < hidden) fold[(int64_t)g * hidden + col + j] = acc[i][j];
     }
     __syncthreads();
     for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) {
@@ -239,7 +282,7 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
       for (int k = 0; k < groups; ++k) s += fold[(int64_t)k * hidden + c];
       partial[(int64_t)blockIdx.x * hidden + c] = s;
     }
-  } else if (in_group) {
+  } else {
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = (int64_t)(i * tpr + t) * VEC;

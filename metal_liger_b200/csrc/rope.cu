@@ -82,6 +82,22 @@ __device__ __forceinline__ void store_n(T* p, const float* f) {
   }
 }
 
+// sin/cos of x for 16-bit outputs: reduce x to r in [-pi, pi] with a
+// two-constant Cody-Waite step (2*pi = kTwoPiHi + kTwoPiLo, the first exactly
+// representable in fp32), then evaluate with the SFU sin/cos, whose absolute
+// error on [-pi, pi] is ~4e-7 -- far below bf16/fp16 resolution.
+constexpr float kInvTwoPi = 0.15915494309189535f;
+constexpr float kTwoPiHi = 6.28318548202514648f;
+constexpr float kTwoPiLo = -1.7484556000744883e-07f;
+
+__device__ __forceinline__ void sincos_reduced(float x, float* s, float* c) {
+  const float k = rintf(x * kInvTwoPi);
+  float r = fmaf(-k, kTwoPiHi, x);
+  r = fmaf(-k, kTwoPiLo, r);
+  *s = __sinf(r);
+  *c = __cosf(r);
+}
+
 // Work unit = (batch, block of kPos positions, block of kHeads heads of the
 // concatenated [q heads..., k heads...] list).  A CTA of kPos*TPH threads owns
 // one position per thread group; each thread owns VEC frequencies, so it
@@ -89,7 +105,25 @@ __device__ __forceinline__ void store_n(T* p, const float* f) {
 // no shared memory, no barrier) and applies them to every head row of the
 // unit.  CTAs take contiguous ranges of units (head blocks fastest), so cos/sin
 // are recomputed only when the position block changes.
-template <typename Tin, typename Tout, int VEC>
+template <int N, typename T>
+struct Raw {  // N elements of T kept packed in registers
+  T v[N];
+};
+
+template <typename T, int N>
+__device__ __forceinline__ void load_raw(const T* p, Raw<N, T>& r) {
+  if constexpr (N * sizeof(T) % 16 == 0) {
+#pragma unroll
+    for (int c = 0; c < (int)(N * sizeof(T) / 16); ++c)
+      *reinterpret_cast<int4*>(&r.v[c * (16 / sizeof(T))]) =
+          __ldcs(reinterpret_cast<const int4*>(p) + c);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) r.v[j] = p[j];
+  }
+}
+
+template <typename Tin, typename Tout, int VEC, bool TABLE>
 __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_t units_per_cta,
                                                         int npos) {
   const int64_t D = a.head_dim;
@@ -106,7 +140,10 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_
   const int64_t u0 = (int64_t)blockIdx.x * units_per_cta;
   const int64_t u1 = u0 + units_per_cta < units ? u0 + units_per_cta : units;
   const float sign = a.sign;
-  float c1[VEC], c2[VEC], s1[VEC], s2[VEC];
+  // cos/sin of this thread's frequencies at its position; the recompute mode
+  // has identical halves, so only the table mode keeps two sets.
+  float c1[VEC], s1[VEC];
+  float c2[TABLE ? VEC : 1], s2[TABLE ? VEC : 1];
   int64_t cached = -1;
   for (int64_t u = u0; u < u1; ++u) {
     const int64_t bp = u / hblocks;            // (batch, position block)
@@ -117,29 +154,28 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_
     if (bp != cached) {
       cached = bp;
       if (pos_ok) {
-        if (a.cos != nullptr) {
+        if constexpr (TABLE) {
           const int64_t base = b * a.cs[0] + s * a.cs[1];
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
             c1[j] = load_as_f32(a.cos, base + (d0 + j) * a.cs[2], a.cs_dtype);
             c2[j] = load_as_f32(a.cos, base + (d0 + j + half) * a.cs[2], a.cs_dtype);
-            s1[j] = load_as_f32(a.sin, base + (d0 + j) * a.cs[2], a.cs_dtype);
-            s2[j] = load_as_f32(a.sin, base + (d0 + j + half) * a.cs[2], a.cs_dtype);
+            s1[j] = sign * load_as_f32(a.sin, base + (d0 + j) * a.cs[2], a.cs_dtype);
+            s2[j] = sign * load_as_f32(a.sin, base + (d0 + j + half) * a.cs[2], a.cs_dtype);
           }
         } else {
           const int64_t pos = a.positions != nullptr ? a.positions[b * a.pos_sb + s] : s;
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
             float sv, cv;
-            sincosf((float)pos * a.inv_freq[d0 + j], &sv, &cv);
-            c1[j] = c2[j] = cv * a.scaling;
-            s1[j] = s2[j] = sv * a.scaling;
+            const float ang = (float)pos * a.inv_freq[d0 + j];
+            if constexpr (sizeof(Tout) == 2)
+              sincos_reduced(ang, &sv, &cv);
+            else
+              sincosf(ang, &sv, &cv);
+            c1[j] = cv * a.scaling;
+            s1[j] = sign * sv * a.scaling;
           }
-        }
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          s1[j] *= sign;
-          s2[j] *= sign;
         }
       }
     }
@@ -149,7 +185,7 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_
     const int64_t h_end = h_begin + kHeads < heads_total ? h_begin + kHeads : heads_total;
 #pragma unroll 1
     for (int64_t h0 = h_begin; h0 < h_end; h0 += kBatch) {
-      float x1[kBatch][VEC], x2[kBatch][VEC];
+      Raw<VEC, Tin> x1[kBatch], x2[kBatch];
 #pragma unroll
       for (int q = 0; q < kBatch; ++q) {
         const int64_t hh = h0 + q;
@@ -158,8 +194,8 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_
           const RopeView& v = a.t[ti];
           const int64_t h = ti == 0 ? hh : hh - a.t[0].heads;
           const Tin* xr = static_cast<const Tin*>(v.in) + b * v.is[0] + h * v.is[1] + s * v.is[2];
-          load_n<Tin, VEC>(xr + d0, x1[q]);
-          load_n<Tin, VEC>(xr + half + d0, x2[q]);
+          load_raw<Tin, VEC>(xr + d0, x1[q]);
+          load_raw<Tin, VEC>(xr + half + d0, x2[q]);
         }
       }
 #pragma unroll
@@ -172,8 +208,15 @@ __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_
           float y1[VEC], y2[VEC];
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
-            y1[j] = x1[q][j] * c1[j] - x2[q][j] * s1[j];
-            y2[j] = x2[q][j] * c2[j] + x1[q][j] * s2[j];
+            const float a1 = to_f32(x1[q].v[j]);
+            const float a2 = to_f32(x2[q].v[j]);
+            if constexpr (TABLE) {
+              y1[j] = a1 * c1[j] - a2 * s1[j];
+              y2[j] = a2 * c2[j] + a1 * s2[j];
+            } else {
+              y1[j] = a1 * c1[j] - a2 * s1[j];
+              y2[j] = a2 * c1[j] + a1 * s1[j];
+            }
           }
           Tout* yr = static_cast<Tout*>(v.out) + b * v.os[0] + h * v.os[1] + s * v.os[2];
           store_n<Tout, VEC>(yr + d0, y1);
@@ -199,21 +242,32 @@ int launch(const RopeArgs& a, bool vec_ok, cudaStream_t st) {
   const int64_t heads_total = a.t[0].heads + (a.ntensors > 1 ? a.t[1].heads : 0);
   const int64_t units = a.batch * ((a.seq + npos - 1) / npos) * ((heads_total + kHeads - 1) / kHeads);
   int per_sm = 0;
-  auto kv = rope_kernel<Tin, Tout, V>;
-  auto k1 = rope_kernel<Tin, Tout, 1>;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, vec_ok ? (const void*)kv : (const void*)k1,
-                                                threads, 0);
+  const bool table = a.cos != nullptr;
+  const void* kfn = table ? (vec_ok ? (const void*)rope_kernel<Tin, Tout, V, true>
+                                    : (const void*)rope_kernel<Tin, Tout, 1, true>)
+                          : (vec_ok ? (const void*)rope_kernel<Tin, Tout, V, false>
+                                    : (const void*)rope_kernel<Tin, Tout, 1, false>);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, threads, 0);
   per_sm = std::max(per_sm, 1);
-  // one unit per CTA while that keeps the grid under ~8 waves (small tail);
-  // beyond that, contiguous unit ranges amortise the cos/sin evaluation
-  int64_t ctas = std::min<int64_t>(units, (int64_t)num_sms() * per_sm * 8);
-  ctas = std::max<int64_t>(ctas, 1);
-  const int64_t per_cta = (units + ctas - 1) / ctas;
-  ctas = (units + per_cta - 1) / per_cta;
-  if (vec_ok)
-    kv<<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
-  else
-    k1<<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
+  // Each CTA takes a contiguous range of units.  Ranges are whole position
+  // blocks (all head blocks of a position block) when that still leaves >= 2
+  // waves, so cos/sin are evaluated once per position; otherwise single units.
+  const int64_t hblocks = (heads_total + kHeads - 1) / kHeads;
+  const int64_t slots = (int64_t)num_sms() * per_sm;
+  int64_t per_cta = units / hblocks >= 2 * slots ? hblocks : 1;
+  while (per_cta > 1 && (units + per_cta - 1) / per_cta < 2 * slots) per_cta /= 2;
+  int64_t ctas = (units + per_cta - 1) / per_cta;
+  if (table) {
+    if (vec_ok)
+      rope_kernel<Tin, Tout, V, true><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
+    else
+      rope_kernel<Tin, Tout, 1, true><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
+  } else {
+    if (vec_ok)
+      rope_kernel<Tin, Tout, V, false><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
+    else
+      rope_kernel<Tin, Tout, 1, false><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
+  }
   ML_CHECK_LAUNCH("rope");
   return ML_OK;
 }

@@ -17,7 +17,9 @@
 namespace ml {
 namespace {
 
-__device__ __forceinline__ float sigmoidf_(float g) { return 1.f / (1.f + __expf(-g)); }
+// 1 / (1 + e^-g) with the SFU exponential and reciprocal (2 ulp each); the
+// quotient tends to exactly 0 for large negative g.
+__device__ __forceinline__ float sigmoidf_(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
 
 template <typename T, int UNROLL>
 __global__ void __launch_bounds__(256)

@@ -114,3 +114,23 @@ def test_bad_inputs_raise():
     with pytest.raises(RuntimeError):
         torch.ops.metal_liger.rope_apply(x, torch.ones(4, 7, device=DEV),
                                          torch.ones(4, 7, device=DEV), 1)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_16bit_large_positions_accuracy(dt):
+    """16-bit inputs evaluate cos/sin after a two-constant range reduction to
+    [-pi, pi]; check against the fp32 oracle (torch cos/sin) for positions up to
+    1e5, where an unreduced fast sin/cos would be visibly wrong."""
+    from metal_liger_b200.ops.fused_rope import apply_fused_rotary_from_positions
+    g = torch.Generator().manual_seed(5)
+    q = torch.randn(2, 4, 64, 128, generator=g).to(dt)
+    k = torch.randn(2, 2, 64, 128, generator=g).to(dt)
+    pos = torch.randint(0, 100_000, (2, 64), generator=g)
+    qr, kr = apply_fused_rotary_from_positions(q.to(DEV), k.to(DEV), pos.to(DEV), theta=10000.0)
+    cos, sin = O.rope_cos_sin(pos, O.rope_inv_freq(128, 10000.0))
+    cos, sin = cos[:, None], sin[:, None]
+    rq = O.rope_apply(q, cos, sin)
+    assert_close(qr.cpu(), rq, dtype=dt, what="q")
+    # the error budget is dominated by the 16-bit output rounding, not cos/sin
+    err = (qr.float().cpu() - rq).abs().max().item()
+    assert err <= 2.0 ** -7 * rq.abs().max().item(), err
