@@ -10,6 +10,7 @@ module replaces the reference's pybind module ``metal_liger_ext``
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -85,6 +86,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemm_bf16_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
     "ml_gemm_bf16": (c_int, [c_int64, c_int64, ctypes.POINTER(GemmSegment), c_int, c_void_p, c_int,
                              c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "ml_gemm_set_cta_pair": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_flce_dx_slabs": (c_int, [c_int64, c_int64, c_int64, c_int64]),
     "ml_flce_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
     "ml_flce_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_int64,
@@ -192,6 +194,18 @@ def require_cuda(name: str, *tensors: torch.Tensor | None) -> None:
             dev = t.device
         elif t.device != dev:
             raise RuntimeError(f"metal_liger_b200 {name}: tensors on different devices")
+
+
+@contextlib.contextmanager
+def gemm_cta_pair(mode: int):
+    """Select the 2-SM GEMM kernel process-wide for the duration of a block:
+    -1 automatic, 0 never, 1 whenever the tile shape allows."""
+    prev = ctypes.c_int(-1)
+    call("ml_gemm_set_cta_pair", int(mode), ctypes.byref(prev))
+    try:
+        yield
+    finally:
+        call("ml_gemm_set_cta_pair", prev.value, None)
 
 
 def exported_symbols() -> list[str]:

@@ -3,6 +3,7 @@
 #include "gemm.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 namespace ml {
@@ -98,6 +99,51 @@ int launch_t(const Params& prm, int grid, cudaStream_t st) {
   return ML_OK;
 }
 
+std::atomic<int> g_pair_mode{-1};
+
+template <bool A_MN, bool B_MN>
+int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t st) {
+  auto k = gemm_pair_kernel<A_MN, B_MN>;
+  const size_t smem = PairCfg::SMEM;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  static int resident_pairs = 0;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)smem);
+    if (attr_err != cudaSuccess) return;
+    // How many CTA pairs fit at once (GPC boundaries can leave an SM unpaired).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (unsigned)(num_sms() / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)k, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms() / 2;
+    }
+    resident_pairs = n;
+  });
+  if (attr_err != cudaSuccess) {
+    set_error("gemm(pair): cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err));
+    return ML_ERR_CUDA;
+  }
+  int64_t pairs = std::min<int64_t>(units, resident_pairs);
+  if (max_ctas > 0) pairs = std::min<int64_t>(pairs, max_ctas / 2);
+  const int grid = 2 * (int)std::max<int64_t>(pairs, 1);
+  k<<<grid, kThreads, smem, st>>>(prm);
+  ML_CHECK_LAUNCH("gemm_pair_kernel");
+  return ML_OK;
+}
+
+int launch_pair(const Params& prm, bool a_mn, bool b_mn, int64_t units, int max_ctas,
+                cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_pair_t<false, false>(prm, units, max_ctas, st);
+  if (!a_mn && b_mn) return launch_pair_t<false, true>(prm, units, max_ctas, st);
+  if (a_mn && !b_mn) return launch_pair_t<true, false>(prm, units, max_ctas, st);
+  return launch_pair_t<true, true>(prm, units, max_ctas, st);
+}
+
 template <int BN>
 int launch_bn(const Params& prm, bool a_mn, bool b_mn, int grid, cudaStream_t st) {
   if (!a_mn && !b_mn) return launch_t<BN, false, false>(prm, grid, st);
@@ -121,6 +167,12 @@ int launch(const Problem& pr, cudaStream_t st) {
     return ML_ERR_INVALID_ARG;
   }
   const int bn = pr.bn ? pr.bn : pick_bn(pr.N);
+  // The CTA-pair kernel computes 256 x 256 tiles; use it when there are
+  // enough of them to occupy every SM pair.
+  const int mode = pr.pair >= 0 ? pr.pair : g_pair_mode.load(std::memory_order_relaxed);
+  const int64_t pair_tiles = ((pr.M + 255) / 256) * ((pr.N + 255) / 256) * std::max(pr.splits, 1);
+  const bool pair = bn == 256 && mode != 0 && pr.M > 128 &&
+                    (mode == 1 || pair_tiles >= num_sms() / 2);
   if (bn != 64 && bn != 128 && bn != 256) {
     set_error("gemm: bad tile width %d", bn);
     return ML_ERR_INVALID_ARG;
@@ -145,9 +197,10 @@ int launch(const Problem& pr, cudaStream_t st) {
     else
       rc = make_map(&prm.tma_a[s], g.a.ptr, pr.M, g.K, g.a.ld, BK, "gemm A (M-major)");
     if (rc) return rc;
-    // B: logical [N, K]
+    // B: logical [N, K]; each CTA of a pair loads 128 of the tile's 256 rows
     if (!pr.b_mn)
-      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, bn, "gemm B (K-major)");
+      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, pair ? 128 : bn,
+                    "gemm B (K-major)");
     else
       rc = make_map(&prm.tma_b[s], g.b.ptr, pr.N, g.K, g.b.ld, BK, "gemm B (N-major)");
     if (rc) return rc;
@@ -157,7 +210,7 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.nseg = pr.nseg;
   prm.M = (int)pr.M;
   prm.N = (int)pr.N;
-  prm.m_tiles = (int)((pr.M + BM - 1) / BM);
+  prm.m_tiles = (int)((pr.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
   prm.n_tiles = (int)((pr.N + bn - 1) / bn);
   int splits = std::max(1, std::min(pr.splits, kb_total));
   const int kb_per = (kb_total + splits - 1) / splits;
@@ -178,7 +231,7 @@ int launch(const Problem& pr, cudaStream_t st) {
     // once per group.
     int64_t k_total = 0;
     for (int s = 0; s < pr.nseg; ++s) k_total += pr.seg[s].K;
-    const int64_t a_bytes_per_mtile = (int64_t)BM * k_total * 2;
+    const int64_t a_bytes_per_mtile = (int64_t)(pair ? 2 * BM : BM) * k_total * 2;
     if ((int64_t)prm.m_tiles * a_bytes_per_mtile > ((int64_t)48 << 20)) {
       const int64_t g = std::max<int64_t>(1, ((int64_t)16 << 20) / a_bytes_per_mtile);
       prm.group_m = (int)std::min<int64_t>(g, prm.m_tiles);
@@ -208,6 +261,7 @@ int launch(const Problem& pr, cudaStream_t st) {
     set_error("gemm: problem too large");
     return ML_ERR_INVALID_ARG;
   }
+  if (pair) return launch_pair(prm, pr.a_mn, pr.b_mn, units, pr.max_ctas, st);
   int grid = (int)std::min<int64_t>(units, pr.max_ctas > 0 ? pr.max_ctas : num_sms());
   grid = std::max(grid, 1);
   switch (bn) {
@@ -323,6 +377,13 @@ extern "C" size_t ml_gemm_bf16_workspace_bytes(int64_t m, int64_t n, int64_t k_t
   if (m <= 0 || n <= 0 || k_total <= 0) return 0;
   const int s = choose_splits(m, n, k_total, gemm::pick_bn(n));
   return s > 1 ? (size_t)s * (size_t)m * (size_t)n * sizeof(float) : 0;
+}
+
+extern "C" int ml_gemm_set_cta_pair(int mode, int* previous) {
+  ML_CHECK_ARG(mode >= -1 && mode <= 1, "gemm_set_cta_pair: mode must be -1, 0 or 1");
+  const int old = gemm::g_pair_mode.exchange(mode);
+  if (previous) *previous = old;
+  return ML_OK;
 }
 
 extern "C" int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int nseg, void* d,

@@ -193,6 +193,87 @@ __device__ __forceinline__ void add_bias32(const Params& p, float (&v)[32], int 
   }
 }
 
+// Drains one accumulator tile (this thread's TMEM lane = output row `row`,
+// BN fp32 columns starting at `taddr`) through the selected epilogue.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, int64_t row,
+                                              bool row_ok, int nt, int sp) {
+  if (p.epi == EPI_FLCE) {
+    if constexpr (BN == 256) {
+      constexpr float kLog2e = 1.4426950408889634f;
+      const int col_base = nt * BN;
+      const int64_t label = row_ok ? p.labels[row] : p.ignore_index;
+      const int64_t lrel =
+          label == p.ignore_index ? (int64_t)-1 : label - p.label_base - col_base;
+      float m = -INFINITY;
+      float tgt = 0.f;
+      bool has_tgt = false;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+        if (p.bias != nullptr) add_bias32(p, v, col_base + c * 32);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int col = col_base + c * 32 + j;
+          if (col < p.vocab) m = fmaxf(m, v[j]);
+          if (lrel == (int64_t)(c * 32 + j)) {
+            tgt = v[j];
+            has_tgt = true;
+          }
+        }
+      }
+      const float mb = m * kLog2e;
+      float s = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+        const int col0 = col_base + c * 32;
+        if (p.bias != nullptr) add_bias32(p, v, col0);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float e = (col0 + j < p.vocab) ? sm100::fast_exp2(fmaf(v[j], kLog2e, -mb)) : 0.f;
+          s += e;
+          v[j] = e;
+        }
+        if (row_ok) {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
+          if (p.vec_ok && col0 + 32 <= p.vocab) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              uint4 o;
+              o.x = pack_bf16x2(v[j], v[j + 1]);
+              o.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              o.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              o.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(dst + j) = o;
+            }
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < p.vocab) dst[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+      if (row_ok) {
+        p.part_m[(int64_t)nt * p.M + row] = m;
+        p.part_s[(int64_t)nt * p.M + row] = s;
+        if (has_tgt) p.tgt[row] = tgt;
+      }
+    }
+  } else {
+    float* partial_base = nullptr;
+    if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.split_stride;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+      const int col0 = nt * BN + c * 32;
+      if (row_ok && col0 < p.N) store_row32(p, v, row, col0, partial_base);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -368,80 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       const uint32_t taddr = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
       const int64_t row = (int64_t)mt * BM + rloc;
       const bool row_ok = row < p.M;
-      if (p.epi == EPI_FLCE) {
-        if constexpr (BN == 256) {
-          constexpr float kLog2e = 1.4426950408889634f;
-          const int col_base = nt * BN;
-          const int64_t label = row_ok ? p.labels[row] : p.ignore_index;
-          const int64_t lrel =
-              label == p.ignore_index ? (int64_t)-1 : label - p.label_base - col_base;
-          float m = -INFINITY;
-          float tgt = 0.f;
-          bool has_tgt = false;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            float v[32];
-            sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
-            if (p.bias != nullptr) add_bias32(p, v, col_base + c * 32);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int col = col_base + c * 32 + j;
-              if (col < p.vocab) m = fmaxf(m, v[j]);
-              if (lrel == (int64_t)(c * 32 + j)) {
-                tgt = v[j];
-                has_tgt = true;
-              }
-            }
-          }
-          const float mb = m * kLog2e;
-          float s = 0.f;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            float v[32];
-            sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
-            const int col0 = col_base + c * 32;
-            if (p.bias != nullptr) add_bias32(p, v, col0);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float e = (col0 + j < p.vocab) ? sm100::fast_exp2(fmaf(v[j], kLog2e, -mb)) : 0.f;
-              s += e;
-              v[j] = e;
-            }
-            if (row_ok) {
-              __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd + col0;
-              if (p.vec_ok && col0 + 32 <= p.vocab) {
-#pragma unroll
-                for (int j = 0; j < 32; j += 8) {
-                  uint4 o;
-                  o.x = pack_bf16x2(v[j], v[j + 1]);
-                  o.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                  o.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                  o.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                  *reinterpret_cast<uint4*>(dst + j) = o;
-                }
-              } else {
-                for (int j = 0; j < 32; ++j)
-                  if (col0 + j < p.vocab) dst[j] = __float2bfloat16_rn(v[j]);
-              }
-            }
-          }
-          if (row_ok) {
-            p.part_m[(int64_t)nt * p.M + row] = m;
-            p.part_s[(int64_t)nt * p.M + row] = s;
-            if (has_tgt) p.tgt[row] = tgt;
-          }
-        }
-      } else {
-        float* partial_base = nullptr;
-        if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.split_stride;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
-          const int col0 = nt * BN + c * 32;
-          if (row_ok && col0 < p.N) store_row32(p, v, row, col0, partial_base);
-        }
-      }
+      epilogue_tile<BN>(p, taddr, row, row_ok, nt, sp);
       sm100::tc_fence_before();
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&tempty[acc]);
@@ -454,6 +462,226 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   __syncthreads();
   sm100::tc_fence_after();
   if (warp == 1) sm100::tmem_dealloc(tmem_base, C::TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a cluster of 2 CTAs computes 256 x 256 tiles with
+// tcgen05.mma.cta_group::2 (M = 256 split 128/128 across the pair's TMEM,
+// N = 256 with each CTA holding half of B).  Per CTA and k-block only
+// 16 KB of A and 16 KB of B cross into shared memory (vs 16 + 32 KB for the
+// 1-SM 128 x 256 tile), which is what lets the tensor cores run near peak.
+// Protocol: both CTAs' producers load their own halves with the pair form of
+// the TMA load, completing bytes on the LEADER's full barrier (the leader
+// arms it with the pair's total); the leader's single MMA thread issues the
+// pair MMA and its commits arrive on the empty / TMEM-full barriers of both
+// CTAs; each CTA drains its own 128 accumulator rows and arrives on the
+// leader's TMEM-empty barrier.  No multicast loads.
+// ---------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+
+struct PairCfg {
+  static constexpr int STAGES = kPairStages;
+  static constexpr uint32_t A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = 128 * BK * 2;   // this CTA's 128 rows/cols of B
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr uint32_t TMEM_COLS = 512;          // 2 x 256 fp32 accumulators
+  static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_pair_kernel(const __grid_constant__ Params p) {
+  using C = PairCfg;
+  constexpr int STAGES = C::STAGES;
+  constexpr int BN = 256;
+  constexpr uint32_t IDESC = sm100::idesc_bf16_f32(256, BN, A_MN, B_MN);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * C::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);   // used in the leader: its producer's arrive + tx
+      sm100::mbar_init(&empty[s], 1);  // one multicast commit per phase
+    }
+    for (int b = 0; b < 2; ++b) {
+      sm100::mbar_init(&tfull[b], 1);
+      sm100::mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs (leader's copy)
+    }
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    sm100::fence_proxy_async_smem();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < p.nseg; ++s) {
+      sm100::tma_prefetch_desc(&p.tma_a[s]);
+      sm100::tma_prefetch_desc(&p.tma_b[s]);
+    }
+  }
+  if (warp == 1) {
+    sm100::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    sm100::tmem_relinquish_pair();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // barriers of both CTAs initialised before any remote use
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_units = p.m_tiles * p.n_tiles * p.splits;
+  const int cluster_id = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+
+  if (warp == 0) {
+    // --------------------------- producer (both CTAs) ------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int inflight = 0;
+      bool ok = true;
+      for (int unit = cluster_id; unit < num_units && ok; unit += nclusters) {
+        int mt, nt, sp;
+        decode_unit(p, unit, mt, nt, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const int m0 = mt * 256 + (int)rank * 128;
+        const int n0 = nt * BN + (int)rank * 128;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, p.err,
+                                        SITE_PROD_EMPTY)) {
+            ok = false;
+            break;
+          }
+          inflight = min(inflight + 1, STAGES);
+          int seg, kl;
+          locate_kb(p, kb, seg, kl);
+          const int kx = kl * BK;
+          if (leader) sm100::mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          const uint32_t bar = sm100::mapa_shared(sm100::smem_u32(&full[stage]), 0);
+          uint8_t* a_dst = sA + stage * C::A_BYTES;
+          uint8_t* b_dst = sB + stage * C::B_BYTES;
+          if constexpr (!A_MN) {
+            sm100::tma_load_2d_pair(a_dst, &p.tma_a[seg], bar, kx, m0);
+          } else {
+            sm100::tma_load_2d_pair(a_dst, &p.tma_a[seg], bar, m0, kx);
+            sm100::tma_load_2d_pair(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, m0 + 64, kx);
+          }
+          if constexpr (!B_MN) {
+            sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, kx, n0);
+          } else {
+            sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, n0, kx);
+            sm100::tma_load_2d_pair(b_dst + 64 * BK * 2, &p.tma_b[seg], bar, n0 + 64, kx);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && leader) {
+        // Drain (bounded): let every copy this pair issued land before exit.
+        int s = stage, ph = phase;
+        for (int i = 0; i < inflight; ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          const uint64_t t0 = sm100::globaltimer_ns();
+          while (!sm100::mbar_try_wait(&full[s], ph) &&
+                 sm100::globaltimer_ns() - t0 < 1000000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------- MMA issuer (leader) -------------------------
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int unit = cluster_id; unit < num_units && ok; unit += nclusters) {
+        int mt, nt, sp;
+        decode_unit(p, unit, mt, nt, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        if (!sm100::mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag, p.err,
+                                      SITE_MMA_TEMPTY)) {
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!sm100::mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          sm100::tc_fence_after();
+          const uint32_t a_base = sm100::smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_base = sm100::smem_u32(sB + stage * C::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sm100::sdesc_sw128(a_base + k * 2048, 64 * BK * 2, 1024)
+                                     : sm100::sdesc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sm100::sdesc_sw128(b_base + k * 2048, 64 * BK * 2, 1024)
+                                     : sm100::sdesc_sw128(b_base + k * 32, 16, 1024);
+            sm100::umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          sm100::umma_commit_pair(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        sm100::umma_commit_pair(&tfull[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+    }
+  } else {
+    // --------------------------- epilogue (both CTAs) ------------------------
+    const int ew = warp & 3;
+    const int rloc = ew * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int unit = cluster_id; unit < num_units; unit += nclusters) {
+      int mt, nt, sp;
+      decode_unit(p, unit, mt, nt, sp);
+      bool ok = sm100::mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag, p.err, SITE_EPI);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      sm100::tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+      const int64_t row = (int64_t)mt * 256 + (int64_t)rank * 128 + rloc;
+      epilogue_tile<BN>(p, taddr, row, row < p.M, nt, sp);
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive_cluster(sm100::mapa_shared(sm100::smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // no CTA leaves while its peer may still signal it
+  sm100::tc_fence_after();
+  if (warp == 1) sm100::tmem_dealloc_pair(tmem_base, C::TMEM_COLS);
 }
 
 // ---------------------------------------------------------------------------
@@ -488,6 +716,7 @@ struct Problem {
   int raster = 0;
   int group_m = 0;
   int bn = 0;          // 0 = choose
+  int pair = -1;       // CTA-pair kernel: -1 = process default, 0 = never, 1 = when possible
   int max_ctas = 0;    // 0 = SM count
   // FLCE
   const int64_t* labels = nullptr;

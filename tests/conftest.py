@@ -46,3 +46,13 @@ def cuda_lib():
     """The built CUDA library (loads it; fails loudly if missing)."""
     from metal_liger_b200 import _C
     return _C.load()
+
+
+@pytest.fixture(params=[0, 1], ids=["1sm", "pair"])
+def pair_mode(request):
+    """Run a GPU test once with every GEMM on the 1-SM kernel and once with the
+    2-SM (CTA pair) kernel forced wherever the tile shape allows."""
+    from metal_liger_b200 import _C
+
+    with _C.gemm_cta_pair(request.param):
+        yield request.param

@@ -63,7 +63,7 @@ def _bf16_case(n, h, v, seed, ignore_frac=0.1):
 
 @pytest.mark.parametrize("n,h,v,chunk", [(1000, 256, 5000, 384), (130, 64, 300, 8192),
                                          (256, 128, 2048, 100)])
-def test_bf16_against_oracle(n, h, v, chunk):
+def test_bf16_against_oracle(n, h, v, chunk, pair_mode):
     hid, w, lab = _bf16_case(n, h, v, seed=n + v)
     loss, dx, dw = run_flce(hid, w, lab, chunk=chunk, grad_output=0.75)
     rl, lse, mask = O.flce_forward(hid, w, lab, None, -100, 4096)

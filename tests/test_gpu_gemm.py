@@ -76,7 +76,7 @@ def rand(*shape, seed=0, scale=1.0):
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, False), (False, True), (True, True)])
 @pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 256, 512), (300, 200, 96), (77, 40, 130)])
-def test_single_segment(a_mn, b_mn, m, n, k):
+def test_single_segment(a_mn, b_mn, m, n, k, pair_mode):
     a = rand(m, k, seed=1)
     b = rand(n, k, seed=2)
     d, _ = run_gemm([(a, b)], m, n, a_mn=a_mn, b_mn=b_mn)
@@ -85,7 +85,7 @@ def test_single_segment(a_mn, b_mn, m, n, k):
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
-def test_multi_segment_accumulates_in_one_tile(a_mn, b_mn):
+def test_multi_segment_accumulates_in_one_tile(a_mn, b_mn, pair_mode):
     m, n = 384, 512
     segs = [(rand(m, 256, seed=3), rand(n, 256, seed=4)),
             (rand(m, 64, seed=5), rand(n, 64, seed=6)),
@@ -95,7 +95,7 @@ def test_multi_segment_accumulates_in_one_tile(a_mn, b_mn):
     assert_close(d, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item(), what="D")
 
 
-def test_bf16_output_and_beta_accumulate():
+def test_bf16_output_and_beta_accumulate(pair_mode):
     m, n, k = 256, 384, 320
     a, b = rand(m, k, seed=9), rand(n, k, seed=10)
     d, _ = run_gemm([(a, b)], m, n, out_dtype=torch.bfloat16)
@@ -118,7 +118,27 @@ def test_split_k_path():
     assert torch.equal(d, d_again), "split-K reduction must be deterministic"
 
 
-def test_large_square():
+def test_split_k_pair_tiles(pair_mode):
+    m, n, k = 512, 256, 8192  # few tiles, long K -> split-K on 256 x 256 tiles
+    a, b = rand(m, k, seed=15), rand(n, k, seed=16)
+    d, ws_bytes = run_gemm([(a, b)], m, n, a_mn=True, b_mn=True)
+    ref = reference([(a, b)])
+    assert_close(d, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item(), what="split-K D")
+    d_again, _ = run_gemm([(a, b)], m, n, a_mn=True, b_mn=True)
+    assert torch.equal(d, d_again), "split-K reduction must be deterministic"
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
+def test_ragged_many_pair_tiles(a_mn, b_mn, pair_mode):
+    # more tiles than SM pairs (persistent loop) with ragged M/N/K edges
+    m, n, k = 2500, 3000, 200
+    a, b = rand(m, k, seed=17), rand(n, k, seed=18)
+    d, _ = run_gemm([(a, b)], m, n, a_mn=a_mn, b_mn=b_mn)
+    ref = reference([(a, b)])
+    assert_close(d, ref, rtol=1e-4, atol=1e-4 * ref.abs().max().item(), what="D")
+
+
+def test_large_square(pair_mode):
     m = n = k = 4096
     a, b = rand(m, k, seed=13), rand(n, k, seed=14)
     d, _ = run_gemm([(a, b)], m, n, out_dtype=torch.bfloat16)

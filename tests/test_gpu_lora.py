@@ -119,7 +119,7 @@ def _proj(gen, out_f, in_f, r, s, dev="cpu", wstd=0.02, astd=0.05):
 
 @pytest.mark.parametrize("T,H,qo,kvo,r", [(400, 512, 512, 128, 16), (130, 256, 256, 64, 8),
                                           (64, 128, 128, 128, 21)])
-def test_qkv_bf16_against_oracle(T, H, qo, kvo, r):
+def test_qkv_bf16_against_oracle(T, H, qo, kvo, r, pair_mode):
     gen = torch.Generator().manual_seed(T + H)
     x = torch.randn(2, T // 2, H, generator=gen).bfloat16()
     q, k, v = _proj(gen, qo, H, r, 2.0), _proj(gen, kvo, H, r, 1.5), _proj(gen, kvo, H, r, 0.5)
@@ -140,7 +140,7 @@ def test_qkv_bf16_against_oracle(T, H, qo, kvo, r):
 
 
 @pytest.mark.parametrize("T,H,I,r", [(300, 256, 768, 16), (128, 128, 384, 32)])
-def test_mlp_bf16_against_oracle(T, H, I, r):
+def test_mlp_bf16_against_oracle(T, H, I, r, pair_mode):
     gen = torch.Generator().manual_seed(T + I)
     x = torch.randn(T, H, generator=gen).bfloat16()
     g, u, d = _proj(gen, I, H, r, 2.0), _proj(gen, I, H, r, 2.0), _proj(gen, H, I, r, 2.0)
