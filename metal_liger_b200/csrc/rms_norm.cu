@@ -22,6 +22,15 @@ namespace {
 
 constexpr int kMaxThreads = 256;  // vector path: per-thread registers hold 2 rows (prefetch)
 
+// Backward CTA size: when a thread's share of two rows (current + prefetch)
+// fits in ~80 registers the CTA holds three 256-thread row groups and runs one
+// per SM, so the dweight partials (one row per CTA) number about the SM count.
+// Larger shares keep 256-thread CTAs (three groups would not fit an SM).
+template <typename TX>
+__host__ __device__ constexpr int bwd_max_threads(int nv) {
+  return (nv == 1 || (nv == 2 && sizeof(TX) == 4)) ? 768 : kMaxThreads;
+}
+
 struct RowCfg {
   int nv = 0;       // 16-byte vectors per thread per row
   int tpr = 0;      // threads per row
@@ -185,7 +194,7 @@ rms_fwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restri
 // ([gridDim.x, hidden]).  Row groups of a CTA fold their partials together
 // through shared memory (fixed order) before the single store.
 template <typename TX, typename TW, int NV>
-__global__ void __launch_bounds__(kMaxThreads)
+__global__ void __launch_bounds__(bwd_max_threads<TX>(NV), 1)
 rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
             const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
             int64_t rows, int64_t hidden, float eps, int tpr, int groups) {
@@ -207,6 +216,9 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   const float inv_h = 1.f / (float)hidden;
   int64_t row = (int64_t)blockIdx.x * groups + g;
   Vec16<TX> xv[NV], gv[NV], xn[NV], gn[NV];
+  // The saved rrms of the next row is fetched with that row's data, so no
+  // load sits on the critical path between the reduction and the stores.
+  float rv = (rrms != nullptr && row < rows) ? __ldg(rrms + row) : 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const int64_t col = (int64_t)(i * tpr + t) * VEC;
@@ -219,6 +231,7 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   for (int64_t it = 0; it < niter; ++it, row += row_stride) {
     const bool active = row < rows;
     const int64_t nrow = row + row_stride;
+    const float rn = (rrms != nullptr && nrow < rows) ? __ldg(rrms + nrow) : 0.f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int64_t col = (int64_t)(i * tpr + t) * VEC;
@@ -243,7 +256,7 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
     const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
     buf ^= 1;
     if (active) {
-      const float r = rrms != nullptr ? rrms[row] : rsqrtf(sums.x * inv_h + eps);
+      const float r = rrms != nullptr ? rv : rsqrtf(sums.x * inv_h + eps);
       const float c = (sums.y * inv_h) * (r * r * r);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
@@ -266,7 +279,11 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
       xv[i] = xn[i];
       gv[i] = gn[i];
     }
+    rv = rn;
   }
+  // The dweight reduction kernel may start launching now; it waits for this
+  // grid to finish (griddepcontrol.wait) before reading the partials.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // Fold the row groups' partials (fixed order) and store one row per CTA.
   if (groups > 1) {
 #pragma unroll
@@ -327,25 +344,31 @@ rms_bwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, const float*
 }
 
 // Second stage: dweight[c] = sum_p partial[p][c], fixed summation order.
-// Block (32 columns x 8 part-lanes); each lane strides over the parts, then
-// the 8 lane sums are added in order through shared memory.
+// Block = 32 columns x 32 part-lanes; each lane sums every 32nd part (about
+// ten independent loads for a full grid, all in flight at once), then lane
+// sums are added in order through shared memory.
+constexpr int kReduceLanes = 32;
+
 template <typename TW>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32 * kReduceLanes)
 rms_dw_reduce(const float* __restrict__ partial, int parts, int64_t hidden, TW* __restrict__ dw) {
-  __shared__ float s[8][33];
+  __shared__ float s[kReduceLanes][33];
+  // Launched as a programmatic dependent of the backward kernel: wait until
+  // that grid has completed and its partials are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + tx;
   float acc = 0.f;
   if (c < hidden) {
-#pragma unroll 4
-    for (int p = ty; p < parts; p += 8) acc += partial[(int64_t)p * hidden + c];
+#pragma unroll 8
+    for (int p = ty; p < parts; p += kReduceLanes) acc += partial[(int64_t)p * hidden + c];
   }
   s[ty][tx] = acc;
   __syncthreads();
   if (ty == 0 && c < hidden) {
     float tot = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) tot += s[k][tx];
+    for (int k = 0; k < kReduceLanes; ++k) tot += s[k][tx];
     dw[c] = from_f32<TW>(tot);
   }
 }
@@ -360,9 +383,18 @@ int occupancy_grid(const void* kernel, int threads, size_t smem, int64_t work_ct
   return static_cast<int>(std::max<int64_t>(grid, 1));
 }
 
+// Fewest CTAs (<= max_grid) that still need the same number of row
+// iterations as max_grid: every CTA then does equal work and the last
+// iteration is not a partial wave.
+int64_t balanced_grid(int64_t work, int64_t max_grid) {
+  max_grid = std::max<int64_t>(max_grid, 1);
+  const int64_t iters = (work + max_grid - 1) / max_grid;
+  return std::max<int64_t>(1, (work + iters - 1) / std::max<int64_t>(iters, 1));
+}
+
 // Grid used by the backward; the workspace size is derived from it, so the
 // two must agree.  It depends only on sizes and the device's SM count.
-constexpr int kBwdCtasPerSm = 2;
+constexpr int kBwdCtasPerSm = 4;
 constexpr int kGenericGrid = 4;  // CTAs per SM for the generic kernels
 
 int64_t bwd_grid_upper_bound(int64_t rows) {
@@ -383,7 +415,7 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
 #define ML_FWD_CASE(NV_)                                                                   \
   case NV_: {                                                                              \
     auto k = rms_fwd_vec<TX, TW, NV_>;                                                     \
-    int grid = occupancy_grid((const void*)k, threads, 0, work);                           \
+    int grid = (int)balanced_grid(work, occupancy_grid((const void*)k, threads, 0, work)); \
     k<<<grid, threads, 0, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups); \
     break;                                                                                 \
   }
@@ -412,6 +444,7 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
   const TX* gp = static_cast<const TX*>(dy);
   TX* dxp = static_cast<TX*>(dx);
   RowCfg cfg = pick_cfg<TX>(hidden, x, dy, dx, x);
+  if (cfg.vec) cfg.groups = std::max(1, std::min(8, bwd_max_threads<TX>(cfg.nv) / cfg.tpr));
   int grid = 0;
   const int64_t max_parts = static_cast<int64_t>(partial_bytes / (sizeof(float) * (size_t)hidden));
   if (cfg.vec) {
@@ -424,9 +457,6 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
     const int threads_eff = cfg.tpr * cfg.groups;
     (void)threads;
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
-    grid = static_cast<int>(std::min<int64_t>(
-        std::min<int64_t>(work, (int64_t)num_sms() * kBwdCtasPerSm), max_parts));
-    grid = std::max(grid, 1);
 #define ML_BWD_CASE(NV_)                                                                     \
   case NV_: {                                                                                \
     auto k = rms_bwd_vec<TX, TW, NV_>;                                                       \
@@ -435,6 +465,10 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,        \
                                          (int)smem),                                         \
                     "rms_norm_backward: smem attribute");                                    \
+    const int per_sm = std::min<int>(                                                        \
+        kBwdCtasPerSm, occupancy_grid((const void*)k, threads_eff, smem, 1 << 30) / num_sms()); \
+    grid = static_cast<int>(balanced_grid(                                                   \
+        work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));      \
     k<<<grid, threads_eff, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps,    \
                                        cfg.tpr, cfg.groups);                                 \
     break;                                                                                   \
@@ -454,9 +488,21 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
     rms_bwd_generic<TX, TW><<<grid, 256, 0, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps);
   }
   ML_CHECK_LAUNCH("rms_norm_backward");
-  const int rblocks = static_cast<int>((hidden + 31) / 32);
-  rms_dw_reduce<TW><<<rblocks, 256, 0, st>>>(partial, grid, hidden, static_cast<TW*>(dw));
-  ML_CHECK_LAUNCH("rms_norm_backward(dweight reduce)");
+  // Programmatic dependent launch: the reduction's launch overlaps the tail
+  // of the backward grid instead of following it.
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(static_cast<unsigned>((hidden + 31) / 32), 1, 1);
+  lc.blockDim = dim3(32 * kReduceLanes, 1, 1);
+  lc.dynamicSmemBytes = 0;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  ML_CHECK_CUDA(cudaLaunchKernelEx(&lc, rms_dw_reduce<TW>, (const float*)partial, grid, hidden,
+                                   static_cast<TW*>(dw)),
+                "rms_norm_backward(dweight reduce)");
   return ML_OK;
 }
 

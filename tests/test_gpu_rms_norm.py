@@ -81,6 +81,9 @@ def test_baseline_config_c1_full_size():
     ((9, 1000), torch.float16, torch.float16),
     ((33, 4096), torch.bfloat16, torch.bfloat16),     # Qwen3-VL-8B hidden
     ((2, 3, 128), torch.bfloat16, torch.bfloat16),    # per-head q_norm/k_norm shape
+    ((1000, 2048), torch.float32, torch.float32),     # 3 row groups per CTA, ragged last wave
+    ((4099, 512), torch.float32, torch.float32),      # 6 row groups per CTA
+    ((700, 256), torch.bfloat16, torch.float32),      # 8 row groups per CTA
 ])
 def test_edge_shapes(shape, xd, wd):
     g = torch.Generator().manual_seed(sum(shape))
