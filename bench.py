@@ -639,7 +639,186 @@ class Lora:
         O.lora_mlp_backward(c["x"], P["g"], P["u"], P["d"], c["dy"])
 
 
-WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce, "lora": Lora}
+class FullStep:
+    """one LoRA training step of the Qwen3-VL-8B text decoder.
+
+    transformers' ``Qwen3VLTextModel`` at the 8B text shape (36 layers, hidden
+    4096, 32 q / 8 kv heads of 128, SwiGLU 12288, vocab 151936, RMSNorm eps
+    1e-6, RoPE theta 5e6), random init, bf16, PEFT-layout LoRA r=16 alpha=32 on
+    q/k/v/o/gate/up/down, patched with ``apply_metal_liger_to_qwen3vl`` (all
+    fusions on, including the B200 extensions: per-head q/k norm, RoPE inside
+    attention, fused o_proj) and the loss from
+    ``MetalLigerFusedLinearCrossEntropy`` over the frozen lm_head.  A step is
+    forward, backward, the NCCL all-reduce of the LoRA gradients (N > 1) and an
+    AdamW step.  One sequence of 4096 random token ids per GPU (8 GPUs = the
+    BASELINE's batch 8 x 4096).  Attention is torch SDPA (library kernel).
+    """
+
+    name = "c5_step"
+    bound = "tensor"
+    dtype = "bf16"
+    L, H, NH, NKV, D, I, V = 36, 4096, 32, 8, 128, 12288, 151936
+    R, ALPHA, SEQ, THETA = 16, 32.0, 4096, 5e6
+    dominant = "train_step"
+    TARGETS = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.batch = 1
+        self.tokens = self.batch * self.SEQ
+        self.flops = {"train_step": self.flops_per_token(self.L) * self.tokens}
+        self.bytes = {}
+        self.launches_per_step = None  # counted with the profiler
+
+    # algorithmic FLOPs per token (frozen base weights: no dW; causal attention)
+    def flops_per_token(self, layers):
+        H, I, r = self.H, self.I, self.R
+        q, kv = self.NH * self.D, self.NKV * self.D
+        dense = 2 * (H * q + 2 * H * kv + q * H + 3 * H * I)        # forward GEMMs
+        adapters = [(H, q), (H, kv), (H, kv), (q, H), (H, I), (H, I), (I, H)]
+        lora = sum(2 * r * 3 * (fin + fout) for fin, fout in adapters)  # fwd + bwd rank terms
+        attn_fwd = 2 * 2 * self.D * self.NH * (self.SEQ // 2)      # QK^T and PV, causal
+        layer = 2 * dense + lora + 3 * attn_fwd                     # fwd + bwd (dX only)
+        head = 2 * 2 * H * self.V                                   # logits + dX
+        return layers * layer + head
+
+    def config(self):
+        return {"workload": "c5_full_step (BASELINE configs[4]): Qwen3-VL-8B text decoder LoRA "
+                            "training step, transformers Qwen3VLTextModel random init, bf16, "
+                            "36 layers, hidden 4096, 32/8 heads x 128, SwiGLU 12288, vocab "
+                            "151936, LoRA r=16 alpha=32 on q/k/v/o/gate/up/down, fused FLCE "
+                            "loss, AdamW on the adapters",
+                "model": "Qwen3-VL-8B (text decoder)", "layers": self.L,
+                "global_batch": self.batch * self.world, "seq_len": self.SEQ,
+                "tokens_per_step_per_gpu": self.tokens,
+                "parallelism": (f"dp{self.world} (token rows; NCCL all-reduce of LoRA grads)"
+                                if self.world > 1 else "single GPU"),
+                "attention": "torch SDPA (causal)",
+                "flops_per_token": self.flops_per_token(self.L),
+                "l2": "inputs larger than L2 (16 GB of frozen weights streamed per step)"}
+
+    def _build(self, device, layers, dtype=torch.bfloat16, fused=True, seed=1238):
+        import torch.nn as nn
+        from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+        from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+        from metal_liger_b200.lora_adapters import inject_lora, lora_parameters
+
+        cfg = Qwen3VLTextConfig(hidden_size=self.H, intermediate_size=self.I,
+                                num_hidden_layers=layers, num_attention_heads=self.NH,
+                                num_key_value_heads=self.NKV, head_dim=self.D, vocab_size=self.V,
+                                rms_norm_eps=1e-6, max_position_embeddings=self.SEQ,
+                                rope_parameters={"rope_type": "default", "rope_theta": self.THETA,
+                                                 "mrope_section": [24, 20, 20]})
+        cfg._attn_implementation = "sdpa"
+        torch.manual_seed(seed)
+        holder = nn.Module()
+        with torch.device(device):
+            holder.model = Qwen3VLTextModel(cfg).to(dtype)
+            holder.lm_head = nn.Linear(self.H, self.V, bias=False).to(dtype)
+            with torch.no_grad():
+                holder.lm_head.weight.normal_(0.0, 0.02)
+        inject_lora(holder, r=self.R, alpha=self.ALPHA, targets=self.TARGETS, init_std=0.01)
+        if fused:
+            from metal_liger_b200 import apply_metal_liger_to_qwen3vl
+
+            apply_metal_liger_to_qwen3vl(holder, fuse_qk_norm=True, fuse_rope_in_attention=True,
+                                         fuse_lora_o_proj=True)
+            # the patched norms hold new (trainable) Parameters, as in the
+            # reference's patcher; LoRA training keeps everything but the
+            # adapters frozen
+            for n, p in holder.named_parameters():
+                if "lora_" not in n:
+                    p.requires_grad_(False)
+        params = lora_parameters(holder)
+        opt = torch.optim.AdamW(params, lr=1e-4, fused=(device != "cpu" and
+                                                         torch.device(device).type == "cuda"))
+        return holder, params, opt
+
+    def make_inputs(self, device, seed=1239):
+        self.model, self.params, self.opt = self._build(device, self.L)
+        g = torch.Generator(device=device).manual_seed(seed + self.rank)
+        ids = torch.randint(0, self.V, (self.batch, self.SEQ), generator=g, device=device)
+        labels = torch.roll(ids, -1, dims=1)
+        labels[:, -1] = -100
+        return {"ids": ids, "labels": labels}
+
+    def _train_step(self, ids, labels):
+        from metal_liger_b200.ops.fused_linear_cross_entropy import \
+            MetalLigerFusedLinearCrossEntropy
+
+        m = self.model
+        h = m.model(input_ids=ids, use_cache=False).last_hidden_state
+        loss = MetalLigerFusedLinearCrossEntropy(m.lm_head)(h, labels)
+        loss.backward()
+        if self.world > 1:
+            import torch.distributed as dist
+
+            grads = [p.grad for p in self.params]
+            flat = torch._utils._flatten_dense_tensors(grads)
+            dist.all_reduce(flat)
+            flat.div_(self.world)
+            for gd, red in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
+                gd.copy_(red)
+        self.opt.step()
+        self.opt.zero_grad(set_to_none=True)
+        return loss.detach()
+
+    def step(self, t, timer=plain):
+        timer("train_step", self._train_step, t["ids"], t["labels"])
+
+    def e2e_setup(self, device):
+        g = torch.Generator().manual_seed(81 + self.rank)
+        ids = torch.randint(0, self.V, (self.batch, self.SEQ), generator=g)
+        labels = torch.roll(ids, -1, dims=1)
+        labels[:, -1] = -100
+        host = {"ids": ids.pin_memory(), "labels": labels.pin_memory()}
+        dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+        host_out = {"loss": torch.empty((), pin_memory=True)}
+        h2d = sum(v.numel() * v.element_size() for v in host.values())
+        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": 4}
+
+    def e2e_step(self, s):
+        d, h, ho = s["dev"], s["host"], s["host_out"]
+        for k in d:
+            d[k].copy_(h[k], non_blocking=True)
+        loss = self._train_step(d["ids"], d["labels"])
+        ho["loss"].copy_(loss.float(), non_blocking=True)
+
+    # CPU baseline: the same step, unfused (transformers' modules, PEFT-layout
+    # adapters, F.cross_entropy) in fp32 with ONE decoder layer; tokens/s are
+    # scaled to 36 layers by the FLOP ratio (labelled as extrapolated).
+    cpu_extrapolated = True
+
+    def cpu_inputs(self, tokens, seed=9):
+        if not hasattr(self, "_cpu_model"):
+            self._cpu_model, self._cpu_params, self._cpu_opt = self._build(
+                "cpu", 1, dtype=torch.float32, fused=False)
+        g = torch.Generator().manual_seed(seed)
+        ids = torch.randint(0, self.V, (1, tokens), generator=g)
+        labels = torch.roll(ids, -1, dims=1)
+        labels[:, -1] = -100
+        return {"ids": ids, "labels": labels}
+
+    def cpu_step(self, c):
+        import torch.nn.functional as F
+
+        m = self._cpu_model
+        h = m.model(input_ids=c["ids"], use_cache=False).last_hidden_state
+        logits = h @ m.lm_head.weight.t()
+        loss = F.cross_entropy(logits.view(-1, self.V), c["labels"].view(-1), ignore_index=-100)
+        loss.backward()
+        self._cpu_opt.step()
+        self._cpu_opt.zero_grad(set_to_none=True)
+
+    def cpu_scale(self):
+        """Multiply the 1-layer CPU tokens/s by this to extrapolate to 36 layers."""
+        return self.flops_per_token(1) / self.flops_per_token(self.L)
+
+
+WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce, "lora": Lora,
+             "c5_step": FullStep}
 
 
 def _register_optional_workloads():
@@ -649,6 +828,37 @@ def _register_optional_workloads():
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
+
+_OUR_KERNEL = None
+
+
+def count_our_launches(wl, t) -> int | None:
+    """Kernels from this repository's library launched by one step, counted
+    with the CUDA profiler (CUPTI) on an extra, untimed step."""
+    global _OUR_KERNEL
+    import re
+
+    if _OUR_KERNEL is None:
+        _OUR_KERNEL = re.compile(r"(^|[^A-Za-z0-9_])(ml|gemm|flce|lora)::")
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        prelude = getattr(wl, "prelude", None)
+        if prelude:
+            prelude(t)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            wl.step(t)
+            torch.cuda.synchronize()
+        n = 0
+        for ev in prof.events():
+            if getattr(ev, "device_type", None) == torch.autograd.DeviceType.CUDA and \
+                    _OUR_KERNEL.search(ev.name or ""):
+                n += 1
+        return n
+    except Exception:
+        return None
+
 
 def cpu_measure(wl, budget_s: float, max_steps: int | None = None):
     """Time the CPU oracle on a bounded sample: returns (tokens/s, tokens, steps, cores)."""
@@ -695,11 +905,17 @@ def run_reference_arm(args, wl):
     value = tokens * args.steps / el
     sample = (f"{tokens} of {wl.tokens} tokens per step (same shapes per token), "
               f"torch CPU fp32 oracle restating the reference ops, TORCHDYNAMO_DISABLE=1")
+    if getattr(wl, "cpu_extrapolated", False):
+        value *= wl.cpu_scale()
+        sample = (f"{tokens} tokens per step of the unfused step with ONE decoder layer "
+                  f"(transformers modules, PEFT-layout adapters, F.cross_entropy, fp32); "
+                  f"tokens/s extrapolated to {wl.L} layers by the FLOP ratio "
+                  f"{wl.cpu_scale():.4f}")
     line = {
         "impl": "reference",
         "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps * wl.tokens / tokens,
+        "warmup": args.warmup, "ms_per_step": 1e3 * wl.tokens / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
         "data": "synthetic", "config": wl.config(),
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": torch.get_num_threads(),
@@ -777,6 +993,9 @@ def run_gpu_arm(args, wl):
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         elapsed_ms = el.item()
     kernel_ms = timer.averages_ms()
+    per_step_launches = count_our_launches(wl, t)
+    if per_step_launches is None:
+        per_step_launches = wl.launches_per_step
     # weak scaling: every rank processes wl.tokens; strong: the job processes wl.tokens
     job_tokens = wl.tokens * (world if getattr(wl, "scaling", "weak") == "weak" else 1)
     value = job_tokens * args.steps / (elapsed_ms / 1e3)
@@ -844,10 +1063,16 @@ def run_gpu_arm(args, wl):
         cpu = None
         if world == 1 and not args.no_cpu:
             v, tok, st, cores = cpu_measure(wl, budget_s=args.cpu_budget)
+            sample = (f"{tok} of {wl.tokens} tokens x {st} steps through the CPU oracle "
+                      f"(torch fp32 restatement of the reference ops), {cores} threads")
+            if getattr(wl, "cpu_extrapolated", False):
+                v *= wl.cpu_scale()
+                sample = (f"{tok} tokens x {st} steps of the unfused step with ONE decoder layer "
+                          f"(transformers modules, PEFT-layout adapters, F.cross_entropy, fp32) "
+                          f"on {cores} threads; tokens/s extrapolated to {wl.L} layers by the "
+                          f"FLOP ratio {wl.cpu_scale():.4f}")
             cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                   "sample": f"{tok} of {wl.tokens} tokens x {st} steps through the CPU oracle "
-                             f"(torch fp32 restatement of the reference ops), "
-                             f"{cores} threads"}
+                   "sample": sample}
         line = {
             "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
             "value": value,
@@ -885,7 +1110,8 @@ def run_gpu_arm(args, wl):
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "api": "public autograd Functions (metal_liger_b200.ops.*), pinned host "
                            "buffers, H2D inputs + D2H all outputs per step"},
-            "gpu_launches": wl.launches_per_step * args.steps,
+            "gpu_launches": (per_step_launches * args.steps
+                             if per_step_launches is not None else None),
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)

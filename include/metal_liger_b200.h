@@ -348,6 +348,26 @@ ML_API int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens, in
                                 void* dx, float* const* da, float* const* db, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/*
+ * The same pair for 1 to 3 LoRA projections of one input (nproj * rank <= 64):
+ * ml_lora_qkv_* are these with nproj = 3.  nproj = 1 is a single fused LoRA
+ * linear (o_proj): y = x W^T + s (x A^T) B^T with the rank term folded into
+ * the base GEMM, and dx / dA / dB as above.  The reference describes this
+ * single-projection form ("LoRA_W", ops/fused_lora.py:26) and falls back to
+ * PEFT's unfused modules (ops/fused_lora.py:69-82) for it.
+ */
+ML_API size_t ml_lora_linear_workspace_bytes(int64_t tokens, int64_t in_features, int nproj,
+                                             const ml_lora_proj* proj, int backward);
+ML_API int ml_lora_linear_forward(const void* x, int64_t tokens, int64_t in_features,
+                                  int64_t rank, int nproj, const ml_lora_proj* proj,
+                                  void* const* out, void* u, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+ML_API int ml_lora_linear_backward(const void* x, const void* u, int64_t tokens,
+                                   int64_t in_features, int64_t rank, int nproj,
+                                   const ml_lora_proj* proj, const void* const* dy, void* dx,
+                                   float* const* da, float* const* db, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Workspace bytes for the MLP entry points (backward = 0 or 1). */
 ML_API size_t ml_lora_mlp_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
                                           int backward);

@@ -110,6 +110,16 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                      ctypes.POINTER(LoraProj), ctypes.POINTER(c_void_p), c_void_p,
                                      ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_void_p,
                                      c_size_t, c_void_p]),
+    "ml_lora_linear_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int,
+                                                  ctypes.POINTER(LoraProj), c_int]),
+    "ml_lora_linear_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int,
+                                       ctypes.POINTER(LoraProj), ctypes.POINTER(c_void_p),
+                                       c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ml_lora_linear_backward": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                                        ctypes.POINTER(LoraProj), ctypes.POINTER(c_void_p),
+                                        c_void_p, ctypes.POINTER(c_void_p),
+                                        ctypes.POINTER(c_void_p), c_void_p, c_size_t,
+                                        c_void_p]),
     "ml_lora_mlp_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int]),
     "ml_lora_mlp_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64,
                                     ctypes.POINTER(LoraProj), c_void_p, c_void_p, c_void_p,

@@ -31,6 +31,7 @@ from metal_liger_b200.ops.fused_linear_cross_entropy import (  # noqa: E402
 from metal_liger_b200.ops.fused_lora import (  # noqa: E402
     apply_fused_lora_qkv,
     apply_fused_lora_mlp,
+    apply_fused_lora_linear,
     patch_fused_lora,
 )
 from metal_liger_b200.patch import apply_metal_liger_to_qwen3vl  # noqa: E402
@@ -44,6 +45,7 @@ __all__ = [
     "apply_metal_liger_to_qwen3vl",
     "apply_fused_lora_qkv",
     "apply_fused_lora_mlp",
+    "apply_fused_lora_linear",
     "patch_fused_lora",
     "apply_compile",
     "register_metal_liger_ops",

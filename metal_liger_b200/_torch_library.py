@@ -415,6 +415,51 @@ def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq
     return (dx.to(x.dtype).view(x.shape), das[0], dbs[0], das[1], dbs[1], das[2], dbs[2])
 
 
+def lora_linear_forward_cuda(x, w, a, b, scaling):
+    _C.require_cuda("lora_linear_forward", x, w, a, b)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    if w.dim() != 2 or w.shape[1] != H:
+        raise RuntimeError("lora_linear_forward: weight must be [out, in] with in == x.shape[-1]")
+    r = _check_rank((a,), (b,), (H,))
+    keep: list = []
+    projs = (_C.LoraProj * 1)()
+    projs[0] = _lora_proj(w, a, b, scaling, keep)
+    dev = x.device
+    out = torch.empty((T, w.shape[0]), dtype=torch.bfloat16, device=dev)
+    u = torch.empty((T, 64), dtype=torch.bfloat16, device=dev)
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_linear_workspace_bytes(T, H, 1, projs, 0))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_linear_forward", _C.ptr(x2), T, H, r, 1, projs, _ptr_array([out]),
+            _C.ptr(u), _C.ptr(ws), nbytes, _C.stream_of(x))
+    return out.to(x.dtype), u
+
+
+def lora_linear_backward_cuda(x, u, w, a, b, scaling, dy):
+    _C.require_cuda("lora_linear_backward", x, u, w, a, b, dy)
+    H = x.shape[-1]
+    x2 = _bf16_2d(x, H)
+    T = x2.shape[0]
+    r = _check_rank((a,), (b,), (H,))
+    keep: list = []
+    projs = (_C.LoraProj * 1)()
+    projs[0] = _lora_proj(w, a, b, scaling, keep)
+    dys = [_bf16_2d(dy, w.shape[0])]
+    dev = x.device
+    dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    da = torch.empty((r, H), dtype=torch.float32, device=dev)
+    db = torch.empty((w.shape[0], r), dtype=torch.float32, device=dev)
+    lib = _C.load()
+    nbytes = int(lib.ml_lora_linear_workspace_bytes(T, H, 1, projs, 1))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    _C.call("ml_lora_linear_backward", _C.ptr(x2), _C.ptr(_contig(u)), T, H, r, 1, projs,
+            _ptr_array(dys), _C.ptr(dx), _ptr_array([da]), _ptr_array([db]), _C.ptr(ws), nbytes,
+            _C.stream_of(x))
+    return dx.to(x.dtype).view(x.shape), da, db
+
+
 def lora_mlp_forward_cuda(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
     _C.require_cuda("lora_mlp_forward", x, gw, ga, gb, uw, ua, ub, dw, da, db)
     H = x.shape[-1]
@@ -503,6 +548,10 @@ _SCHEMAS = {
                          "Tensor kw, Tensor ka, Tensor kb, Tensor vw, Tensor va, Tensor vb, "
                          "float[] scaling, Tensor dq, Tensor dk, Tensor dv) -> (Tensor, Tensor, "
                          "Tensor, Tensor, Tensor, Tensor, Tensor)",
+    "lora_linear_forward": "lora_linear_forward(Tensor x, Tensor w, Tensor a, Tensor b, "
+                           "float scaling) -> (Tensor, Tensor)",
+    "lora_linear_backward": "lora_linear_backward(Tensor x, Tensor u, Tensor w, Tensor a, "
+                            "Tensor b, float scaling, Tensor dy) -> (Tensor, Tensor, Tensor)",
     "lora_mlp_forward": "lora_mlp_forward(Tensor x, Tensor gw, Tensor ga, Tensor gb, Tensor uw, "
                         "Tensor ua, Tensor ub, Tensor dw, Tensor da, Tensor db, float[] scaling) "
                         "-> (Tensor, Tensor, Tensor, Tensor, Tensor, Tensor)",
@@ -525,6 +574,8 @@ _CUDA_IMPLS = {
     "flce_backward": flce_backward_cuda,
     "lora_qkv_forward": lora_qkv_forward_cuda,
     "lora_qkv_backward": lora_qkv_backward_cuda,
+    "lora_linear_forward": lora_linear_forward_cuda,
+    "lora_linear_backward": lora_linear_backward_cuda,
     "lora_mlp_forward": lora_mlp_forward_cuda,
     "lora_mlp_backward": lora_mlp_backward_cuda,
 }
@@ -592,6 +643,16 @@ def _fake_impls():
         return (torch.empty_like(x), f(r, H), f(qw.shape[0], r), f(r, H), f(kw.shape[0], r),
                 f(r, H), f(vw.shape[0], r))
 
+    def llin_fwd(x, w, a, b, scaling):
+        T = x.numel() // x.shape[-1]
+        return (torch.empty((T, w.shape[0]), dtype=x.dtype, device=x.device),
+                torch.empty((T, 64), dtype=torch.bfloat16, device=x.device))
+
+    def llin_bwd(x, u, w, a, b, scaling, dy):
+        r, H = a.shape
+        return (torch.empty_like(x), torch.empty((r, H), dtype=torch.float32, device=x.device),
+                torch.empty((w.shape[0], r), dtype=torch.float32, device=x.device))
+
     def lmlp_fwd(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
         T = x.numel() // x.shape[-1]
         inter = gw.shape[0]
@@ -609,6 +670,8 @@ def _fake_impls():
     return {
         "lora_qkv_forward": lqkv_fwd,
         "lora_qkv_backward": lqkv_bwd,
+        "lora_linear_forward": llin_fwd,
+        "lora_linear_backward": llin_bwd,
         "lora_mlp_forward": lmlp_fwd,
         "lora_mlp_backward": lmlp_bwd,
         "flce_forward": flce_fwd,

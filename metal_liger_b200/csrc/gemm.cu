@@ -313,9 +313,14 @@ int auto_splits(int64_t M, int64_t N, int64_t K) {
 
 int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partial,
                   size_t partial_bytes, cudaStream_t st) {
+  return launch_splitk_to(pr, splits, out, true, ldo, partial, partial_bytes, st);
+}
+
+int launch_splitk_to(Problem pr, int splits, void* out, bool out_f32, int64_t ldo,
+                     float* partial, size_t partial_bytes, cudaStream_t st) {
   if (splits <= 1) {
     pr.epi = EPI_STORE;
-    pr.d_f32 = true;
+    pr.d_f32 = out_f32;
     pr.D = out;
     pr.ldd = ldo;
     pr.splits = 1;
@@ -336,8 +341,8 @@ int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partia
   if (rc) return rc;
   const int64_t total = pr.M * pr.N;
   int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
-  splitk_reduce<<<std::max(grid, 1), 256, 0, st>>>(partial, splits, pr.M, pr.N, pr.N, out, ldo, 1,
-                                                    0.f);
+  splitk_reduce<<<std::max(grid, 1), 256, 0, st>>>(partial, splits, pr.M, pr.N, pr.N, out, ldo,
+                                                    out_f32 ? 1 : 0, 0.f);
   ML_CHECK_LAUNCH("gemm split-K reduce");
   return ML_OK;
 }

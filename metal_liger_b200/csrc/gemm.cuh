@@ -745,6 +745,9 @@ int* device_error_word();
 // fixed-order reduction.  pr.epi / pr.D / pr.splits are filled in here.
 int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partial,
                   size_t partial_bytes, cudaStream_t stream);
+// Same with the output type chosen: fp32 (out_f32) or bf16.
+int launch_splitk_to(Problem pr, int splits, void* out, bool out_f32, int64_t ldo,
+                     float* partial, size_t partial_bytes, cudaStream_t stream);
 
 // Split count launch_splitk would pick to fill the GPU for these sizes.
 int auto_splits(int64_t M, int64_t N, int64_t K);

@@ -19,6 +19,8 @@
 #include "gemm.cuh"
 
 #include <algorithm>
+#include <initializer_list>
+#include <vector>
 
 extern "C" int ml_swiglu_forward(const void* gate, const void* up, void* out, int64_t n, int dtype,
                                  void* stream);
@@ -139,14 +141,18 @@ gemm::Seg seg(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t k)
   return s;
 }
 
-// D[M, N] (bf16, pitch ldd) = sum of segments.
-int gemm_bf16(int64_t M, int64_t N, std::initializer_list<gemm::Seg> segs, bool a_mn, bool b_mn,
+// D[M, N] (bf16, pitch ldd) = sum of segments (at most gemm::kMaxSeg).
+int gemm_bf16(int64_t M, int64_t N, const gemm::Seg* segs, size_t nseg, bool a_mn, bool b_mn,
               void* D, int64_t ldd, cudaStream_t st) {
+  if (nseg == 0 || nseg > (size_t)gemm::kMaxSeg) {
+    set_error("lora: %zu GEMM segments (1..%d supported)", nseg, gemm::kMaxSeg);
+    return ML_ERR_INVALID_ARG;
+  }
   gemm::Problem p;
   p.M = M;
   p.N = N;
   p.nseg = 0;
-  for (const auto& s : segs) p.seg[p.nseg++] = s;
+  for (size_t i = 0; i < nseg; ++i) p.seg[p.nseg++] = segs[i];
   p.a_mn = a_mn;
   p.b_mn = b_mn;
   p.epi = gemm::EPI_STORE;
@@ -154,6 +160,16 @@ int gemm_bf16(int64_t M, int64_t N, std::initializer_list<gemm::Seg> segs, bool 
   p.D = D;
   p.ldd = ldd;
   return gemm::launch(p, st);
+}
+
+int gemm_bf16(int64_t M, int64_t N, std::initializer_list<gemm::Seg> segs, bool a_mn, bool b_mn,
+              void* D, int64_t ldd, cudaStream_t st) {
+  return gemm_bf16(M, N, segs.begin(), segs.size(), a_mn, b_mn, D, ldd, st);
+}
+
+int gemm_bf16(int64_t M, int64_t N, const std::vector<gemm::Seg>& segs, bool a_mn, bool b_mn,
+              void* D, int64_t ldd, cudaStream_t st) {
+  return gemm_bf16(M, N, segs.data(), segs.size(), a_mn, b_mn, D, ldd, st);
 }
 
 // out[M, 64] fp32 = A^T-style skinny product over the token dimension, split-K.
@@ -174,30 +190,70 @@ size_t skinny_partial_floats(int64_t M, int64_t K) {
   return (size_t)gemm::auto_splits(M, kSlot, K) * (size_t)M * kSlot;
 }
 
+// out[T, 64] bf16 = sum of segments: the rank projections (U = X A^T,
+// G = dY B).  With few tokens the 128-row tiles do not cover the GPU, so the
+// reduction over K is split (fixed-order fp32 reduce) when the caller's
+// partial buffer (skinny_partial_floats(T, K)) allows.
+int rank_proj(int64_t T, const gemm::Seg* segs, size_t nseg, bf16* out, float* part,
+              size_t part_floats, cudaStream_t st) {
+  int64_t K = 0;
+  for (size_t i = 0; i < nseg; ++i) K += segs[i].K;
+  const int splits = gemm::auto_splits(T, kSlot, K);
+  if (splits <= 1 || part == nullptr || part_floats < (size_t)splits * (size_t)T * kSlot)
+    return gemm_bf16(T, kSlot, segs, nseg, false, false, out, kSlot, st);
+  if (nseg == 0 || nseg > (size_t)gemm::kMaxSeg) {
+    set_error("lora: %zu GEMM segments (1..%d supported)", nseg, gemm::kMaxSeg);
+    return ML_ERR_INVALID_ARG;
+  }
+  gemm::Problem p;
+  p.M = T;
+  p.N = kSlot;
+  p.nseg = 0;
+  for (size_t i = 0; i < nseg; ++i) p.seg[p.nseg++] = segs[i];
+  p.a_mn = false;
+  p.b_mn = false;
+  return gemm::launch_splitk_to(p, splits, out, false, kSlot, part, part_floats * 4, st);
+}
+
+int rank_proj(int64_t T, std::initializer_list<gemm::Seg> segs, bf16* out, float* part,
+              size_t part_floats, cudaStream_t st) {
+  return rank_proj(T, segs.begin(), segs.size(), out, part, part_floats, st);
+}
+
+int rank_proj(int64_t T, const std::vector<gemm::Seg>& segs, bf16* out, float* part,
+              size_t part_floats, cudaStream_t st) {
+  return rank_proj(T, segs.data(), segs.size(), out, part, part_floats, st);
+}
+
 bool valid_proj(const ml_lora_proj& p) {
   return p.w && p.a && p.b && p.out_features > 0 && p.a_dtype >= 0 && p.a_dtype <= 2 &&
          p.b_dtype >= 0 && p.b_dtype <= 2;
 }
 
-// ------------------------------- QKV --------------------------------------
-int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, const ml_lora_proj* pj,
+// --------------------------- QKV (1-3 projections) -------------------------
+// `np` projections of one input X (Q/K/V: np = 3; a single LoRA linear such as
+// o_proj: np = 1).  Adapter i owns rank slot [i r, (i + 1) r) of the 64-wide
+// rank operands, so np * r <= 64.
+int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, int np, const ml_lora_proj* pj,
                 void* const* out, bf16* u, Arena& ar, cudaStream_t st) {
   bf16* acat = ar.take<bf16>((size_t)kSlot * H);
-  bf16* bpad[3];
-  for (int i = 0; i < 3; ++i) bpad[i] = ar.take<bf16>((size_t)pj[i].out_features * kSlot);
+  bf16* bpad[3] = {};
+  for (int i = 0; i < np; ++i) bpad[i] = ar.take<bf16>((size_t)pj[i].out_features * kSlot);
+  const size_t rpf = skinny_partial_floats(T, H);
+  float* rpart = ar.take<float>(rpf);
   if (ar.dry) return ML_OK;
   LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
     LORA_TRY(zero(bpad[i], (size_t)o * kSlot * 2, st));
     LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[i].a, pj[i].a_dtype, r, H, i * r, 1.f);
     LORA_LAUNCH(pack_cols_k, o * r, bpad[i], kSlot, pj[i].b, pj[i].b_dtype, o, r, i * r,
                 pj[i].scaling);
   }
-  // U = X [A_q; A_k; A_v]^T   [T, 64]
-  LORA_TRY(gemm_bf16(T, kSlot, {seg(x, H, acat, H, H)}, false, false, u, kSlot, st));
+  // U = X [A_0; A_1; ...]^T   [T, 64]
+  LORA_TRY(rank_proj(T, {seg(x, H, acat, H, H)}, u, rpart, rpf, st));
   // y_i = [X | U] [W_i | s_i B_i (in its slot)]^T
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
     LORA_TRY(gemm_bf16(T, o, {seg(x, H, pj[i].w, H, H), seg(u, kSlot, bpad[i], kSlot, kSlot)},
                        false, false, out[i], o, st));
@@ -205,45 +261,49 @@ int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, const ml_lora_pr
   return ML_OK;
 }
 
-int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r,
+int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, int np,
                  const ml_lora_proj* pj, const void* const* dy, bf16* dx, float* const* da,
                  float* const* db, Arena& ar, cudaStream_t st) {
-  int64_t omax = 0;
-  for (int i = 0; i < 3; ++i) omax = std::max(omax, pj[i].out_features);
-  bf16* bt[3];
-  for (int i = 0; i < 3; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
+  int64_t omax = 0, osum = 0;
+  for (int i = 0; i < np; ++i) {
+    omax = std::max(omax, pj[i].out_features);
+    osum += pj[i].out_features;
+  }
+  bf16* bt[3] = {};
+  for (int i = 0; i < np; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
   bf16* acat_s = ar.take<bf16>((size_t)kSlot * H);
   bf16* G = ar.take<bf16>((size_t)T * kSlot);
   float* dAT = ar.take<float>((size_t)H * kSlot);
   float* dBt = ar.take<float>((size_t)omax * kSlot);
-  const size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(omax, T));
+  const size_t pf = std::max({skinny_partial_floats(H, T), skinny_partial_floats(omax, T),
+                              skinny_partial_floats(T, osum)});
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
   LORA_TRY(zero(acat_s, (size_t)kSlot * H * 2, st));
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
     LORA_TRY(zero(bt[i], (size_t)kSlot * o * 2, st));
     LORA_LAUNCH(pack_t_k, o * r, bt[i], o, pj[i].b, pj[i].b_dtype, o, r, i * r, 1.f);
     LORA_LAUNCH(pack_rows_k, r * H, acat_s, H, pj[i].a, pj[i].a_dtype, r, H, i * r,
                 pj[i].scaling);
   }
-  const int64_t o0 = pj[0].out_features, o1 = pj[1].out_features, o2 = pj[2].out_features;
-  // G = [dQ Bq | dK Bk | dV Bv]   [T, 64]
-  LORA_TRY(gemm_bf16(T, kSlot,
-                     {seg(dy[0], o0, bt[0], o0, o0), seg(dy[1], o1, bt[1], o1, o1),
-                      seg(dy[2], o2, bt[2], o2, o2)},
-                     false, false, G, kSlot, st));
-  // dX = dQ Wq + dK Wk + dV Wv + G (s A)   — one accumulator, W read in place (N-major)
-  LORA_TRY(gemm_bf16(T, H,
-                     {seg(dy[0], o0, pj[0].w, H, o0), seg(dy[1], o1, pj[1].w, H, o1),
-                      seg(dy[2], o2, pj[2].w, H, o2), seg(G, kSlot, acat_s, H, kSlot)},
-                     false, true, dx, H, st));
+  // G = [dY_0 B_0 | dY_1 B_1 | ...]   [T, 64]
+  std::vector<gemm::Seg> gsegs, xsegs;
+  for (int i = 0; i < np; ++i) {
+    const int64_t o = pj[i].out_features;
+    gsegs.push_back(seg(dy[i], o, bt[i], o, o));
+    xsegs.push_back(seg(dy[i], o, pj[i].w, H, o));
+  }
+  xsegs.push_back(seg(G, kSlot, acat_s, H, kSlot));
+  LORA_TRY(rank_proj(T, gsegs, G, part, pf, st));
+  // dX = sum_i dY_i W_i + G (s A)   — one accumulator, W read in place (N-major)
+  LORA_TRY(gemm_bf16(T, H, xsegs, false, true, dx, H, st));
   // dA_i = s_i (X^T G)[:, slot_i]^T
   LORA_TRY(gemm_skinny_f32(H, seg(x, H, G, kSlot, T), dAT, part, pf * 4, st));
-  for (int i = 0; i < 3; ++i)
+  for (int i = 0; i < np; ++i)
     LORA_LAUNCH(unpack_t_k, r * H, da[i], dAT, H, r, i * r, pj[i].scaling);
   // dB_i = s_i dY_i^T U[:, slot_i]
-  for (int i = 0; i < 3; ++i) {
+  for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
     LORA_TRY(gemm_skinny_f32(o, seg(dy[i], o, u, kSlot, T), dBt, part, pf * 4, st));
     LORA_LAUNCH(unpack_cols_k, o * r, db[i], dBt, o, r, i * r, pj[i].scaling);
@@ -261,6 +321,8 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
   bf16* bup = ar.take<bf16>((size_t)I * kSlot);     // cols [r,2r) = s_u Bu
   bf16* ad = ar.take<bf16>((size_t)kSlot * I);      // rows [0,r) = Ad
   bf16* bdp = ar.take<bf16>((size_t)H * kSlot);     // cols [0,r) = s_d Bd
+  const size_t rpf = std::max(skinny_partial_floats(T, H), skinny_partial_floats(T, I));
+  float* rpart = ar.take<float>(rpf);
   if (ar.dry) return ML_OK;
   LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
   LORA_TRY(zero(bgp, (size_t)I * kSlot * 2, st));
@@ -274,7 +336,7 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
   LORA_LAUNCH(pack_rows_k, r * I, ad, I, pj[2].a, pj[2].a_dtype, r, I, 0, 1.f);
   LORA_LAUNCH(pack_cols_k, H * r, bdp, kSlot, pj[2].b, pj[2].b_dtype, H, r, 0, pj[2].scaling);
   // U1 = X [Ag; Au]^T
-  LORA_TRY(gemm_bf16(T, kSlot, {seg(x, H, acat, H, H)}, false, false, u1, kSlot, st));
+  LORA_TRY(rank_proj(T, {seg(x, H, acat, H, H)}, u1, rpart, rpf, st));
   // gate / up = [X | U1] [W | s B]^T
   LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[0].w, H, H), seg(u1, kSlot, bgp, kSlot, kSlot)}, false,
                      false, gate, I, st));
@@ -283,7 +345,7 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
   // h = silu(gate) * up (fp32 math)
   LORA_TRY(ml_swiglu_forward(gate, up, h, T * I, ML_DTYPE_BF16, st));
   // U2 = h Ad^T ; out = [h | U2] [Wd | s Bd]^T
-  LORA_TRY(gemm_bf16(T, kSlot, {seg(h, I, ad, I, I)}, false, false, u2, kSlot, st));
+  LORA_TRY(rank_proj(T, {seg(h, I, ad, I, I)}, u2, rpart, rpf, st));
   LORA_TRY(gemm_bf16(T, H, {seg(h, I, pj[2].w, I, I), seg(u2, kSlot, bdp, kSlot, kSlot)}, false,
                      false, out, H, st));
   return ML_OK;
@@ -306,7 +368,8 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   const int64_t mmax = std::max(H, I);
   float* dAT = ar.take<float>((size_t)mmax * kSlot);
   float* dBt = ar.take<float>((size_t)mmax * kSlot);
-  const size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(I, T));
+  const size_t pf = std::max({skinny_partial_floats(H, T), skinny_partial_floats(I, T),
+                              skinny_partial_floats(T, H), skinny_partial_floats(T, 2 * I)});
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
   LORA_TRY(zero(bdT, (size_t)kSlot * H * 2, st));
@@ -321,7 +384,7 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[0].a, pj[0].a_dtype, r, H, 0, pj[0].scaling);
   LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[1].a, pj[1].a_dtype, r, H, r, pj[1].scaling);
   // G_d = dY Bd ; dH = dY Wd + G_d (s_d Ad)      (Wd stored [H, I]: N-major)
-  LORA_TRY(gemm_bf16(T, kSlot, {seg(dy, H, bdT, H, H)}, false, false, Gd, kSlot, st));
+  LORA_TRY(rank_proj(T, {seg(dy, H, bdT, H, H)}, Gd, part, pf, st));
   LORA_TRY(gemm_bf16(T, I, {seg(dy, H, pj[2].w, I, H), seg(Gd, kSlot, ads, I, kSlot)}, false,
                      true, dH, I, st));
   // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
@@ -332,8 +395,7 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   // SwiGLU backward (sigmoid recomputed)
   LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
   // G_gu = [d_gate Bg | d_up Bu]
-  LORA_TRY(gemm_bf16(T, kSlot, {seg(dgate, I, bgT, I, I), seg(dup, I, buT, I, I)}, false, false,
-                     Ggu, kSlot, st));
+  LORA_TRY(rank_proj(T, {seg(dgate, I, bgT, I, I), seg(dup, I, buT, I, I)}, Ggu, part, pf, st));
   // dX = d_gate Wg + d_up Wu + G_gu (s A)        (Wg/Wu stored [I, H]: N-major)
   LORA_TRY(gemm_bf16(T, H,
                      {seg(dgate, I, pj[0].w, H, I), seg(dup, I, pj[1].w, H, I),
@@ -369,47 +431,96 @@ int check_ws(const Arena& need, size_t have, void* ws, const char* what) {
 using namespace ml;
 using lora::Arena;
 
-#define LORA_ARGCHECK_COMMON(what)                                                           \
+#define LORA_ARGCHECK_COMMON(what, NP)                                                       \
   ML_CHECK_ARG(tokens >= 0 && in_features > 0 && rank > 0, what ": bad sizes");              \
   ML_CHECK_ARG(in_features % 8 == 0, what ": in_features must be a multiple of 8");          \
+  ML_CHECK_ARG((NP) >= 1 && (NP) <= 3, what ": nproj must be 1, 2 or 3");                    \
+  ML_CHECK_ARG((NP) * rank <= lora::kSlot, what ": nproj * rank = %lld > 64 is not supported", \
+               (long long)((NP) * rank));                                                    \
   ML_CHECK_ARG(proj != nullptr, what ": null projections");                                   \
-  for (int _i = 0; _i < 3; ++_i)                                                              \
+  for (int _i = 0; _i < (NP); ++_i)                                                           \
     ML_CHECK_ARG(lora::valid_proj(proj[_i]) && proj[_i].out_features % 8 == 0,                \
                  what ": projection %d is invalid (null pointer, bad dtype, or out_features " \
                  "not a multiple of 8)", _i);
 
-extern "C" size_t ml_lora_qkv_workspace_bytes(int64_t tokens, int64_t in_features,
-                                              const ml_lora_proj* proj, int backward) {
-  if (tokens <= 0 || in_features <= 0 || proj == nullptr) return 256;
+extern "C" size_t ml_lora_linear_workspace_bytes(int64_t tokens, int64_t in_features, int nproj,
+                                                 const ml_lora_proj* proj, int backward) {
+  if (tokens <= 0 || in_features <= 0 || proj == nullptr || nproj < 1 || nproj > 3) return 256;
   Arena ar;
   const int64_t r = 1;
   if (backward)
-    lora::qkv_backward(nullptr, nullptr, tokens, in_features, r, proj, nullptr, nullptr, nullptr,
-                       nullptr, ar, nullptr);
+    lora::qkv_backward(nullptr, nullptr, tokens, in_features, r, nproj, proj, nullptr, nullptr,
+                       nullptr, nullptr, ar, nullptr);
   else
-    lora::qkv_forward(nullptr, tokens, in_features, r, proj, nullptr, nullptr, ar, nullptr);
+    lora::qkv_forward(nullptr, tokens, in_features, r, nproj, proj, nullptr, nullptr, ar, nullptr);
   return std::max<size_t>(ar.off, 256);
+}
+
+extern "C" int ml_lora_linear_forward(const void* x, int64_t tokens, int64_t in_features,
+                                      int64_t rank, int nproj, const ml_lora_proj* proj,
+                                      void* const* out, void* u, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  LORA_ARGCHECK_COMMON("lora_linear_forward", nproj)
+  if (tokens == 0) return ML_OK;
+  ML_CHECK_ARG(x && out && u, "lora_linear_forward: null pointer");
+  for (int i = 0; i < nproj; ++i) ML_CHECK_ARG(out[i], "lora_linear_forward: null output %d", i);
+  Arena need;
+  lora::qkv_forward(nullptr, tokens, in_features, rank, nproj, proj, nullptr, nullptr, need,
+                    nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_linear_forward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  return lora::qkv_forward(static_cast<const __nv_bfloat16*>(x), tokens, in_features, rank,
+                           nproj, proj, out, static_cast<__nv_bfloat16*>(u), ar,
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int ml_lora_linear_backward(const void* x, const void* u, int64_t tokens,
+                                       int64_t in_features, int64_t rank, int nproj,
+                                       const ml_lora_proj* proj, const void* const* dy, void* dx,
+                                       float* const* da, float* const* db, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  LORA_ARGCHECK_COMMON("lora_linear_backward", nproj)
+  ML_CHECK_ARG(dy && da && db, "lora_linear_backward: null pointer arrays");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tokens == 0) {
+    for (int i = 0; i < nproj; ++i) {
+      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_features * 4, st), "memset dA");
+      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
+                    "memset dB");
+    }
+    return ML_OK;
+  }
+  ML_CHECK_ARG(x && u && dx, "lora_linear_backward: null pointer");
+  for (int i = 0; i < nproj; ++i)
+    ML_CHECK_ARG(dy[i] && da[i] && db[i], "lora_linear_backward: null pointer for projection %d",
+                 i);
+  Arena need;
+  lora::qkv_backward(nullptr, nullptr, tokens, in_features, rank, nproj, proj, nullptr, nullptr,
+                     nullptr, nullptr, need, nullptr);
+  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_linear_backward");
+  if (rc) return rc;
+  Arena ar;
+  ar.base = static_cast<uint8_t*>(workspace);
+  ar.dry = false;
+  return lora::qkv_backward(static_cast<const __nv_bfloat16*>(x),
+                            static_cast<const __nv_bfloat16*>(u), tokens, in_features, rank,
+                            nproj, proj, dy, static_cast<__nv_bfloat16*>(dx), da, db, ar, st);
+}
+
+extern "C" size_t ml_lora_qkv_workspace_bytes(int64_t tokens, int64_t in_features,
+                                              const ml_lora_proj* proj, int backward) {
+  return ml_lora_linear_workspace_bytes(tokens, in_features, 3, proj, backward);
 }
 
 extern "C" int ml_lora_qkv_forward(const void* x, int64_t tokens, int64_t in_features,
                                    int64_t rank, const ml_lora_proj* proj, void* const* out,
                                    void* u, void* workspace, size_t workspace_bytes,
                                    void* stream) {
-  LORA_ARGCHECK_COMMON("lora_qkv_forward")
-  ML_CHECK_ARG(3 * rank <= lora::kSlot, "lora_qkv_forward: rank %lld > 21 is not supported",
-               (long long)rank);
-  if (tokens == 0) return ML_OK;
-  ML_CHECK_ARG(x && out && out[0] && out[1] && out[2] && u, "lora_qkv_forward: null pointer");
-  Arena need;
-  lora::qkv_forward(nullptr, tokens, in_features, rank, proj, nullptr, nullptr, need, nullptr);
-  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_qkv_forward");
-  if (rc) return rc;
-  Arena ar;
-  ar.base = static_cast<uint8_t*>(workspace);
-  ar.dry = false;
-  return lora::qkv_forward(static_cast<const __nv_bfloat16*>(x), tokens, in_features, rank, proj,
-                           out, static_cast<__nv_bfloat16*>(u), ar,
-                           static_cast<cudaStream_t>(stream));
+  return ml_lora_linear_forward(x, tokens, in_features, rank, 3, proj, out, u, workspace,
+                                workspace_bytes, stream);
 }
 
 extern "C" int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens,
@@ -417,31 +528,8 @@ extern "C" int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens
                                     const void* const* dy, void* dx, float* const* da,
                                     float* const* db, void* workspace, size_t workspace_bytes,
                                     void* stream) {
-  LORA_ARGCHECK_COMMON("lora_qkv_backward")
-  ML_CHECK_ARG(3 * rank <= lora::kSlot, "lora_qkv_backward: rank %lld > 21 is not supported",
-               (long long)rank);
-  ML_CHECK_ARG(dy && da && db, "lora_qkv_backward: null pointer arrays");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (tokens == 0) {
-    for (int i = 0; i < 3; ++i) {
-      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_features * 4, st), "memset dA");
-      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
-                    "memset dB");
-    }
-    return ML_OK;
-  }
-  ML_CHECK_ARG(x && u && dx && dy[0] && dy[1] && dy[2], "lora_qkv_backward: null pointer");
-  Arena need;
-  lora::qkv_backward(nullptr, nullptr, tokens, in_features, rank, proj, nullptr, nullptr, nullptr,
-                     nullptr, need, nullptr);
-  int rc = lora::check_ws(need, workspace_bytes, workspace, "lora_qkv_backward");
-  if (rc) return rc;
-  Arena ar;
-  ar.base = static_cast<uint8_t*>(workspace);
-  ar.dry = false;
-  return lora::qkv_backward(static_cast<const __nv_bfloat16*>(x),
-                            static_cast<const __nv_bfloat16*>(u), tokens, in_features, rank, proj,
-                            dy, static_cast<__nv_bfloat16*>(dx), da, db, ar, st);
+  return ml_lora_linear_backward(x, u, tokens, in_features, rank, 3, proj, dy, dx, da, db,
+                                 workspace, workspace_bytes, stream);
 }
 
 #define LORA_MLP_CHECK(what)                                                                   \

@@ -4,7 +4,8 @@ Same public names, signatures and results as the reference
 (ops/fused_lora.py:43-421): ``_get_lora_params``, ``_lora_linear``,
 ``_LoRA_QKV.apply(X, QW,QA,QB,QS, KW,KA,KB,KS, VW,VA,VB,VS)``,
 ``_LoRA_MLP.apply(X, GW,GA,GB,GS, UW,UA,UB,US, DW,DA,DB,DS)``,
-``apply_fused_lora_qkv``, ``apply_fused_lora_mlp`` and ``patch_fused_lora``.
+``apply_fused_lora_qkv``, ``apply_fused_lora_mlp`` and ``patch_fused_lora``;
+plus ``_LoRA_W`` / ``apply_fused_lora_linear`` for a single LoRA projection.
 
 Each Function is two ``metal_liger::`` ops (forward, backward) that run every
 product on the tcgen05 GEMM: the rank-r update is an extra K-segment of the
@@ -108,6 +109,37 @@ class _LoRA_MLP(torch.autograd.Function):
                 None, dDA, dDB, None)
 
 
+class _LoRA_W(torch.autograd.Function):
+    """One LoRA linear y = X W^T + s (X A^T) B^T with the rank term folded into
+    the base GEMM (the single-projection form the reference describes as
+    "LoRA_W", ops/fused_lora.py:26, and leaves to PEFT).  Saves X and the
+    [tokens, 64] rank projection; A/B gradients in fp32, W frozen."""
+
+    @staticmethod
+    def forward(ctx, X, W, A, B, S):
+        s = float(S)
+        Y, U = torch.ops.metal_liger.lora_linear_forward(X, W, A, B, s)
+        ctx.save_for_backward(X, U, W, A, B)
+        ctx.s = s
+        return Y.view(*X.shape[:-1], -1)
+
+    @staticmethod
+    def backward(ctx, dY):
+        X, U, W, A, B = ctx.saved_tensors
+        dX, dA, dB = torch.ops.metal_liger.lora_linear_backward(X, U, W, A, B, ctx.s,
+                                                                dY.contiguous())
+        return dX, None, dA, dB, None
+
+
+def apply_fused_lora_linear(linear, X: torch.Tensor) -> torch.Tensor:
+    """A single PEFT LoRA linear (e.g. o_proj) through one fused op; falls back
+    to the module itself when it carries no adapter."""
+    W, A, B, S = _get_lora_params(linear)
+    if A is None:
+        return linear(X)
+    return _LoRA_W.apply(X, W, A, B, S)
+
+
 def apply_fused_lora_qkv(attn_module, X: torch.Tensor):
     """(Q, K, V) of an attention module's q/k/v_proj in one fused op; falls back
     to the modules themselves when any projection is not LoRA
@@ -151,9 +183,11 @@ def _has_lora(module, names):
                for n in names)
 
 
-def patch_fused_lora(model: nn.Module) -> int:
+def patch_fused_lora(model: nn.Module, fuse_o_proj: bool = False) -> int:
     """Route every decoder layer's q/k/v and gate/up/down LoRA projections
     through the fused Functions (reference ops/fused_lora.py:323-421).
+    ``fuse_o_proj=True`` (a B200 extension, off by default as in the
+    reference) also routes a LoRA ``o_proj`` through ``_LoRA_W``.
 
     The module tree is not modified: the attention forward is wrapped so that,
     for the duration of one call, q_proj/k_proj/v_proj are shadowed in the
@@ -187,6 +221,14 @@ def patch_fused_lora(model: nn.Module) -> int:
 
             attn.forward = types.MethodType(fused_attn_forward, attn)
             attn._metal_liger_fused_lora = True
+            patched += 1
+        o_proj = getattr(attn, "o_proj", None) if attn is not None else None
+        if fuse_o_proj and o_proj is not None and _get_lora_params(o_proj)[1] is not None:
+            def fused_o_forward(self_linear, x):
+                return apply_fused_lora_linear(self_linear, x)
+
+            o_proj.forward = types.MethodType(fused_o_forward, o_proj)
+            o_proj._metal_liger_fused_lora = True
             patched += 1
         if mlp is not None and _has_lora(mlp, ("gate_proj", "up_proj", "down_proj")):
             def fused_mlp_forward(self_mlp, x):

@@ -26,6 +26,7 @@ import torch.nn as nn
 from metal_liger_b200.generation import patch_generator
 from metal_liger_b200.ops.fused_lora import patch_fused_lora
 from metal_liger_b200.ops.fused_rms_norm import MetalLigerRMSNorm
+from metal_liger_b200.ops.fused_rope import apply_fused_rotary
 from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU
 
 logger = logging.getLogger(__name__)
@@ -115,6 +116,54 @@ def _replace_mlps(model: nn.Module) -> int:
     return count
 
 
+def _replace_qk_norms(model: nn.Module) -> int:
+    """Per-head q_norm / k_norm of every attention block -> MetalLigerRMSNorm."""
+    layers = _find_layers(model)
+    if layers is None:
+        return 0
+    count = 0
+    for layer in layers:
+        attn = getattr(layer, "self_attn", None)
+        for attr in ("q_norm", "k_norm"):
+            norm = getattr(attn, attr, None) if attn is not None else None
+            if norm is not None and hasattr(norm, "weight"):
+                setattr(attn, attr, _fused_norm_like(norm))
+                count += 1
+    return count
+
+
+def _fused_rotary_pos_emb(q, k, cos, sin, position_ids=None, unsqueeze_dim=1):
+    """HF ``apply_rotary_pos_emb`` signature, computed by the fused RoPE kernel
+    (q and k in one launch; strided [B, H, S, D] views read in place)."""
+    return apply_fused_rotary(q, k, cos.unsqueeze(unsqueeze_dim), sin.unsqueeze(unsqueeze_dim))
+
+
+def _patch_attention_rope(model: nn.Module) -> int:
+    """Rebind ``apply_rotary_pos_emb`` in the modeling module(s) of the model's
+    attention classes to the fused kernel.  Returns the number of modules
+    rebound (the originals are kept as ``_metal_liger_original_rope``)."""
+    import sys
+
+    layers = _find_layers(model)
+    if layers is None:
+        return 0
+    done = 0
+    seen = set()
+    for layer in layers:
+        attn = getattr(layer, "self_attn", None)
+        if attn is None:
+            continue
+        mod = sys.modules.get(type(attn).__module__)
+        if mod is None or id(mod) in seen or not hasattr(mod, "apply_rotary_pos_emb"):
+            continue
+        seen.add(id(mod))
+        if getattr(mod, "apply_rotary_pos_emb") is not _fused_rotary_pos_emb:
+            mod._metal_liger_original_rope = mod.apply_rotary_pos_emb
+            mod.apply_rotary_pos_emb = _fused_rotary_pos_emb
+        done += 1
+    return done
+
+
 def apply_metal_liger_to_qwen3vl(
     model: nn.Module,
     fuse_rms_norm: bool = True,
@@ -123,18 +172,34 @@ def apply_metal_liger_to_qwen3vl(
     fuse_cross_entropy: bool = False,
     fuse_lora: bool = True,
     use_optimized_generator: bool = False,
+    *,
+    fuse_qk_norm: bool = False,
+    fuse_rope_in_attention: bool = False,
+    fuse_lora_o_proj: bool = False,
 ) -> nn.Module:
-    """Apply the fused B200 ops to a Qwen3-VL (or similar) model in place; returns it."""
+    """Apply the fused B200 ops to a Qwen3-VL (or similar) model in place; returns it.
+
+    The positional flags are the reference's.  The keyword-only flags are B200
+    extensions, off by default so the default patch matches the reference:
+    ``fuse_qk_norm`` swaps the per-head q_norm/k_norm for the fused RMSNorm,
+    ``fuse_rope_in_attention`` rebinds the attention module's
+    ``apply_rotary_pos_emb`` to the fused RoPE, and ``fuse_lora_o_proj``
+    routes a LoRA o_proj through the fused single-projection op.
+    """
     stats = {}
     if fuse_rms_norm:
         stats["rms_norm"] = _replace_rms_norms(model)
         logger.info("MetalLiger: replaced %d RMSNorm layers with fused versions",
                     stats["rms_norm"])
+    if fuse_qk_norm:
+        stats["qk_norm"] = _replace_qk_norms(model)
+    if fuse_rope_in_attention:
+        stats["rope_in_attention"] = _patch_attention_rope(model)
     if fuse_swiglu:
         stats["swiglu"] = _replace_mlps(model)
         logger.info("MetalLiger: replaced %d MLP layers with fused SwiGLU", stats["swiglu"])
     if fuse_lora:
-        stats["fused_lora"] = patch_fused_lora(model)
+        stats["fused_lora"] = patch_fused_lora(model, fuse_o_proj=fuse_lora_o_proj)
         logger.info("MetalLiger: fused LoRA QKV+MLP on %d modules", stats["fused_lora"])
     if use_optimized_generator:
         patch_generator(model)

@@ -254,6 +254,24 @@ def lora_qkv_backward(x, q, k, v, dq, dk, dv, dtype=None, store_dtype=None):
     return dx.view(*x.shape), grads
 
 
+def lora_w_forward(x, p, dtype=None, store_dtype=None):
+    """One LoRA projection p = (W, A, B, s) of x: the per-projection step of
+    ops/fused_lora.py:96-119 (the single-projection form of ops/fused_lora.py:26)."""
+    return lora_qkv_forward(x, p, p, p, dtype, store_dtype)[0]
+
+
+def lora_w_backward(x, p, dy, dtype=None, store_dtype=None):
+    """Backward of lora_w_forward: the per-projection terms of
+    ops/fused_lora.py:142-161.  Returns (dX, (dA, dB))."""
+    cast = (lambda t: t) if dtype is None else (lambda t: t.to(dtype))
+    w, a, b, s = p
+    xf = cast(x).reshape(-1, x.shape[-1])
+    dyf = cast(dy).reshape(-1, dy.shape[-1])
+    da, db = _lora_grads(dyf, xf, cast(a), cast(b), s, store_dtype)
+    dx = _lora_dx(dyf, cast(w), cast(a), cast(b), s, store_dtype)
+    return dx.view(*x.shape), (da, db)
+
+
 def lora_mlp_forward(x, g, u, d, dtype=None, store_dtype=None):
     """ops/fused_lora.py:182-207: gate/up LoRA linears, h = silu(gate)*up (fp32 math,
     cast to x dtype), down LoRA linear.  Returns (out, gate, up, h)."""

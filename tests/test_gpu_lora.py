@@ -155,6 +155,29 @@ def test_mlp_bf16_against_oracle(T, H, I, r, pair_mode):
         close_reduction(db, rdb, f"d{n}B")
 
 
+@pytest.mark.parametrize("T,H,OUT,r", [(300, 512, 384, 16), (130, 256, 1024, 64), (64, 128, 128, 8)])
+def test_single_projection_against_oracle(T, H, OUT, r, pair_mode):
+    """_LoRA_W (one fused LoRA linear, e.g. o_proj) vs the oracle's per-projection
+    math; rank up to the full 64-wide slot."""
+    from metal_liger_b200.ops.fused_lora import _LoRA_W
+    gen = torch.Generator().manual_seed(T + OUT + r)
+    x = torch.randn(2, T // 2, H, generator=gen).bfloat16()
+    p = _proj(gen, OUT, H, r, 2.0)
+    dy = torch.randn(2, T // 2, OUT, generator=gen).bfloat16()
+    xl = _leaf(x)
+    a, b = _leaf(p[1]), _leaf(p[2])
+    y = _LoRA_W.apply(xl, p[0].to(DEV), a, b, p[3])
+    y.backward(dy.to(DEV))
+    torch.cuda.synchronize()
+    assert y.shape == (2, T // 2, OUT) and y.dtype == torch.bfloat16
+    ry = O.lora_w_forward(x, p, dtype=F32, store_dtype=BF)
+    rdx, (rda, rdb) = O.lora_w_backward(x, p, dy, dtype=F32, store_dtype=BF)
+    close(y.detach(), ry, "Y")
+    close(xl.grad, rdx, "dX")
+    close_reduction(a.grad, rda, "dA")
+    close_reduction(b.grad, rdb, "dB")
+
+
 def test_reference_test_case():
     """tests/test_fused_ops.py:198-240 (seed 42, X [2,16,128], W 128x128, r=8, s=2),
     checked against autograd of the plain expression in fp32."""

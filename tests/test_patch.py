@@ -55,3 +55,42 @@ def test_non_peft_model_paths():
     model = make_model(n_layers=2).base_model.model  # bare Qwen3-VL-shaped model
     apply_metal_liger_to_qwen3vl(model, fuse_lora=False)
     assert isinstance(model.model.language_model.norm, MetalLigerRMSNorm)
+
+
+def test_extension_flags_on_hf_qwen3vl_text_model():
+    """The keyword-only B200 extensions on transformers' Qwen3VLTextModel (CPU,
+    structure only): q/k norms swapped, o_proj routed through _LoRA_W, the
+    attention module's rotary function rebound (and restored here)."""
+    import sys
+
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+    from metal_liger_b200.lora_adapters import LoraLinear, inject_lora, lora_parameters
+
+    cfg = Qwen3VLTextConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=2,
+                            num_attention_heads=2, num_key_value_heads=1, head_dim=32,
+                            vocab_size=100)
+    holder = torch.nn.Module()
+    holder.model = Qwen3VLTextModel(cfg)
+    assert inject_lora(holder, r=4, alpha=8) == 14
+    assert len(lora_parameters(holder)) == 28
+    assert all(not p.requires_grad for n, p in holder.named_parameters() if "lora_" not in n)
+    keys = set(holder.state_dict())
+    mod = sys.modules[type(holder.model.layers[0].self_attn).__module__]
+    original = mod.apply_rotary_pos_emb
+    try:
+        apply_metal_liger_to_qwen3vl(holder, fuse_qk_norm=True, fuse_rope_in_attention=True,
+                                     fuse_lora_o_proj=True)
+        assert mod.apply_rotary_pos_emb is not original
+        assert mod._metal_liger_original_rope is original
+    finally:
+        mod.apply_rotary_pos_emb = original
+    for layer in holder.model.layers:
+        assert isinstance(layer.self_attn.q_norm, MetalLigerRMSNorm)
+        assert isinstance(layer.self_attn.k_norm, MetalLigerRMSNorm)
+        assert isinstance(layer.self_attn.o_proj, LoraLinear)
+        assert layer.self_attn.o_proj._metal_liger_fused_lora
+        assert isinstance(layer.mlp, MetalLigerSwiGLU)
+    assert isinstance(holder.model.norm, MetalLigerRMSNorm)
+    assert set(holder.state_dict()) == keys
