@@ -749,7 +749,11 @@ class FullStep:
             MetalLigerFusedLinearCrossEntropy
 
         m = self.model
-        h = m.model(input_ids=ids, use_cache=False).last_hidden_state
+        # Text-only positions (0..S-1 in every mrope section) passed as the 3-D
+        # [3, B, S] ids the model builds itself; as 3-D ids they skip HF's
+        # packed-sequence probe, a device-to-host sync every step.
+        pos = self._positions(ids)
+        h = m.model(input_ids=ids, position_ids=pos, use_cache=False).last_hidden_state
         loss = MetalLigerFusedLinearCrossEntropy(m.lm_head)(h, labels)
         loss.backward()
         if self.world > 1:
@@ -764,6 +768,14 @@ class FullStep:
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return loss.detach()
+
+    def _positions(self, ids):
+        key = (ids.shape, ids.device)
+        if getattr(self, "_pos_key", None) != key:
+            b, s = ids.shape
+            self._pos = torch.arange(s, device=ids.device).view(1, 1, s).expand(3, b, s)
+            self._pos_key = key
+        return self._pos
 
     def step(self, t, timer=plain):
         timer("train_step", self._train_step, t["ids"], t["labels"])
@@ -802,15 +814,28 @@ class FullStep:
         return {"ids": ids, "labels": labels}
 
     def cpu_step(self, c):
+        import sys
+
         import torch.nn.functional as F
 
         m = self._cpu_model
-        h = m.model(input_ids=c["ids"], use_cache=False).last_hidden_state
-        logits = h @ m.lm_head.weight.t()
-        loss = F.cross_entropy(logits.view(-1, self.V), c["labels"].view(-1), ignore_index=-100)
-        loss.backward()
-        self._cpu_opt.step()
-        self._cpu_opt.zero_grad(set_to_none=True)
+        # The GPU model's patch rebinds the modeling module's rotary function
+        # (shared with this unpatched CPU model): use the original here.
+        mod = sys.modules[type(m.model.layers[0].self_attn).__module__]
+        orig = getattr(mod, "_metal_liger_original_rope", None)
+        fused = mod.apply_rotary_pos_emb
+        if orig is not None:
+            mod.apply_rotary_pos_emb = orig
+        try:
+            h = m.model(input_ids=c["ids"], use_cache=False).last_hidden_state
+            logits = h @ m.lm_head.weight.t()
+            loss = F.cross_entropy(logits.view(-1, self.V), c["labels"].view(-1),
+                                   ignore_index=-100)
+            loss.backward()
+            self._cpu_opt.step()
+            self._cpu_opt.zero_grad(set_to_none=True)
+        finally:
+            mod.apply_rotary_pos_emb = fused
 
     def cpu_scale(self):
         """Multiply the 1-layer CPU tokens/s by this to extrapolate to 36 layers."""

@@ -305,6 +305,16 @@ ML_API int ml_flce_shard_grads(const void* hidden, const void* weight, const int
                                float* dx, float* dw, int dw_accumulate, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/*
+ * Phase 2 split in two: after ml_flce_shard_grads ran with dw == NULL (it
+ * leaves the (softmax - onehot) * scale chunk in `workspace`), this runs the
+ * shard's dW GEMM alone, so a caller can start the all-reduce of dx before
+ * it and overlap the two.  Same arguments and layout as above.
+ */
+ML_API int ml_flce_shard_grads_dw(const void* hidden, int64_t rows, int64_t h, int64_t v_local,
+                                  float* dw, int dw_accumulate, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------
  * Fused LoRA QKV / MLP
  * ------------------------------------------------------------------------ */

@@ -102,6 +102,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_flce_shard_grads": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                     c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_int, c_void_p, c_size_t, c_void_p]),
+    "ml_flce_shard_grads_dw": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
+                                       c_void_p, c_size_t, c_void_p]),
     "ml_lora_qkv_workspace_bytes": (c_size_t, [c_int64, c_int64, ctypes.POINTER(LoraProj), c_int]),
     "ml_lora_qkv_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, ctypes.POINTER(LoraProj),
                                     ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_size_t,

@@ -497,6 +497,32 @@ extern "C" int ml_flce_count_valid(const int64_t* labels, int64_t n, int64_t ign
   return ML_OK;
 }
 
+namespace ml {
+namespace flce {
+// dW [v_local, h] (+)= P^T hidden for a (softmax - onehot) * scale chunk P
+// held in the workspace (both operands read in place: MN-major).
+int shard_dw_gemm(const void* hidden, const __nv_bfloat16* E, int64_t ldE, int64_t rows,
+                  int64_t h, int64_t v_local, float* dw, int dw_accumulate, cudaStream_t st) {
+  gemm::Problem g3;
+  g3.M = v_local;
+  g3.N = h;
+  g3.nseg = 1;
+  g3.seg[0].a = {E, rows, v_local, ldE};
+  g3.seg[0].b = {hidden, rows, h, h};
+  g3.seg[0].K = rows;
+  g3.a_mn = true;
+  g3.b_mn = true;
+  g3.epi = gemm::EPI_STORE;
+  g3.d_f32 = true;
+  g3.D = dw;
+  g3.ldd = h;
+  g3.beta = dw_accumulate ? 1.f : 0.f;
+  g3.raster = 1;
+  return gemm::launch(g3, st);
+}
+}  // namespace flce
+}  // namespace ml
+
 extern "C" size_t ml_flce_shard_workspace_bytes(int64_t rows, int64_t v_local) {
   if (rows <= 0 || v_local <= 0) return 256;
   return flce::layout(rows, v_local, rows).total;
@@ -595,24 +621,23 @@ extern "C" int ml_flce_shard_grads(const void* hidden, const void* weight, const
     int rc = gemm::launch(g2, st);
     if (rc) return rc;
   }
-  if (dw != nullptr) {
-    gemm::Problem g3;
-    g3.M = v_local;
-    g3.N = h;
-    g3.nseg = 1;
-    g3.seg[0].a = {E, rows, v_local, L.ldE};
-    g3.seg[0].b = {hidden, rows, h, h};
-    g3.seg[0].K = rows;
-    g3.a_mn = true;
-    g3.b_mn = true;
-    g3.epi = gemm::EPI_STORE;
-    g3.d_f32 = true;
-    g3.D = dw;
-    g3.ldd = h;
-    g3.beta = dw_accumulate ? 1.f : 0.f;
-    g3.raster = 1;
-    int rc = gemm::launch(g3, st);
-    if (rc) return rc;
-  }
+  if (dw != nullptr) return flce::shard_dw_gemm(hidden, E, L.ldE, rows, h, v_local, dw,
+                                                 dw_accumulate, st);
   return ML_OK;
+}
+
+extern "C" int ml_flce_shard_grads_dw(const void* hidden, int64_t rows, int64_t h,
+                                      int64_t v_local, float* dw, int dw_accumulate,
+                                      void* workspace, size_t workspace_bytes, void* stream) {
+  ML_CHECK_ARG(rows > 0 && h > 0 && v_local > 0, "flce_shard_grads_dw: bad sizes");
+  ML_CHECK_ARG(hidden && dw, "flce_shard_grads_dw: null pointer");
+  const flce::Layout L = flce::layout(rows, v_local, rows);
+  ML_CHECK_ARG(workspace != nullptr && ((uintptr_t)workspace & 255) == 0 &&
+                   workspace_bytes >= L.total,
+               "flce_shard_grads_dw: workspace must be 256-byte aligned and >= %zu bytes",
+               L.total);
+  const __nv_bfloat16* E =
+      reinterpret_cast<const __nv_bfloat16*>(static_cast<uint8_t*>(workspace) + L.off_E);
+  return flce::shard_dw_gemm(hidden, E, L.ldE, rows, h, v_local, dw, dw_accumulate,
+                             static_cast<cudaStream_t>(stream));
 }

@@ -20,7 +20,7 @@
 //
 // Every mbarrier wait is bounded (see sm100::mbar_wait_bounded): on timeout
 // the CTA records an error in the library's device error word, all roles drain and the
-// kernel frees its TMEM and returns.  No TMA multicast is used.
+// kernel frees its TMEM and returns.
 #pragma once
 
 #include "common.cuh"
@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // arms it with the pair's total); the leader's single MMA thread issues the
 // pair MMA and its commits arrive on the empty / TMEM-full barriers of both
 // CTAs; each CTA drains its own 128 accumulator rows and arrives on the
-// leader's TMEM-empty barrier.  No multicast loads.
+// leader's TMEM-empty barrier.
 // ---------------------------------------------------------------------------
 constexpr int kPairStages = 6;
 
@@ -515,7 +515,7 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       sm100::mbar_init(&full[s], 1);   // used in the leader: its producer's arrive + tx
-      sm100::mbar_init(&empty[s], 1);  // one multicast commit per phase
+      sm100::mbar_init(&empty[s], 1);  // one commit (issued to both CTAs) per phase
     }
     for (int b = 0; b < 2; ++b) {
       sm100::mbar_init(&tfull[b], 1);

@@ -52,58 +52,90 @@ struct Arena {
 };
 
 // ------------------------------ pack kernels -------------------------------
-// dst[(row0 + i) * ld + c] = scale * src[i * cols + c]     (i < rows, c < cols)
-__global__ void pack_rows_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t rows,
-                            int64_t cols, int64_t row0, float scale) {
-  const int64_t n = rows * cols;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = e / cols, c = e - (e / cols) * cols;
-    dst[(row0 + i) * ld + c] = __float2bfloat16_rn(scale * load_as_f32(src, e, dt));
+// The rank operands of one call (stacked A's, slot-padded B's, their
+// transposes, scaled copies) are assembled by ONE launch: every element of
+// every destination operand is written exactly once — the value of the
+// adapter block covering it, else 0 — so no memset precedes it.
+constexpr int kMaxPieces = 3;
+constexpr int kMaxOperands = 6;
+
+// dst(r0 + i, c0 + j) = scale * src[i * cols + j]   (trans = 0: src is [rows, cols])
+// dst(r0 + i, c0 + j) = scale * src[j * rows + i]   (trans = 1: src is [cols, rows])
+struct Piece {
+  const void* src;
+  int64_t r0, c0, rows, cols;
+  float scale;
+  int dt;
+  int trans;
+};
+
+struct Operand {
+  bf16* dst;
+  int64_t ld, rows, cols;
+  int npieces;
+  Piece p[kMaxPieces];
+};
+
+struct Assembly {
+  Operand op[kMaxOperands];
+  int64_t start[kMaxOperands + 1];  // prefix sums of rows * cols
+  int nops;
+};
+
+// One thread per destination element (the operands total a few million
+// elements; 32-bit index math — the host checks the total fits).
+__global__ void __launch_bounds__(256) assemble_k(const __grid_constant__ Assembly a) {
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= (int)a.start[a.nops]) return;
+  int k = 0;
+  while (k + 1 < a.nops && e >= (int)a.start[k + 1]) ++k;
+  const Operand& o = a.op[k];
+  const int local = e - (int)a.start[k];
+  const int cols = (int)o.cols;
+  const int r = local / cols, c = local - r * cols;
+  float v = 0.f;
+  for (int q = 0; q < o.npieces; ++q) {
+    const Piece& pc = o.p[q];
+    const int i = r - (int)pc.r0, j = c - (int)pc.c0;
+    if (i >= 0 && i < (int)pc.rows && j >= 0 && j < (int)pc.cols)
+      v = pc.scale * load_as_f32(pc.src,
+                                 pc.trans ? (int64_t)j * pc.rows + i : (int64_t)i * pc.cols + j,
+                                 pc.dt);
   }
+  o.dst[(int64_t)r * o.ld + c] = __float2bfloat16_rn(v);
 }
 
-// dst[i * ld + col0 + j] = scale * src[i * r + j]           (i < rows, j < r)
-__global__ void pack_cols_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t rows, int64_t r,
-                            int64_t col0, float scale) {
-  const int64_t n = rows * r;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = e / r, j = e - (e / r) * r;
-    dst[i * ld + col0 + j] = __float2bfloat16_rn(scale * load_as_f32(src, e, dt));
-  }
-}
+// Scatter of the fp32 [n, 64] skinny-GEMM results into the per-adapter
+// gradients, several adapters per launch:
+//   trans = 0 (dB): dst[i * cols + j] = scale * src[i * 64 + off + j]   dst [rows, cols = r]
+//   trans = 1 (dA): dst[i * cols + j] = scale * src[j * 64 + off + i]   dst [rows = r, cols]
+struct UnpackJob {
+  float* dst;
+  const float* src;
+  int64_t rows, cols, off;
+  float scale;
+  int trans;
+};
 
-// dst[(row0 + j) * ld + i] = scale * src[i * r + j]         (transpose of [out, r])
-__global__ void pack_t_k(bf16* dst, int64_t ld, const void* src, int dt, int64_t out, int64_t r,
-                         int64_t row0, float scale) {
-  const int64_t n = out * r;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = e / out, i = e - (e / out) * out;  // coalesced writes along i
-    dst[(row0 + j) * ld + i] = __float2bfloat16_rn(scale * load_as_f32(src, i * r + j, dt));
-  }
-}
+constexpr int kMaxUnpack = 6;
 
-// dst[j * cols + c] = scale * src[c * 64 + col0 + j]        (dA from X^T G)
-__global__ void unpack_t_k(float* dst, const float* src, int64_t cols, int64_t r, int64_t col0,
-                           float scale) {
-  const int64_t n = r * cols;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t j = e / cols, c = e - (e / cols) * cols;
-    dst[e] = scale * src[c * kSlot + col0 + j];
-  }
-}
+struct Unpacks {
+  UnpackJob j[kMaxUnpack];
+  int64_t start[kMaxUnpack + 1];
+  int n;
+};
 
-// dst[i * r + j] = scale * src[i * 64 + col0 + j]           (dB from dY^T U)
-__global__ void unpack_cols_k(float* dst, const float* src, int64_t rows, int64_t r, int64_t col0,
-                              float scale) {
-  const int64_t n = rows * r;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+__global__ void unpack_k(const __grid_constant__ Unpacks u) {
+  const int64_t total = u.start[u.n];
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t i = e / r, j = e - (e / r) * r;
-    dst[e] = scale * src[i * kSlot + col0 + j];
+    int k = 0;
+    while (k + 1 < u.n && e >= u.start[k + 1]) ++k;
+    const UnpackJob& jb = u.j[k];
+    const int64_t local = e - u.start[k];
+    const int64_t i = local / jb.cols, j = local - (local / jb.cols) * jb.cols;
+    jb.dst[local] = jb.scale * (jb.trans ? jb.src[j * kSlot + jb.off + i]
+                                         : jb.src[i * kSlot + jb.off + j]);
   }
 }
 
@@ -129,6 +161,81 @@ int zero(void* p, size_t bytes, cudaStream_t st) {
   ML_CHECK_CUDA(cudaMemsetAsync(p, 0, bytes, st), "lora: memset");
   return ML_OK;
 }
+
+Piece piece(const void* src, int dt, int64_t r0, int64_t c0, int64_t rows, int64_t cols,
+            float scale, bool trans) {
+  Piece p;
+  p.src = src;
+  p.dt = dt;
+  p.r0 = r0;
+  p.c0 = c0;
+  p.rows = rows;
+  p.cols = cols;
+  p.scale = scale;
+  p.trans = trans ? 1 : 0;
+  return p;
+}
+
+// Collects the operands of one call and launches assemble_k once.
+struct Assembler {
+  Assembly a{};
+  int add(bf16* dst, int64_t rows, int64_t cols, std::initializer_list<Piece> pieces) {
+    if (a.nops >= kMaxOperands || pieces.size() > (size_t)kMaxPieces) {
+      set_error("lora: too many rank operands in one assembly");
+      return ML_ERR_INVALID_ARG;
+    }
+    Operand& o = a.op[a.nops];
+    o.dst = dst;
+    o.ld = cols;
+    o.rows = rows;
+    o.cols = cols;
+    o.npieces = 0;
+    for (const Piece& p : pieces) o.p[o.npieces++] = p;
+    a.start[a.nops + 1] = a.start[a.nops] + rows * cols;
+    ++a.nops;
+    return ML_OK;
+  }
+  int launch(cudaStream_t st) {
+    const int64_t n = a.start[a.nops];
+    if (n == 0) return ML_OK;
+    if (n >= ((int64_t)1 << 31)) {
+      set_error("lora: rank operands too large (%lld elements)", (long long)n);
+      return ML_ERR_INVALID_ARG;
+    }
+    assemble_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+    ML_CHECK_LAUNCH("lora: assemble rank operands");
+    return ML_OK;
+  }
+};
+
+struct Unpacker {
+  Unpacks u{};
+  int add(float* dst, const float* src, int64_t rows, int64_t cols, int64_t off, float scale,
+          bool trans) {
+    if (u.n >= kMaxUnpack) {
+      set_error("lora: too many gradient scatters in one launch");
+      return ML_ERR_INVALID_ARG;
+    }
+    UnpackJob& j = u.j[u.n];
+    j.dst = dst;
+    j.src = src;
+    j.rows = rows;
+    j.cols = cols;
+    j.off = off;
+    j.scale = scale;
+    j.trans = trans ? 1 : 0;
+    u.start[u.n + 1] = u.start[u.n] + rows * cols;
+    ++u.n;
+    return ML_OK;
+  }
+  int launch(cudaStream_t st) {
+    const int64_t n = u.start[u.n];
+    if (n == 0) return ML_OK;
+    unpack_k<<<egrid(n), 256, 0, st>>>(u);
+    ML_CHECK_LAUNCH("lora: scatter adapter gradients");
+    return ML_OK;
+  }
+};
 
 // One K-segment: A [M, K] / B [N, K] logical views.
 gemm::Seg seg(const void* a, int64_t lda, const void* b, int64_t ldb, int64_t k) {
@@ -242,14 +349,21 @@ int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, int np, const ml
   const size_t rpf = skinny_partial_floats(T, H);
   float* rpart = ar.take<float>(rpf);
   if (ar.dry) return ML_OK;
-  LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
+  // acat = [A_0; A_1; ...] (rows i r ..), bpad_i = s_i B_i in columns [i r, (i + 1) r)
+  Assembler as;
+  {
+    Piece pa[3];
+    for (int i = 0; i < np; ++i) pa[i] = piece(pj[i].a, pj[i].a_dtype, i * r, 0, r, H, 1.f, false);
+    if (np == 1) LORA_TRY(as.add(acat, kSlot, H, {pa[0]}));
+    if (np == 2) LORA_TRY(as.add(acat, kSlot, H, {pa[0], pa[1]}));
+    if (np == 3) LORA_TRY(as.add(acat, kSlot, H, {pa[0], pa[1], pa[2]}));
+  }
   for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
-    LORA_TRY(zero(bpad[i], (size_t)o * kSlot * 2, st));
-    LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[i].a, pj[i].a_dtype, r, H, i * r, 1.f);
-    LORA_LAUNCH(pack_cols_k, o * r, bpad[i], kSlot, pj[i].b, pj[i].b_dtype, o, r, i * r,
-                pj[i].scaling);
+    LORA_TRY(as.add(bpad[i], o, kSlot,
+                    {piece(pj[i].b, pj[i].b_dtype, 0, i * r, o, r, pj[i].scaling, false)}));
   }
+  LORA_TRY(as.launch(st));
   // U = X [A_0; A_1; ...]^T   [T, 64]
   LORA_TRY(rank_proj(T, {seg(x, H, acat, H, H)}, u, rpart, rpf, st));
   // y_i = [X | U] [W_i | s_i B_i (in its slot)]^T
@@ -264,29 +378,36 @@ int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, int np, const ml
 int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, int np,
                  const ml_lora_proj* pj, const void* const* dy, bf16* dx, float* const* da,
                  float* const* db, Arena& ar, cudaStream_t st) {
-  int64_t omax = 0, osum = 0;
-  for (int i = 0; i < np; ++i) {
-    omax = std::max(omax, pj[i].out_features);
-    osum += pj[i].out_features;
-  }
+  int64_t osum = 0;
+  for (int i = 0; i < np; ++i) osum += pj[i].out_features;
   bf16* bt[3] = {};
   for (int i = 0; i < np; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
   bf16* acat_s = ar.take<bf16>((size_t)kSlot * H);
   bf16* G = ar.take<bf16>((size_t)T * kSlot);
   float* dAT = ar.take<float>((size_t)H * kSlot);
-  float* dBt = ar.take<float>((size_t)omax * kSlot);
-  const size_t pf = std::max({skinny_partial_floats(H, T), skinny_partial_floats(omax, T),
-                              skinny_partial_floats(T, osum)});
+  float* dBt[3] = {};
+  size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(T, osum));
+  for (int i = 0; i < np; ++i) {
+    dBt[i] = ar.take<float>((size_t)pj[i].out_features * kSlot);
+    pf = std::max(pf, skinny_partial_floats(pj[i].out_features, T));
+  }
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
-  LORA_TRY(zero(acat_s, (size_t)kSlot * H * 2, st));
+  // bt_i = B_i^T in rows [i r, (i + 1) r); acat_s = [s_0 A_0; s_1 A_1; ...]
+  Assembler as;
   for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
-    LORA_TRY(zero(bt[i], (size_t)kSlot * o * 2, st));
-    LORA_LAUNCH(pack_t_k, o * r, bt[i], o, pj[i].b, pj[i].b_dtype, o, r, i * r, 1.f);
-    LORA_LAUNCH(pack_rows_k, r * H, acat_s, H, pj[i].a, pj[i].a_dtype, r, H, i * r,
-                pj[i].scaling);
+    LORA_TRY(as.add(bt[i], kSlot, o, {piece(pj[i].b, pj[i].b_dtype, i * r, 0, r, o, 1.f, true)}));
   }
+  {
+    Piece pa[3];
+    for (int i = 0; i < np; ++i)
+      pa[i] = piece(pj[i].a, pj[i].a_dtype, i * r, 0, r, H, pj[i].scaling, false);
+    if (np == 1) LORA_TRY(as.add(acat_s, kSlot, H, {pa[0]}));
+    if (np == 2) LORA_TRY(as.add(acat_s, kSlot, H, {pa[0], pa[1]}));
+    if (np == 3) LORA_TRY(as.add(acat_s, kSlot, H, {pa[0], pa[1], pa[2]}));
+  }
+  LORA_TRY(as.launch(st));
   // G = [dY_0 B_0 | dY_1 B_1 | ...]   [T, 64]
   std::vector<gemm::Seg> gsegs, xsegs;
   for (int i = 0; i < np; ++i) {
@@ -298,17 +419,18 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   LORA_TRY(rank_proj(T, gsegs, G, part, pf, st));
   // dX = sum_i dY_i W_i + G (s A)   — one accumulator, W read in place (N-major)
   LORA_TRY(gemm_bf16(T, H, xsegs, false, true, dx, H, st));
-  // dA_i = s_i (X^T G)[:, slot_i]^T
+  // dA_i = s_i (X^T G)[:, slot_i]^T ;  dB_i = s_i dY_i^T U[:, slot_i]
   LORA_TRY(gemm_skinny_f32(H, seg(x, H, G, kSlot, T), dAT, part, pf * 4, st));
-  for (int i = 0; i < np; ++i)
-    LORA_LAUNCH(unpack_t_k, r * H, da[i], dAT, H, r, i * r, pj[i].scaling);
-  // dB_i = s_i dY_i^T U[:, slot_i]
   for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
-    LORA_TRY(gemm_skinny_f32(o, seg(dy[i], o, u, kSlot, T), dBt, part, pf * 4, st));
-    LORA_LAUNCH(unpack_cols_k, o * r, db[i], dBt, o, r, i * r, pj[i].scaling);
+    LORA_TRY(gemm_skinny_f32(o, seg(dy[i], o, u, kSlot, T), dBt[i], part, pf * 4, st));
   }
-  return ML_OK;
+  Unpacker un;
+  for (int i = 0; i < np; ++i) {
+    LORA_TRY(un.add(da[i], dAT, r, H, i * r, pj[i].scaling, true));
+    LORA_TRY(un.add(db[i], dBt[i], pj[i].out_features, r, i * r, pj[i].scaling, false));
+  }
+  return un.launch(st);
 }
 
 // ------------------------------- MLP --------------------------------------
@@ -324,17 +446,15 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
   const size_t rpf = std::max(skinny_partial_floats(T, H), skinny_partial_floats(T, I));
   float* rpart = ar.take<float>(rpf);
   if (ar.dry) return ML_OK;
-  LORA_TRY(zero(acat, (size_t)kSlot * H * 2, st));
-  LORA_TRY(zero(bgp, (size_t)I * kSlot * 2, st));
-  LORA_TRY(zero(bup, (size_t)I * kSlot * 2, st));
-  LORA_TRY(zero(ad, (size_t)kSlot * I * 2, st));
-  LORA_TRY(zero(bdp, (size_t)H * kSlot * 2, st));
-  LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[0].a, pj[0].a_dtype, r, H, 0, 1.f);
-  LORA_LAUNCH(pack_rows_k, r * H, acat, H, pj[1].a, pj[1].a_dtype, r, H, r, 1.f);
-  LORA_LAUNCH(pack_cols_k, I * r, bgp, kSlot, pj[0].b, pj[0].b_dtype, I, r, 0, pj[0].scaling);
-  LORA_LAUNCH(pack_cols_k, I * r, bup, kSlot, pj[1].b, pj[1].b_dtype, I, r, r, pj[1].scaling);
-  LORA_LAUNCH(pack_rows_k, r * I, ad, I, pj[2].a, pj[2].a_dtype, r, I, 0, 1.f);
-  LORA_LAUNCH(pack_cols_k, H * r, bdp, kSlot, pj[2].b, pj[2].b_dtype, H, r, 0, pj[2].scaling);
+  Assembler as;
+  LORA_TRY(as.add(acat, kSlot, H,
+                  {piece(pj[0].a, pj[0].a_dtype, 0, 0, r, H, 1.f, false),
+                   piece(pj[1].a, pj[1].a_dtype, r, 0, r, H, 1.f, false)}));
+  LORA_TRY(as.add(bgp, I, kSlot, {piece(pj[0].b, pj[0].b_dtype, 0, 0, I, r, pj[0].scaling, false)}));
+  LORA_TRY(as.add(bup, I, kSlot, {piece(pj[1].b, pj[1].b_dtype, 0, r, I, r, pj[1].scaling, false)}));
+  LORA_TRY(as.add(ad, kSlot, I, {piece(pj[2].a, pj[2].a_dtype, 0, 0, r, I, 1.f, false)}));
+  LORA_TRY(as.add(bdp, H, kSlot, {piece(pj[2].b, pj[2].b_dtype, 0, 0, H, r, pj[2].scaling, false)}));
+  LORA_TRY(as.launch(st));
   // U1 = X [Ag; Au]^T
   LORA_TRY(rank_proj(T, {seg(x, H, acat, H, H)}, u1, rpart, rpf, st));
   // gate / up = [X | U1] [W | s B]^T
@@ -365,33 +485,31 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   bf16* dH = ar.take<bf16>((size_t)T * I);
   bf16* dgate = ar.take<bf16>((size_t)T * I);
   bf16* dup = ar.take<bf16>((size_t)T * I);
-  const int64_t mmax = std::max(H, I);
-  float* dAT = ar.take<float>((size_t)mmax * kSlot);
-  float* dBt = ar.take<float>((size_t)mmax * kSlot);
+  float* dAT_d = ar.take<float>((size_t)I * kSlot);   // h^T G_d
+  float* dAT_gu = ar.take<float>((size_t)H * kSlot);  // X^T G_gu
+  float* dBt_d = ar.take<float>((size_t)H * kSlot);   // dY^T U2
+  float* dBt_g = ar.take<float>((size_t)I * kSlot);   // d_gate^T U1
+  float* dBt_u = ar.take<float>((size_t)I * kSlot);   // d_up^T U1
   const size_t pf = std::max({skinny_partial_floats(H, T), skinny_partial_floats(I, T),
                               skinny_partial_floats(T, H), skinny_partial_floats(T, 2 * I)});
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
-  LORA_TRY(zero(bdT, (size_t)kSlot * H * 2, st));
-  LORA_TRY(zero(ads, (size_t)kSlot * I * 2, st));
-  LORA_TRY(zero(bgT, (size_t)kSlot * I * 2, st));
-  LORA_TRY(zero(buT, (size_t)kSlot * I * 2, st));
-  LORA_TRY(zero(acs, (size_t)kSlot * H * 2, st));
-  LORA_LAUNCH(pack_t_k, H * r, bdT, H, pj[2].b, pj[2].b_dtype, H, r, 0, 1.f);
-  LORA_LAUNCH(pack_rows_k, r * I, ads, I, pj[2].a, pj[2].a_dtype, r, I, 0, pj[2].scaling);
-  LORA_LAUNCH(pack_t_k, I * r, bgT, I, pj[0].b, pj[0].b_dtype, I, r, 0, 1.f);
-  LORA_LAUNCH(pack_t_k, I * r, buT, I, pj[1].b, pj[1].b_dtype, I, r, r, 1.f);
-  LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[0].a, pj[0].a_dtype, r, H, 0, pj[0].scaling);
-  LORA_LAUNCH(pack_rows_k, r * H, acs, H, pj[1].a, pj[1].a_dtype, r, H, r, pj[1].scaling);
+  Assembler as;
+  LORA_TRY(as.add(bdT, kSlot, H, {piece(pj[2].b, pj[2].b_dtype, 0, 0, r, H, 1.f, true)}));
+  LORA_TRY(as.add(ads, kSlot, I, {piece(pj[2].a, pj[2].a_dtype, 0, 0, r, I, pj[2].scaling, false)}));
+  LORA_TRY(as.add(bgT, kSlot, I, {piece(pj[0].b, pj[0].b_dtype, 0, 0, r, I, 1.f, true)}));
+  LORA_TRY(as.add(buT, kSlot, I, {piece(pj[1].b, pj[1].b_dtype, r, 0, r, I, 1.f, true)}));
+  LORA_TRY(as.add(acs, kSlot, H,
+                  {piece(pj[0].a, pj[0].a_dtype, 0, 0, r, H, pj[0].scaling, false),
+                   piece(pj[1].a, pj[1].a_dtype, r, 0, r, H, pj[1].scaling, false)}));
+  LORA_TRY(as.launch(st));
   // G_d = dY Bd ; dH = dY Wd + G_d (s_d Ad)      (Wd stored [H, I]: N-major)
   LORA_TRY(rank_proj(T, {seg(dy, H, bdT, H, H)}, Gd, part, pf, st));
   LORA_TRY(gemm_bf16(T, I, {seg(dy, H, pj[2].w, I, H), seg(Gd, kSlot, ads, I, kSlot)}, false,
                      true, dH, I, st));
   // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
-  LORA_TRY(gemm_skinny_f32(I, seg(h, I, Gd, kSlot, T), dAT, part, pf * 4, st));
-  LORA_LAUNCH(unpack_t_k, r * I, da[2], dAT, I, r, 0, pj[2].scaling);
-  LORA_TRY(gemm_skinny_f32(H, seg(dy, H, u2, kSlot, T), dBt, part, pf * 4, st));
-  LORA_LAUNCH(unpack_cols_k, H * r, db[2], dBt, H, r, 0, pj[2].scaling);
+  LORA_TRY(gemm_skinny_f32(I, seg(h, I, Gd, kSlot, T), dAT_d, part, pf * 4, st));
+  LORA_TRY(gemm_skinny_f32(H, seg(dy, H, u2, kSlot, T), dBt_d, part, pf * 4, st));
   // SwiGLU backward (sigmoid recomputed)
   LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
   // G_gu = [d_gate Bg | d_up Bu]
@@ -402,14 +520,17 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                       seg(Ggu, kSlot, acs, H, kSlot)},
                      false, true, dx, H, st));
   // gate/up adapter grads
-  LORA_TRY(gemm_skinny_f32(H, seg(x, H, Ggu, kSlot, T), dAT, part, pf * 4, st));
-  LORA_LAUNCH(unpack_t_k, r * H, da[0], dAT, H, r, 0, pj[0].scaling);
-  LORA_LAUNCH(unpack_t_k, r * H, da[1], dAT, H, r, r, pj[1].scaling);
-  LORA_TRY(gemm_skinny_f32(I, seg(dgate, I, u1, kSlot, T), dBt, part, pf * 4, st));
-  LORA_LAUNCH(unpack_cols_k, I * r, db[0], dBt, I, r, 0, pj[0].scaling);
-  LORA_TRY(gemm_skinny_f32(I, seg(dup, I, u1, kSlot, T), dBt, part, pf * 4, st));
-  LORA_LAUNCH(unpack_cols_k, I * r, db[1], dBt, I, r, r, pj[1].scaling);
-  return ML_OK;
+  LORA_TRY(gemm_skinny_f32(H, seg(x, H, Ggu, kSlot, T), dAT_gu, part, pf * 4, st));
+  LORA_TRY(gemm_skinny_f32(I, seg(dgate, I, u1, kSlot, T), dBt_g, part, pf * 4, st));
+  LORA_TRY(gemm_skinny_f32(I, seg(dup, I, u1, kSlot, T), dBt_u, part, pf * 4, st));
+  Unpacker un;
+  LORA_TRY(un.add(da[2], dAT_d, r, I, 0, pj[2].scaling, true));
+  LORA_TRY(un.add(db[2], dBt_d, H, r, 0, pj[2].scaling, false));
+  LORA_TRY(un.add(da[0], dAT_gu, r, H, 0, pj[0].scaling, true));
+  LORA_TRY(un.add(da[1], dAT_gu, r, H, r, pj[1].scaling, true));
+  LORA_TRY(un.add(db[0], dBt_g, I, r, 0, pj[0].scaling, false));
+  LORA_TRY(un.add(db[1], dBt_u, I, r, r, pj[1].scaling, false));
+  return un.launch(st);
 }
 
 int check_ws(const Arena& need, size_t have, void* ws, const char* what) {

@@ -89,7 +89,7 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2-D tiled load, no multicast.  x = innermost coordinate (elements).
+// 2-D tiled load into this CTA's shared memory.  x = innermost coordinate (elements).
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
   asm volatile(
@@ -222,7 +222,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
 
 // 2-D tiled load into this CTA's shared memory whose bytes complete on the
 // barrier at cluster address `bar_cluster` (the pair leader's), as the
-// 2-SM MMA expects.  No multicast.
+// 2-SM MMA expects.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map,
                                                  uint32_t bar_cluster, int x, int y) {
   asm volatile(

@@ -129,6 +129,14 @@ class CudaShardPhases:
                 dw_out.data_ptr() if dw_out is not None else None, int(dw_accumulate),
                 state.data_ptr(), state.numel(), _C.stream_of(hidden))
 
+    def grads_dw(self, state, hidden, weight, dw_out, dw_accumulate):
+        """The dW GEMM alone, after grads(..., dw_out=None, ...) on the same state."""
+        from metal_liger_b200 import _C
+        rows, h = hidden.shape
+        _C.call("ml_flce_shard_grads_dw", hidden.data_ptr(), rows, h, weight.shape[0],
+                dw_out.data_ptr(), int(dw_accumulate), state.data_ptr(), state.numel(),
+                _C.stream_of(hidden))
+
 
 def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=None,
                         ignore_index=-100, chunk_size=8192, group=None, phases=None,
@@ -178,11 +186,14 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
         lse = mg + torch.log(st[0])
         mask = (lc != ignore_index).to(torch.float32)
         row_loss[r0:r1] = (lse - st[1]) * mask
+        # dX first, so its all-reduce runs while this chunk's dW GEMM does
         phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index, lse.contiguous(),
-                     cnt[1:2], dx[r0:r1] if need_dx else None, dw, r0 > 0)
+                     cnt[1:2], dx[r0:r1] if need_dx else None, None, r0 > 0)
         if need_dx:
             pending.append(dist.all_reduce(dx[r0:r1], op=dist.ReduceOp.SUM, group=group,
                                            async_op=True))
+        if need_dw:
+            phases.grads_dw(state, hc, weight_shard, dw, r0 > 0)
     for work in pending:
         work.wait()
     loss = row_loss.sum() * cnt[1]

@@ -164,6 +164,27 @@ def _patch_attention_rope(model: nn.Module) -> int:
     return done
 
 
+def restore_attention_rope(model: nn.Module) -> int:
+    """Undo ``fuse_rope_in_attention``: put back the modeling module's original
+    ``apply_rotary_pos_emb``.  The rebinding is per modeling module, so it also
+    reaches other models of the same class in the process; this restores them
+    all.  Returns the number of modules restored."""
+    import sys
+
+    layers = _find_layers(model)
+    if layers is None:
+        return 0
+    done = 0
+    for layer in layers:
+        attn = getattr(layer, "self_attn", None)
+        mod = sys.modules.get(type(attn).__module__) if attn is not None else None
+        orig = getattr(mod, "_metal_liger_original_rope", None) if mod is not None else None
+        if orig is not None and mod.apply_rotary_pos_emb is _fused_rotary_pos_emb:
+            mod.apply_rotary_pos_emb = orig
+            done += 1
+    return done
+
+
 def apply_metal_liger_to_qwen3vl(
     model: nn.Module,
     fuse_rms_norm: bool = True,

@@ -35,14 +35,18 @@ class OraclePhases:
         inside = (labels != ignore_index) & (rel >= 0) & (rel < weight.shape[0])
         idx = torch.nonzero(inside)[:, 0]
         p[idx, rel[idx]] -= scale
+        self._p = p
         if dx_out is not None:
             dx_out.copy_(p @ weight.float())
         if dw_out is not None:
-            g = p.t() @ hidden.float()
-            if dw_accumulate:
-                dw_out += g
-            else:
-                dw_out.copy_(g)
+            self.grads_dw(state, hidden, weight, dw_out, dw_accumulate)
+
+    def grads_dw(self, state, hidden, weight, dw_out, dw_accumulate):
+        g = self._p.t() @ hidden.float()
+        if dw_accumulate:
+            dw_out += g
+        else:
+            dw_out.copy_(g)
 
 
 def free_port():
