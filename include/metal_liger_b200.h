@@ -214,12 +214,13 @@ ML_API int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int n
                         size_t workspace_bytes, void* stream);
 
 /*
- * Process-wide choice of the 2-SM (CTA pair, tcgen05 cta_group::2) GEMM
- * kernel for 256-wide tiles: -1 = automatic (default; pairs when there are
- * enough 256 x 256 tiles to occupy every SM pair), 0 = never, 1 = whenever
- * the tile shape allows.  Applies to every GEMM in this library (plain,
- * FLCE, LoRA).  The previous mode is stored to *previous when non-NULL.
- * A tuning and test knob with no reference counterpart.
+ * Process-wide choice of GEMM kernel: -1 = automatic (default: the 2-SM
+ * CTA-pair kernel (tcgen05 cta_group::2, 256 rows x 256 or 128 columns per
+ * pair) or the 1-SM kernel, whichever fills the SMs best for the shape),
+ * 0 = 1-SM kernel only, 1 = CTA pair whenever the shape allows, 2 / 3 = CTA
+ * pair with 256- / 128-wide tiles only.  Applies to every GEMM in this
+ * library (plain, FLCE, LoRA).  The previous mode is stored to *previous
+ * when non-NULL.  A tuning and test knob with no reference counterpart.
  */
 ML_API int ml_gemm_set_cta_pair(int mode, int* previous);
 

@@ -185,7 +185,11 @@ def _rope_launch(tensors, cos, sin, sign, positions=None, inv_freq=None, scaling
     in_dtype = first.dtype
     if out_dtype is None:
         out_dtype = in_dtype
-    outs = [torch.empty(t.shape, dtype=out_dtype, device=t.device) for t in tensors]
+    # Outputs take the input's memory layout when it is dense (e.g. q as the
+    # [B, H, S, D] transpose of a [B, S, H, D] projection, as in HF attention):
+    # the gradient then flows back in the projection's own layout and needs no
+    # copy before the q/k norm and projection backward.
+    outs = [torch.empty_like(t, dtype=out_dtype) for t in tensors]
     views = [_rope_view(t, o) for t, o in zip(tensors, outs)]
     qv = ctypes.pointer(views[0])
     kv = ctypes.pointer(views[1]) if len(views) > 1 else None

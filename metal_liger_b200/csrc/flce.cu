@@ -62,17 +62,31 @@ Layout layout(int64_t n, int64_t v, int64_t chunk) {
   return L;
 }
 
-// Split-K slabs for the dX GEMM: enough (m, n) tiles to fill the SMs.
+// Split-K slabs for the dX GEMM.  Its (m, n) tiles are few (rows/256 x h/256
+// on the CTA-pair kernel), so their last wave over the SM pairs can be mostly
+// empty (8192 x 2048: 256 tiles on 74 pairs = 3.46 waves, 86% busy).  Pick the
+// split count (1..4) whose units fill whole waves best; a split is taken only
+// if it gains more than 2% of wave efficiency.
 int dx_slabs(int64_t chunk_rows, int64_t h, int64_t v) {
-  const int64_t tiles = ((chunk_rows + 127) / 128) * ((h + 255) / 256);
   const int64_t kb = (v + 63) / 64;
-  const int sms = num_sms();
-  if (tiles >= 4 * (int64_t)sms || kb < 64) return 1;
-  int64_t s = (2 * (int64_t)sms + tiles - 1) / tiles;
-  s = std::min<int64_t>(s, 4);
-  s = std::max<int64_t>(1, std::min<int64_t>(s, kb / 32));
+  if (kb < 64) return 1;
+  const int64_t tiles = ((chunk_rows + 255) / 256) * ((h + 255) / 256);
+  const int64_t slots = std::max(1, num_sms() / 2);
+  auto eff = [&](int64_t s) {
+    const int64_t units = tiles * s;
+    const int64_t waves = (units + slots - 1) / slots;
+    return (double)units / (double)(waves * slots);
+  };
+  int64_t best = 1;
+  double best_eff = eff(1);
+  for (int64_t s = 2; s <= 4 && s <= kb / 32; ++s) {
+    if (eff(s) > best_eff + 0.02) {
+      best = s;
+      best_eff = eff(s);
+    }
+  }
   // the split count gemm::launch will actually use for this request
-  const int64_t per = (kb + s - 1) / s;
+  const int64_t per = (kb + best - 1) / best;
   return (int)((kb + per - 1) / per);
 }
 

@@ -101,10 +101,10 @@ int launch_t(const Params& prm, int grid, cudaStream_t st) {
 
 std::atomic<int> g_pair_mode{-1};
 
-template <bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN>
 int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t st) {
-  auto k = gemm_pair_kernel<A_MN, B_MN>;
-  const size_t smem = PairCfg::SMEM;
+  auto k = gemm_pair_kernel<BN, A_MN, B_MN>;
+  const size_t smem = PairCfg<BN>::SMEM;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   static int resident_pairs = 0;
@@ -136,12 +136,54 @@ int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t s
   return ML_OK;
 }
 
-int launch_pair(const Params& prm, bool a_mn, bool b_mn, int64_t units, int max_ctas,
+template <int BN>
+int launch_pair_bn(const Params& prm, bool a_mn, bool b_mn, int64_t units, int max_ctas,
+                   cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_pair_t<BN, false, false>(prm, units, max_ctas, st);
+  if (!a_mn && b_mn) return launch_pair_t<BN, false, true>(prm, units, max_ctas, st);
+  if (a_mn && !b_mn) return launch_pair_t<BN, true, false>(prm, units, max_ctas, st);
+  return launch_pair_t<BN, true, true>(prm, units, max_ctas, st);
+}
+
+int launch_pair(const Params& prm, int bn, bool a_mn, bool b_mn, int64_t units, int max_ctas,
                 cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_pair_t<false, false>(prm, units, max_ctas, st);
-  if (!a_mn && b_mn) return launch_pair_t<false, true>(prm, units, max_ctas, st);
-  if (a_mn && !b_mn) return launch_pair_t<true, false>(prm, units, max_ctas, st);
-  return launch_pair_t<true, true>(prm, units, max_ctas, st);
+  return bn == 256 ? launch_pair_bn<256>(prm, a_mn, b_mn, units, max_ctas, st)
+                   : launch_pair_bn<128>(prm, a_mn, b_mn, units, max_ctas, st);
+}
+
+// Tile choice, from B200 measurements of both kernels over the shapes of
+// this library (bf16, 64-deep k-blocks).  In isolation (short bursts at full
+// clock) the CTA-pair kernel with 256 x 256 tiles is 8-28% faster on large
+// problems (8192^3: 1.47 vs 1.35 PFLOP/s; FLCE logits / dW shapes: +27%; the
+// 1-SM 128 x 256 tile is limited by shared-memory bandwidth) and 3-7% slower
+// on a few waves (4096^3).  Inside a long training step, which runs under the
+// 1 kW power cap, the pair kernel is the faster one at every size measured:
+// it moves fewer shared-memory and L2 bytes per FLOP, so the cap leaves it a
+// higher clock (Qwen3-VL-8B LoRA step: 163.6 ms with the pair kernel on every
+// GEMM it can take vs 171.0 ms with the burst-tuned split).  So the pair
+// kernel takes every GEMM with 256-wide tiles and more than 128 rows.  Its
+// 128-wide tile is smem-bound (about half the 256-wide throughput) and is
+// used only when forced.
+// `mode` (ml_gemm_set_cta_pair): -1 auto, 0 1-SM only, 1 pair when possible,
+// 2 / 3 pair with 256 / 128-wide tiles only (tuning and tests).
+struct TileChoice {
+  int bn;
+  bool pair;
+};
+
+TileChoice choose_tile(const Problem& pr, int mode) {
+  const int one_bn = pr.bn ? pr.bn : pick_bn(pr.N);
+  const bool pair_ok = mode != 0 && pr.M > BM;
+  const bool w256 = pr.bn ? pr.bn == 256 : pr.N > 128;
+  const bool w128 = pr.bn ? pr.bn == 128 : (pr.N > 64 && pr.epi != EPI_FLCE);
+  if (mode == 3) return w128 && pair_ok ? TileChoice{128, true} : TileChoice{one_bn, false};
+  if (mode == 1 || mode == 2) {
+    if (pair_ok && w256) return {256, true};
+    if (pair_ok && w128 && mode == 1) return {128, true};
+    return {one_bn, false};
+  }
+  if (mode == 0 || !pair_ok || !w256) return {one_bn, false};
+  return {256, true};
 }
 
 template <int BN>
@@ -151,7 +193,6 @@ int launch_bn(const Params& prm, bool a_mn, bool b_mn, int grid, cudaStream_t st
   if (a_mn && !b_mn) return launch_t<BN, true, false>(prm, grid, st);
   return launch_t<BN, true, true>(prm, grid, st);
 }
-
 }  // namespace
 
 int pick_bn(int64_t N) {
@@ -166,13 +207,10 @@ int launch(const Problem& pr, cudaStream_t st) {
               pr.nseg);
     return ML_ERR_INVALID_ARG;
   }
-  const int bn = pr.bn ? pr.bn : pick_bn(pr.N);
-  // The CTA-pair kernel computes 256 x 256 tiles; use it when there are
-  // enough of them to occupy every SM pair.
   const int mode = pr.pair >= 0 ? pr.pair : g_pair_mode.load(std::memory_order_relaxed);
-  const int64_t pair_tiles = ((pr.M + 255) / 256) * ((pr.N + 255) / 256) * std::max(pr.splits, 1);
-  const bool pair = bn == 256 && mode != 0 && pr.M > 128 &&
-                    (mode == 1 || pair_tiles >= num_sms() / 2);
+  const TileChoice tc = choose_tile(pr, mode);
+  const int bn = tc.bn;
+  const bool pair = tc.pair;
   if (bn != 64 && bn != 128 && bn != 256) {
     set_error("gemm: bad tile width %d", bn);
     return ML_ERR_INVALID_ARG;
@@ -199,7 +237,7 @@ int launch(const Problem& pr, cudaStream_t st) {
     if (rc) return rc;
     // B: logical [N, K]; each CTA of a pair loads 128 of the tile's 256 rows
     if (!pr.b_mn)
-      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, pair ? 128 : bn,
+      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, pair ? bn / 2 : bn,
                     "gemm B (K-major)");
     else
       rc = make_map(&prm.tma_b[s], g.b.ptr, pr.N, g.K, g.b.ld, BK, "gemm B (N-major)");
@@ -261,7 +299,7 @@ int launch(const Problem& pr, cudaStream_t st) {
     set_error("gemm: problem too large");
     return ML_ERR_INVALID_ARG;
   }
-  if (pair) return launch_pair(prm, pr.a_mn, pr.b_mn, units, pr.max_ctas, st);
+  if (pair) return launch_pair(prm, bn, pr.a_mn, pr.b_mn, units, pr.max_ctas, st);
   int grid = (int)std::min<int64_t>(units, pr.max_ctas > 0 ? pr.max_ctas : num_sms());
   grid = std::max(grid, 1);
   switch (bn) {
@@ -299,16 +337,32 @@ __global__ void splitk_reduce(const float* __restrict__ part, int splits, int64_
 
 namespace gemm {
 
+// Split count for a GEMM with fewer tiles than SMs: the s in [1, 16] (each
+// split keeping >= 4 k-blocks) whose tiles * s units keep the largest share
+// of SM slots busy over whole waves; ties go to the smaller s.  E.g. 32 tiles
+// on 148 SMs: s = 9 (288 units, 97% of two waves) rather than s = 10 (320
+// units, a third wave 16% full).
 int auto_splits(int64_t M, int64_t N, int64_t K) {
   const int bn = pick_bn(N);
   const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
   const int64_t kb = (K + BK - 1) / BK;
-  const int sms = num_sms();
+  const int64_t sms = num_sms();
   if (tiles >= sms || kb < 8) return 1;
-  int64_t s = std::min<int64_t>((2 * (int64_t)sms + tiles - 1) / tiles, kb / 4);
-  s = std::max<int64_t>(1, std::min<int64_t>(s, 16));
-  const int64_t per = (kb + s - 1) / s;
-  return (int)((kb + per - 1) / per);
+  int64_t best = 1;
+  double best_busy = 0.0;
+  const int64_t smax = std::max<int64_t>(1, std::min<int64_t>(16, kb / 4));
+  for (int64_t s = 1; s <= smax; ++s) {
+    const int64_t per = (kb + s - 1) / s;
+    const int64_t actual = (kb + per - 1) / per;  // what launch() will run
+    const int64_t units = tiles * actual;
+    const int64_t waves = (units + sms - 1) / sms;
+    const double busy = (double)units / (double)(waves * sms);
+    if (busy > best_busy + 1e-9) {
+      best_busy = busy;
+      best = actual;
+    }
+  }
+  return (int)best;
 }
 
 int launch_splitk(Problem pr, int splits, float* out, int64_t ldo, float* partial,
@@ -385,7 +439,7 @@ extern "C" size_t ml_gemm_bf16_workspace_bytes(int64_t m, int64_t n, int64_t k_t
 }
 
 extern "C" int ml_gemm_set_cta_pair(int mode, int* previous) {
-  ML_CHECK_ARG(mode >= -1 && mode <= 1, "gemm_set_cta_pair: mode must be -1, 0 or 1");
+  ML_CHECK_ARG(mode >= -1 && mode <= 3, "gemm_set_cta_pair: mode must be in [-1, 3]");
   const int old = gemm::g_pair_mode.exchange(mode);
   if (previous) *previous = old;
   return ML_OK;

@@ -477,23 +477,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 // CTAs; each CTA drains its own 128 accumulator rows and arrives on the
 // leader's TMEM-empty barrier.
 // ---------------------------------------------------------------------------
-constexpr int kPairStages = 6;
-
+// BN = 256 (each CTA holds 128 columns of B) or 128 (64 columns): the
+// narrower tile fills the SM pairs better when 256-wide tiles would leave a
+// mostly empty last wave.
+template <int BN>
 struct PairCfg {
-  static constexpr int STAGES = kPairStages;
-  static constexpr uint32_t A_BYTES = 128 * BK * 2;   // this CTA's 128 rows of A
-  static constexpr uint32_t B_BYTES = 128 * BK * 2;   // this CTA's 128 rows/cols of B
+  static constexpr int STAGES = BN == 256 ? 6 : 8;
+  static constexpr uint32_t A_BYTES = 128 * BK * 2;        // this CTA's 128 rows of A
+  static constexpr uint32_t B_BYTES = (BN / 2) * BK * 2;   // this CTA's BN/2 rows/cols of B
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr uint32_t TMEM_COLS = 512;          // 2 x 256 fp32 accumulators
+  static constexpr uint32_t TMEM_COLS = 2 * BN;            // two fp32 accumulators
   static constexpr size_t SMEM = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
 };
 
-template <bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ Params p) {
-  using C = PairCfg;
+  static_assert(BN == 128 || BN == 256, "pair tile width");
+  using C = PairCfg<BN>;
   constexpr int STAGES = C::STAGES;
-  constexpr int BN = 256;
+  constexpr int BH = BN / 2;  // columns of B per CTA
   constexpr uint32_t IDESC = sm100::idesc_bf16_f32(256, BN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -557,7 +560,7 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
         const int kb0 = sp * p.kb_per_split;
         const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
         const int m0 = mt * 256 + (int)rank * 128;
-        const int n0 = nt * BN + (int)rank * 128;
+        const int n0 = nt * BN + (int)rank * BH;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!sm100::mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag, p.err,
                                         SITE_PROD_EMPTY)) {
@@ -581,8 +584,9 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
           if constexpr (!B_MN) {
             sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, kx, n0);
           } else {
-            sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, n0, kx);
-            sm100::tma_load_2d_pair(b_dst + 64 * BK * 2, &p.tma_b[seg], bar, n0 + 64, kx);
+#pragma unroll
+            for (int c = 0; c < BH / 64; ++c)
+              sm100::tma_load_2d_pair(b_dst + c * 64 * BK * 2, &p.tma_b[seg], bar, n0 + 64 * c, kx);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -716,7 +720,7 @@ struct Problem {
   int raster = 0;
   int group_m = 0;
   int bn = 0;          // 0 = choose
-  int pair = -1;       // CTA-pair kernel: -1 = process default, 0 = never, 1 = when possible
+  int pair = -1;       // CTA-pair kernel: -1 = process default, else a ml_gemm_set_cta_pair mode
   int max_ctas = 0;    // 0 = SM count
   // FLCE
   const int64_t* labels = nullptr;

@@ -48,10 +48,11 @@ def cuda_lib():
     return _C.load()
 
 
-@pytest.fixture(params=[0, 1], ids=["1sm", "pair"])
+@pytest.fixture(params=[0, 1, 3], ids=["1sm", "pair", "pair128"])
 def pair_mode(request):
-    """Run a GPU test once with every GEMM on the 1-SM kernel and once with the
-    2-SM (CTA pair) kernel forced wherever the tile shape allows."""
+    """Run a GPU test with every GEMM on the 1-SM kernel, with the 2-SM (CTA
+    pair) kernel forced wherever the tile shape allows, and with the pair
+    kernel's 128-wide tiles forced."""
     from metal_liger_b200 import _C
 
     with _C.gemm_cta_pair(request.param):
