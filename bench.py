@@ -857,9 +857,10 @@ def _register_optional_workloads():
 _OUR_KERNEL = None
 
 
-def count_our_launches(wl, t) -> int | None:
+def count_our_launches(wl, t, table: bool = False) -> int | None:
     """Kernels from this repository's library launched by one step, counted
-    with the CUDA profiler (CUPTI) on an extra, untimed step."""
+    with the CUDA profiler (CUPTI) on an extra, untimed step.  With `table`,
+    also prints that step's per-kernel device time (all kernels) to stderr."""
     global _OUR_KERNEL
     import re
 
@@ -876,10 +877,23 @@ def count_our_launches(wl, t) -> int | None:
             wl.step(t)
             torch.cuda.synchronize()
         n = 0
+        per = {}
         for ev in prof.events():
-            if getattr(ev, "device_type", None) == torch.autograd.DeviceType.CUDA and \
-                    _OUR_KERNEL.search(ev.name or ""):
-                n += 1
+            if getattr(ev, "device_type", None) != torch.autograd.DeviceType.CUDA:
+                continue
+            name = ev.name or ""
+            ours = bool(_OUR_KERNEL.search(name))
+            n += ours
+            c, us = per.get(name, (0, 0.0))
+            tr = getattr(ev, "time_range", None)
+            per[name] = (c + 1, us + ((tr.end - tr.start) if tr is not None else 0.0))
+        if table:
+            total = sum(us for _, us in per.values()) or 1.0
+            print(f"# one step, per-kernel device time (CUPTI): total {total / 1e3:.2f} ms",
+                  file=sys.stderr)
+            for name, (c, us) in sorted(per.items(), key=lambda kv: -kv[1][1])[:40]:
+                print(f"# {us / 1e3:9.3f} ms {100 * us / total:5.1f}% {c:6d}  {name[:120]}",
+                      file=sys.stderr)
         return n
     except Exception:
         return None
@@ -1018,7 +1032,7 @@ def run_gpu_arm(args, wl):
         dist.all_reduce(el, op=dist.ReduceOp.MAX)
         elapsed_ms = el.item()
     kernel_ms = timer.averages_ms()
-    per_step_launches = count_our_launches(wl, t)
+    per_step_launches = count_our_launches(wl, t, table=args.kernel_table and rank == 0)
     if per_step_launches is None:
         per_step_launches = wl.launches_per_step
     # weak scaling: every rank processes wl.tokens; strong: the job processes wl.tokens
@@ -1155,6 +1169,8 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu_rope")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--kernel-table", action="store_true",
+                    help="print one extra step's per-kernel device times (CUPTI) to stderr")
     ap.add_argument("--spin-us", type=float, default=200.0,
                     help="untimed GPU spin before each timed step (host run-ahead); 0 = off")
     ap.add_argument("--cpu-budget", type=float, default=15.0,

@@ -120,6 +120,11 @@ __device__ __forceinline__ void st_vec_stream(T* p, const Vec16<T>& v) {
   __stcs(reinterpret_cast<int4*>(p), *reinterpret_cast<const int4*>(&v));
 }
 
+// Shared-window address of a generic pointer to shared memory.
+__device__ __forceinline__ uint32_t smem_u32_of(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

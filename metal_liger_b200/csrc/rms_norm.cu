@@ -28,30 +28,55 @@ constexpr int kMaxThreads = 256;  // vector path: per-thread registers hold 2 ro
 // Larger shares keep 256-thread CTAs (three groups would not fit an SM).
 template <typename TX>
 __host__ __device__ constexpr int bwd_max_threads(int nv) {
-  return (nv == 1 || (nv == 2 && sizeof(TX) == 4)) ? 768 : kMaxThreads;
+  return nv == 1 ? 512 : (nv == 2 && sizeof(TX) == 4) ? 768 : kMaxThreads;
 }
+// One vector per thread: 512-thread CTAs, two per SM (<= 64 registers), so
+// twice the rows are in flight of a single CTA per SM.
+__host__ __device__ constexpr int bwd_min_blocks(int nv) { return nv == 1 ? 2 : 1; }
+
+// Forward CTA size: one vector per thread allows 512-thread rows (16-bit
+// rows of up to 4096 elements); wider shares keep 256 threads.
+__host__ __device__ constexpr int fwd_max_threads(int nv) { return nv == 1 ? 512 : kMaxThreads; }
 
 struct RowCfg {
   int nv = 0;       // 16-byte vectors per thread per row
-  int tpr = 0;      // threads per row
+  int tpr = 0;      // threads per row (4, 8, 16, or a multiple of 32)
   int groups = 0;   // rows in flight per CTA
   bool vec = false; // false -> generic scalar kernels
 };
 
+// Rows of up to 32 vectors get sub-warp groups (4/8/16 lanes, reduced with
+// shuffles alone: the per-head q/k norm has 16 vectors per bf16 row), so no
+// lane idles.  16-bit rows of 257-512 vectors (hidden 4096 bf16) take one
+// vector per thread on 512 threads instead of two on 256: two 8-element
+// vectors per thread and row cost ~160 registers (one CTA of 8 warps per
+// SM), one costs ~80.
 template <typename TX>
-RowCfg pick_cfg(int64_t hidden, const void* a, const void* b, const void* c, const void* d) {
+RowCfg pick_cfg(int64_t hidden, const void* a, const void* b, const void* c, const void* d,
+                bool backward) {
   RowCfg cfg;
   constexpr int VEC = 16 / sizeof(TX);
   if (hidden % VEC != 0 || !aligned16(a) || !aligned16(b) || !aligned16(c) || !aligned16(d))
     return cfg;
-  int64_t nvec = hidden / VEC;
+  const int64_t nvec = hidden / VEC;
   int nv = 1;
-  while ((nvec + nv - 1) / nv > 256 && nv < 8) nv *= 2;
-  int64_t tpr = ((nvec + nv - 1) / nv + 31) / 32 * 32;
-  if (tpr > kMaxThreads) return cfg;
+  // Measured on B200 (bf16 [16384, 4096]): the forward is faster with two
+  // vectors per thread on 256 threads (4.4 vs 2.8 TB/s), the backward with
+  // one on 512 threads and the ring kernel (2.9 vs 2.6 TB/s).
+  const int64_t one_vec_limit = (sizeof(TX) == 2 && backward) ? 512 : 256;
+  if (nvec > one_vec_limit)
+    while ((nvec + nv - 1) / nv > kMaxThreads && nv < 8) nv *= 2;
+  const int64_t per = (nvec + nv - 1) / nv;
+  int64_t tpr;
+  if (per <= 4) tpr = 4;
+  else if (per <= 8) tpr = 8;
+  else if (per <= 16) tpr = 16;
+  else tpr = (per + 31) / 32 * 32;
+  if (tpr > (nv == 1 ? 512 : kMaxThreads)) return cfg;
   cfg.nv = nv;
   cfg.tpr = static_cast<int>(tpr);
-  cfg.groups = std::max(1, std::min(8, kMaxThreads / cfg.tpr));
+  const int max_groups = tpr < 32 ? 32 : 8;  // named barriers are only needed for tpr >= 32
+  cfg.groups = std::max(1, std::min<int>(max_groups, kMaxThreads / cfg.tpr));
   cfg.vec = true;
   return cfg;
 }
@@ -71,6 +96,13 @@ __device__ __forceinline__ void group_barrier(int tpr) {
 
 __device__ __forceinline__ float2 group_sum2(float v, float v2, float (*red)[32][2], int buf,
                                             int tpr) {
+  if (tpr < 32) {  // sub-warp group aligned within its warp: shuffles alone
+    for (int o = tpr >> 1; o > 0; o >>= 1) {
+      v += __shfl_xor_sync(0xffffffffu, v, o);
+      v2 += __shfl_xor_sync(0xffffffffu, v2, o);
+    }
+    return make_float2(v, v2);
+  }
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   v = warp_sum(v);
@@ -98,7 +130,7 @@ __device__ __forceinline__ void load_weight(const TW* w, int64_t col, int64_t hi
 
 // ------------------------------- forward ----------------------------------
 template <typename TX, typename TW, int NV>
-__global__ void __launch_bounds__(kMaxThreads)
+__global__ void __launch_bounds__(fwd_max_threads(NV))
 rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
             float* __restrict__ rrms, int64_t rows, int64_t hidden, float eps, int tpr,
             int groups) {
@@ -165,6 +197,88 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
   }
 }
 
+// ---------------------- ring-prefetch variants (NV = 1) ----------------------
+// With one 16-byte vector per thread and row, the register double buffer of
+// the kernels above keeps only ~16 B per thread in flight and each row
+// iteration waits out a full memory latency.  These variants stream the rows
+// through a per-group ring of S slots in shared memory with cp.async (every
+// thread copies, and later reads, only its own vectors, so no barrier guards
+// the ring); S - 1 rows are in flight while one is reduced.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32_of(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32_of(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+constexpr int kRingStages = 6;
+
+template <typename TX, typename TW, int S>
+__global__ void __launch_bounds__(512)
+rms_fwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
+             float* __restrict__ rrms, int64_t rows, int64_t hidden, float eps, int tpr,
+             int groups) {
+  constexpr int VEC = 16 / sizeof(TX);
+  __shared__ float red[2][32][2];
+  extern __shared__ __align__(16) uint8_t ring_raw[];
+  const int g = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  Vec16<TX>* ring = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)g * S * tpr;
+  const int64_t col = (int64_t)t * VEC;
+  const bool has_col = col < hidden;
+  float wr[VEC];
+  load_weight<TW, VEC>(w, col, hidden, wr);
+  const int64_t row_stride = (int64_t)gridDim.x * groups;
+  const int64_t niter = (rows + row_stride - 1) / row_stride;
+  const float inv_h = 1.f / (float)hidden;
+  const int64_t row0 = (int64_t)blockIdx.x * groups + g;
+  auto issue = [&](int64_t r, int slot) {
+    if (r < rows && has_col) cp_async16(&ring[slot * tpr + t], x + r * hidden + col);
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int j = 0; j < S - 1; ++j) issue(row0 + j * row_stride, j);
+  int buf = 0;
+  for (int64_t it = 0; it < niter; ++it) {
+    const int64_t row = row0 + it * row_stride;
+    issue(row + (S - 1) * row_stride, (int)((it + S - 1) % S));
+    cp_async_wait<S - 1>();
+    const bool active = row < rows && has_col;
+    Vec16<TX> xv;
+    float ss = 0.f;
+    if (active) {
+      xv = ring[(int)(it % S) * tpr + t];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float f = to_f32(xv.v[j]);
+        ss = fmaf(f, f, ss);
+      }
+    }
+    const float tot = group_sum2(ss, 0.f, red, buf, tpr).x;
+    buf ^= 1;
+    if (row < rows) {
+      const float r = rsqrtf(tot * inv_h + eps);
+      if (t == 0 && rrms != nullptr) rrms[row] = r;
+      if (has_col) {
+        Vec16<TX> o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) o.v[j] = from_f32<TX>((to_f32(xv.v[j]) * r) * wr[j]);
+        st_vec_stream(y + row * hidden + col, o);
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
+
 // Generic path: any hidden size / alignment.  One CTA per row (grid-stride),
 // two passes over the row (the second hits L1/L2).
 template <typename TX, typename TW>
@@ -194,7 +308,7 @@ rms_fwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restri
 // ([gridDim.x, hidden]).  Row groups of a CTA fold their partials together
 // through shared memory (fixed order) before the single store.
 template <typename TX, typename TW, int NV>
-__global__ void __launch_bounds__(bwd_max_threads<TX>(NV), 1)
+__global__ void __launch_bounds__(bwd_max_threads<TX>(NV), bwd_min_blocks(NV))
 rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
             const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
             int64_t rows, int64_t hidden, float eps, int tpr, int groups) {
@@ -310,6 +424,101 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   }
 }
 
+// Backward, ring-prefetch variant (NV = 1): x, dY and the saved rrms of the
+// next S - 1 rows stream into shared memory while the current row is reduced.
+// Dynamic shared memory: [groups][S][tpr] x vectors, the same for dY,
+// [groups][S][tpr] rrms words, then the [groups][hidden] dweight fold.
+template <typename TX, typename TW, int S>
+__global__ void __launch_bounds__(512)
+rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
+             const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
+             int64_t rows, int64_t hidden, float eps, int tpr, int groups) {
+  constexpr int VEC = 16 / sizeof(TX);
+  __shared__ float red[2][32][2];
+  extern __shared__ __align__(16) uint8_t ring_raw[];
+  const int g = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const int nthreads = tpr * groups;
+  Vec16<TX>* ringx = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)g * S * tpr;
+  Vec16<TX>* ringg = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)(groups + g) * S * tpr;
+  float* ringr = reinterpret_cast<float*>(reinterpret_cast<Vec16<TX>*>(ring_raw) +
+                                          (size_t)2 * groups * S * tpr) +
+                 (size_t)g * S * tpr;
+  float* fold = reinterpret_cast<float*>(ring_raw + (size_t)2 * groups * S * tpr * 16 +
+                                         (size_t)groups * S * tpr * 4);
+  const int64_t col = (int64_t)t * VEC;
+  const bool has_col = col < hidden;
+  float wr[VEC], acc[VEC];
+  load_weight<TW, VEC>(w, col, hidden, wr);
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+  const int64_t row_stride = (int64_t)gridDim.x * groups;
+  const int64_t niter = (rows + row_stride - 1) / row_stride;
+  const float inv_h = 1.f / (float)hidden;
+  const int64_t row0 = (int64_t)blockIdx.x * groups + g;
+  auto issue = [&](int64_t r, int slot) {
+    if (r < rows) {
+      if (has_col) {
+        cp_async16(&ringx[slot * tpr + t], x + r * hidden + col);
+        cp_async16(&ringg[slot * tpr + t], dy + r * hidden + col);
+      }
+      if (rrms != nullptr) cp_async4(&ringr[slot * tpr + t], rrms + r);
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int j = 0; j < S - 1; ++j) issue(row0 + j * row_stride, j);
+  int buf = 0;
+  for (int64_t it = 0; it < niter; ++it) {
+    const int64_t row = row0 + it * row_stride;
+    issue(row + (S - 1) * row_stride, (int)((it + S - 1) % S));
+    cp_async_wait<S - 1>();
+    const int slot = (int)(it % S);
+    const bool active = row < rows && has_col;
+    Vec16<TX> xv, gv;
+    float ss = 0.f, gwx = 0.f;
+    if (active) {
+      xv = ringx[slot * tpr + t];
+      gv = ringg[slot * tpr + t];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xf = to_f32(xv.v[j]);
+        ss = fmaf(xf, xf, ss);
+        gwx = fmaf(to_f32(gv.v[j]) * wr[j], xf, gwx);
+      }
+    }
+    const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
+    buf ^= 1;
+    if (active) {
+      const float r = rrms != nullptr ? ringr[slot * tpr + t] : rsqrtf(sums.x * inv_h + eps);
+      const float c = (sums.y * inv_h) * (r * r * r);
+      Vec16<TX> o;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        const float xf = to_f32(xv.v[j]);
+        const float gf = to_f32(gv.v[j]);
+        o.v[j] = from_f32<TX>((gf * wr[j]) * r - xf * c);
+        acc[j] = fmaf(gf, xf * r, acc[j]);
+      }
+      st_vec_stream(dx + row * hidden + col, o);
+    }
+  }
+  cp_async_wait<0>();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // Fold the row groups' partials (fixed order) and store one row per CTA.
+  if (has_col) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j)
+      if (col + j < hidden) fold[(int64_t)g * hidden + col + j] = acc[j];
+  }
+  __syncthreads();
+  for (int64_t c = threadIdx.x; c < hidden; c += nthreads) {
+    float sum = 0.f;
+    for (int k = 0; k < groups; ++k) sum += fold[(int64_t)k * hidden + c];
+    partial[(int64_t)blockIdx.x * hidden + c] = sum;
+  }
+}
+
 template <typename TX, typename TW>
 __global__ void __launch_bounds__(256)
 rms_bwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
@@ -408,8 +617,24 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
   const TX* xp = static_cast<const TX*>(x);
   const TW* wp = static_cast<const TW*>(w);
   TX* yp = static_cast<TX*>(y);
-  RowCfg cfg = pick_cfg<TX>(hidden, x, y, x, y);
-  if (cfg.vec) {
+  RowCfg cfg = pick_cfg<TX>(hidden, x, y, x, y, false);
+  // Sub-warp rows (the per-head q/k norm) stream through the cp.async ring:
+  // 1.8x the register-prefetch kernel on [131072, 128] bf16.
+  if (cfg.vec && cfg.nv == 1 && cfg.tpr < 32) {
+    constexpr int S = kRingStages;
+    cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8, 512 / cfg.tpr));
+    const int threads = cfg.tpr * cfg.groups;
+    const size_t smem = (size_t)cfg.groups * S * cfg.tpr * 16;
+    auto k = rms_fwd_ring<TX, TW, S>;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           96 * 1024);
+    });
+    const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
+    const int grid = (int)balanced_grid(work, occupancy_grid((const void*)k, threads, smem, work));
+    k<<<grid, threads, smem, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups);
+  } else if (cfg.vec) {
     const int threads = cfg.tpr * cfg.groups;
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
 #define ML_FWD_CASE(NV_)                                                                   \
@@ -443,11 +668,37 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
   const TW* wp = static_cast<const TW*>(w);
   const TX* gp = static_cast<const TX*>(dy);
   TX* dxp = static_cast<TX*>(dx);
-  RowCfg cfg = pick_cfg<TX>(hidden, x, dy, dx, x);
-  if (cfg.vec) cfg.groups = std::max(1, std::min(8, bwd_max_threads<TX>(cfg.nv) / cfg.tpr));
+  RowCfg cfg = pick_cfg<TX>(hidden, x, dy, dx, x, true);
+  if (cfg.vec)
+    cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8,
+                                      bwd_max_threads<TX>(cfg.nv) / cfg.tpr));
   int grid = 0;
   const int64_t max_parts = static_cast<int64_t>(partial_bytes / (sizeof(float) * (size_t)hidden));
-  if (cfg.vec) {
+  if (cfg.vec && cfg.nv == 1) {
+    constexpr int S = 4;
+    cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8, 512 / cfg.tpr));
+    size_t smem = (size_t)cfg.groups * S * cfg.tpr * (2 * 16 + 4) +
+                  (size_t)cfg.groups * hidden * sizeof(float);
+    while (smem > 112 * 1024 && cfg.groups > 1) {
+      cfg.groups /= 2;
+      smem = (size_t)cfg.groups * S * cfg.tpr * (2 * 16 + 4) +
+             (size_t)cfg.groups * hidden * sizeof(float);
+    }
+    const int threads = cfg.tpr * cfg.groups;
+    auto k = rms_bwd_ring<TX, TW, S>;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           112 * 1024);
+    });
+    const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
+    const int per_sm = std::min<int>(
+        kBwdCtasPerSm, occupancy_grid((const void*)k, threads, smem, 1 << 30) / num_sms());
+    grid = static_cast<int>(balanced_grid(
+        work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));
+    k<<<grid, threads, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps, cfg.tpr,
+                                   cfg.groups);
+  } else if (cfg.vec) {
     const int threads = cfg.tpr * cfg.groups;
     size_t smem = cfg.groups > 1 ? (size_t)cfg.groups * hidden * sizeof(float) : 0;
     if (smem > 96 * 1024) {  // fold buffer too large: one row group per CTA

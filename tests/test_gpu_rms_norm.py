@@ -84,6 +84,10 @@ def test_baseline_config_c1_full_size():
     ((1000, 2048), torch.float32, torch.float32),     # 3 row groups per CTA, ragged last wave
     ((4099, 512), torch.float32, torch.float32),      # 6 row groups per CTA
     ((700, 256), torch.bfloat16, torch.float32),      # 8 row groups per CTA
+    ((4099, 128), torch.bfloat16, torch.bfloat16),    # 16-lane sub-warp rows (q/k norm)
+    ((77, 32), torch.bfloat16, torch.bfloat16),       # 4-lane rows
+    ((50, 64), torch.float32, torch.float32),         # 16-lane rows, fp32
+    ((300, 4096), torch.bfloat16, torch.float32),     # one vector per thread, 512-thread rows
 ])
 def test_edge_shapes(shape, xd, wd):
     g = torch.Generator().manual_seed(sum(shape))
