@@ -317,6 +317,8 @@ namespace {
 __global__ void splitk_reduce(const float* __restrict__ part, int splits, int64_t M, int64_t N,
                               int64_t ldp, void* __restrict__ D, int64_t ldd, int d_f32,
                               float beta) {
+  // Launched as a programmatic dependent of the GEMM that wrote `part`.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int64_t total = M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -395,9 +397,20 @@ int launch_splitk_to(Problem pr, int splits, void* out, bool out_f32, int64_t ld
   if (rc) return rc;
   const int64_t total = pr.M * pr.N;
   int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 8);
-  splitk_reduce<<<std::max(grid, 1), 256, 0, st>>>(partial, splits, pr.M, pr.N, pr.N, out, ldo,
-                                                    out_f32 ? 1 : 0, 0.f);
-  ML_CHECK_LAUNCH("gemm split-K reduce");
+  // Programmatic dependent launch: the reduction's launch overlaps the GEMM's
+  // tail; it waits (griddepcontrol.wait) for the GEMM grid before reading.
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3((unsigned)std::max(grid, 1), 1, 1);
+  lc.blockDim = dim3(256, 1, 1);
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  ML_CHECK_CUDA(cudaLaunchKernelEx(&lc, splitk_reduce, (const float*)partial, splits, pr.M, pr.N,
+                                   (int64_t)pr.N, out, ldo, out_f32 ? 1 : 0, 0.f),
+                "gemm split-K reduce");
   return ML_OK;
 }
 

@@ -458,6 +458,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
   }
 
+  // A programmatic dependent (e.g. the split-K reduction) may begin launching.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
@@ -681,6 +683,8 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
     }
   }
 
+  // A programmatic dependent (e.g. the split-K reduction) may begin launching.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   sm100::tc_fence_before();
   __syncthreads();
   sm100::cluster_sync();  // no CTA leaves while its peer may still signal it

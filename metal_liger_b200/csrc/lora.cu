@@ -82,27 +82,35 @@ struct Assembly {
   int nops;
 };
 
-// One thread per destination element (the operands total a few million
-// elements; 32-bit index math — the host checks the total fits).
+// One thread per 8 consecutive destination elements of a row (every operand
+// width is a multiple of 8), written as one 16-byte store; 32-bit index math
+// (the host checks the total fits).
 __global__ void __launch_bounds__(256) assemble_k(const __grid_constant__ Assembly a) {
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= (int)a.start[a.nops]) return;
+  const int e8 = blockIdx.x * blockDim.x + threadIdx.x;  // index of an 8-element chunk
+  if (e8 >= (int)(a.start[a.nops] >> 3)) return;
+  const int e = e8 << 3;
   int k = 0;
   while (k + 1 < a.nops && e >= (int)a.start[k + 1]) ++k;
   const Operand& o = a.op[k];
   const int local = e - (int)a.start[k];
   const int cols = (int)o.cols;
-  const int r = local / cols, c = local - r * cols;
-  float v = 0.f;
-  for (int q = 0; q < o.npieces; ++q) {
-    const Piece& pc = o.p[q];
-    const int i = r - (int)pc.r0, j = c - (int)pc.c0;
-    if (i >= 0 && i < (int)pc.rows && j >= 0 && j < (int)pc.cols)
-      v = pc.scale * load_as_f32(pc.src,
-                                 pc.trans ? (int64_t)j * pc.rows + i : (int64_t)i * pc.cols + j,
-                                 pc.dt);
+  const int r = local / cols, c0 = local - r * cols;
+  Vec16<bf16> out;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int c = c0 + j;
+    float v = 0.f;
+    for (int q = 0; q < o.npieces; ++q) {
+      const Piece& pc = o.p[q];
+      const int i = r - (int)pc.r0, jj = c - (int)pc.c0;
+      if (i >= 0 && i < (int)pc.rows && jj >= 0 && jj < (int)pc.cols)
+        v = pc.scale * load_as_f32(pc.src,
+                                   pc.trans ? (int64_t)jj * pc.rows + i : (int64_t)i * pc.cols + jj,
+                                   pc.dt);
+    }
+    out.v[j] = __float2bfloat16_rn(v);
   }
-  o.dst[(int64_t)r * o.ld + c] = __float2bfloat16_rn(v);
+  *reinterpret_cast<Vec16<bf16>*>(o.dst + (int64_t)r * o.ld + c0) = out;
 }
 
 // Scatter of the fp32 [n, 64] skinny-GEMM results into the per-adapter
@@ -202,7 +210,14 @@ struct Assembler {
       set_error("lora: rank operands too large (%lld elements)", (long long)n);
       return ML_ERR_INVALID_ARG;
     }
-    assemble_k<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
+    for (int k = 0; k < a.nops; ++k)
+      if (a.op[k].cols % 8 != 0 || a.op[k].ld % 8 != 0 ||
+          (reinterpret_cast<uintptr_t>(a.op[k].dst) & 15) != 0) {
+        set_error("lora: rank operand %d is not 16-byte granular", k);
+        return ML_ERR_INVALID_ARG;
+      }
+    const int64_t chunks = n / 8;
+    assemble_k<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(a);
     ML_CHECK_LAUNCH("lora: assemble rank operands");
     return ML_OK;
   }
