@@ -351,12 +351,14 @@ ML_API int ml_lora_qkv_forward(const void* x, int64_t tokens, int64_t in_feature
  * Backward of ml_lora_qkv_forward for upstream dy[0..2] (bf16): dx [tokens,
  * in] bf16 = sum_i dy_i W_i + s_i (dy_i B_i) A_i (one GEMM), and per adapter
  * da[i] [rank, in] = s_i (dy_i B_i)^T x, db[i] [out_i, rank] = s_i dy_i^T u_i,
- * both fp32.  W gets no gradient.  Replaces _LoRA_QKV.backward (reference
- * ops/fused_lora.py:121-171).
+ * accumulated in fp32 and written in the adapter's own dtype (proj[i].a_dtype
+ * / b_dtype) — the value autograd gives the parameter after the reference's
+ * fp32 `.float()` result.  W gets no gradient.  Replaces _LoRA_QKV.backward
+ * (reference ops/fused_lora.py:121-171).
  */
 ML_API int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens, int64_t in_features,
                                 int64_t rank, const ml_lora_proj* proj, const void* const* dy,
-                                void* dx, float* const* da, float* const* db, void* workspace,
+                                void* dx, void* const* da, void* const* db, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
 /*
@@ -376,7 +378,7 @@ ML_API int ml_lora_linear_forward(const void* x, int64_t tokens, int64_t in_feat
 ML_API int ml_lora_linear_backward(const void* x, const void* u, int64_t tokens,
                                    int64_t in_features, int64_t rank, int nproj,
                                    const ml_lora_proj* proj, const void* const* dy, void* dx,
-                                   float* const* da, float* const* db, void* workspace,
+                                   void* const* da, void* const* db, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
 /* Workspace bytes for the MLP entry points (backward = 0 or 1). */
@@ -396,14 +398,15 @@ ML_API int ml_lora_mlp_forward(const void* x, int64_t tokens, int64_t hidden, in
                                size_t workspace_bytes, void* stream);
 
 /*
- * Backward of ml_lora_mlp_forward: dx [tokens, hidden] bf16 and fp32 da[i]
- * [rank, in_i], db[i] [out_i, rank] for gate, up, down.  Replaces
- * _LoRA_MLP.backward (reference ops/fused_lora.py:209-266).
+ * Backward of ml_lora_mlp_forward: dx [tokens, hidden] bf16 and da[i]
+ * [rank, in_i], db[i] [out_i, rank] for gate, up, down (fp32 accumulation,
+ * written in each adapter's dtype as above).  Replaces _LoRA_MLP.backward
+ * (reference ops/fused_lora.py:209-266).
  */
 ML_API int ml_lora_mlp_backward(const void* x, const void* gate, const void* up, const void* h,
                                 const void* u1, const void* u2, int64_t tokens, int64_t hidden,
                                 int64_t inter, int64_t rank, const ml_lora_proj* proj,
-                                const void* dy, void* dx, float* const* da, float* const* db,
+                                const void* dy, void* dx, void* const* da, void* const* db,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* Synchronises `stream`, then returns and clears the device error word set

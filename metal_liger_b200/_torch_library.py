@@ -408,8 +408,10 @@ def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq
     dys = [_bf16_2d(d, w.shape[0]) for d, w in ((dq, qw), (dk, kw), (dv, vw))]
     dev = x.device
     dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    das = [torch.empty((r, H), dtype=torch.float32, device=dev) for _ in range(3)]
-    dbs = [torch.empty((w.shape[0], r), dtype=torch.float32, device=dev) for w in (qw, kw, vw)]
+    # adapter gradients in the adapters' own dtypes (fp32 accumulation inside)
+    das = [torch.empty((r, H), dtype=a.dtype, device=dev) for a in (qa, ka, va)]
+    dbs = [torch.empty((w.shape[0], r), dtype=b.dtype, device=dev)
+           for w, b in ((qw, qb), (kw, kb), (vw, vb))]
     lib = _C.load()
     nbytes = int(lib.ml_lora_qkv_workspace_bytes(T, H, projs, 1))
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -453,8 +455,8 @@ def lora_linear_backward_cuda(x, u, w, a, b, scaling, dy):
     dys = [_bf16_2d(dy, w.shape[0])]
     dev = x.device
     dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    da = torch.empty((r, H), dtype=torch.float32, device=dev)
-    db = torch.empty((w.shape[0], r), dtype=torch.float32, device=dev)
+    da = torch.empty((r, H), dtype=a.dtype, device=dev)
+    db = torch.empty((w.shape[0], r), dtype=b.dtype, device=dev)
     lib = _C.load()
     nbytes = int(lib.ml_lora_linear_workspace_bytes(T, H, 1, projs, 1))
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -509,8 +511,10 @@ def lora_mlp_backward_cuda(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, d
     dy2 = _bf16_2d(dy, H)
     dev = x.device
     dx = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    das = [torch.empty((r, fin), dtype=torch.float32, device=dev) for fin in (H, H, inter)]
-    dbs = [torch.empty((fo, r), dtype=torch.float32, device=dev) for fo in (inter, inter, H)]
+    das = [torch.empty((r, fin), dtype=a.dtype, device=dev)
+           for fin, a in ((H, ga), (H, ua), (inter, da))]
+    dbs = [torch.empty((fo, r), dtype=b.dtype, device=dev)
+           for fo, b in ((inter, gb), (inter, ub), (H, db))]
     lib = _C.load()
     nbytes = int(lib.ml_lora_mlp_workspace_bytes(T, H, inter, 1))
     ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -642,10 +646,10 @@ def _fake_impls():
         return mk(qw), mk(kw), mk(vw), torch.empty((T, 64), dtype=torch.bfloat16, device=x.device)
 
     def lqkv_bwd(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq, dk, dv):
-        f = lambda *s: torch.empty(s, dtype=torch.float32, device=x.device)  # noqa: E731
         r, H = qa.shape
-        return (torch.empty_like(x), f(r, H), f(qw.shape[0], r), f(r, H), f(kw.shape[0], r),
-                f(r, H), f(vw.shape[0], r))
+        return (torch.empty_like(x), torch.empty_like(qa), torch.empty_like(qb),
+                torch.empty_like(ka), torch.empty_like(kb), torch.empty_like(va),
+                torch.empty_like(vb))
 
     def llin_fwd(x, w, a, b, scaling):
         T = x.numel() // x.shape[-1]
@@ -653,9 +657,7 @@ def _fake_impls():
                 torch.empty((T, 64), dtype=torch.bfloat16, device=x.device))
 
     def llin_bwd(x, u, w, a, b, scaling, dy):
-        r, H = a.shape
-        return (torch.empty_like(x), torch.empty((r, H), dtype=torch.float32, device=x.device),
-                torch.empty((w.shape[0], r), dtype=torch.float32, device=x.device))
+        return torch.empty_like(x), torch.empty_like(a), torch.empty_like(b)
 
     def lmlp_fwd(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
         T = x.numel() // x.shape[-1]
@@ -665,11 +667,9 @@ def _fake_impls():
                 bf(T, 64))
 
     def lmlp_bwd(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, da, db, scaling, dy):
-        f = lambda *s: torch.empty(s, dtype=torch.float32, device=x.device)  # noqa: E731
-        r, H = ga.shape
-        inter = gw.shape[0]
-        return (torch.empty_like(x), f(r, H), f(inter, r), f(r, H), f(inter, r), f(r, inter),
-                f(H, r))
+        return (torch.empty_like(x), torch.empty_like(ga), torch.empty_like(gb),
+                torch.empty_like(ua), torch.empty_like(ub), torch.empty_like(da),
+                torch.empty_like(db))
 
     return {
         "lora_qkv_forward": lqkv_fwd,

@@ -118,11 +118,12 @@ __global__ void __launch_bounds__(256) assemble_k(const __grid_constant__ Assemb
 //   trans = 0 (dB): dst[i * cols + j] = scale * src[i * 64 + off + j]   dst [rows, cols = r]
 //   trans = 1 (dA): dst[i * cols + j] = scale * src[j * 64 + off + i]   dst [rows = r, cols]
 struct UnpackJob {
-  float* dst;
+  void* dst;         // in the adapter parameter's dtype (dt)
   const float* src;
   int64_t rows, cols, off;
   float scale;
   int trans;
+  int dt;
 };
 
 constexpr int kMaxUnpack = 6;
@@ -142,8 +143,9 @@ __global__ void unpack_k(const __grid_constant__ Unpacks u) {
     const UnpackJob& jb = u.j[k];
     const int64_t local = e - u.start[k];
     const int64_t i = local / jb.cols, j = local - (local / jb.cols) * jb.cols;
-    jb.dst[local] = jb.scale * (jb.trans ? jb.src[j * kSlot + jb.off + i]
-                                         : jb.src[i * kSlot + jb.off + j]);
+    store_from_f32(jb.dst, local, jb.dt,
+                   jb.scale * (jb.trans ? jb.src[j * kSlot + jb.off + i]
+                                        : jb.src[i * kSlot + jb.off + j]));
   }
 }
 
@@ -225,8 +227,8 @@ struct Assembler {
 
 struct Unpacker {
   Unpacks u{};
-  int add(float* dst, const float* src, int64_t rows, int64_t cols, int64_t off, float scale,
-          bool trans) {
+  int add(void* dst, int dt, const float* src, int64_t rows, int64_t cols, int64_t off,
+          float scale, bool trans) {
     if (u.n >= kMaxUnpack) {
       set_error("lora: too many gradient scatters in one launch");
       return ML_ERR_INVALID_ARG;
@@ -239,6 +241,7 @@ struct Unpacker {
     j.off = off;
     j.scale = scale;
     j.trans = trans ? 1 : 0;
+    j.dt = dt;
     u.start[u.n + 1] = u.start[u.n] + rows * cols;
     ++u.n;
     return ML_OK;
@@ -347,6 +350,8 @@ int rank_proj(int64_t T, const std::vector<gemm::Seg>& segs, bf16* out, float* p
   return rank_proj(T, segs.data(), segs.size(), out, part, part_floats, st);
 }
 
+inline size_t esize(int dtype) { return dtype == ML_DTYPE_F32 ? 4 : 2; }
+
 bool valid_proj(const ml_lora_proj& p) {
   return p.w && p.a && p.b && p.out_features > 0 && p.a_dtype >= 0 && p.a_dtype <= 2 &&
          p.b_dtype >= 0 && p.b_dtype <= 2;
@@ -391,8 +396,8 @@ int qkv_forward(const bf16* x, int64_t T, int64_t H, int64_t r, int np, const ml
 }
 
 int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, int np,
-                 const ml_lora_proj* pj, const void* const* dy, bf16* dx, float* const* da,
-                 float* const* db, Arena& ar, cudaStream_t st) {
+                 const ml_lora_proj* pj, const void* const* dy, bf16* dx, void* const* da,
+                 void* const* db, Arena& ar, cudaStream_t st) {
   int64_t osum = 0;
   for (int i = 0; i < np; ++i) osum += pj[i].out_features;
   bf16* bt[3] = {};
@@ -442,8 +447,9 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   }
   Unpacker un;
   for (int i = 0; i < np; ++i) {
-    LORA_TRY(un.add(da[i], dAT, r, H, i * r, pj[i].scaling, true));
-    LORA_TRY(un.add(db[i], dBt[i], pj[i].out_features, r, i * r, pj[i].scaling, false));
+    LORA_TRY(un.add(da[i], pj[i].a_dtype, dAT, r, H, i * r, pj[i].scaling, true));
+    LORA_TRY(un.add(db[i], pj[i].b_dtype, dBt[i], pj[i].out_features, r, i * r, pj[i].scaling,
+                    false));
   }
   return un.launch(st);
 }
@@ -488,8 +494,8 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
 
 int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h, const bf16* u1,
                  const bf16* u2, int64_t T, int64_t H, int64_t I, int64_t r,
-                 const ml_lora_proj* pj, const bf16* dy, bf16* dx, float* const* da,
-                 float* const* db, Arena& ar, cudaStream_t st) {
+                 const ml_lora_proj* pj, const bf16* dy, bf16* dx, void* const* da,
+                 void* const* db, Arena& ar, cudaStream_t st) {
   bf16* bdT = ar.take<bf16>((size_t)kSlot * H);     // rows [0,r) = Bd^T
   bf16* ads = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = s_d Ad
   bf16* bgT = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = Bg^T
@@ -539,12 +545,12 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   LORA_TRY(gemm_skinny_f32(I, seg(dgate, I, u1, kSlot, T), dBt_g, part, pf * 4, st));
   LORA_TRY(gemm_skinny_f32(I, seg(dup, I, u1, kSlot, T), dBt_u, part, pf * 4, st));
   Unpacker un;
-  LORA_TRY(un.add(da[2], dAT_d, r, I, 0, pj[2].scaling, true));
-  LORA_TRY(un.add(db[2], dBt_d, H, r, 0, pj[2].scaling, false));
-  LORA_TRY(un.add(da[0], dAT_gu, r, H, 0, pj[0].scaling, true));
-  LORA_TRY(un.add(da[1], dAT_gu, r, H, r, pj[1].scaling, true));
-  LORA_TRY(un.add(db[0], dBt_g, I, r, 0, pj[0].scaling, false));
-  LORA_TRY(un.add(db[1], dBt_u, I, r, r, pj[1].scaling, false));
+  LORA_TRY(un.add(da[2], pj[2].a_dtype, dAT_d, r, I, 0, pj[2].scaling, true));
+  LORA_TRY(un.add(db[2], pj[2].b_dtype, dBt_d, H, r, 0, pj[2].scaling, false));
+  LORA_TRY(un.add(da[0], pj[0].a_dtype, dAT_gu, r, H, 0, pj[0].scaling, true));
+  LORA_TRY(un.add(da[1], pj[1].a_dtype, dAT_gu, r, H, r, pj[1].scaling, true));
+  LORA_TRY(un.add(db[0], pj[0].b_dtype, dBt_g, I, r, 0, pj[0].scaling, false));
+  LORA_TRY(un.add(db[1], pj[1].b_dtype, dBt_u, I, r, r, pj[1].scaling, false));
   return un.launch(st);
 }
 
@@ -616,15 +622,19 @@ extern "C" int ml_lora_linear_forward(const void* x, int64_t tokens, int64_t in_
 extern "C" int ml_lora_linear_backward(const void* x, const void* u, int64_t tokens,
                                        int64_t in_features, int64_t rank, int nproj,
                                        const ml_lora_proj* proj, const void* const* dy, void* dx,
-                                       float* const* da, float* const* db, void* workspace,
+                                       void* const* da, void* const* db, void* workspace,
                                        size_t workspace_bytes, void* stream) {
   LORA_ARGCHECK_COMMON("lora_linear_backward", nproj)
   ML_CHECK_ARG(dy && da && db, "lora_linear_backward: null pointer arrays");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (tokens == 0) {
     for (int i = 0; i < nproj; ++i) {
-      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_features * 4, st), "memset dA");
-      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
+      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_features * lora::esize(proj[i].a_dtype),
+                                    st),
+                    "memset dA");
+      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0,
+                                    (size_t)proj[i].out_features * rank * lora::esize(proj[i].b_dtype),
+                                    st),
                     "memset dB");
     }
     return ML_OK;
@@ -661,8 +671,8 @@ extern "C" int ml_lora_qkv_forward(const void* x, int64_t tokens, int64_t in_fea
 
 extern "C" int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens,
                                     int64_t in_features, int64_t rank, const ml_lora_proj* proj,
-                                    const void* const* dy, void* dx, float* const* da,
-                                    float* const* db, void* workspace, size_t workspace_bytes,
+                                    const void* const* dy, void* dx, void* const* da,
+                                    void* const* db, void* workspace, size_t workspace_bytes,
                                     void* stream) {
   return ml_lora_linear_backward(x, u, tokens, in_features, rank, 3, proj, dy, dx, da, db,
                                  workspace, workspace_bytes, stream);
@@ -721,7 +731,7 @@ extern "C" int ml_lora_mlp_backward(const void* x, const void* gate, const void*
                                     const void* h, const void* u1, const void* u2, int64_t tokens,
                                     int64_t hidden, int64_t inter, int64_t rank,
                                     const ml_lora_proj* proj, const void* dy, void* dx,
-                                    float* const* da, float* const* db, void* workspace,
+                                    void* const* da, void* const* db, void* workspace,
                                     size_t workspace_bytes, void* stream) {
   LORA_MLP_CHECK("lora_mlp_backward")
   ML_CHECK_ARG(da && db, "lora_mlp_backward: null pointer arrays");
@@ -729,8 +739,12 @@ extern "C" int ml_lora_mlp_backward(const void* x, const void* gate, const void*
   if (tokens == 0) {
     const int64_t in_f[3] = {hidden, hidden, inter};
     for (int i = 0; i < 3; ++i) {
-      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_f[i] * 4, st), "memset dA");
-      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0, (size_t)proj[i].out_features * rank * 4, st),
+      ML_CHECK_CUDA(cudaMemsetAsync(da[i], 0, (size_t)rank * in_f[i] * lora::esize(proj[i].a_dtype),
+                                    st),
+                    "memset dA");
+      ML_CHECK_CUDA(cudaMemsetAsync(db[i], 0,
+                                    (size_t)proj[i].out_features * rank * lora::esize(proj[i].b_dtype),
+                                    st),
                     "memset dB");
     }
     return ML_OK;

@@ -13,8 +13,10 @@ base-weight GEMM (one TMEM accumulator per output tile), dX for Q/K/V (or
 gate/up) is ONE GEMM over the concatenated K dimension, and the A/B
 gradients are split-K GEMMs over the tokens.  X is saved once (as in the
 reference), plus the tiny [tokens, 64] rank projections so the backward does
-not recompute them.  A/B gradients are returned in fp32 like the reference's
-``.float()``; the frozen base weights get no gradient.
+not recompute them.  A/B gradients are accumulated in fp32 and returned in
+the adapters' own dtype — the value autograd assigns after the reference's
+fp32 ``.float()`` result, without a separate cast kernel per adapter; the
+frozen base weights get no gradient.
 """
 
 import logging
@@ -113,7 +115,8 @@ class _LoRA_W(torch.autograd.Function):
     """One LoRA linear y = X W^T + s (X A^T) B^T with the rank term folded into
     the base GEMM (the single-projection form the reference describes as
     "LoRA_W", ops/fused_lora.py:26, and leaves to PEFT).  Saves X and the
-    [tokens, 64] rank projection; A/B gradients in fp32, W frozen."""
+    [tokens, 64] rank projection; A/B gradients in the adapters' dtype
+    (fp32 accumulation), W frozen."""
 
     @staticmethod
     def forward(ctx, X, W, A, B, S):
