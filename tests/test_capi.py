@@ -75,3 +75,25 @@ def test_empty_inputs_are_noops(cuda_lib):
 def test_python_raises_with_library_message():
     with pytest.raises(RuntimeError, match="status 1"):
         _C.check(1, "probe")
+
+
+def test_gemm_kernel_mode_knob(cuda_lib):
+    prev = ctypes.c_int(-7)
+    assert cuda_lib.ml_gemm_set_cta_pair(0, ctypes.byref(prev)) == 0
+    assert prev.value == -1  # process default: automatic
+    assert cuda_lib.ml_gemm_set_cta_pair(5, None) == 1
+    assert b"mode" in cuda_lib.ml_last_error()
+    assert cuda_lib.ml_gemm_set_cta_pair(-1, ctypes.byref(prev)) == 0
+    assert prev.value == 0
+
+
+def test_lora_linear_rejects_bad_projection_counts(cuda_lib):
+    projs = (_C.LoraProj * 3)()
+    for i in range(3):
+        projs[i].w = projs[i].a = projs[i].b = 16
+        projs[i].out_features = 64
+    # four projections, and three of rank 32 (3 x 32 > the 64-wide rank slot)
+    assert cuda_lib.ml_lora_linear_forward(16, 8, 64, 8, 4, projs, None, 16, None, 0, None) == 1
+    assert b"nproj" in cuda_lib.ml_last_error()
+    assert cuda_lib.ml_lora_linear_forward(16, 8, 64, 32, 3, projs, None, 16, None, 0, None) == 1
+    assert b"64" in cuda_lib.ml_last_error()

@@ -59,3 +59,14 @@ def test_rms_module_repr_and_params():
     m = ml.MetalLigerRMSNorm(16, eps=1e-5)
     assert m.weight.shape == (16,)
     assert "hidden_size=16" in repr(m)
+
+
+def test_lora_fakes_return_adapter_dtypes():
+    x = torch.empty(2, 8, 64, device="meta", dtype=torch.bfloat16)
+    w = torch.empty(32, 64, device="meta", dtype=torch.bfloat16)
+    a = torch.empty(4, 64, device="meta", dtype=torch.bfloat16)
+    b = torch.empty(32, 4, device="meta", dtype=torch.float32)
+    y, u = torch.ops.metal_liger.lora_linear_forward(x, w, a, b, 2.0)
+    assert y.shape == (16, 32) and u.shape == (16, 64)
+    dx, da, db = torch.ops.metal_liger.lora_linear_backward(x, u, w, a, b, 2.0, y)
+    assert dx.shape == x.shape and da.dtype == a.dtype and db.dtype == b.dtype
