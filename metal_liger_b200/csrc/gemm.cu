@@ -265,13 +265,19 @@ int launch(const Problem& pr, cudaStream_t st) {
   if (pr.raster == 0 && pr.group_m == 0 && prm.n_tiles > 1) {
     // M-fastest raster re-reads all of A once per N-tile column.  When A does
     // not fit comfortably in L2, sweep the N-tiles in groups of M-tiles whose
-    // A rows (~16 MB) stay resident, so A is read from HBM about once and B
-    // once per group.
+    // A rows stay resident, so A is read from HBM about once and B once per
+    // group.  Group size, from ncu DRAM counts on the LoRA shapes: with short
+    // K (A rows of a 256-row tile <= 4 MB) up to ~48 MB of A per group cuts
+    // the B sweeps (gate/up 16384 x 12288 x 4160: 1.18 -> 0.85 GB per launch,
+    // less DRAM energy under the power cap); with long K the larger groups
+    // thrash L2 (dX 16384 x 4096 x 24640: 3.9 -> 6.2 GB), so ~16 MB.
     int64_t k_total = 0;
     for (int s = 0; s < pr.nseg; ++s) k_total += pr.seg[s].K;
     const int64_t a_bytes_per_mtile = (int64_t)(pair ? 2 * BM : BM) * k_total * 2;
     if ((int64_t)prm.m_tiles * a_bytes_per_mtile > ((int64_t)48 << 20)) {
-      const int64_t g = std::max<int64_t>(1, ((int64_t)16 << 20) / a_bytes_per_mtile);
+      const int64_t target = a_bytes_per_mtile <= ((int64_t)4 << 20) ? ((int64_t)48 << 20)
+                                                                         : ((int64_t)16 << 20);
+      const int64_t g = std::max<int64_t>(1, target / a_bytes_per_mtile);
       prm.group_m = (int)std::min<int64_t>(g, prm.m_tiles);
     }
   }
