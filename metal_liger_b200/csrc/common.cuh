@@ -7,6 +7,8 @@
 // with ml_last_error().
 #pragma once
 
+#include <mutex>
+
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -119,6 +121,31 @@ template <typename T>
 __device__ __forceinline__ void st_vec_stream(T* p, const Vec16<T>& v) {
   __stcs(reinterpret_cast<int4*>(p), *reinterpret_cast<const int4*>(&v));
 }
+
+// Runs a setup step (a kernel attribute, an occupancy query) once per CUDA
+// device — the current one — and returns its cached result: kernel
+// attributes belong to the device context they were set in.
+template <typename T>
+class PerDevice {
+ public:
+  template <typename F>
+  T get(F&& fn) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) dev = 0;
+    std::lock_guard<std::mutex> lock(mu_);
+    if (!done_[dev]) {
+      val_[dev] = fn();
+      done_[dev] = true;
+    }
+    return val_[dev];
+  }
+
+ private:
+  static constexpr int kMaxDev = 64;
+  std::mutex mu_;
+  bool done_[kMaxDev] = {};
+  T val_[kMaxDev] = {};
+};
 
 // Shared-window address of a generic pointer to shared memory.
 __device__ __forceinline__ uint32_t smem_u32_of(const void* p) {

@@ -84,11 +84,10 @@ template <int BN, bool A_MN, bool B_MN>
 int launch_t(const Params& prm, int grid, cudaStream_t st) {
   auto k = gemm_kernel<BN, A_MN, B_MN>;
   const size_t smem = Cfg<BN>::SMEM;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)smem);
+  static PerDevice<cudaError_t> attr;
+  const cudaError_t attr_err = attr.get([&] {
+    return cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)smem);
   });
   if (attr_err != cudaSuccess) {
     set_error("gemm: cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err));
@@ -105,14 +104,15 @@ template <int BN, bool A_MN, bool B_MN>
 int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t st) {
   auto k = gemm_pair_kernel<BN, A_MN, B_MN>;
   const size_t smem = PairCfg<BN>::SMEM;
-  static std::once_flag once;
-  static cudaError_t attr_err = cudaSuccess;
-  static int resident_pairs = 0;
-  std::call_once(once, [&] {
-    attr_err = cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)smem);
-    if (attr_err != cudaSuccess) return;
-    // How many CTA pairs fit at once (GPC boundaries can leave an SM unpaired).
+  // Per device: the smem attribute, then how many CTA pairs fit at once (GPC
+  // boundaries can leave an SM unpaired); -1 = the attribute failed.
+  static PerDevice<int> setup;
+  const int resident_pairs = setup.get([&]() -> int {
+    if (cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess) {
+      cudaGetLastError();
+      return -1;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (unsigned)(num_sms() / 2), 1, 1);
     cfg.blockDim = dim3(kThreads, 1, 1);
@@ -122,8 +122,9 @@ int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t s
       cudaGetLastError();
       n = num_sms() / 2;
     }
-    resident_pairs = n;
+    return n;
   });
+  const cudaError_t attr_err = resident_pairs < 0 ? cudaErrorInvalidValue : cudaSuccess;
   if (attr_err != cudaSuccess) {
     set_error("gemm(pair): cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err));
     return ML_ERR_CUDA;

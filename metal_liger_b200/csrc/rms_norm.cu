@@ -626,11 +626,12 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
     const int threads = cfg.tpr * cfg.groups;
     const size_t smem = (size_t)cfg.groups * S * cfg.tpr * 16;
     auto k = rms_fwd_ring<TX, TW, S>;
-    static std::once_flag once;
-    std::call_once(once, [&] {
-      cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           96 * 1024);
-    });
+    static PerDevice<cudaError_t> attr;
+    ML_CHECK_CUDA(attr.get([&] {
+                    return cudaFuncSetAttribute(
+                        (const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+                  }),
+                  "rms_norm_forward: smem attribute");
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
     const int grid = (int)balanced_grid(work, occupancy_grid((const void*)k, threads, smem, work));
     k<<<grid, threads, smem, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups);
@@ -686,11 +687,12 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
     }
     const int threads = cfg.tpr * cfg.groups;
     auto k = rms_bwd_ring<TX, TW, S>;
-    static std::once_flag once;
-    std::call_once(once, [&] {
-      cudaFuncSetAttribute((const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           112 * 1024);
-    });
+    static PerDevice<cudaError_t> attr;
+    ML_CHECK_CUDA(attr.get([&] {
+                    return cudaFuncSetAttribute(
+                        (const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+                  }),
+                  "rms_norm_backward: smem attribute");
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
     const int per_sm = std::min<int>(
         kBwdCtasPerSm, occupancy_grid((const void*)k, threads, smem, 1 << 30) / num_sms());
