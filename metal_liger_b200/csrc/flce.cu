@@ -172,33 +172,49 @@ __global__ void __launch_bounds__(256)
 flce_transform(__nv_bfloat16* __restrict__ E, int64_t ldE, int64_t rows, int64_t vocab,
                const float* __restrict__ f, const int64_t* __restrict__ labels, int64_t ignore,
                const float* __restrict__ scale_ptr, int64_t label_base) {
+  // Rows over blocks (grid-stride), 16-byte vectors of a row over threads, 4
+  // vectors in flight per thread: no per-element index division, one label
+  // and scale per row, one tile factor per 32 vectors (from L1).
+  constexpr int U = 4;
   const int64_t vpr = (vocab + 7) / 8;  // vectors per row
-  const int64_t total = rows * vpr;
   const float scale = scale_ptr[0];
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / vpr;
-    const int64_t c0 = (i - r * vpr) * 8;
-    const int64_t t = c0 / kTileV;
-    const float fr = f[t * rows + r];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const int64_t lab0 = labels[r];
     const float sub = lab0 != ignore ? scale : 0.f;
     const int64_t lab = lab0 != ignore ? lab0 - label_base : (int64_t)-1;
-    __nv_bfloat16* p = E + r * ldE + c0;
-    if (c0 + 8 <= vocab) {
-      Vec16<__nv_bfloat16> v = *reinterpret_cast<Vec16<__nv_bfloat16>*>(p);
+    __nv_bfloat16* row = E + r * ldE;
+    for (int64_t base = threadIdx.x; base < vpr; base += (int64_t)blockDim.x * U) {
+      Vec16<__nv_bfloat16> v[U];
+      float fr[U];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float x = __bfloat162float(v.v[j]) * fr;
-        if (lab == c0 + j) x -= sub;
-        v.v[j] = __float2bfloat16_rn(x);
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = base + (int64_t)u * blockDim.x;
+        if (vi < vpr && vi * 8 + 8 <= vocab) {
+          v[u] = *reinterpret_cast<const Vec16<__nv_bfloat16>*>(row + vi * 8);
+          fr[u] = f[((vi * 8) / kTileV) * rows + r];
+        }
       }
-      *reinterpret_cast<Vec16<__nv_bfloat16>*>(p) = v;
-    } else {
-      for (int j = 0; c0 + j < vocab; ++j) {
-        float x = __bfloat162float(p[j]) * fr;
-        if (lab == c0 + j) x -= sub;
-        p[j] = __float2bfloat16_rn(x);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t vi = base + (int64_t)u * blockDim.x;
+        if (vi >= vpr) continue;
+        const int64_t c0 = vi * 8;
+        if (c0 + 8 <= vocab) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float x = __bfloat162float(v[u].v[j]) * fr[u];
+            if (lab == c0 + j) x -= sub;
+            v[u].v[j] = __float2bfloat16_rn(x);
+          }
+          *reinterpret_cast<Vec16<__nv_bfloat16>*>(row + c0) = v[u];
+        } else {  // ragged last vector of the row
+          const float fl = f[(c0 / kTileV) * rows + r];
+          for (int j = 0; c0 + j < vocab; ++j) {
+            float x = __bfloat162float(row[c0 + j]) * fl;
+            if (lab == c0 + j) x -= sub;
+            row[c0 + j] = __float2bfloat16_rn(x);
+          }
+        }
       }
     }
   }
@@ -429,8 +445,7 @@ extern "C" int ml_flce_forward(const void* hidden, const void* weight, const voi
     if (dx_slabs == nullptr && dw_acc == nullptr) continue;
     // 3. P = softmax - onehot (scaled), in place
     {
-      const int64_t total = rows * ((v + 7) / 8);
-      const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+      const int grid = (int)std::min<int64_t>(rows, (int64_t)1 << 20);  // a row per block
       flce::flce_transform<<<grid, 256, 0, st>>>(E, L.ldE, rows, v, pm, labels + r0,
                                                  ignore_index, cnt + 1, 0);
       ML_CHECK_LAUNCH("flce_transform");
@@ -612,8 +627,7 @@ extern "C" int ml_flce_shard_grads(const void* hidden, const void* weight, const
     ML_CHECK_LAUNCH("flce_factors");
   }
   {
-    const int64_t total = rows * ((v_local + 7) / 8);
-    const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)num_sms() * 16);
+    const int grid = (int)std::min<int64_t>(rows, (int64_t)1 << 20);  // a row per block
     flce::flce_transform<<<grid, 256, 0, st>>>(E, L.ldE, rows, v_local, pm, labels, ignore_index,
                                                scale, vocab_offset);
     ML_CHECK_LAUNCH("flce_transform");
