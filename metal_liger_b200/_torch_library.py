@@ -278,10 +278,18 @@ def flce_forward_cuda(hidden: Tensor, weight: Tensor, labels: Tensor, bias: Tens
     """(loss, dx_slabs, dw_acc): loss and, when requested, the fp32 gradients at
     grad_output = 1 (dx as split-K slabs [s, N, H], dw [V, H]).
 
-    Operands enter the tensor cores as bf16 (inputs of other dtypes are cast).
+    bf16/fp16 inputs run the fused kernels with bf16 operands; fp32 inputs take
+    the fp32-accurate path (three-part bf16 splits, six GEMM products, _fp32_path.py).
     """
     _C.require_cuda("flce_forward", hidden, weight, labels, bias)
     H = hidden.shape[-1]
+    if _fp32_mode(hidden):
+        from metal_liger_b200 import _fp32_path as F
+        if weight.dim() != 2 or weight.shape[1] != H:
+            raise RuntimeError(
+                f"flce_forward: weight {tuple(weight.shape)} does not match hidden {H}")
+        return F.flce_forward(hidden, weight, labels, bias, int(ignore_index), int(chunk_size),
+                              need_dx, need_dw)
     if weight.dim() != 2 or weight.shape[1] != H:
         raise RuntimeError(f"flce_forward: weight {tuple(weight.shape)} does not match hidden {H}")
     h2 = _bf16_2d(hidden, H)
@@ -370,9 +378,21 @@ def _check_rank(a_list, b_list, in_list):
     return r
 
 
+def _fp32_mode(x: Tensor) -> bool:
+    """fp32 inputs take the fp32-accurate path (three-part bf16 splits, six GEMM products, _fp32_path.py)."""
+    return x.dtype == torch.float32
+
+
 def lora_qkv_forward_cuda(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
     _C.require_cuda("lora_qkv_forward", x, qw, qa, qb, kw, ka, kb, vw, va, vb)
     H = x.shape[-1]
+    if _fp32_mode(x):
+        from metal_liger_b200 import _fp32_path as F
+        r = _check_rank((qa, ka, va), (qb, kb, vb), (H, H, H))
+        outs, u = F.lora_proj_forward(x.reshape(-1, H), [(qw, qa, qb, scaling[0]),
+                                                         (kw, ka, kb, scaling[1]),
+                                                         (vw, va, vb, scaling[2])], r)
+        return outs[0], outs[1], outs[2], u
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     keep: list = []
@@ -398,6 +418,16 @@ def lora_qkv_forward_cuda(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
 def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq, dk, dv):
     _C.require_cuda("lora_qkv_backward", x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, dq, dk, dv)
     H = x.shape[-1]
+    if u.dtype == torch.float32:
+        from metal_liger_b200 import _fp32_path as F
+        r = _check_rank((qa, ka, va), (qb, kb, vb), (H, H, H))
+        projs = [(qw, qa, qb, scaling[0]), (kw, ka, kb, scaling[1]), (vw, va, vb, scaling[2])]
+        dys = [d.reshape(-1, w.shape[0]) for d, w in ((dq, qw), (dk, kw), (dv, vw))]
+        dx, grads = F.lora_proj_backward(x.reshape(-1, H).float(), u, projs, r, dys)
+        flat = []
+        for (da, db), (_, a, b, _) in zip(grads, projs):
+            flat += [da.to(a.dtype), db.to(b.dtype)]
+        return (dx.to(x.dtype).view(x.shape), *flat)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     keep: list = []
@@ -424,6 +454,11 @@ def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq
 def lora_linear_forward_cuda(x, w, a, b, scaling):
     _C.require_cuda("lora_linear_forward", x, w, a, b)
     H = x.shape[-1]
+    if _fp32_mode(x):
+        from metal_liger_b200 import _fp32_path as F
+        r = _check_rank((a,), (b,), (H,))
+        (y,), u = F.lora_proj_forward(x.reshape(-1, H), [(w, a, b, scaling)], r)
+        return y, u
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     if w.dim() != 2 or w.shape[1] != H:
@@ -446,6 +481,12 @@ def lora_linear_forward_cuda(x, w, a, b, scaling):
 def lora_linear_backward_cuda(x, u, w, a, b, scaling, dy):
     _C.require_cuda("lora_linear_backward", x, u, w, a, b, dy)
     H = x.shape[-1]
+    if u.dtype == torch.float32:
+        from metal_liger_b200 import _fp32_path as F
+        r = _check_rank((a,), (b,), (H,))
+        dx, ((da, db),) = F.lora_proj_backward(x.reshape(-1, H).float(), u, [(w, a, b, scaling)],
+                                               r, [dy.reshape(-1, w.shape[0])])
+        return dx.to(x.dtype).view(x.shape), da.to(a.dtype), db.to(b.dtype)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     r = _check_rank((a,), (b,), (H,))
@@ -469,6 +510,14 @@ def lora_linear_backward_cuda(x, u, w, a, b, scaling, dy):
 def lora_mlp_forward_cuda(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
     _C.require_cuda("lora_mlp_forward", x, gw, ga, gb, uw, ua, ub, dw, da, db)
     H = x.shape[-1]
+    if _fp32_mode(x):
+        from metal_liger_b200 import _fp32_path as F
+        inter = gw.shape[0]
+        r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
+        out, g_, u_, h, u1, u2 = F.lora_mlp_forward(
+            x.reshape(-1, H), (gw, ga, gb, scaling[0]), (uw, ua, ub, scaling[1]),
+            (dw, da, db, scaling[2]), r)
+        return out.view(x.shape), g_, u_, h, u1, u2
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     inter = gw.shape[0]
@@ -500,6 +549,17 @@ def lora_mlp_backward_cuda(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, d
     _C.require_cuda("lora_mlp_backward", x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, da,
                     db, dy)
     H = x.shape[-1]
+    if u1.dtype == torch.float32:
+        from metal_liger_b200 import _fp32_path as F
+        inter = gw.shape[0]
+        r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
+        projs = ((gw, ga, gb, scaling[0]), (uw, ua, ub, scaling[1]), (dw, da, db, scaling[2]))
+        dx, grads = F.lora_mlp_backward(x.reshape(-1, H).float(), gate, up, h, u1, u2, *projs, r,
+                                        dy.reshape(-1, H))
+        flat = []
+        for (ga_, gb_), (_, a, b, _) in zip(grads, projs):
+            flat += [ga_.to(a.dtype), gb_.to(b.dtype)]
+        return (dx.to(x.dtype).view(x.shape), *flat)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     inter = gw.shape[0]
@@ -640,10 +700,13 @@ def _fake_impls():
               if dw_acc.dim() == 2 else torch.empty(0, device=dev))
         return dh, dw
 
+    def _u_dtype(x):
+        return torch.float32 if x.dtype == torch.float32 else torch.bfloat16
+
     def lqkv_fwd(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
         T = x.numel() // x.shape[-1]
         mk = lambda w: torch.empty((T, w.shape[0]), dtype=x.dtype, device=x.device)  # noqa: E731
-        return mk(qw), mk(kw), mk(vw), torch.empty((T, 64), dtype=torch.bfloat16, device=x.device)
+        return mk(qw), mk(kw), mk(vw), torch.empty((T, 64), dtype=_u_dtype(x), device=x.device)
 
     def lqkv_bwd(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq, dk, dv):
         r, H = qa.shape
@@ -654,7 +717,7 @@ def _fake_impls():
     def llin_fwd(x, w, a, b, scaling):
         T = x.numel() // x.shape[-1]
         return (torch.empty((T, w.shape[0]), dtype=x.dtype, device=x.device),
-                torch.empty((T, 64), dtype=torch.bfloat16, device=x.device))
+                torch.empty((T, 64), dtype=_u_dtype(x), device=x.device))
 
     def llin_bwd(x, u, w, a, b, scaling, dy):
         return torch.empty_like(x), torch.empty_like(a), torch.empty_like(b)
@@ -662,7 +725,8 @@ def _fake_impls():
     def lmlp_fwd(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
         T = x.numel() // x.shape[-1]
         inter = gw.shape[0]
-        bf = lambda *s: torch.empty(s, dtype=torch.bfloat16, device=x.device)  # noqa: E731
+        dt = _u_dtype(x)
+        bf = lambda *s: torch.empty(s, dtype=dt, device=x.device)  # noqa: E731
         return (torch.empty_like(x), bf(T, inter), bf(T, inter), bf(T, inter), bf(T, 64),
                 bf(T, 64))
 
