@@ -88,6 +88,9 @@ def test_baseline_config_c1_full_size():
     ((77, 32), torch.bfloat16, torch.bfloat16),       # 4-lane rows
     ((50, 64), torch.float32, torch.float32),         # 16-lane rows, fp32
     ((300, 4096), torch.bfloat16, torch.float32),     # one vector per thread, 512-thread rows
+    ((5003, 1024), torch.float32, torch.float32),     # one vector per thread, fp32, ragged
+    ((9001, 2048), torch.bfloat16, torch.bfloat16),   # 16-bit rows, many row iterations
+    ((2999, 4096), torch.float16, torch.float32),     # 512-thread rows, fp16
 ])
 def test_edge_shapes(shape, xd, wd):
     g = torch.Generator().manual_seed(sum(shape))
@@ -106,6 +109,38 @@ def test_edge_shapes(shape, xd, wd):
         assert_close(dw, rdw, rtol=1e-5, atol=1e-5 * scale, what="dw")
     else:
         assert_close(dw, rdw.float(), rtol=2e-2, atol=1e-2 * scale, norm_rtol=1e-2, what="dw")
+
+
+@pytest.mark.parametrize("shape,xd", [((8192, 2048), torch.float32),    # register rows
+                                      ((4099, 128), torch.bfloat16),   # cp.async ring rows
+                                      ((37, 40000), torch.float32)])   # generic rows
+def test_dweight_is_deterministic_and_streams_do_not_interfere(shape, xd):
+    """The backward's last CTAs reduce dweight in a fixed order: repeated calls
+    give bitwise-equal dweight, also with two calls in flight on two streams
+    (each call has its own workspace ticket)."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(*shape, generator=g, device=DEV).to(xd)
+    w = (1 + 0.1 * torch.randn(shape[-1], generator=g, device=DEV)).to(xd)
+    dy = torch.randn(*shape, generator=g, device=DEV).to(xd)
+    ops = torch.ops.metal_liger
+    _, rrms = ops.rms_norm_forward(x, w, 1e-6, "")
+    _, dw0 = ops.rms_norm_backward(x, w, dy, 1e-6, "", rrms)
+    for _ in range(3):
+        assert torch.equal(ops.rms_norm_backward(x, w, dy, 1e-6, "", rrms)[1], dw0)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    s1.wait_stream(torch.cuda.current_stream())
+    s2.wait_stream(torch.cuda.current_stream())
+    outs = []
+    for st in (s1, s2, s1, s2):
+        with torch.cuda.stream(st):
+            outs.append(ops.rms_norm_backward(x, w, dy, 1e-6, "", rrms)[1])
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, dw0)
+    rdx, rdw = O.rms_norm_backward(x.cpu(), w.cpu(), rrms.cpu(), dy.cpu())
+    scale = max(rdw.float().abs().max().item(), 1.0)
+    assert_close(dw0.cpu(), rdw.float(), dtype=xd, rtol=2e-2 if xd != torch.float32 else 1e-5,
+                 atol=(1e-2 if xd != torch.float32 else 1e-5) * scale, what="dw")
 
 
 def test_noncontiguous_input_and_empty():
