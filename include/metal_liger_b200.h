@@ -409,6 +409,28 @@ ML_API int ml_lora_mlp_backward(const void* x, const void* gate, const void* up,
                                 const void* dy, void* dx, void* const* da, void* const* db,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Greedy decoding head: index[b] = argmax over v < vocab of the logit
+ * round_to(logit_dtype, sum_k hidden[b, k] * weight[v, k] (+ bias[v])), the
+ * products accumulated in fp32 on the tcgen05 GEMM core and never stored;
+ * value[b] (optional) = that logit.  Ties and NaN follow torch.argmax (NaN
+ * first, then the lowest index).  hidden [batch, hidden_size] and weight
+ * [vocab, hidden_size] are bf16 with row pitches ld_hidden / ld_weight
+ * (elements, multiples of 8; 16-byte aligned bases); logit_dtype is the
+ * dtype the model's logits have (ML_DTYPE_BF16 for a bf16 lm_head); bias is
+ * optional ([vocab], bias_dtype).  workspace >=
+ * ml_lm_head_argmax_workspace_bytes(batch, vocab), 16-byte aligned.
+ * Replaces the reference's greedy step of MetalLigerGenerator.generate,
+ * logits = model(...).logits[:, -1, :]; argmax(logits, -1)
+ * (generation.py:99-101,118-122), without the [batch, vocab] logits.
+ */
+ML_API size_t ml_lm_head_argmax_workspace_bytes(int64_t batch, int64_t vocab);
+ML_API int ml_lm_head_argmax(const void* hidden, int64_t ld_hidden, const void* weight,
+                             int64_t ld_weight, const void* bias, int bias_dtype, int64_t batch,
+                             int64_t hidden_size, int64_t vocab, int logit_dtype, int64_t* index,
+                             float* value, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

@@ -589,7 +589,41 @@ def lora_mlp_backward_cuda(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, d
 # Registration
 # ---------------------------------------------------------------------------
 
+def lm_head_argmax_cuda(hidden: Tensor, weight: Tensor, bias: Tensor | None, logit_dtype: int):
+    """Greedy decoding head: (index int64 [B], value fp32 [B]) of the largest
+    logit of each row of hidden [B, H] against weight [V, H] (bf16), the
+    logits rounded to the dtype ``logit_dtype`` (an ML_DTYPE_* code) and never
+    stored; ties and NaN as torch.argmax."""
+    _C.require_cuda("lm_head_argmax", hidden, weight, bias)
+    if hidden.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError("lm_head_argmax: hidden and weight must be bfloat16")
+    if hidden.dim() != 2 or weight.dim() != 2 or hidden.shape[1] != weight.shape[1]:
+        raise RuntimeError(f"lm_head_argmax: shapes {tuple(hidden.shape)} x "
+                           f"{tuple(weight.shape)} do not match")
+    B, H = hidden.shape
+    V = weight.shape[0]
+    if hidden.stride(1) != 1 or hidden.stride(0) % 8 or hidden.data_ptr() % 16:
+        hidden = hidden.contiguous()
+    weight = _contig(weight)
+    if bias is not None:
+        bias = _contig(bias)
+    index = torch.empty(B, dtype=torch.int64, device=hidden.device)
+    value = torch.empty(B, dtype=torch.float32, device=hidden.device)
+    if B == 0:
+        return index, value
+    lib = _C.load()
+    ws_bytes = int(lib.ml_lm_head_argmax_workspace_bytes(B, V))
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=hidden.device)
+    _C.call("ml_lm_head_argmax", _C.ptr(hidden), hidden.stride(0), _C.ptr(weight),
+            weight.stride(0), _C.ptr(bias), _C.dtype_code(bias) if bias is not None else 0,
+            B, H, V, int(logit_dtype), _C.ptr(index), _C.ptr(value), _C.ptr(ws), ws_bytes,
+            _C.stream_of(hidden))
+    return index, value
+
+
 _SCHEMAS = {
+    "lm_head_argmax": "lm_head_argmax(Tensor hidden, Tensor weight, Tensor? bias, "
+                      "int logit_dtype) -> (Tensor, Tensor)",
     "rms_norm_forward": "rms_norm_forward(Tensor x, Tensor weight, float eps, str kernel_dir) "
                         "-> (Tensor, Tensor)",
     "rms_norm_backward": "rms_norm_backward(Tensor x, Tensor weight, Tensor grad_out, float eps, "
@@ -630,6 +664,7 @@ _SCHEMAS = {
 }
 
 _CUDA_IMPLS = {
+    "lm_head_argmax": lm_head_argmax_cuda,
     "rms_norm_forward": rms_norm_forward_cuda,
     "rms_norm_backward": rms_norm_backward_cuda,
     "swiglu_forward": swiglu_forward_cuda,
@@ -735,7 +770,13 @@ def _fake_impls():
                 torch.empty_like(ua), torch.empty_like(ub), torch.empty_like(da),
                 torch.empty_like(db))
 
+    def lm_argmax(hidden, weight, bias, logit_dtype):
+        B = hidden.shape[0]
+        return (torch.empty(B, dtype=torch.int64, device=hidden.device),
+                torch.empty(B, dtype=torch.float32, device=hidden.device))
+
     return {
+        "lm_head_argmax": lm_argmax,
         "lora_qkv_forward": lqkv_fwd,
         "lora_qkv_backward": lqkv_bwd,
         "lora_linear_forward": llin_fwd,

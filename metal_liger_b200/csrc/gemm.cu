@@ -299,6 +299,8 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.vocab = pr.N;
   prm.bias = pr.bias;
   prm.bias_dtype = pr.bias_dtype;
+  prm.part_i = pr.part_i;
+  prm.logit_dtype = pr.logit_dtype;
   prm.split_stride = pr.split_stride ? pr.split_stride : pr.M * pr.ldd;
   prm.err = device_error_word();
   const int64_t units = (int64_t)prm.m_tiles * prm.n_tiles * prm.splits;

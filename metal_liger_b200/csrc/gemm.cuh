@@ -38,6 +38,8 @@ enum Epi : int {
   EPI_STORE = 0,        // D = alpha*acc (+ beta*D), D bf16 or fp32
   EPI_PARTIAL = 1,      // split-K: fp32 partial [split][M][ldd] = alpha*acc
   EPI_FLCE = 2,         // fused linear-cross-entropy logits epilogue (BN = 256)
+  EPI_ARGMAX = 3,       // greedy decoding head: per tile, the row's largest logit (rounded
+                        // to the logit dtype) and the first column holding it
 };
 
 // Wait sites recorded in the device error word.
@@ -69,8 +71,11 @@ struct alignas(64) Params {
   float* part_s;           // [n_tiles][M] sum exp(logit - tile max)
   float* tgt;              // [M] target logit
   int64_t vocab;           // valid logit columns (= N)
-  const void* bias;        // optional [vocab] logit bias (EPI_FLCE)
+  const void* bias;        // optional [vocab] logit bias (EPI_FLCE, EPI_ARGMAX)
   int bias_dtype;
+  // EPI_ARGMAX (also uses part_m, vocab, bias)
+  int* part_i;             // [n_tiles][M] first column of the tile's row maximum
+  int logit_dtype;         // ML_DTYPE_* the logits are rounded to before comparing
   int* err;                // device error word (bounded-wait timeouts)
 };
 
@@ -193,6 +198,22 @@ __device__ __forceinline__ void add_bias32(const Params& p, float (&v)[32], int 
   }
 }
 
+// Logit value as a model whose logits have dtype `dt` would hold it.
+__device__ __forceinline__ float round_logit(float v, int dt) {
+  if (dt == ML_DTYPE_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == ML_DTYPE_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
+// torch.argmax order: NaN above every number, then larger values, then the
+// earlier column.
+__device__ __forceinline__ bool argmax_better(float a, int ca, float b, int cb) {
+  const bool na = a != a, nb = b != b;
+  if (na != nb) return na;
+  if (!na && a != b) return a > b;
+  return ca < cb;
+}
+
 // Drains one accumulator tile (this thread's TMEM lane = output row `row`,
 // BN fp32 columns starting at `taddr`) through the selected epilogue.
 template <int BN>
@@ -260,6 +281,29 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
         p.part_s[(int64_t)nt * p.M + row] = s;
         if (has_tgt) p.tgt[row] = tgt;
       }
+    }
+  } else if (p.epi == EPI_ARGMAX) {
+    const int col_base = nt * BN;
+    float best = 0.f;
+    int best_col = -1;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+      if (p.bias != nullptr) add_bias32(p, v, col_base + c * 32);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = col_base + c * 32 + j;
+        const float x = round_logit(v[j], p.logit_dtype);
+        if (col < p.vocab && (best_col < 0 || argmax_better(x, col, best, best_col))) {
+          best = x;
+          best_col = col;
+        }
+      }
+    }
+    if (row_ok) {
+      p.part_m[(int64_t)nt * p.M + row] = best;
+      p.part_i[(int64_t)nt * p.M + row] = best_col;
     }
   } else {
     float* partial_base = nullptr;
@@ -736,6 +780,9 @@ struct Problem {
   const void* bias = nullptr;
   int bias_dtype = 0;
   int64_t split_stride = 0;   // EPI_PARTIAL; 0 = M * ldd
+  // EPI_ARGMAX
+  int* part_i = nullptr;
+  int logit_dtype = 0;
 };
 
 // Builds tensor maps, picks the tile width and launches.  Returns ML_OK or an

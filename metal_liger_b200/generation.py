@@ -1,13 +1,253 @@
-"""Static-KV generator of the reference (generation.py:18-164) — out of scope here.
+"""Static-KV generator on CUDA (reference: generation.py:18-164).
 
-Generation is an inference side path, disabled by default in the reference's
-patcher (patch.py:188).  The name is kept so imports resolve; calling it raises.
+Same surface as the reference: ``MetalLigerStaticCache(model, batch_size,
+max_seq_len)``, ``MetalLigerGenerator(model).generate(input_ids,
+max_new_tokens=128, temperature=1.0, top_p=1.0, eos_token_id=None, **kwargs)``
+and ``patch_generator(model, force=False)``, with the reference's decoding
+rule: greedy (argmax) when ``temperature == 0`` or when ``temperature == 1.0
+and top_p == 1.0``, otherwise one multinomial draw from softmax(logits /
+temperature) (``top_p`` only selects between the two rules, as in the
+reference, generation.py:118-123).
+
+On B200:
+
+* the KV cache is two preallocated HBM buffers, [layers, batch, kv_heads,
+  max_seq_len, head_dim] for keys and for values (the reference's layout,
+  generation.py:36-45), handed to transformers 5.x as a ``Cache`` whose
+  per-layer views write the new positions in place and return the filled
+  prefix (generation.py:48-60);
+* the greedy step never forms the [batch, vocab] logits: the decoder's last
+  hidden state goes through ``metal_liger::lm_head_argmax``, one pass over
+  the lm_head weight on the tcgen05 GEMM core with an argmax epilogue that
+  rounds each logit to the model's logit dtype first, so the choice is the
+  reference's ``argmax(model(...).logits[:, -1, :])``;
+* the sampling step takes its logits from this library's GEMM (bf16, the
+  logit dtype of a bf16 model) and samples with torch;
+* generated ids go into one preallocated [batch, prompt + max_new_tokens]
+  device buffer instead of a ``torch.cat`` per token.
+
+The model is a transformers causal LM with a decoder at ``model.model`` (its
+forward returns ``last_hidden_state``) and a bias-free or biased
+``model.lm_head`` with a bf16 weight.
 """
 
+from __future__ import annotations
+
+import logging
+from typing import Optional
+
+import torch
 import torch.nn as nn
+from torch import Tensor
+
+try:  # transformers 5.x: a Cache is a list of per-layer cache objects
+    from transformers.cache_utils import Cache, CacheLayerMixin
+except ImportError:  # pragma: no cover - transformers is part of the image
+    Cache = object
+    CacheLayerMixin = object
+
+logger = logging.getLogger(__name__)
 
 
-def patch_generator(model: nn.Module) -> nn.Module:
-    raise NotImplementedError(
-        "metal_liger_b200 implements the fused training-op path only; the MPS static-KV "
-        "generator (use_optimized_generator=True) is not provided")
+def _text_config(model: nn.Module):
+    cfg = model.config
+    return getattr(cfg, "text_config", None) or getattr(cfg, "get_text_config", lambda: cfg)()
+
+
+class _StaticKVLayer(CacheLayerMixin):
+    """One decoder layer's view of the static buffers (transformers' per-layer
+    cache interface).  ``update`` writes positions [seen, seen + q) and returns
+    keys/values [0, seen + q), as the reference's cache does."""
+
+    is_compileable = False
+    is_sliding = False
+
+    def __init__(self, owner: "MetalLigerStaticCache", idx: int):
+        super().__init__()
+        self.owner = owner
+        self.idx = idx
+        self.keys = owner.key_cache[idx]
+        self.values = owner.value_cache[idx]
+        self.is_initialized = True
+        self.max_batch_size = owner.batch_size
+        self.max_cache_len = owner.max_seq_len
+
+    def lazy_initialization(self, key_states, value_states):  # buffers exist up front
+        return None
+
+    def update(self, key_states: Tensor, value_states: Tensor, *args, **kwargs):
+        return self.owner.update(key_states, value_states, self.idx)
+
+    def get_mask_sizes(self, query_length) -> tuple[int, int]:
+        q = query_length if isinstance(query_length, int) else int(query_length.shape[0])
+        return self.owner.seen_tokens + q, 0
+
+    def get_seq_length(self) -> int:
+        return self.owner.seen_tokens
+
+    def get_max_cache_shape(self) -> int:
+        return self.owner.max_seq_len
+
+
+class MetalLigerStaticCache(Cache):
+    """Static KV cache that fits the transformers Cache API (reference:
+    generation.py:18-66)."""
+
+    def __init__(self, model: nn.Module, batch_size: int, max_seq_len: int):
+        p = next(model.parameters())
+        self.device = p.device
+        self.dtype = p.dtype
+        cfg = _text_config(model)
+        self.config = cfg
+        self.num_layers = getattr(cfg, "num_hidden_layers", 28)
+        self.num_heads = getattr(cfg, "num_attention_heads", 16)
+        self.num_kv_heads = getattr(cfg, "num_key_value_heads", None) or self.num_heads
+        self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.num_heads
+        self.batch_size = int(batch_size)
+        self.max_seq_len = int(max_seq_len)
+        shape = (self.num_layers, self.batch_size, self.num_kv_heads, self.max_seq_len,
+                 self.head_dim)
+        self.key_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
+        self.value_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
+        self.seen_tokens = 0
+        super().__init__(layers=[_StaticKVLayer(self, i) for i in range(self.num_layers)])
+
+    def update(self, key_states: Tensor, value_states: Tensor, layer_idx: int,
+               cache_kwargs=None):
+        """Write the new positions of layer ``layer_idx`` and return its
+        keys/values up to the current length (reference generation.py:48-60)."""
+        seq_len = key_states.shape[-2]
+        start = self.seen_tokens
+        end = start + seq_len
+        if end > self.max_seq_len:
+            raise RuntimeError(f"MetalLigerStaticCache: {end} positions exceed max_seq_len "
+                               f"{self.max_seq_len}")
+        self.key_cache[layer_idx, :, :, start:end, :] = key_states
+        self.value_cache[layer_idx, :, :, start:end, :] = value_states
+        return (self.key_cache[layer_idx, :, :, :end, :],
+                self.value_cache[layer_idx, :, :, :end, :])
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        return self.seen_tokens
+
+    def get_max_length(self) -> int:
+        return self.max_seq_len
+
+    def get_max_cache_shape(self, layer_idx: int = 0) -> int:
+        return self.max_seq_len
+
+
+def _logit_code(dtype: torch.dtype) -> int:
+    from metal_liger_b200 import _C
+    return _C.dtype_code(dtype)
+
+
+class MetalLigerGenerator:
+    """Token generator with a static KV cache and a fused greedy head
+    (reference: generation.py:68-129)."""
+
+    def __init__(self, model: nn.Module):
+        self.model = model
+        self.device = next(model.parameters()).device
+        self.tokenizer = None
+        decoder = getattr(model, "model", None)
+        head = getattr(model, "lm_head", None)
+        if decoder is None or head is None or not hasattr(head, "weight"):
+            raise TypeError("MetalLigerGenerator needs a causal LM with .model (decoder) and "
+                            ".lm_head")
+        if head.weight.dtype != torch.bfloat16:
+            raise TypeError(f"MetalLigerGenerator: the fused head takes a bfloat16 lm_head "
+                            f"weight, not {head.weight.dtype}")
+        self.decoder = decoder
+        self.head = head
+
+    def _hidden_last(self, ids: Tensor, cache: MetalLigerStaticCache, kwargs) -> Tensor:
+        out = self.decoder(input_ids=ids, past_key_values=cache, use_cache=True,
+                           return_dict=True, **kwargs)
+        return out.last_hidden_state[:, -1, :]
+
+    def _greedy(self, h: Tensor) -> Tensor:
+        from metal_liger_b200 import _torch_library  # noqa: F401  (registers the ops)
+
+        idx, _ = torch.ops.metal_liger.lm_head_argmax(
+            h, self.head.weight, getattr(self.head, "bias", None),
+            _logit_code(self.head.weight.dtype))
+        return idx
+
+    def _logits(self, h: Tensor) -> Tensor:
+        """[B, V] logits in the head's dtype from this library's GEMM."""
+        from metal_liger_b200 import _C
+
+        w = self.head.weight
+        h = h.contiguous()
+        B, H = h.shape
+        V = w.shape[0]
+        out = torch.empty((B, V), dtype=torch.float32, device=h.device)
+        lib = _C.load()
+        segs = (_C.GemmSegment * 1)()
+        segs[0].a.ptr = h.data_ptr()
+        segs[0].a.ld = h.stride(0)
+        segs[0].a.mn_major = 0
+        segs[0].b.ptr = w.data_ptr()
+        segs[0].b.ld = w.stride(0)
+        segs[0].b.mn_major = 0
+        segs[0].k = H
+        ws_bytes = int(lib.ml_gemm_bf16_workspace_bytes(B, V, H))
+        ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=h.device)
+        _C.call("ml_gemm_bf16", B, V, segs, 1, out.data_ptr(), _C.dtype_code(torch.float32),
+                out.stride(0), 1.0, 0.0, ws.data_ptr(), ws_bytes, _C.stream_of(h))
+        bias = getattr(self.head, "bias", None)
+        if bias is not None:
+            out = out + bias.float()
+        return out.to(w.dtype)
+
+    @torch.inference_mode()
+    def generate(self, input_ids: Tensor, max_new_tokens: int = 128, temperature: float = 1.0,
+                 top_p: float = 1.0, eos_token_id: Optional[int] = None, **kwargs) -> Tensor:
+        """Prefill the prompt, then decode one token per step (reference
+        generation.py:74-129); returns [batch, prompt + generated] ids."""
+        batch_size, prompt_len = input_ids.shape
+        max_len = prompt_len + max_new_tokens
+        greedy = temperature == 0 or (temperature == 1.0 and top_p == 1.0)
+        cache = MetalLigerStaticCache(self.model, batch_size, max_len)
+        ids = torch.empty((batch_size, max_len), dtype=input_ids.dtype, device=input_ids.device)
+        ids[:, :prompt_len] = input_ids
+
+        # Prefill; the first token is the argmax in every mode (reference :99-101).
+        h = self._hidden_last(input_ids, cache, kwargs)
+        cache.seen_tokens += prompt_len
+        next_token = self._greedy(h).to(ids.dtype).view(batch_size, 1)
+        ids[:, prompt_len:prompt_len + 1] = next_token
+        n = prompt_len + 1
+
+        for _ in range(max_new_tokens - 1):
+            if eos_token_id is not None and bool((next_token == eos_token_id).all()):
+                break
+            h = self._hidden_last(next_token, cache, kwargs)
+            cache.seen_tokens += 1
+            if greedy:
+                next_token = self._greedy(h).to(ids.dtype).view(batch_size, 1)
+            else:
+                probs = torch.softmax(self._logits(h) / temperature, dim=-1)
+                next_token = torch.multinomial(probs, num_samples=1).to(ids.dtype)
+            ids[:, n:n + 1] = next_token
+            n += 1
+        return ids[:, :n]
+
+
+def patch_generator(model: nn.Module, force: bool = False) -> nn.Module:
+    """Replace ``model.generate`` with ``MetalLigerGenerator.generate``
+    (reference generation.py:131-164): skipped while the model is training
+    unless ``force``; the original stays at ``model._orig_generate``.
+
+    Like the reference's, this generator ignores GenerationConfig,
+    attention masks / padding and the other generate() arguments."""
+    if model.training and not force:
+        logger.info("MetalLiger: skipping the generator patch - the model is in training mode "
+                    "(the custom generator does not do GRPO/RL sampling); force=True overrides")
+        return model
+    generator = MetalLigerGenerator(model)
+    if not hasattr(model, "_orig_generate"):
+        model._orig_generate = getattr(model, "generate", None)
+    model.generate = generator.generate
+    return model

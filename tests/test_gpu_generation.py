@@ -1,0 +1,188 @@
+"""Fused greedy head (metal_liger::lm_head_argmax, the tcgen05 GEMM with the
+argmax epilogue) and the static-KV generator on the GPU.
+
+The head's choice is an index, so it is checked exactly: the oracle
+(oracle/generation.py:argmax_rounded) forms fp64 logits, rounds them to fp32
+and then to the logit dtype, and takes torch.argmax.  The kernel accumulates
+in fp32 in another order, so a logit within one fp32 rounding of a
+logit-dtype rounding boundary may land one ulp (of the logit dtype) away from
+the oracle's (fp32 logits: a few fp32 ulps, bounded here by 1e-5 relative);
+the tests therefore require (a) the logit the kernel picked to be the
+oracle's maximum up to that tolerance, and (b) the same index wherever the
+oracle's best logit beats the runner-up by more than twice the tolerance.  Exact ties
+(duplicate vocabulary rows) and NaN follow torch.argmax: the lowest index.
+"""
+
+import pytest
+import torch
+import torch.nn as nn
+
+from oracle import generation as OG
+from metal_liger_b200 import _torch_library  # noqa: F401  (registers metal_liger:: ops)
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _ulp(x: torch.Tensor, dt: torch.dtype) -> torch.Tensor:
+    mant = {torch.bfloat16: 8, torch.float16: 11, torch.float32: 24}[dt]
+    e = torch.floor(torch.log2(x.abs().clamp(min=1e-30)))
+    return torch.pow(2.0, e - (mant - 1))
+
+
+def _check(idx, val, hidden, weight, dt, bias=None):
+    ridx, rval, logits = OG.argmax_rounded(hidden.cpu(), weight.cpu(), dt,
+                                           None if bias is None else bias.cpu())
+    idx, val = idx.cpu(), val.cpu()
+    picked = logits.gather(1, idx[:, None])[:, 0]
+    # one ulp of the logit dtype, or (fp32 logits) the fp32 accumulation-order
+    # difference, 1e-5 relative
+    tol = torch.maximum(_ulp(rval, dt), 1e-5 * rval.abs().clamp(min=1.0))
+    assert torch.all((rval - picked) <= tol), "kernel picked a logit below the maximum"
+    top2 = logits.topk(2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]) > 2 * tol
+    assert torch.equal(idx[clear], ridx[clear]), "index differs on a clearly separated row"
+    assert torch.all((val - rval).abs() <= tol)
+
+
+@pytest.mark.parametrize("B,H,V,dt", [
+    (1, 4096, 151936, torch.bfloat16),   # Qwen3-VL-8B lm_head, one sequence (GEMV kernel)
+    (2, 520, 20000, torch.bfloat16),     # GEMV kernel, hidden not a multiple of 256
+    (2, 2048, 151936, torch.float32),    # GEMV kernel, fp32 logits
+    (1, 256, 1001, torch.bfloat16),      # small vocabulary: tensor-core path at batch 1
+    (3, 256, 1001, torch.bfloat16),      # ragged vocabulary tile
+    (16, 512, 5000, torch.float16),
+    (8, 128, 100, torch.float32),        # vocabulary narrower than one tile
+    (130, 256, 3000, torch.bfloat16),    # two row tiles (CTA-pair kernel by default)
+])
+def test_lm_head_argmax_against_oracle(B, H, V, dt):
+    g = torch.Generator(device=DEV).manual_seed(B * 7 + V)
+    hidden = torch.randn(B, H, generator=g, device=DEV).bfloat16()
+    weight = (torch.randn(V, H, generator=g, device=DEV) * 0.05).bfloat16()
+    idx, val = torch.ops.metal_liger.lm_head_argmax(hidden, weight, None, CODES[dt])
+    assert idx.dtype == torch.int64 and idx.shape == (B,)
+    _check(idx, val, hidden, weight, dt)
+
+
+def test_lm_head_argmax_bias_strided_ties_and_nan():
+    g = torch.Generator(device=DEV).manual_seed(3)
+    H, V = 256, 2048
+    full = torch.randn(4, 3, H, generator=g, device=DEV).bfloat16()
+    hidden = full[:, -1, :]                                  # strided rows, as h[:, -1, :]
+    # the GEMV kernel (batch <= 2) with the same bias, on a vocabulary large
+    # enough to take it
+    w_big = (torch.randn(30000, H, generator=g, device=DEV) * 0.05).bfloat16()
+    b_big = torch.randn(30000, generator=g, device=DEV).bfloat16()
+    i2, v2 = torch.ops.metal_liger.lm_head_argmax(hidden[:2], w_big, b_big, 1)
+    _check(i2, v2, hidden[:2], w_big, torch.bfloat16, b_big.float())
+    weight = (torch.randn(V, H, generator=g, device=DEV) * 0.05).bfloat16()
+    bias = torch.randn(V, generator=g, device=DEV) * 0.1
+    idx, val = torch.ops.metal_liger.lm_head_argmax(hidden, weight, bias, 1)
+    _check(idx, val, hidden, weight, torch.bfloat16, bias)
+    # exact ties: the row that wins for sequence 0 is duplicated at a higher
+    # and a lower index; the lowest copy must win
+    win = int(idx[0])
+    w2 = weight.clone()
+    lo, hi = (win // 2, min(V - 1, win + 700))
+    w2[hi] = weight[win]
+    w2[lo] = weight[win]
+    idx2, _ = torch.ops.metal_liger.lm_head_argmax(hidden, w2, None, 1)
+    assert int(idx2[0]) == min(lo, win)
+    # NaN logits win, first NaN first (torch.argmax)
+    w3 = weight.clone()
+    w3[1500] = float("nan")
+    w3[900] = float("nan")
+    idx3, _ = torch.ops.metal_liger.lm_head_argmax(hidden, w3, None, 1)
+    assert idx3.tolist() == [900] * 4
+    wb = w_big.clone()
+    wb[29000] = float("nan")
+    wb[12345] = float("nan")
+    idx4, _ = torch.ops.metal_liger.lm_head_argmax(hidden[:1], wb, None, 1)
+    assert idx4.tolist() == [12345]
+    win = int(torch.ops.metal_liger.lm_head_argmax(hidden[:1], w_big, None, 1)[0][0])
+    wt = w_big.clone()
+    wt[win // 3] = w_big[win]
+    assert int(torch.ops.metal_liger.lm_head_argmax(hidden[:1], wt, None, 1)[0][0]) == win // 3
+
+
+def test_lm_head_argmax_errors_and_empty():
+    w = torch.randn(64, 32, device=DEV).bfloat16()
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        torch.ops.metal_liger.lm_head_argmax(torch.randn(2, 32, device=DEV), w, None, 1)
+    with pytest.raises(RuntimeError, match="do not match"):
+        torch.ops.metal_liger.lm_head_argmax(torch.randn(2, 16, device=DEV).bfloat16(), w,
+                                             None, 1)
+    idx, val = torch.ops.metal_liger.lm_head_argmax(torch.empty(0, 32, device=DEV).bfloat16(),
+                                                    w, None, 1)
+    assert idx.shape == (0,) and val.shape == (0,)
+
+
+class _CausalLM(nn.Module):
+    def __init__(self, text_model, vocab, hidden):
+        super().__init__()
+        self.model = text_model
+        self.config = text_model.config
+        self.lm_head = nn.Linear(hidden, vocab, bias=False, device=DEV, dtype=torch.bfloat16)
+
+
+def _model(seed=0, layers=2, vocab=1000):
+    from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+    from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+    cfg = Qwen3VLTextConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=layers,
+                            num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                            vocab_size=vocab, rms_norm_eps=1e-6,
+                            rope_parameters={"rope_type": "default", "rope_theta": 5e6,
+                                             "mrope_section": [12, 10, 10]})
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    with torch.device(DEV):
+        text = Qwen3VLTextModel(cfg).to(torch.bfloat16)
+    m = _CausalLM(text, vocab, 256)
+    with torch.no_grad():
+        m.lm_head.weight.normal_(0, 0.5)
+    return m.eval()
+
+
+def test_generator_matches_reference_loop():
+    """Greedy tokens equal the reference loop's (oracle loop on the same GPU
+    model with transformers' DynamicCache and the model's own lm_head); where
+    they part, the reference's two best logits at that step are within one
+    bf16 ulp of each other (a rounding-order near-tie), never further."""
+    from metal_liger_b200.generation import MetalLigerGenerator
+
+    m = _model()
+    ids = torch.randint(0, 1000, (3, 6), generator=torch.Generator().manual_seed(4)).to(DEV)
+    got = MetalLigerGenerator(m).generate(ids, max_new_tokens=24)
+    ref = OG.generate(m, ids, max_new_tokens=24)
+    assert got.shape == ref.shape == (3, 30)
+    for b in range(3):
+        diff = (got[b] != ref[b]).nonzero()
+        if diff.numel() == 0:
+            continue
+        t = int(diff[0])
+        with torch.no_grad():
+            h = m.model(input_ids=ref[b:b + 1, :t]).last_hidden_state[:, -1]
+            logits = m.lm_head(h).float()[0]
+        top2 = logits.topk(2).values
+        assert float(top2[0] - top2[1]) <= float(_ulp(top2[0:1], torch.bfloat16)[0]), \
+            f"row {b} diverges at {t} without a near-tie"
+
+
+def test_generator_eos_sampling_and_patch():
+    from metal_liger_b200.generation import patch_generator
+
+    m = _model(seed=1)
+    ids = torch.randint(0, 1000, (1, 5), generator=torch.Generator().manual_seed(6)).to(DEV)
+    patch_generator(m)
+    out = m.generate(ids, max_new_tokens=8)
+    assert out.shape == (1, 13) and torch.equal(out[:, :5], ids)
+    eos = int(out[0, 7])
+    stopped = m.generate(ids, max_new_tokens=8, eos_token_id=eos)
+    first = int((out[0, 5:] == eos).nonzero()[0]) + 5
+    assert torch.equal(stopped, out[:, :first + 1])
+    torch.manual_seed(0)
+    sampled = m.generate(ids, max_new_tokens=8, temperature=0.8)
+    assert sampled.shape == (1, 13) and int(sampled.max()) < 1000 and int(sampled.min()) >= 0
+    assert int(sampled[0, 5]) == int(out[0, 5])  # the first token is always the argmax

@@ -5,6 +5,7 @@ import torch
 
 from conftest import golden_names, load_golden
 from oracle import ops as O
+from metal_liger_b200 import _torch_library  # noqa: F401  (registers metal_liger:: ops)
 from tolerances import assert_close
 
 pytestmark = pytest.mark.gpu
