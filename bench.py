@@ -802,6 +802,8 @@ class FullStep:
     # adapters, F.cross_entropy) in fp32 with ONE decoder layer; tokens/s are
     # scaled to 36 layers by the FLOP ratio (labelled as extrapolated).
     cpu_extrapolated = True
+    cpu_desc = ("the unfused step with ONE decoder layer (transformers modules, PEFT-layout "
+                "adapters, F.cross_entropy, fp32)")
 
     def cpu_inputs(self, tokens, seed=9):
         if not hasattr(self, "_cpu_model"):
@@ -842,8 +844,208 @@ class FullStep:
         return self.flops_per_token(1) / self.flops_per_token(self.L)
 
 
+class Generate:
+    """Greedy decoding with the static-KV generator (the reference's
+    generation.py:68-129 path) on the Qwen3-VL-8B text decoder.
+
+    transformers' ``Qwen3VLTextModel`` at the 8B text shape, random init,
+    bf16, patched for inference (fused RMSNorm incl. the per-head q/k norms,
+    fused SwiGLU, RoPE inside attention), with a bf16 lm_head.  A step is one
+    ``MetalLigerGenerator.generate`` call: a 128-token prompt, then 64 new
+    tokens for one sequence, greedy.  Decode is HBM-bound on the weights
+    (16.4 GB per token); the roofline line is this library's kernel on that
+    path, the fused lm_head argmax (one pass over the 1.24 GB lm_head per
+    token).  The decoder's projections and attention are transformers
+    modules (cuBLAS / SDPA, library kernels).  Decoding replays a CUDA graph
+    of one self-advancing decode step per token (the generator's default)."""
+
+    name = "generate"
+    bound = "hbm"
+    dtype = "bf16"
+    L, H, NH, NKV, D, I, V = 36, 4096, 32, 8, 128, 12288, 151936
+    PROMPT, NEW, THETA = 128, 64, 5e6
+    dominant = "lm_head_argmax"
+
+    def __init__(self):
+        self.batch = 1
+        self.tokens = self.batch * self.NEW           # generated tokens per step
+        self.bytes = {"lm_head_argmax": self.V * self.H * 2}
+        self.launches_per_step = None
+
+    def flops_per_token(self, layers):
+        H, I = self.H, self.I
+        q, kv = self.NH * self.D, self.NKV * self.D
+        return layers * 2 * (H * q + 2 * H * kv + q * H + 3 * H * I) + 2 * H * self.V
+
+    def config(self):
+        return {"workload": "generate (static-KV greedy generator): Qwen3-VL-8B text "
+                            "decoder, transformers Qwen3VLTextModel random init, bf16, 36 layers, "
+                            "hidden 4096, 32/8 heads x 128, SwiGLU 12288, vocab 151936; prompt "
+                            f"{self.PROMPT} tokens, {self.NEW} new tokens, batch 1, greedy",
+                "model": "Qwen3-VL-8B (text decoder)", "layers": self.L,
+                "global_batch": self.batch, "seq_len": self.PROMPT + self.NEW,
+                "tokens_per_step": self.tokens, "parallelism": "replicas",
+                "metric_note": "value = generated tokens/s including the prefill of each call",
+                "l2": "inputs larger than L2 (16.4 GB of weights streamed per token)"}
+
+    def _build(self, device, layers, dtype=torch.bfloat16, fused=True, seed=1240):
+        import torch.nn as nn
+        from transformers.models.qwen3_vl.configuration_qwen3_vl import Qwen3VLTextConfig
+        from transformers.models.qwen3_vl.modeling_qwen3_vl import Qwen3VLTextModel
+
+        cfg = Qwen3VLTextConfig(hidden_size=self.H, intermediate_size=self.I,
+                                num_hidden_layers=layers, num_attention_heads=self.NH,
+                                num_key_value_heads=self.NKV, head_dim=self.D, vocab_size=self.V,
+                                rms_norm_eps=1e-6, max_position_embeddings=4096,
+                                rope_parameters={"rope_type": "default", "rope_theta": self.THETA,
+                                                 "mrope_section": [24, 20, 20]})
+        cfg._attn_implementation = "sdpa"
+        torch.manual_seed(seed)
+        holder = nn.Module()
+        with torch.device(device):
+            holder.model = Qwen3VLTextModel(cfg).to(dtype)
+            holder.lm_head = nn.Linear(self.H, self.V, bias=False).to(dtype)
+            with torch.no_grad():
+                holder.lm_head.weight.normal_(0.0, 0.02)
+        holder.config = cfg
+        if fused:
+            from metal_liger_b200 import apply_metal_liger_to_qwen3vl
+
+            apply_metal_liger_to_qwen3vl(holder, fuse_lora=False, fuse_qk_norm=True,
+                                         fuse_rope_in_attention=True)
+        holder.eval()
+        for p in holder.parameters():
+            p.requires_grad_(False)
+        return holder
+
+    def make_inputs(self, device, seed=1241):
+        from metal_liger_b200.generation import MetalLigerGenerator
+
+        self.model = self._build(device, self.L)
+        outer = self
+
+        class _Timed(MetalLigerGenerator):
+            # The head is timed where it runs eagerly (prefill and the steps
+            # before the decode graph is captured); inside the captured step
+            # events cannot be timed.
+            def _greedy(self, h):
+                if torch.cuda.is_current_stream_capturing():
+                    return super()._greedy(h)
+                return outer._timer("lm_head_argmax", super()._greedy, h)
+
+        self.gen = _Timed(self.model)
+        self._timer = plain
+        g = torch.Generator(device=device).manual_seed(seed)
+        ids = torch.randint(0, self.V, (self.batch, self.PROMPT), generator=g, device=device)
+        return {"ids": ids}
+
+    def step(self, t, timer=plain):
+        self._timer = timer
+        try:
+            return self.gen.generate(t["ids"], max_new_tokens=self.NEW)
+        finally:
+            self._timer = plain
+
+    def e2e_setup(self, device):
+        g = torch.Generator().manual_seed(82)
+        host = {"ids": torch.randint(0, self.V, (self.batch, self.PROMPT), generator=g)
+                .pin_memory()}
+        dev = {"ids": torch.empty_like(host["ids"], device=device)}
+        host_out = {"out": torch.empty((self.batch, self.PROMPT + self.NEW), dtype=torch.int64,
+                                       pin_memory=True)}
+        return {"host": host, "dev": dev, "host_out": host_out,
+                "h2d": host["ids"].numel() * 8, "d2h": host_out["out"].numel() * 8}
+
+    def e2e_step(self, s):
+        from metal_liger_b200.generation import MetalLigerGenerator
+
+        if not hasattr(self, "_plain_gen"):
+            self._plain_gen = MetalLigerGenerator(self.model)
+        s["dev"]["ids"].copy_(s["host"]["ids"], non_blocking=True)
+        out = self._plain_gen.generate(s["dev"]["ids"], max_new_tokens=self.NEW)
+        s["host_out"]["out"][:, :out.shape[1]].copy_(out, non_blocking=True)
+
+    def extra_measurements(self, device, steps=3):
+        """The reference's decode loop run on the same GPU model for
+        comparison: transformers' DynamicCache, [batch, vocab] logits from
+        the lm_head, torch.argmax and a torch.cat per token
+        (generation.py:88-127), timed with CUDA events."""
+        from transformers.cache_utils import DynamicCache
+
+        m = self.model
+
+        @torch.inference_mode()
+        def loop(ids):
+            cache = DynamicCache()
+            h = m.model(input_ids=ids, past_key_values=cache, use_cache=True).last_hidden_state
+            nxt = torch.argmax(m.lm_head(h[:, -1:, :])[:, -1, :], dim=-1, keepdim=True)
+            out = torch.cat([ids, nxt], dim=-1)
+            for _ in range(self.NEW - 1):
+                h = m.model(input_ids=nxt, past_key_values=cache, use_cache=True).last_hidden_state
+                nxt = torch.argmax(m.lm_head(h[:, -1:, :])[:, -1, :], dim=-1, keepdim=True)
+                out = torch.cat([out, nxt], dim=-1)
+            return out
+
+        g = torch.Generator(device=device).manual_seed(83)
+        ids = torch.randint(0, self.V, (self.batch, self.PROMPT), generator=g, device=device)
+        loop(ids)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            ref = loop(ids)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        ours = self.gen.generate(ids, max_new_tokens=self.NEW)
+        return {"reference_loop_on_gpu": {
+            "value": self.tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+            "what": "the reference's decode loop (transformers DynamicCache, full-vocabulary "
+                    "logits, argmax, torch.cat) on the same patched model and GPU",
+            "same_tokens": bool(torch.equal(ref, ours))}}
+
+    # CPU baseline: the reference's decode loop (oracle/generation.py: a
+    # transformers KV cache, full-vocabulary logits, argmax, torch.cat) in
+    # fp32 with ONE decoder layer; tokens/s scaled to 36 layers by the FLOP
+    # ratio (labelled as extrapolated).
+    cpu_extrapolated = True
+    cpu_desc = ("the reference's greedy decode loop (transformers KV cache, full-vocabulary "
+                "logits, argmax, torch.cat; oracle/generation.py) with ONE decoder layer, fp32")
+    metric = "greedy decode tokens/s (static-KV generator, Qwen3-VL-8B text)"
+    e2e_api = ("MetalLigerGenerator.generate from pinned host prompt ids; the generated ids "
+               "copied back to pinned host memory every step")
+
+    def cpu_inputs(self, tokens, seed=10):
+        if not hasattr(self, "_cpu_model"):
+            self._cpu_model = self._build("cpu", 1, dtype=torch.float32, fused=False)
+        g = torch.Generator().manual_seed(seed)
+        return {"ids": torch.randint(0, self.V, (1, self.PROMPT), generator=g),
+                "new": max(1, int(tokens))}
+
+    def cpu_step(self, c):
+        import sys
+
+        from oracle import generation as OG
+
+        m = self._cpu_model
+        mod = sys.modules[type(m.model.layers[0].self_attn).__module__]
+        orig = getattr(mod, "_metal_liger_original_rope", None)
+        fused = mod.apply_rotary_pos_emb
+        if orig is not None:
+            mod.apply_rotary_pos_emb = orig
+        try:
+            OG.generate(m, c["ids"], max_new_tokens=c["new"])
+        finally:
+            mod.apply_rotary_pos_emb = fused
+
+    def cpu_scale(self):
+        return self.flops_per_token(1) / self.flops_per_token(self.L)
+
+
+METRIC = "fwd+bwd tokens/s per fused op at Qwen3-VL shapes"
+
 WORKLOADS = {"swiglu_rope": SwigluRope, "rmsnorm": RmsNorm, "flce": Flce, "lora": Lora,
-             "c5_step": FullStep}
+             "c5_step": FullStep, "generate": Generate}
 
 
 def _register_optional_workloads():
@@ -946,13 +1148,12 @@ def run_reference_arm(args, wl):
               f"torch CPU fp32 oracle restating the reference ops, TORCHDYNAMO_DISABLE=1")
     if getattr(wl, "cpu_extrapolated", False):
         value *= wl.cpu_scale()
-        sample = (f"{tokens} tokens per step of the unfused step with ONE decoder layer "
-                  f"(transformers modules, PEFT-layout adapters, F.cross_entropy, fp32); "
+        sample = (f"{tokens} tokens per step of {wl.cpu_desc}; "
                   f"tokens/s extrapolated to {wl.L} layers by the FLOP ratio "
                   f"{wl.cpu_scale():.4f}")
     line = {
         "impl": "reference",
-        "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
+        "metric": getattr(wl, "metric", METRIC),
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * wl.tokens / value,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype,
@@ -1097,6 +1298,10 @@ def run_gpu_arm(args, wl):
                               tf / float(peaks.get("bf16_tflops_sustained", 1))})
         per_kernel[k] = entry
 
+    extra = None
+    if rank == 0 and hasattr(wl, "extra_measurements"):
+        extra = wl.extra_measurements(device)
+
     line = None
     if rank == 0:
         cpu = None
@@ -1106,14 +1311,13 @@ def run_gpu_arm(args, wl):
                       f"(torch fp32 restatement of the reference ops), {cores} threads")
             if getattr(wl, "cpu_extrapolated", False):
                 v *= wl.cpu_scale()
-                sample = (f"{tok} tokens x {st} steps of the unfused step with ONE decoder layer "
-                          f"(transformers modules, PEFT-layout adapters, F.cross_entropy, fp32) "
-                          f"on {cores} threads; tokens/s extrapolated to {wl.L} layers by the "
-                          f"FLOP ratio {wl.cpu_scale():.4f}")
+                sample = (f"{tok} tokens x {st} steps of {wl.cpu_desc} on {cores} threads; "
+                          f"tokens/s extrapolated to {wl.L} layers by the FLOP ratio "
+                          f"{wl.cpu_scale():.4f}")
             cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                    "sample": sample}
         line = {
-            "metric": "fwd+bwd tokens/s per fused op at Qwen3-VL shapes",
+            "metric": getattr(wl, "metric", METRIC),
             "value": value,
             "unit": "tokens/s",
             "n_gpus": world,
@@ -1147,12 +1351,14 @@ def run_gpu_arm(args, wl):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "api": "public autograd Functions (metal_liger_b200.ops.*), pinned host "
-                           "buffers, H2D inputs + D2H all outputs per step"},
+                    "api": getattr(wl, "e2e_api", "public autograd Functions (metal_liger_b200.ops.*), pinned "
+                                   "host buffers, H2D inputs + D2H all outputs per step")},
             "gpu_launches": (per_step_launches * args.steps
                              if per_step_launches is not None else None),
             "clocks": clk.summary(),
         }
+        if extra:
+            line.update(extra)
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()

@@ -18,9 +18,12 @@ On B200:
   prefix (generation.py:48-60);
 * the greedy step never forms the [batch, vocab] logits: the decoder's last
   hidden state goes through ``metal_liger::lm_head_argmax``, one pass over
-  the lm_head weight on the tcgen05 GEMM core with an argmax epilogue that
-  rounds each logit to the model's logit dtype first, so the choice is the
-  reference's ``argmax(model(...).logits[:, -1, :])``;
+  the lm_head weight (an HBM-streaming GEMV for batch <= 2, else the tcgen05
+  GEMM core with an argmax epilogue) that rounds each logit to the model's
+  logit dtype first, so the choice is the reference's
+  ``argmax(model(...).logits[:, -1, :])``;
+* for Qwen3-VL text prompts the decoder gets explicit [3, B, q] positions,
+  which skips its per-forward device-to-host sync;
 * the sampling step takes its logits from this library's GEMM (bf16, the
   logit dtype of a bf16 model) and samples with torch;
 * generated ids go into one preallocated [batch, prompt + max_new_tokens]
@@ -110,12 +113,24 @@ class MetalLigerStaticCache(Cache):
         self.key_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
         self.value_cache = torch.zeros(shape, device=self.device, dtype=self.dtype)
         self.seen_tokens = 0
+        # Set while decoding on a CUDA graph: the int64 [1] device tensor
+        # holding the position being written (see MetalLigerGenerator).
+        self.graph_pos: Optional[Tensor] = None
         super().__init__(layers=[_StaticKVLayer(self, i) for i in range(self.num_layers)])
 
     def update(self, key_states: Tensor, value_states: Tensor, layer_idx: int,
                cache_kwargs=None):
         """Write the new positions of layer ``layer_idx`` and return its
-        keys/values up to the current length (reference generation.py:48-60)."""
+        keys/values up to the current length (reference generation.py:48-60).
+
+        With ``graph_pos`` set (one token per call, decoding on a CUDA graph)
+        the position comes from that device tensor and the whole
+        ``max_seq_len`` buffers are returned; the caller's attention mask
+        hides the positions not yet written."""
+        if self.graph_pos is not None:
+            self.key_cache[layer_idx].index_copy_(2, self.graph_pos, key_states)
+            self.value_cache[layer_idx].index_copy_(2, self.graph_pos, value_states)
+            return self.key_cache[layer_idx], self.value_cache[layer_idx]
         seq_len = key_states.shape[-2]
         start = self.seen_tokens
         end = start + seq_len
@@ -160,10 +175,23 @@ class MetalLigerGenerator:
                             f"weight, not {head.weight.dtype}")
         self.decoder = decoder
         self.head = head
+        # Qwen3-VL text decoders take [3, B, q] multimodal-RoPE ids; for a text
+        # prompt all three rows are the plain positions.  Passing them (instead
+        # of letting the decoder build them) skips the decoder's
+        # packed-sequence probe, a device-to-host sync per forward, so the host
+        # can queue the next step while the GPU runs this one.
+        cfg = _text_config(model)
+        rope = getattr(cfg, "rope_parameters", None) or getattr(cfg, "rope_scaling", None) or {}
+        self._mrope = isinstance(rope, dict) and "mrope_section" in rope
 
     def _hidden_last(self, ids: Tensor, cache: MetalLigerStaticCache, kwargs) -> Tensor:
+        extra = dict(kwargs)
+        if self._mrope and not kwargs:
+            q = ids.shape[1]
+            pos = torch.arange(cache.seen_tokens, cache.seen_tokens + q, device=ids.device)
+            extra["position_ids"] = pos.view(1, 1, q).expand(3, ids.shape[0], q)
         out = self.decoder(input_ids=ids, past_key_values=cache, use_cache=True,
-                           return_dict=True, **kwargs)
+                           return_dict=True, **extra)
         return out.last_hidden_state[:, -1, :]
 
     def _greedy(self, h: Tensor) -> Tensor:
@@ -201,11 +229,104 @@ class MetalLigerGenerator:
             out = out + bias.float()
         return out.to(w.dtype)
 
+    # ------------------------------------------------------------------
+    # Greedy decode on a CUDA graph.  One decode step is captured once and
+    # replayed per token; it advances itself: the device scalar `pos` (the
+    # position of the token fed in) drives the KV write (index_copy_), the
+    # RoPE positions (a view of it) and the [B, 1, 1, max_len] boolean
+    # attention mask (index_fill_ at pos; positions not yet written stay
+    # False), and the step writes its token into the output buffer at pos + 1
+    # and into the input buffer of the next replay.  No host work or
+    # device-to-host copy happens per token, so the decoder's ~20 kernels per
+    # layer run back to back instead of at the host's launch rate.
+    # ------------------------------------------------------------------
+    _GRAPH_WARMUP = 2       # eager steps before capture (library workspaces)
+    _EOS_CHECK_EVERY = 16   # replays between end-of-sequence checks
+
+    def _static_step(self, st):
+        cache, tok, pos, mask, out = st["cache"], st["tok"], st["pos"], st["mask"], st["out"]
+        B = tok.shape[0]
+        mask.index_fill_(3, pos, True)
+        extra = {"position_ids": pos.view(1, 1, 1).expand(3, B, 1)} if self._mrope else {}
+        h = self.decoder(input_ids=tok, attention_mask=mask, past_key_values=cache,
+                         use_cache=True, return_dict=True, **extra).last_hidden_state[:, -1, :]
+        tok.copy_(self._greedy(h).view(B, 1))
+        out.index_copy_(1, pos + 1, tok)
+        pos.add_(1)
+
+    @staticmethod
+    def _all_eos_at(out: Tensor, lo: int, hi: int, eos_token_id) -> Optional[int]:
+        """First position p in [lo, hi) where every sequence holds eos."""
+        if eos_token_id is None or hi <= lo:
+            return None
+        hit = (out[:, lo:hi] == eos_token_id).all(dim=0).nonzero()
+        return lo + int(hit[0]) if hit.numel() else None
+
+    def _decode_static(self, cache, ids, n, steps, eos_token_id, capture: bool) -> int:
+        """Greedy decode of `steps` tokens after position n - 1 (the prefill's
+        token); returns the number of ids filled.  `capture` replays a CUDA
+        graph of the step; without it the same step runs eagerly."""
+        B, L = ids.shape
+        dev = ids.device
+        pos = torch.full((1,), n - 1, dtype=torch.int64, device=dev)
+        mask = torch.zeros((B, 1, 1, L), dtype=torch.bool, device=dev)
+        mask[..., :n - 1] = True
+        st = {"cache": cache, "tok": ids[:, n - 1:n].clone(), "pos": pos, "mask": mask,
+              "out": ids}
+        cache.graph_pos = pos
+        done = 0
+        try:
+            stop = self._all_eos_at(ids, n - 1, n, eos_token_id)
+            if stop is not None:
+                return stop + 1
+            warm = min(steps, self._GRAPH_WARMUP if capture else steps)
+            side = torch.cuda.Stream(device=dev) if capture else None
+            if side is not None:
+                side.wait_stream(torch.cuda.current_stream(dev))
+            ctx = torch.cuda.stream(side) if side is not None else _nullcontext()
+            with ctx:
+                for _ in range(warm):
+                    self._static_step(st)
+                    done += 1
+                    stop = self._all_eos_at(ids, n - 1 + done, n + done, eos_token_id)
+                    if stop is not None:
+                        break
+            if side is not None:
+                torch.cuda.current_stream(dev).wait_stream(side)
+            if stop is not None:
+                return stop + 1
+            if done < steps:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    self._static_step(st)
+                checked = n + done
+                while done < steps:
+                    graph.replay()
+                    done += 1
+                    if eos_token_id is not None and (done % self._EOS_CHECK_EVERY == 0
+                                                     or done == steps):
+                        stop = self._all_eos_at(ids, checked, n + done, eos_token_id)
+                        checked = n + done
+                        if stop is not None:
+                            return stop + 1
+                del graph
+            return n + done
+        finally:
+            cache.graph_pos = None
+            cache.seen_tokens = n - 1 + done
+
     @torch.inference_mode()
     def generate(self, input_ids: Tensor, max_new_tokens: int = 128, temperature: float = 1.0,
-                 top_p: float = 1.0, eos_token_id: Optional[int] = None, **kwargs) -> Tensor:
+                 top_p: float = 1.0, eos_token_id: Optional[int] = None,
+                 cuda_graph: Optional[bool] = None, **kwargs) -> Tensor:
         """Prefill the prompt, then decode one token per step (reference
-        generation.py:74-129); returns [batch, prompt + generated] ids."""
+        generation.py:74-129); returns [batch, prompt + generated] ids.
+
+        ``cuda_graph`` (not in the reference; default: on for greedy decoding
+        of text prompts on a CUDA device) decodes on a replayed CUDA graph of
+        the step; the tokens are the same as the eager loop's up to
+        near-ties at the logits' rounding (the attention then runs over the
+        full static buffers under a mask)."""
         batch_size, prompt_len = input_ids.shape
         max_len = prompt_len + max_new_tokens
         greedy = temperature == 0 or (temperature == 1.0 and top_p == 1.0)
@@ -220,6 +341,13 @@ class MetalLigerGenerator:
         ids[:, prompt_len:prompt_len + 1] = next_token
         n = prompt_len + 1
 
+        if cuda_graph is None:
+            cuda_graph = ids.device.type == "cuda" and max_new_tokens > self._GRAPH_WARMUP + 2
+        if greedy and not kwargs and cuda_graph and max_new_tokens > 1:
+            filled = self._decode_static(cache, ids, n, max_new_tokens - 1, eos_token_id,
+                                         capture=ids.device.type == "cuda")
+            return ids[:, :filled]
+
         for _ in range(max_new_tokens - 1):
             if eos_token_id is not None and bool((next_token == eos_token_id).all()):
                 break
@@ -233,6 +361,14 @@ class MetalLigerGenerator:
             ids[:, n:n + 1] = next_token
             n += 1
         return ids[:, :n]
+
+
+class _nullcontext:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
 
 
 def patch_generator(model: nn.Module, force: bool = False) -> nn.Module:

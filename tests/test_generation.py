@@ -105,6 +105,23 @@ def test_greedy_loop_matches_reference_loop(eos):
     assert torch.equal(got, ref)
 
 
+@pytest.mark.parametrize("eos", [None, "late"])
+def test_static_decode_steps_match_reference_loop(eos):
+    """The self-advancing decode step (the one replayed on a CUDA graph on the
+    GPU; here run eagerly): device-side position, in-place KV write, boolean
+    mask over the full static buffers, token written to the output buffer."""
+    m = _model()
+    ids = torch.randint(0, 300, (2, 5), generator=torch.Generator().manual_seed(12))
+    ref = OG.generate(m, ids, max_new_tokens=12)
+    eos_id = None
+    if eos == "late":
+        eos_id = int(ref[1, 9])
+        ref = OG.generate(m, ids, max_new_tokens=12, eos_token_id=eos_id)
+    got = _TorchHeadGenerator.make(m).generate(ids, max_new_tokens=12, eos_token_id=eos_id,
+                                               cuda_graph=True)
+    assert torch.equal(got, ref)
+
+
 def test_sampling_rule_matches_reference():
     """temperature != 1 samples; temperature 1 with top_p 1 is greedy, as in
     the reference (generation.py:118-123)."""

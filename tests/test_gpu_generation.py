@@ -145,16 +145,18 @@ def _model(seed=0, layers=2, vocab=1000):
     return m.eval()
 
 
-def test_generator_matches_reference_loop():
+@pytest.mark.parametrize("graph", [False, True], ids=["eager", "cuda_graph"])
+def test_generator_matches_reference_loop(graph):
     """Greedy tokens equal the reference loop's (oracle loop on the same GPU
     model with transformers' DynamicCache and the model's own lm_head); where
     they part, the reference's two best logits at that step are within one
-    bf16 ulp of each other (a rounding-order near-tie), never further."""
+    bf16 ulp of each other (a rounding-order near-tie), never further.  The
+    CUDA-graph decode replays one captured, self-advancing step per token."""
     from metal_liger_b200.generation import MetalLigerGenerator
 
     m = _model()
     ids = torch.randint(0, 1000, (3, 6), generator=torch.Generator().manual_seed(4)).to(DEV)
-    got = MetalLigerGenerator(m).generate(ids, max_new_tokens=24)
+    got = MetalLigerGenerator(m).generate(ids, max_new_tokens=24, cuda_graph=graph)
     ref = OG.generate(m, ids, max_new_tokens=24)
     assert got.shape == ref.shape == (3, 30)
     for b in range(3):
@@ -186,3 +188,20 @@ def test_generator_eos_sampling_and_patch():
     sampled = m.generate(ids, max_new_tokens=8, temperature=0.8)
     assert sampled.shape == (1, 13) and int(sampled.max()) < 1000 and int(sampled.min()) >= 0
     assert int(sampled[0, 5]) == int(out[0, 5])  # the first token is always the argmax
+
+
+def test_cuda_graph_decode_stops_at_eos_like_the_eager_loop():
+    """End of sequence found inside a chunk of graph replays: the output is
+    cut exactly where the eager loop (and the reference) stops."""
+    from metal_liger_b200.generation import MetalLigerGenerator
+
+    m = _model(seed=2)
+    g = MetalLigerGenerator(m)
+    ids = torch.randint(0, 1000, (1, 4), generator=torch.Generator().manual_seed(9)).to(DEV)
+    full = g.generate(ids, max_new_tokens=40, cuda_graph=False)
+    eos = int(full[0, 4 + 9])              # a token produced after the graph warm-up
+    first = int((full[0, 4:] == eos).nonzero()[0]) + 4
+    eager = g.generate(ids, max_new_tokens=40, eos_token_id=eos, cuda_graph=False)
+    graph = g.generate(ids, max_new_tokens=40, eos_token_id=eos, cuda_graph=True)
+    assert torch.equal(eager, full[:, :first + 1])
+    assert torch.equal(graph, eager)
