@@ -998,7 +998,34 @@ class Generate:
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / steps
         ours = self.gen.generate(ids, max_new_tokens=self.NEW)
-        return {"reference_loop_on_gpu": {
+
+        # The head alone at batch 1 (one decode step's lm_head pass), against
+        # the reference's logits GEMM + argmax (torch / cuBLAS).
+        h1 = torch.randn(1, self.H, generator=g, device=device).bfloat16()
+        w = m.lm_head.weight
+        from metal_liger_b200.generation import _logit_code
+
+        def head_ms(fn, reps=50):
+            for _ in range(5):
+                fn()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
+            for a, b in ev:
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize()
+            return sorted(a.elapsed_time(b) for a, b in ev)[reps // 2]
+
+        fused = head_ms(lambda: torch.ops.metal_liger.lm_head_argmax(h1, w, None,
+                                                                     _logit_code(w.dtype)))
+        plain_head = head_ms(lambda: torch.argmax(torch.nn.functional.linear(h1, w), dim=-1))
+        return {"lm_head_argmax_alone": {
+            "batch": 1, "median_us": fused * 1e3,
+            "GB/s": self.bytes["lm_head_argmax"] / (fused / 1e3) / 1e9,
+            "torch_linear_argmax_us": plain_head * 1e3,
+            "what": "one lm_head pass (151936 x 4096 bf16), median of 50 event-timed calls"},
+            "reference_loop_on_gpu": {
             "value": self.tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "what": "the reference's decode loop (transformers DynamicCache, full-vocabulary "
                     "logits, argmax, torch.cat) on the same patched model and GPU",
