@@ -1020,6 +1020,22 @@ class Generate:
         fused = head_ms(lambda: torch.ops.metal_liger.lm_head_argmax(h1, w, None,
                                                                      _logit_code(w.dtype)))
         plain_head = head_ms(lambda: torch.argmax(torch.nn.functional.linear(h1, w), dim=-1))
+        # Token agreement: equal prefix length, and whether the first
+        # difference is a near-tie of the reference's own logits there (the
+        # best two within one bf16 ulp), i.e. a rounding-order divergence.
+        same = bool(torch.equal(ref, ours))
+        agree = int(ref.shape[1])
+        near_tie = None
+        if not same:
+            diff = (ref[0] != ours[0]).nonzero()
+            agree = int(diff[0]) if diff.numel() else int(ref.shape[1])
+            with torch.inference_mode():
+                hh = m.model(input_ids=ref[:, :agree]).last_hidden_state[:, -1]
+                top2 = m.lm_head(hh).float()[0].topk(2).values
+            gap = float(top2[0] - top2[1])
+            ulp = 2.0 ** (int(torch.floor(torch.log2(top2[0].abs()))) - 7)
+            near_tie = gap <= ulp
+
         return {"lm_head_argmax_alone": {
             "batch": 1, "median_us": fused * 1e3,
             "GB/s": self.bytes["lm_head_argmax"] / (fused / 1e3) / 1e9,
@@ -1029,7 +1045,8 @@ class Generate:
             "value": self.tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
             "what": "the reference's decode loop (transformers DynamicCache, full-vocabulary "
                     "logits, argmax, torch.cat) on the same patched model and GPU",
-            "same_tokens": bool(torch.equal(ref, ours))}}
+            "same_tokens": same, "generated_tokens_agreeing": agree - self.PROMPT,
+            "first_difference_is_bf16_near_tie": near_tie}}
 
     # CPU baseline: the reference's decode loop (oracle/generation.py: a
     # transformers KV cache, full-vocabulary logits, argmax, torch.cat) in

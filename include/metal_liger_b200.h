@@ -431,6 +431,20 @@ ML_API int ml_lm_head_argmax(const void* hidden, int64_t ld_hidden, const void* 
                              float* value, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/*
+ * Decode-time linear layer: y[b, n] = sum_k x[b, k] * weight[n, k] (+ bias[n])
+ * for batch = 1 or 2 activation rows (bf16, pitch ld_x), weight [N, K] bf16
+ * (pitch ld_w), fp32 accumulation, y (pitch ld_y) in y_dtype (ML_DTYPE_BF16
+ * or ML_DTYPE_F32).  K and the pitches are multiples of 8, bases 16-byte
+ * aligned, batch * K * 2 <= 96 KiB.  An HBM-streaming kernel (one pass over
+ * the weight) for the generator's decode steps; no reference counterpart
+ * (the reference's decode runs the model's nn.Linear modules,
+ * generation.py:109-115).
+ */
+ML_API int ml_gemv_bf16(const void* x, int64_t ld_x, const void* weight, int64_t ld_w,
+                        const void* bias, int bias_dtype, int64_t batch, int64_t K, int64_t N,
+                        void* y, int y_dtype, int64_t ld_y, void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

@@ -621,7 +621,36 @@ def lm_head_argmax_cuda(hidden: Tensor, weight: Tensor, bias: Tensor | None, log
     return index, value
 
 
+def gemv_cuda(x: Tensor, weight: Tensor, bias: Tensor | None):
+    """Decode-time linear layer for 1-2 activation rows: x [..., K] bf16 with
+    at most 2 rows, weight [N, K] bf16 -> [..., N] bf16 (fp32 accumulation,
+    one HBM pass over the weight)."""
+    _C.require_cuda("gemv", x, weight, bias)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError("gemv: x and weight must be bfloat16")
+    K = x.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != K:
+        raise RuntimeError(f"gemv: weight {tuple(weight.shape)} does not match x {tuple(x.shape)}")
+    rows = x.numel() // K if K else 0
+    if rows > 2:
+        raise RuntimeError(f"gemv: {rows} rows; the GEMV path takes at most 2")
+    x2 = x.reshape(rows, K)
+    if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    weight = _contig(weight)
+    if bias is not None:
+        bias = _contig(bias)
+    N = weight.shape[0]
+    y = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
+    if rows:
+        _C.call("ml_gemv_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K, _C.ptr(weight),
+                weight.stride(0), _C.ptr(bias), _C.dtype_code(bias) if bias is not None else 0,
+                rows, K, N, _C.ptr(y), _C.dtype_code(torch.bfloat16), N, _C.stream_of(x))
+    return y.reshape(*x.shape[:-1], N)
+
+
 _SCHEMAS = {
+    "gemv": "gemv(Tensor x, Tensor weight, Tensor? bias) -> Tensor",
     "lm_head_argmax": "lm_head_argmax(Tensor hidden, Tensor weight, Tensor? bias, "
                       "int logit_dtype) -> (Tensor, Tensor)",
     "rms_norm_forward": "rms_norm_forward(Tensor x, Tensor weight, float eps, str kernel_dir) "
@@ -664,6 +693,7 @@ _SCHEMAS = {
 }
 
 _CUDA_IMPLS = {
+    "gemv": gemv_cuda,
     "lm_head_argmax": lm_head_argmax_cuda,
     "rms_norm_forward": rms_norm_forward_cuda,
     "rms_norm_backward": rms_norm_backward_cuda,
@@ -775,7 +805,11 @@ def _fake_impls():
         return (torch.empty(B, dtype=torch.int64, device=hidden.device),
                 torch.empty(B, dtype=torch.float32, device=hidden.device))
 
+    def gemv_fake(x, weight, bias):
+        return torch.empty((*x.shape[:-1], weight.shape[0]), dtype=x.dtype, device=x.device)
+
     return {
+        "gemv": gemv_fake,
         "lm_head_argmax": lm_argmax,
         "lora_qkv_forward": lqkv_fwd,
         "lora_qkv_backward": lqkv_bwd,

@@ -11,6 +11,7 @@
 // index), so the choice is exactly argmax of the dtype-rounded fp32 logits.
 // Decode is HBM-bound on W: one pass over [vocab, hidden] bf16 per step.
 #include "gemm.cuh"
+#include "gemv.cuh"
 
 namespace ml {
 namespace {
@@ -60,38 +61,17 @@ __global__ void argmax_reduce(const float* __restrict__ part_m, const int* __res
 // rows sit in shared memory as bf16; products are exact in fp32 and summed
 // per lane, then across the warp by a fixed butterfly.  Each CTA writes one
 // (max, column) candidate per sequence; argmax_reduce picks among CTAs.
-constexpr int kGemvThreads = 512;
-constexpr int kGemvBatch = 16;  // 16-byte weight loads in flight per lane
-
-__device__ __forceinline__ float dot8_bf16(const uint4& a, const uint4& b, float acc) {
-  const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&a);
-  const __nv_bfloat162* y = reinterpret_cast<const __nv_bfloat162*>(&b);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 fx = __bfloat1622float2(x[i]);
-    const float2 fy = __bfloat1622float2(y[i]);
-    acc = fmaf(fx.x, fy.x, acc);
-    acc = fmaf(fx.y, fy.y, acc);
-  }
-  return acc;
-}
-
 template <int NB>
-__global__ void __launch_bounds__(kGemvThreads)
+__global__ void __launch_bounds__(gemv::kThreads)
 gemv_argmax(const __nv_bfloat16* __restrict__ hidden, int64_t ld_h,
             const __nv_bfloat16* __restrict__ weight, int64_t ld_w, const void* __restrict__ bias,
             int bias_dtype, int64_t H, int64_t V, int logit_dtype, float* __restrict__ part_m,
             int* __restrict__ part_i) {
   extern __shared__ uint4 hs[];  // [NB][H / 8] hidden chunks
-  __shared__ float cand_v[kGemvThreads / 32][NB];
-  __shared__ int cand_c[kGemvThreads / 32][NB];
+  __shared__ float cand_v[gemv::kThreads / 32][NB];
+  __shared__ int cand_c[gemv::kThreads / 32][NB];
   const int64_t nchunk = H / 8;
-  for (int64_t i = threadIdx.x; i < NB * nchunk; i += blockDim.x) {
-    const int b = (int)(i / nchunk);
-    const int64_t c = i - b * nchunk;
-    hs[i] = *reinterpret_cast<const uint4*>(hidden + b * ld_h + c * 8);
-  }
-  __syncthreads();
+  gemv::stage_rows<NB>(hs, hidden, ld_h, nchunk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   const int64_t per = (V + gridDim.x - 1) / gridDim.x;
@@ -107,26 +87,7 @@ gemv_argmax(const __nv_bfloat16* __restrict__ hidden, int64_t ld_h,
   for (int64_t r = r0 + warp; r < r1; r += nwarps) {
     const uint4* wrow = reinterpret_cast<const uint4*>(weight + r * ld_w);
     float acc[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-    // Blocks of kGemvBatch chunks per lane: every load of a block is issued
-    // before the first product uses one (hidden 4096: one block per row).
-    for (int64_t c0 = lane; c0 < nchunk; c0 += 32 * kGemvBatch) {
-      uint4 wv[kGemvBatch];
-#pragma unroll
-      for (int u = 0; u < kGemvBatch; ++u) {
-        const int64_t c = c0 + 32 * u;
-        if (c < nchunk) wv[u] = __ldcs(wrow + c);
-      }
-#pragma unroll
-      for (int u = 0; u < kGemvBatch; ++u) {
-        const int64_t c = c0 + 32 * u;
-        if (c < nchunk) {
-#pragma unroll
-          for (int b = 0; b < NB; ++b) acc[b] = dot8_bf16(wv[u], hs[b * nchunk + c], acc[b]);
-        }
-      }
-    }
+    gemv::row_dot<NB>(wrow, hs, nchunk, lane, acc);
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       float v = warp_sum(acc[b]);
@@ -228,9 +189,8 @@ extern "C" int ml_lm_head_argmax(const void* hidden, int64_t ld_hidden, const vo
   int* part_i = reinterpret_cast<int*>(part_m + n_tiles_max * batch);
 
   const int sms = num_sms();
-  if (batch <= 2 && hidden_size % 8 == 0 && ld_hidden % 8 == 0 && ld_weight % 8 == 0 &&
-      aligned16(hidden) && aligned16(weight) && n_tiles_max >= sms &&
-      (size_t)batch * hidden_size * 2 <= 96 * 1024) {
+  if (gemv::eligible(batch, hidden_size, ld_hidden, ld_weight, hidden, weight) &&
+      n_tiles_max >= sms) {
     const size_t smem = (size_t)batch * hidden_size * 2;
     auto launch_gemv = [&](auto kernel) -> int {
       if (smem > 48 * 1024)
@@ -238,7 +198,7 @@ extern "C" int ml_lm_head_argmax(const void* hidden, int64_t ld_hidden, const vo
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            96 * 1024),
                       "lm_head_argmax: smem attribute");
-      kernel<<<sms, kGemvThreads, smem, st>>>(
+      kernel<<<sms, gemv::kThreads, smem, st>>>(
           static_cast<const __nv_bfloat16*>(hidden), ld_hidden,
           static_cast<const __nv_bfloat16*>(weight), ld_weight, bias, bias_dtype, hidden_size,
           vocab, logit_dtype, part_m, part_i);

@@ -37,6 +37,7 @@ forward returns ``last_hidden_state``) and a bias-free or biased
 from __future__ import annotations
 
 import logging
+from collections import OrderedDict
 from typing import Optional
 
 import torch
@@ -152,6 +153,45 @@ class MetalLigerStaticCache(Cache):
         return self.max_seq_len
 
 
+class _DecodeLinears:
+    """While active, the bf16 CUDA ``nn.Linear`` layers of ``module`` run
+    calls with at most two activation rows (one decode token per sequence)
+    through ``metal_liger::gemv``, one HBM pass over the weight; every other
+    call keeps the layer's own forward.  Restores the forwards on exit."""
+
+    def __init__(self, module: nn.Module):
+        self.module = module
+        self.patched = []
+
+    def __enter__(self):
+        from metal_liger_b200 import _torch_library  # noqa: F401  (registers the ops)
+
+        for mod in self.module.modules():
+            if (type(mod) is nn.Linear and mod.weight.dtype == torch.bfloat16
+                    and mod.weight.is_cuda and mod.in_features % 8 == 0
+                    and "forward" not in mod.__dict__):
+                mod.forward = _decode_forward(mod)
+                self.patched.append(mod)
+        return self
+
+    def __exit__(self, *exc):
+        for mod in self.patched:
+            del mod.forward
+        self.patched = []
+        return False
+
+
+def _decode_forward(mod: nn.Linear):
+    orig = type(mod).forward
+
+    def forward(x: Tensor) -> Tensor:
+        if x.dtype == torch.bfloat16 and x.numel() <= 2 * mod.in_features and x.is_cuda:
+            return torch.ops.metal_liger.gemv(x, mod.weight, mod.bias)
+        return orig(mod, x)
+
+    return forward
+
+
 def _logit_code(dtype: torch.dtype) -> int:
     from metal_liger_b200 import _C
     return _C.dtype_code(dtype)
@@ -262,54 +302,89 @@ class MetalLigerGenerator:
         hit = (out[:, lo:hi] == eos_token_id).all(dim=0).nonzero()
         return lo + int(hit[0]) if hit.numel() else None
 
-    def _decode_static(self, cache, ids, n, steps, eos_token_id, capture: bool) -> int:
+    _MAX_STATES = 4         # (batch, length) decode graphs kept per generator
+
+    def _fingerprint(self):
+        return tuple(p.data_ptr() for p in self.model.parameters())
+
+    def _state(self, B: int, L: int, dtype, dev) -> "_DecodeState":
+        """The static buffers (KV cache, ids, position, mask, input token)
+        and, once captured, the decode graph for this (batch, length); kept
+        across calls while the model's parameters stay where they are."""
+        fp = self._fingerprint()
+        if fp != getattr(self, "_states_fp", None):
+            self._states = OrderedDict()
+            self._states_fp = fp
+        key = (B, L, dtype, str(dev))
+        st = self._states.get(key)
+        if st is None:
+            st = _DecodeState(self.model, B, L, dtype, dev)
+            self._states[key] = st
+            while len(self._states) > self._MAX_STATES:
+                self._states.popitem(last=False)
+        else:
+            self._states.move_to_end(key)
+        return st
+
+    def _decode_static(self, st: "_DecodeState", n, steps, eos_token_id, capture: bool) -> int:
         """Greedy decode of `steps` tokens after position n - 1 (the prefill's
-        token); returns the number of ids filled.  `capture` replays a CUDA
-        graph of the step; without it the same step runs eagerly."""
-        B, L = ids.shape
+        token) in st.ids; returns the number of ids filled.  With `capture`
+        the step is captured once per state (after two eager steps) and
+        replayed; on CUDA the decoder's bf16 linear layers take the
+        HBM-streaming GEMV while the step is built (batch <= 2)."""
+        B = st.ids.shape[0]
+        if capture and B <= 2 and st.graph is None:
+            with _DecodeLinears(self.decoder):
+                return self._decode_static_inner(st, n, steps, eos_token_id, capture)
+        return self._decode_static_inner(st, n, steps, eos_token_id, capture)
+
+    def _decode_static_inner(self, st: "_DecodeState", n, steps, eos_token_id,
+                             capture: bool) -> int:
+        cache, ids = st.cache, st.ids
         dev = ids.device
-        pos = torch.full((1,), n - 1, dtype=torch.int64, device=dev)
-        mask = torch.zeros((B, 1, 1, L), dtype=torch.bool, device=dev)
-        mask[..., :n - 1] = True
-        st = {"cache": cache, "tok": ids[:, n - 1:n].clone(), "pos": pos, "mask": mask,
-              "out": ids}
-        cache.graph_pos = pos
+        st.pos.fill_(n - 1)
+        st.mask.zero_()
+        st.mask[..., :n - 1] = True
+        st.tok.copy_(ids[:, n - 1:n])
+        step = {"cache": cache, "tok": st.tok, "pos": st.pos, "mask": st.mask, "out": ids}
+        cache.graph_pos = st.pos
         done = 0
         try:
             stop = self._all_eos_at(ids, n - 1, n, eos_token_id)
             if stop is not None:
                 return stop + 1
-            warm = min(steps, self._GRAPH_WARMUP if capture else steps)
-            side = torch.cuda.Stream(device=dev) if capture else None
-            if side is not None:
-                side.wait_stream(torch.cuda.current_stream(dev))
-            ctx = torch.cuda.stream(side) if side is not None else _nullcontext()
-            with ctx:
-                for _ in range(warm):
-                    self._static_step(st)
-                    done += 1
-                    stop = self._all_eos_at(ids, n - 1 + done, n + done, eos_token_id)
-                    if stop is not None:
-                        break
-            if side is not None:
-                torch.cuda.current_stream(dev).wait_stream(side)
-            if stop is not None:
-                return stop + 1
-            if done < steps:
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
-                    self._static_step(st)
-                checked = n + done
-                while done < steps:
-                    graph.replay()
-                    done += 1
-                    if eos_token_id is not None and (done % self._EOS_CHECK_EVERY == 0
-                                                     or done == steps):
-                        stop = self._all_eos_at(ids, checked, n + done, eos_token_id)
-                        checked = n + done
+            if st.graph is None:
+                warm = min(steps, self._GRAPH_WARMUP if capture else steps)
+                side = torch.cuda.Stream(device=dev) if capture else None
+                if side is not None:
+                    side.wait_stream(torch.cuda.current_stream(dev))
+                ctx = torch.cuda.stream(side) if side is not None else _nullcontext()
+                with ctx:
+                    for _ in range(warm):
+                        self._static_step(step)
+                        done += 1
+                        stop = self._all_eos_at(ids, n - 1 + done, n + done, eos_token_id)
                         if stop is not None:
-                            return stop + 1
-                del graph
+                            break
+                if side is not None:
+                    torch.cuda.current_stream(dev).wait_stream(side)
+                if stop is not None:
+                    return stop + 1
+                if capture and done < steps:
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        self._static_step(step)
+                    st.graph = graph
+            checked = n + done
+            while done < steps:
+                st.graph.replay()
+                done += 1
+                if eos_token_id is not None and (done % self._EOS_CHECK_EVERY == 0
+                                                 or done == steps):
+                    stop = self._all_eos_at(ids, checked, n + done, eos_token_id)
+                    checked = n + done
+                    if stop is not None:
+                        return stop + 1
             return n + done
         finally:
             cache.graph_pos = None
@@ -330,8 +405,18 @@ class MetalLigerGenerator:
         batch_size, prompt_len = input_ids.shape
         max_len = prompt_len + max_new_tokens
         greedy = temperature == 0 or (temperature == 1.0 and top_p == 1.0)
-        cache = MetalLigerStaticCache(self.model, batch_size, max_len)
-        ids = torch.empty((batch_size, max_len), dtype=input_ids.dtype, device=input_ids.device)
+        if cuda_graph is None:
+            cuda_graph = (input_ids.device.type == "cuda"
+                          and max_new_tokens > self._GRAPH_WARMUP + 2)
+        static = greedy and not kwargs and cuda_graph and max_new_tokens > 1
+        if static:
+            st = self._state(batch_size, max_len, input_ids.dtype, input_ids.device)
+            cache, ids = st.cache, st.ids
+            cache.seen_tokens = 0
+        else:
+            cache = MetalLigerStaticCache(self.model, batch_size, max_len)
+            ids = torch.empty((batch_size, max_len), dtype=input_ids.dtype,
+                              device=input_ids.device)
         ids[:, :prompt_len] = input_ids
 
         # Prefill; the first token is the argmax in every mode (reference :99-101).
@@ -341,12 +426,10 @@ class MetalLigerGenerator:
         ids[:, prompt_len:prompt_len + 1] = next_token
         n = prompt_len + 1
 
-        if cuda_graph is None:
-            cuda_graph = ids.device.type == "cuda" and max_new_tokens > self._GRAPH_WARMUP + 2
-        if greedy and not kwargs and cuda_graph and max_new_tokens > 1:
-            filled = self._decode_static(cache, ids, n, max_new_tokens - 1, eos_token_id,
+        if static:
+            filled = self._decode_static(st, n, max_new_tokens - 1, eos_token_id,
                                          capture=ids.device.type == "cuda")
-            return ids[:, :filled]
+            return ids[:, :filled].clone()
 
         for _ in range(max_new_tokens - 1):
             if eos_token_id is not None and bool((next_token == eos_token_id).all()):
@@ -361,6 +444,21 @@ class MetalLigerGenerator:
             ids[:, n:n + 1] = next_token
             n += 1
         return ids[:, :n]
+
+
+class _DecodeState:
+    """Buffers of the self-advancing decode step for one (batch, length):
+    the static KV cache, the [B, L] ids, the device position, the [B, 1, 1,
+    L] attention mask, the input token, and the captured graph (None until
+    the first call long enough to capture it)."""
+
+    def __init__(self, model: nn.Module, B: int, L: int, dtype, dev):
+        self.cache = MetalLigerStaticCache(model, B, L)
+        self.ids = torch.empty((B, L), dtype=dtype, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.mask = torch.zeros((B, 1, 1, L), dtype=torch.bool, device=dev)
+        self.tok = torch.empty((B, 1), dtype=dtype, device=dev)
+        self.graph = None
 
 
 class _nullcontext:
