@@ -445,6 +445,31 @@ ML_API int ml_gemv_bf16(const void* x, int64_t ld_x, const void* weight, int64_t
                         const void* bias, int bias_dtype, int64_t batch, int64_t K, int64_t N,
                         void* y, int y_dtype, int64_t ld_y, void* stream);
 
+/*
+ * ml_gemv_bf16 for nmat (1-4) projections of the same activations in one
+ * launch (q, k and v of an attention block): for each i, y[i][b, n] =
+ * sum_k x[b, k] * weight[i][n, k] (+ bias[i][n]) for n < n[i], output pitch
+ * ld_y[i]; bias is NULL or an array of nmat pointers (entries may be NULL).
+ * The layout rules of ml_gemv_bf16 hold for every matrix.
+ */
+ML_API int ml_gemv_multi_bf16(const void* x, int64_t ld_x, int nmat, const void* const* weight,
+                              const int64_t* ld_w, const int64_t* n, const void* const* bias,
+                              int bias_dtype, int64_t batch, int64_t K, void* const* y,
+                              const int64_t* ld_y, int y_dtype, void* stream);
+
+/*
+ * Decode-time SwiGLU MLP input side: y[b, i] = bf16(silu(g) * u) with
+ * g = bf16(x[b] . w_gate[i]), u = bf16(x[b] . w_up[i]) (fp32 accumulation;
+ * bitwise equal to two ml_gemv_bf16 calls and ml_swiglu_forward), for
+ * batch = 1 or 2; w_gate / w_up [inter, K] bf16; the same layout rules as
+ * ml_gemv_bf16.  One pass over both weights, gate and up never stored.  No
+ * reference counterpart (the reference's decode runs gate_proj, up_proj and
+ * the activation separately, ops/fused_swiglu.py:71-75).
+ */
+ML_API int ml_gemv_swiglu_bf16(const void* x, int64_t ld_x, const void* w_gate, int64_t ld_g,
+                               const void* w_up, int64_t ld_u, int64_t batch, int64_t K,
+                               int64_t inter, void* y, int64_t ld_y, void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

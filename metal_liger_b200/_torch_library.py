@@ -649,7 +649,74 @@ def gemv_cuda(x: Tensor, weight: Tensor, bias: Tensor | None):
     return y.reshape(*x.shape[:-1], N)
 
 
+def gemv_swiglu_cuda(x: Tensor, w_gate: Tensor, w_up: Tensor):
+    """Decode-time SwiGLU input side for 1-2 rows: silu(x W_g^T) * (x W_u^T),
+    bf16, equal bit for bit to gemv, gemv and swiglu_forward."""
+    _C.require_cuda("gemv_swiglu", x, w_gate, w_up)
+    if x.dtype != torch.bfloat16 or w_gate.dtype != torch.bfloat16 or w_up.dtype != torch.bfloat16:
+        raise RuntimeError("gemv_swiglu: x and the weights must be bfloat16")
+    K = x.shape[-1]
+    if w_gate.shape != w_up.shape or w_gate.dim() != 2 or w_gate.shape[1] != K:
+        raise RuntimeError(f"gemv_swiglu: weights {tuple(w_gate.shape)} / {tuple(w_up.shape)} "
+                           f"do not match x {tuple(x.shape)}")
+    rows = x.numel() // K if K else 0
+    if rows > 2:
+        raise RuntimeError(f"gemv_swiglu: {rows} rows; the GEMV path takes at most 2")
+    x2 = x.reshape(rows, K)
+    if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    w_gate, w_up = _contig(w_gate), _contig(w_up)
+    inter = w_gate.shape[0]
+    y = torch.empty((rows, inter), dtype=torch.bfloat16, device=x.device)
+    if rows:
+        _C.call("ml_gemv_swiglu_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K,
+                _C.ptr(w_gate), w_gate.stride(0), _C.ptr(w_up), w_up.stride(0), rows, K, inter,
+                _C.ptr(y), inter, _C.stream_of(x))
+    return y.reshape(*x.shape[:-1], inter)
+
+
+def gemv_multi_cuda(x: Tensor, weights: list[Tensor], biases: list[Tensor | None]):
+    """Several decode-time projections of the same 1-2 activation rows in one
+    launch (q, k and v): [x W_i^T (+ b_i)] as bf16 tensors [..., N_i]."""
+    import ctypes
+
+    _C.require_cuda("gemv_multi", x, *weights, *[b for b in biases if b is not None])
+    if not 1 <= len(weights) <= 4 or (biases and len(biases) != len(weights)):
+        raise RuntimeError("gemv_multi: 1-4 weights, and one bias entry per weight if any")
+    K = x.shape[-1]
+    if x.dtype != torch.bfloat16 or any(w.dtype != torch.bfloat16 or w.dim() != 2 or
+                                        w.shape[1] != K for w in weights):
+        raise RuntimeError("gemv_multi: bf16 x [..., K] and bf16 weights [N_i, K]")
+    rows = x.numel() // K if K else 0
+    if rows > 2:
+        raise RuntimeError(f"gemv_multi: {rows} rows; the GEMV path takes at most 2")
+    x2 = x.reshape(rows, K)
+    if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+    weights = [_contig(w) for w in weights]
+    biases = [None if b is None else _contig(b) for b in (biases or [None] * len(weights))]
+    bdt = {b.dtype for b in biases if b is not None}
+    if len(bdt) > 1:
+        raise RuntimeError("gemv_multi: biases of different dtypes")
+    outs = [torch.empty((rows, w.shape[0]), dtype=torch.bfloat16, device=x.device)
+            for w in weights]
+    if rows:
+        m = len(weights)
+        P = ctypes.c_void_p * m
+        I64 = ctypes.c_int64 * m
+        _C.call("ml_gemv_multi_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K, m,
+                P(*[w.data_ptr() for w in weights]), I64(*[w.stride(0) for w in weights]),
+                I64(*[w.shape[0] for w in weights]),
+                P(*[0 if b is None else b.data_ptr() for b in biases]) if bdt else None,
+                _C.dtype_code(bdt.pop()) if bdt else 0, rows, K,
+                P(*[o.data_ptr() for o in outs]), I64(*[o.shape[1] for o in outs]),
+                _C.dtype_code(torch.bfloat16), _C.stream_of(x))
+    return [o.reshape(*x.shape[:-1], o.shape[1]) for o in outs]
+
+
 _SCHEMAS = {
+    "gemv_multi": "gemv_multi(Tensor x, Tensor[] weights, Tensor?[] biases) -> Tensor[]",
+    "gemv_swiglu": "gemv_swiglu(Tensor x, Tensor w_gate, Tensor w_up) -> Tensor",
     "gemv": "gemv(Tensor x, Tensor weight, Tensor? bias) -> Tensor",
     "lm_head_argmax": "lm_head_argmax(Tensor hidden, Tensor weight, Tensor? bias, "
                       "int logit_dtype) -> (Tensor, Tensor)",
@@ -693,6 +760,8 @@ _SCHEMAS = {
 }
 
 _CUDA_IMPLS = {
+    "gemv_multi": gemv_multi_cuda,
+    "gemv_swiglu": gemv_swiglu_cuda,
     "gemv": gemv_cuda,
     "lm_head_argmax": lm_head_argmax_cuda,
     "rms_norm_forward": rms_norm_forward_cuda,
@@ -808,7 +877,16 @@ def _fake_impls():
     def gemv_fake(x, weight, bias):
         return torch.empty((*x.shape[:-1], weight.shape[0]), dtype=x.dtype, device=x.device)
 
+    def gemv_swiglu_fake(x, w_gate, w_up):
+        return torch.empty((*x.shape[:-1], w_gate.shape[0]), dtype=x.dtype, device=x.device)
+
+    def gemv_multi_fake(x, weights, biases):
+        return [torch.empty((*x.shape[:-1], w.shape[0]), dtype=x.dtype, device=x.device)
+                for w in weights]
+
     return {
+        "gemv_multi": gemv_multi_fake,
+        "gemv_swiglu": gemv_swiglu_fake,
         "gemv": gemv_fake,
         "lm_head_argmax": lm_argmax,
         "lora_qkv_forward": lqkv_fwd,

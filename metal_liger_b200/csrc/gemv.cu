@@ -9,6 +9,8 @@
 // 8 KB of one row in flight: 8 MB across the GPU for hidden 4096).
 #include "gemv.cuh"
 
+#include <cstring>
+
 namespace ml {
 namespace {
 
@@ -30,6 +32,106 @@ gemv_rows(const __nv_bfloat16* __restrict__ x, int64_t ld_x,
       float v = warp_sum(acc[b]);
       if (bias != nullptr) v += load_as_f32(bias, r, bias_dtype);
       if (lane == 0) y[b * ld_y + r] = from_f32<TO>(v);
+    }
+  }
+}
+
+// SwiGLU MLP input side for decoding: h[b, i] = silu(gate) * up with
+// gate = bf16(x . Wg[i]), up = bf16(x . Wu[i]) — one launch instead of two
+// GEMVs and the activation kernel, and neither gate nor up is stored.  Each
+// warp takes row i of both weights, 8 chunks of each in flight per lane per
+// batch, in the same chunk order as row_dot (so gate and up are bitwise the
+// two GEMVs' outputs), and the activation is the SwiGLU kernel's expression
+// ((g * sigmoid(g)) * u, sigmoid = 1 / (1 + e^-g) on the SFU), so the fused
+// step equals GEMV, GEMV, swiglu_forward bit for bit.
+__device__ __forceinline__ float sigmoid_sfu(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
+
+template <int NB>
+__global__ void __launch_bounds__(gemv::kThreads)
+gemv_swiglu_rows(const __nv_bfloat16* __restrict__ x, int64_t ld_x,
+                 const __nv_bfloat16* __restrict__ wg, int64_t ld_g,
+                 const __nv_bfloat16* __restrict__ wu, int64_t ld_u, int64_t K, int64_t I,
+                 __nv_bfloat16* __restrict__ y, int64_t ld_y) {
+  constexpr int kHalf = gemv::kBatch / 2;
+  extern __shared__ uint4 hs[];
+  const int64_t nchunk = K / 8;
+  gemv::stage_rows<NB>(hs, x, ld_x, nchunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t r = (int64_t)warp * gridDim.x + blockIdx.x; r < I; r += total) {
+    const uint4* grow = reinterpret_cast<const uint4*>(wg + r * ld_g);
+    const uint4* urow = reinterpret_cast<const uint4*>(wu + r * ld_u);
+    float ag[NB], au[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) ag[b] = au[b] = 0.f;
+    for (int64_t c0 = lane; c0 < nchunk; c0 += 32 * kHalf) {
+      uint4 gv[kHalf], uv[kHalf];
+#pragma unroll
+      for (int u = 0; u < kHalf; ++u) {
+        const int64_t c = c0 + 32 * u;
+        if (c < nchunk) {
+          gv[u] = __ldcs(grow + c);
+          uv[u] = __ldcs(urow + c);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kHalf; ++u) {
+        const int64_t c = c0 + 32 * u;
+        if (c < nchunk) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            ag[b] = gemv::dot8_bf16(gv[u], hs[b * nchunk + c], ag[b]);
+            au[b] = gemv::dot8_bf16(uv[u], hs[b * nchunk + c], au[b]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      const float g = __bfloat162float(__float2bfloat16_rn(warp_sum(ag[b])));
+      const float u = __bfloat162float(__float2bfloat16_rn(warp_sum(au[b])));
+      if (lane == 0) y[b * ld_y + r] = __float2bfloat16_rn((g * sigmoid_sfu(g)) * u);
+    }
+  }
+}
+
+// Up to kMaxMats projections of the same activations in one launch (q, k
+// and v of an attention block): their rows are concatenated in one row space
+// and each warp row writes to its own matrix's output.
+constexpr int kMaxMats = 4;
+struct MultiArgs {
+  const __nv_bfloat16* w[kMaxMats];
+  const void* bias[kMaxMats];
+  void* y[kMaxMats];
+  int64_t ld_w[kMaxMats], ld_y[kMaxMats], first[kMaxMats + 1];  // first[i]: row offset of matrix i
+  int nmat;
+  int bias_dtype;
+};
+
+template <int NB, typename TO>
+__global__ void __launch_bounds__(gemv::kThreads)
+gemv_multi_rows(const __nv_bfloat16* __restrict__ x, int64_t ld_x, int64_t K,
+                const __grid_constant__ MultiArgs a) {
+  extern __shared__ uint4 hs[];
+  const int64_t nchunk = K / 8;
+  gemv::stage_rows<NB>(hs, x, ld_x, nchunk);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t R = a.first[a.nmat];
+  for (int64_t r = (int64_t)warp * gridDim.x + blockIdx.x; r < R; r += total) {
+    int m = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxMats; ++i)
+      if (i < a.nmat && r >= a.first[i]) m = i;
+    const int64_t rr = r - a.first[m];
+    float acc[NB];
+    gemv::row_dot<NB>(reinterpret_cast<const uint4*>(a.w[m] + rr * a.ld_w[m]), hs, nchunk, lane,
+                      acc);
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      float v = warp_sum(acc[b]);
+      if (a.bias[m] != nullptr) v += load_as_f32(a.bias[m], rr, a.bias_dtype);
+      if (lane == 0) static_cast<TO*>(a.y[m])[b * a.ld_y[m] + rr] = from_f32<TO>(v);
     }
   }
 }
@@ -90,4 +192,88 @@ extern "C" int ml_gemv_bf16(const void* x, int64_t ld_x, const void* weight, int
   return batch == 1
              ? launch_rows<1, float>(x, ld_x, weight, ld_w, bias, bias_dtype, K, N, y, ld_y, st)
              : launch_rows<2, float>(x, ld_x, weight, ld_w, bias, bias_dtype, K, N, y, ld_y, st);
+}
+
+extern "C" int ml_gemv_swiglu_bf16(const void* x, int64_t ld_x, const void* w_gate, int64_t ld_g,
+                                   const void* w_up, int64_t ld_u, int64_t batch, int64_t K,
+                                   int64_t inter, void* y, int64_t ld_y, void* stream) {
+  ML_CHECK_ARG(batch >= 0 && K > 0 && inter > 0,
+               "gemv_swiglu_bf16: bad sizes batch=%lld K=%lld inter=%lld", (long long)batch,
+               (long long)K, (long long)inter);
+  if (batch == 0) return ML_OK;
+  ML_CHECK_ARG(x && w_gate && w_up && y, "gemv_swiglu_bf16: null pointer");
+  ML_CHECK_ARG(gemv::eligible(batch, K, ld_x, ld_g, x, w_gate) &&
+                   gemv::eligible(batch, K, ld_x, ld_u, x, w_up),
+               "gemv_swiglu_bf16: needs 1-2 rows, K and row pitches multiples of 8, 16-byte "
+               "aligned bases and rows*K*2 <= 96 KiB (batch=%lld K=%lld)",
+               (long long)batch, (long long)K);
+  ML_CHECK_ARG(ld_y >= inter, "gemv_swiglu_bf16: output pitch %lld below %lld",
+               (long long)ld_y, (long long)inter);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)batch * K * 2;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), inter));
+  auto run = [&](auto kernel) -> int {
+    if (smem > 48 * 1024)
+      ML_CHECK_CUDA(cudaFuncSetAttribute((const void*)kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024),
+                    "gemv_swiglu_bf16: smem attribute");
+    kernel<<<grid, gemv::kThreads, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(w_gate),
+        ld_g, static_cast<const __nv_bfloat16*>(w_up), ld_u, K, inter,
+        static_cast<__nv_bfloat16*>(y), ld_y);
+    ML_CHECK_LAUNCH("gemv_swiglu_bf16");
+    return ML_OK;
+  };
+  return batch == 1 ? run(gemv_swiglu_rows<1>) : run(gemv_swiglu_rows<2>);
+}
+
+extern "C" int ml_gemv_multi_bf16(const void* x, int64_t ld_x, int nmat, const void* const* weight,
+                                  const int64_t* ld_w, const int64_t* n, const void* const* bias,
+                                  int bias_dtype, int64_t batch, int64_t K, void* const* y,
+                                  const int64_t* ld_y, int y_dtype, void* stream) {
+  ML_CHECK_ARG(nmat >= 1 && nmat <= kMaxMats, "gemv_multi_bf16: %d matrices (1-%d)", nmat,
+               kMaxMats);
+  ML_CHECK_ARG(batch >= 0 && K > 0, "gemv_multi_bf16: bad sizes batch=%lld K=%lld",
+               (long long)batch, (long long)K);
+  if (batch == 0) return ML_OK;
+  ML_CHECK_ARG(x && weight && ld_w && n && y && ld_y, "gemv_multi_bf16: null pointer");
+  ML_CHECK_ARG(y_dtype == ML_DTYPE_BF16 || y_dtype == ML_DTYPE_F32,
+               "gemv_multi_bf16: output dtype %d is neither bf16 nor fp32", y_dtype);
+  ML_CHECK_ARG(bias == nullptr || bias_dtype == ML_DTYPE_F32 || bias_dtype == ML_DTYPE_BF16 ||
+                   bias_dtype == ML_DTYPE_F16,
+               "gemv_multi_bf16: bad bias dtype %d", bias_dtype);
+  MultiArgs a;
+  memset(&a, 0, sizeof(a));
+  a.nmat = nmat;
+  a.bias_dtype = bias_dtype;
+  a.first[0] = 0;
+  for (int i = 0; i < nmat; ++i) {
+    ML_CHECK_ARG(weight[i] && y[i] && n[i] > 0, "gemv_multi_bf16: matrix %d is empty or null", i);
+    ML_CHECK_ARG(gemv::eligible(batch, K, ld_x, ld_w[i], x, weight[i]),
+                 "gemv_multi_bf16: matrix %d: needs 1-2 rows, K and row pitches multiples of 8, "
+                 "16-byte aligned bases and rows*K*2 <= 96 KiB", i);
+    ML_CHECK_ARG(ld_y[i] >= n[i], "gemv_multi_bf16: output %d pitch below its rows", i);
+    a.w[i] = static_cast<const __nv_bfloat16*>(weight[i]);
+    a.bias[i] = bias != nullptr ? bias[i] : nullptr;
+    a.y[i] = y[i];
+    a.ld_w[i] = ld_w[i];
+    a.ld_y[i] = ld_y[i];
+    a.first[i + 1] = a.first[i] + n[i];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t smem = (size_t)batch * K * 2;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(num_sms(), a.first[nmat]));
+  auto run = [&](auto kernel) -> int {
+    if (smem > 48 * 1024)
+      ML_CHECK_CUDA(cudaFuncSetAttribute((const void*)kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024),
+                    "gemv_multi_bf16: smem attribute");
+    kernel<<<grid, gemv::kThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ld_x, K, a);
+    ML_CHECK_LAUNCH("gemv_multi_bf16");
+    return ML_OK;
+  };
+  if (y_dtype == ML_DTYPE_BF16)
+    return batch == 1 ? run(gemv_multi_rows<1, __nv_bfloat16>)
+                      : run(gemv_multi_rows<2, __nv_bfloat16>);
+  return batch == 1 ? run(gemv_multi_rows<1, float>) : run(gemv_multi_rows<2, float>);
 }

@@ -156,8 +156,11 @@ class MetalLigerStaticCache(Cache):
 class _DecodeLinears:
     """While active, the bf16 CUDA ``nn.Linear`` layers of ``module`` run
     calls with at most two activation rows (one decode token per sequence)
-    through ``metal_liger::gemv``, one HBM pass over the weight; every other
-    call keeps the layer's own forward.  Restores the forwards on exit."""
+    through ``metal_liger::gemv``, one HBM pass over the weight; the q, k
+    and v projections of an attention block share one ``gemv_multi`` launch
+    and the fused SwiGLU MLPs take gate, up and the activation in one
+    ``metal_liger::gemv_swiglu`` launch; every other call keeps the module's
+    own forward.  Restores the forwards on exit."""
 
     def __init__(self, module: nn.Module):
         self.module = module
@@ -166,11 +169,29 @@ class _DecodeLinears:
     def __enter__(self):
         from metal_liger_b200 import _torch_library  # noqa: F401  (registers the ops)
 
+        from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU
+
+        # q, k and v of an attention block in one launch: the q_proj call
+        # computes all three and leaves k and v for the k_proj / v_proj calls
+        # on the same activation tensor.
         for mod in self.module.modules():
-            if (type(mod) is nn.Linear and mod.weight.dtype == torch.bfloat16
-                    and mod.weight.is_cuda and mod.in_features % 8 == 0
-                    and "forward" not in mod.__dict__):
+            projs = [getattr(mod, n, None) for n in ("q_proj", "k_proj", "v_proj")]
+            if (all(_gemv_ok(p) and "forward" not in p.__dict__ for p in projs)
+                    and len({p.in_features for p in projs}) == 1):
+                stash = {}
+                for i, p in enumerate(projs):
+                    p.forward = _decode_qkv_forward(p, projs, i, stash)
+                    self.patched.append(p)
+        for mod in self.module.modules():
+            if "forward" in mod.__dict__:
+                continue
+            if _gemv_ok(mod):
                 mod.forward = _decode_forward(mod)
+                self.patched.append(mod)
+            elif (type(mod) is MetalLigerSwiGLU and _gemv_ok(mod.gate_proj)
+                  and _gemv_ok(mod.up_proj) and mod.gate_proj.bias is None
+                  and mod.up_proj.bias is None):
+                mod.forward = _decode_mlp_forward(mod)
                 self.patched.append(mod)
         return self
 
@@ -179,6 +200,46 @@ class _DecodeLinears:
             del mod.forward
         self.patched = []
         return False
+
+
+def _gemv_ok(mod) -> bool:
+    return (type(mod) is nn.Linear and mod.weight.dtype == torch.bfloat16 and mod.weight.is_cuda
+            and mod.in_features % 8 == 0)
+
+
+def _decode_mlp_forward(mod):
+    """The fused SwiGLU MLP for a decode token: gate, up and the activation in
+    one GEMV launch (metal_liger::gemv_swiglu), then down_proj."""
+    orig = type(mod).forward
+    wg, wu = mod.gate_proj.weight, mod.up_proj.weight
+
+    def forward(x: Tensor) -> Tensor:
+        if x.dtype == torch.bfloat16 and x.numel() <= 2 * wg.shape[1] and x.is_cuda:
+            return mod.down_proj(torch.ops.metal_liger.gemv_swiglu(x, wg, wu))
+        return orig(mod, x)
+
+    return forward
+
+
+def _decode_qkv_forward(mod: nn.Linear, projs, i: int, stash: dict):
+    orig = type(mod).forward
+
+    def forward(x: Tensor) -> Tensor:
+        if not (x.dtype == torch.bfloat16 and x.numel() <= 2 * mod.in_features and x.is_cuda):
+            return orig(mod, x)
+        if i == 0:
+            q, k, v = torch.ops.metal_liger.gemv_multi(x, [p.weight for p in projs],
+                                                       [p.bias for p in projs])
+            stash["x"], stash[1], stash[2] = x, k, v
+            return q
+        if stash.get("x") is x and i in stash:
+            out = stash.pop(i)
+            if 1 not in stash and 2 not in stash:
+                stash.clear()
+            return out
+        return torch.ops.metal_liger.gemv(x, mod.weight, mod.bias)
+
+    return forward
 
 
 def _decode_forward(mod: nn.Linear):
