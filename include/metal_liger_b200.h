@@ -470,6 +470,15 @@ ML_API int ml_gemv_swiglu_bf16(const void* x, int64_t ld_x, const void* w_gate, 
                                const void* w_up, int64_t ld_u, int64_t batch, int64_t K,
                                int64_t inter, void* y, int64_t ld_y, void* stream);
 
+/*
+ * Self-test of the bounded device-side waits (no reference counterpart):
+ * enqueues on `stream` a one-warp kernel whose mbarrier wait can never
+ * complete, bounded to limit_us (1,000 - 1,000,000 us); the wait gives up and
+ * records (6 << 8) | ML_ERR_TIMEOUT in the device error word, which
+ * ml_device_error then returns.  Nothing faults, traps or hangs.
+ */
+ML_API int ml_selftest_bounded_wait(int64_t limit_us, void* stream);
+
 /* Synchronises `stream`, then returns and clears the device error word set
  * by a bounded wait inside a tcgen05 kernel that gave up ((site << 8) |
  * ML_ERR_TIMEOUT), or 0.  A negative-free ML_ERR_CUDA is returned if the

@@ -87,6 +87,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemm_bf16": (c_int, [c_int64, c_int64, ctypes.POINTER(GemmSegment), c_int, c_void_p, c_int,
                              c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "ml_gemm_set_cta_pair": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "ml_selftest_bounded_wait": (c_int, [c_int64, c_void_p]),
     "ml_lm_head_argmax_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ml_gemv_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,
                              c_int64, c_int64, c_void_p, c_int, c_int64, c_void_p]),

@@ -439,7 +439,47 @@ int choose_splits(int64_t m, int64_t n, int64_t k_total, int bn) {
 }  // namespace
 }  // namespace ml
 
+namespace ml {
+namespace gemm {
+namespace {
+
+// Self-test of the bounded-wait path the tcgen05 kernels use: one thread
+// waits on an mbarrier phase that nothing completes, through
+// sm100::mbar_wait_bounded with the limit shortened to `limit_ns`; the wait
+// gives up, records (SITE_SELFTEST << 8) | ML_ERR_TIMEOUT in the device error
+// word, and the kernel returns normally (no trap, the context stays usable).
+__global__ void selftest_bounded_wait(uint64_t limit_ns, int* err) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(&bar, 1);
+    abort_flag = 0;
+    sm100::fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0)
+    (void)sm100::mbar_wait_bounded(&bar, 0, &abort_flag, err, SITE_SELFTEST, limit_ns);
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace ml
+
 using namespace ml;
+
+extern "C" int ml_selftest_bounded_wait(int64_t limit_us, void* stream) {
+  ML_CHECK_ARG(limit_us >= 1000 && limit_us <= 1000000,
+               "selftest_bounded_wait: limit %lld us outside [1 ms, 1 s]", (long long)limit_us);
+  int* err = gemm::device_error_word();
+  if (err == nullptr) {
+    set_error("selftest_bounded_wait: device error word unavailable");
+    return ML_ERR_CUDA;
+  }
+  gemm::selftest_bounded_wait<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      (uint64_t)limit_us * 1000ull, err);
+  ML_CHECK_LAUNCH("selftest_bounded_wait");
+  return ML_OK;
+}
 
 extern "C" int ml_device_error(void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);

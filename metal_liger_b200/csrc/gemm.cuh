@@ -44,7 +44,7 @@ enum Epi : int {
 
 // Wait sites recorded in the device error word.
 enum Site : int { SITE_PROD_EMPTY = 1, SITE_MMA_TEMPTY = 2, SITE_MMA_FULL = 3, SITE_EPI = 4,
-                  SITE_DRAIN = 5 };
+                  SITE_DRAIN = 5, SITE_SELFTEST = 6 };
 
 struct alignas(64) Params {
   CUtensorMap tma_a[kMaxSeg];

@@ -159,3 +159,21 @@ def test_bad_arguments_rejected():
     rc = lib.ml_gemm_bf16(64, 64, arr, 1, d.data_ptr(), 0, 64, 1.0, 0.0, None, 0,
                           torch.cuda.current_stream().cuda_stream)
     assert rc == 1 and b"multiple of 8" in lib.ml_last_error()
+
+
+def test_bounded_wait_gives_up_and_reports():
+    """The bounded mbarrier wait of the tcgen05 kernels, made to run out on
+    purpose (a phase nothing completes, 20 ms limit): the kernel returns, the
+    device error word holds (site 6 << 8) | ML_ERR_TIMEOUT, reading it clears
+    it, and the context stays usable (a GEMM runs and checks after it)."""
+    lib = _C.load()
+    st = torch.cuda.current_stream().cuda_stream
+    assert lib.ml_device_error(st) == 0
+    assert lib.ml_selftest_bounded_wait(20000, st) == 0
+    assert lib.ml_device_error(st) == (6 << 8) | 4
+    assert lib.ml_device_error(st) == 0
+    assert lib.ml_selftest_bounded_wait(10, st) != 0      # limits below 1 ms are refused
+    a = torch.randn(256, 128, device=DEV).bfloat16()
+    b = torch.randn(192, 128, device=DEV).bfloat16()
+    d, _ = run_gemm([(a, b)], 256, 192)
+    torch.testing.assert_close(d.float(), reference([(a, b)]), rtol=2e-2, atol=2e-1)

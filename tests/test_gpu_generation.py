@@ -287,17 +287,23 @@ def test_generator_on_the_patched_model():
     from metal_liger_b200 import apply_metal_liger_to_qwen3vl
     from metal_liger_b200.generation import MetalLigerGenerator
 
+    from metal_liger_b200.patch import restore_attention_rope
+
     m = _model(seed=5)
     apply_metal_liger_to_qwen3vl(m, fuse_lora=False, fuse_qk_norm=True,
                                  fuse_rope_in_attention=True)
-    for p in m.parameters():
-        p.requires_grad_(False)
-    ids = torch.randint(0, 1000, (2, 7), generator=torch.Generator().manual_seed(13)).to(DEV)
-    g = MetalLigerGenerator(m)
-    graph = g.generate(ids, max_new_tokens=30)
-    eager = g.generate(ids, max_new_tokens=30, cuda_graph=False)
-    _same_or_near_tie(m, graph, eager)
-    _same_or_near_tie(m, graph, OG.generate(m, ids, max_new_tokens=30))
+    try:
+        for p in m.parameters():
+            p.requires_grad_(False)
+        ids = torch.randint(0, 1000, (2, 7), generator=torch.Generator().manual_seed(13)).to(DEV)
+        g = MetalLigerGenerator(m)
+        graph = g.generate(ids, max_new_tokens=30)
+        eager = g.generate(ids, max_new_tokens=30, cuda_graph=False)
+        _same_or_near_tie(m, graph, eager)
+        _same_or_near_tie(m, graph, OG.generate(m, ids, max_new_tokens=30))
+    finally:
+        # the RoPE rebinding is per modeling module (process-wide): undo it
+        restore_attention_rope(m)
 
 
 @pytest.mark.parametrize("rows", [1, 2])
