@@ -7,7 +7,11 @@ BASELINE configs[1] — SwiGLU (gate/up [8,2048,6144] bf16) plus RoPE (q
 [8,16,2048,128], k [8,8,2048,128] bf16, positions 0..2047, theta 5e6, cos/sin
 recomputed in-kernel), forward + backward — one "step" = one fwd+bwd pass of
 both ops over the 16,384 tokens.  Other configs are selectable with
-``--workload`` (they are parity-test cases; the default line is configs[1]).
+``--workload`` (they are parity-test cases; the default line is configs[1]):
+rmsnorm, flce (configs[2]; vocabulary-parallel under torchrun),
+lora, c5_step (configs[4], the Qwen3-VL-8B LoRA training step)
+and generate (greedy decoding with the static-KV generator on the Qwen3-VL-8B
+text decoder; its metric is generated tokens/s).
 
   value    device-timed tokens/s, inputs resident in HBM, CUDA events on the
            launching stream, max over ranks (weak scaling: every rank runs
