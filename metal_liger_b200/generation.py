@@ -36,6 +36,7 @@ forward returns ``last_hidden_state``) and a bias-free or biased
 
 from __future__ import annotations
 
+import contextlib
 import logging
 from collections import OrderedDict
 from typing import Optional
@@ -419,7 +420,7 @@ class MetalLigerGenerator:
                 side = torch.cuda.Stream(device=dev) if capture else None
                 if side is not None:
                     side.wait_stream(torch.cuda.current_stream(dev))
-                ctx = torch.cuda.stream(side) if side is not None else _nullcontext()
+                ctx = torch.cuda.stream(side) if side is not None else contextlib.nullcontext()
                 with ctx:
                     for _ in range(warm):
                         self._static_step(step)
@@ -520,14 +521,6 @@ class _DecodeState:
         self.mask = torch.zeros((B, 1, 1, L), dtype=torch.bool, device=dev)
         self.tok = torch.empty((B, 1), dtype=dtype, device=dev)
         self.graph = None
-
-
-class _nullcontext:
-    def __enter__(self):
-        return None
-
-    def __exit__(self, *exc):
-        return False
 
 
 def patch_generator(model: nn.Module, force: bool = False) -> nn.Module:
