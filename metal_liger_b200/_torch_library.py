@@ -273,6 +273,32 @@ def _bf16_2d(t: Tensor, cols: int) -> Tensor:
     return _contig(t)
 
 
+# The tcgen05 paths read 2-D operands with TMA, whose row pitch must be a
+# multiple of 16 bytes (8 bf16).  Other sizes are zero-padded to the next
+# multiple of 8 (the added rows/columns contribute zero products, and the
+# padding is sliced off the results), so every shape the reference accepts
+# works; multiples of 8 (all Qwen3-VL shapes) take no copies.
+def _p8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+def _pad2(t: Tensor, rows: int, cols: int) -> Tensor:
+    """Zero-padded [rows, cols] copy of 2-D ``t`` (``t`` itself when it has that shape)."""
+    if t.shape[0] == rows and t.shape[1] == cols:
+        return t
+    out = torch.zeros((rows, cols), dtype=t.dtype, device=t.device)
+    out[:t.shape[0], :t.shape[1]] = t
+    return out
+
+
+def _pad_proj(w: Tensor, a: Tensor, b: Tensor, fin8: int):
+    """Pads one adapter (W [out, in], A [r, in], B [out, r]) to in = fin8,
+    out = multiple of 8."""
+    o8 = _p8(w.shape[0])
+    r = a.shape[0]
+    return _pad2(w, o8, fin8), _pad2(a, r, fin8), _pad2(b, o8, r)
+
+
 def flce_forward_cuda(hidden: Tensor, weight: Tensor, labels: Tensor, bias: Tensor | None,
                       ignore_index: int, chunk_size: int, need_dx: bool, need_dw: bool):
     """(loss, dx_slabs, dw_acc): loss and, when requested, the fp32 gradients at
@@ -292,6 +318,16 @@ def flce_forward_cuda(hidden: Tensor, weight: Tensor, labels: Tensor, bias: Tens
                               need_dx, need_dw)
     if weight.dim() != 2 or weight.shape[1] != H:
         raise RuntimeError(f"flce_forward: weight {tuple(weight.shape)} does not match hidden {H}")
+    if H % 8:
+        H8 = _p8(H)
+        h2 = hidden.reshape(-1, H)
+        loss, dx, dw = flce_forward_cuda(_pad2(h2, h2.shape[0], H8), _pad2(weight, weight.shape[0], H8),
+                                         labels, bias, ignore_index, chunk_size, need_dx, need_dw)
+        if dx.numel():
+            dx = dx[..., :H].contiguous()
+        if dw.numel():
+            dw = dw[:, :H].contiguous()
+        return loss, dx, dw
     h2 = _bf16_2d(hidden, H)
     w2 = _bf16_2d(weight, H)
     lab = _contig(labels.reshape(-1).to(torch.int64))
@@ -393,6 +429,14 @@ def lora_qkv_forward_cuda(x, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling):
                                                          (kw, ka, kb, scaling[1]),
                                                          (vw, va, vb, scaling[2])], r)
         return outs[0], outs[1], outs[2], u
+    if H % 8 or any(w.shape[0] % 8 for w in (qw, kw, vw)):
+        H8 = _p8(H)
+        x2 = x.reshape(-1, H)
+        pq, pk, pv = (_pad_proj(w, a, b, H8) for w, a, b in ((qw, qa, qb), (kw, ka, kb),
+                                                             (vw, va, vb)))
+        q, k, v, u = lora_qkv_forward_cuda(_pad2(x2, x2.shape[0], H8), *pq, *pk, *pv, scaling)
+        return (q[:, :qw.shape[0]].contiguous(), k[:, :kw.shape[0]].contiguous(),
+                v[:, :vw.shape[0]].contiguous(), u)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     keep: list = []
@@ -428,6 +472,20 @@ def lora_qkv_backward_cuda(x, u, qw, qa, qb, kw, ka, kb, vw, va, vb, scaling, dq
         for (da, db), (_, a, b, _) in zip(grads, projs):
             flat += [da.to(a.dtype), db.to(b.dtype)]
         return (dx.to(x.dtype).view(x.shape), *flat)
+    if H % 8 or any(w.shape[0] % 8 for w in (qw, kw, vw)):
+        H8 = _p8(H)
+        x2 = x.reshape(-1, H)
+        T = x2.shape[0]
+        trip = ((qw, qa, qb, dq), (kw, ka, kb, dk), (vw, va, vb, dv))
+        padded = [_pad_proj(w, a, b, H8) for w, a, b, _ in trip]
+        dys = [_pad2(d.reshape(T, w.shape[0]), T, _p8(w.shape[0])) for w, _, _, d in trip]
+        res = lora_qkv_backward_cuda(_pad2(x2, T, H8), u, *padded[0], *padded[1], *padded[2],
+                                     scaling, *dys)
+        dx = res[0][:, :H].reshape(x.shape)
+        grads = []
+        for i, (w, _, _, _) in enumerate(trip):
+            grads += [res[1 + 2 * i][:, :H].contiguous(), res[2 + 2 * i][:w.shape[0]].contiguous()]
+        return (dx.contiguous(), *grads)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     keep: list = []
@@ -459,6 +517,11 @@ def lora_linear_forward_cuda(x, w, a, b, scaling):
         r = _check_rank((a,), (b,), (H,))
         (y,), u = F.lora_proj_forward(x.reshape(-1, H), [(w, a, b, scaling)], r)
         return y, u
+    if w.dim() == 2 and (H % 8 or w.shape[0] % 8):
+        x2 = x.reshape(-1, H)
+        y, u = lora_linear_forward_cuda(_pad2(x2, x2.shape[0], _p8(H)),
+                                        *_pad_proj(w, a, b, _p8(H)), scaling)
+        return y[:, :w.shape[0]].contiguous(), u
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     if w.dim() != 2 or w.shape[1] != H:
@@ -487,6 +550,15 @@ def lora_linear_backward_cuda(x, u, w, a, b, scaling, dy):
         dx, ((da, db),) = F.lora_proj_backward(x.reshape(-1, H).float(), u, [(w, a, b, scaling)],
                                                r, [dy.reshape(-1, w.shape[0])])
         return dx.to(x.dtype).view(x.shape), da.to(a.dtype), db.to(b.dtype)
+    if w.dim() == 2 and (H % 8 or w.shape[0] % 8):
+        x2 = x.reshape(-1, H)
+        T = x2.shape[0]
+        o8 = _p8(w.shape[0])
+        dxp, dap, dbp = lora_linear_backward_cuda(
+            _pad2(x2, T, _p8(H)), u, *_pad_proj(w, a, b, _p8(H)), scaling,
+            _pad2(dy.reshape(T, w.shape[0]), T, o8))
+        return (dxp[:, :H].reshape(x.shape).contiguous(), dap[:, :H].contiguous(),
+                dbp[:w.shape[0]].contiguous())
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
     r = _check_rank((a,), (b,), (H,))
@@ -518,9 +590,17 @@ def lora_mlp_forward_cuda(x, gw, ga, gb, uw, ua, ub, dw, da, db, scaling):
             x.reshape(-1, H), (gw, ga, gb, scaling[0]), (uw, ua, ub, scaling[1]),
             (dw, da, db, scaling[2]), r)
         return out.view(x.shape), g_, u_, h, u1, u2
+    inter = gw.shape[0]
+    if H % 8 or inter % 8:
+        H8, I8 = _p8(H), _p8(inter)
+        x2 = x.reshape(-1, H)
+        out, g_, u_, h, u1, u2 = lora_mlp_forward_cuda(
+            _pad2(x2, x2.shape[0], H8), *_pad_proj(gw, ga, gb, H8), *_pad_proj(uw, ua, ub, H8),
+            *_pad_proj(dw, da, db, I8), scaling)
+        return (out[:, :H].reshape(x.shape).contiguous(), g_[:, :inter].contiguous(),
+                u_[:, :inter].contiguous(), h[:, :inter].contiguous(), u1, u2)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
-    inter = gw.shape[0]
     if uw.shape[0] != inter or dw.shape != (H, inter) or gw.shape[1] != H or uw.shape[1] != H:
         raise RuntimeError("lora_mlp_forward: gate/up must be [inter, hidden], down [hidden, inter]")
     r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
@@ -560,9 +640,23 @@ def lora_mlp_backward_cuda(x, gate, up, h, u1, u2, gw, ga, gb, uw, ua, ub, dw, d
         for (ga_, gb_), (_, a, b, _) in zip(grads, projs):
             flat += [ga_.to(a.dtype), gb_.to(b.dtype)]
         return (dx.to(x.dtype).view(x.shape), *flat)
+    inter = gw.shape[0]
+    if H % 8 or inter % 8:
+        H8, I8 = _p8(H), _p8(inter)
+        x2 = x.reshape(-1, H)
+        T = x2.shape[0]
+        res = lora_mlp_backward_cuda(
+            _pad2(x2, T, H8), _pad2(gate.reshape(T, inter), T, I8),
+            _pad2(up.reshape(T, inter), T, I8), _pad2(h.reshape(T, inter), T, I8), u1, u2,
+            *_pad_proj(gw, ga, gb, H8), *_pad_proj(uw, ua, ub, H8), *_pad_proj(dw, da, db, I8),
+            scaling, _pad2(dy.reshape(T, H), T, H8))
+        cut = ((H, inter), (H, inter), (inter, H))    # (in, out) of gate, up, down
+        grads = []
+        for i, (fin, fout) in enumerate(cut):
+            grads += [res[1 + 2 * i][:, :fin].contiguous(), res[2 + 2 * i][:fout].contiguous()]
+        return (res[0][:, :H].reshape(x.shape).contiguous(), *grads)
     x2 = _bf16_2d(x, H)
     T = x2.shape[0]
-    inter = gw.shape[0]
     r = _check_rank((ga, ua, da), (gb, ub, db), (H, H, inter))
     keep: list = []
     projs = (_C.LoraProj * 3)()

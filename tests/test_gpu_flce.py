@@ -67,7 +67,8 @@ def _bf16_case(n, h, v, seed, ignore_frac=0.1):
 
 
 @pytest.mark.parametrize("n,h,v,chunk", [(1000, 256, 5000, 384), (130, 64, 300, 8192),
-                                         (256, 128, 2048, 100)])
+                                         (256, 128, 2048, 100),
+                                         (77, 100, 1001, 32)])   # hidden not a multiple of 8
 def test_bf16_against_oracle(n, h, v, chunk, pair_mode):
     hid, w, lab = _bf16_case(n, h, v, seed=n + v)
     loss, dx, dw = run_flce(hid, w, lab, chunk=chunk, grad_output=0.75)

@@ -122,7 +122,8 @@ def _proj(gen, out_f, in_f, r, s, dev="cpu", wstd=0.02, astd=0.05):
 
 
 @pytest.mark.parametrize("T,H,qo,kvo,r", [(400, 512, 512, 128, 16), (130, 256, 256, 64, 8),
-                                          (64, 128, 128, 128, 21)])
+                                          (64, 128, 128, 128, 21),
+                                          (70, 100, 100, 36, 8)])   # sizes not multiples of 8
 def test_qkv_bf16_against_oracle(T, H, qo, kvo, r, pair_mode):
     gen = torch.Generator().manual_seed(T + H)
     x = torch.randn(2, T // 2, H, generator=gen).bfloat16()
@@ -143,7 +144,8 @@ def test_qkv_bf16_against_oracle(T, H, qo, kvo, r, pair_mode):
         close_reduction(db, rdb, f"d{n}B")
 
 
-@pytest.mark.parametrize("T,H,I,r", [(300, 256, 768, 16), (128, 128, 384, 32)])
+@pytest.mark.parametrize("T,H,I,r", [(300, 256, 768, 16), (128, 128, 384, 32),
+                                     (50, 100, 204, 8)])   # sizes not multiples of 8
 def test_mlp_bf16_against_oracle(T, H, I, r, pair_mode):
     gen = torch.Generator().manual_seed(T + I)
     x = torch.randn(T, H, generator=gen).bfloat16()
@@ -159,7 +161,8 @@ def test_mlp_bf16_against_oracle(T, H, I, r, pair_mode):
         close_reduction(db, rdb, f"d{n}B")
 
 
-@pytest.mark.parametrize("T,H,OUT,r", [(300, 512, 384, 16), (130, 256, 1024, 64), (64, 128, 128, 8)])
+@pytest.mark.parametrize("T,H,OUT,r", [(300, 512, 384, 16), (130, 256, 1024, 64), (64, 128, 128, 8),
+                                       (33, 60, 44, 4)])   # sizes not multiples of 8
 def test_single_projection_against_oracle(T, H, OUT, r, pair_mode):
     """_LoRA_W (one fused LoRA linear, e.g. o_proj) vs the oracle's per-projection
     math; rank up to the full 64-wide slot."""
