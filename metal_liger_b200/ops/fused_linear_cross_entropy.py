@@ -164,6 +164,13 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
         weight_shard = weight_shard.to(torch.bfloat16)
     hidden = hidden.contiguous()
     weight_shard = weight_shard.contiguous()
+    h_in = hidden.shape[1]
+    if h_in % 8 and isinstance(phases, CudaShardPhases):
+        # TMA row pitch: zero-pad the hidden size to a multiple of 8 (zero
+        # columns add nothing to the logits; sliced off the gradients below)
+        from metal_liger_b200._torch_library import _p8, _pad2
+        hidden = _pad2(hidden, hidden.shape[0], _p8(h_in))
+        weight_shard = _pad2(weight_shard, weight_shard.shape[0], _p8(h_in))
     labels = labels.reshape(-1).to(torch.int64).contiguous()
     n, h = hidden.shape
     dev = hidden.device
@@ -197,6 +204,9 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
     for work in pending:
         work.wait()
     loss = row_loss.sum() * cnt[1]
+    if h != h_in:
+        dx = dx[:, :h_in].contiguous() if dx is not None else None
+        dw = dw[:, :h_in].contiguous() if dw is not None else None
     return loss, dx, dw
 
 
