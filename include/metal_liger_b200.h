@@ -458,6 +458,26 @@ ML_API int ml_gemv_multi_bf16(const void* x, int64_t ld_x, int nmat, const void*
                               const int64_t* ld_y, int y_dtype, void* stream);
 
 /*
+ * Decode-step attention (no reference counterpart; the reference's decode
+ * runs the model's attention over its growing cache, generation.py:109-115):
+ * out[b, 0, h, :] = sum_{j < n} softmax_j(scale * q[b, h] . k[b, h / G, j])
+ * v[b, h / G, j] with n = min(max_len, *pos + len_offset) read from device
+ * memory, G = q_heads / kv_heads (<= 16).  q is [B, q_heads, 1, head_dim] at
+ * element strides (sq_b, sq_h), head_dim contiguous; k_cache / v_cache
+ * [B, kv_heads, max_len, head_dim] contiguous bf16; out [B, 1, q_heads,
+ * head_dim] bf16; head_dim a multiple of 32 up to 256; fp32 scores and
+ * accumulation; workspace >= ml_decode_attention_workspace_bytes.
+ */
+ML_API size_t ml_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads,
+                                                  int64_t max_len, int64_t head_dim);
+ML_API int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_h,
+                                    const void* k_cache, const void* v_cache,
+                                    const int64_t* pos, int64_t len_offset, int64_t batch,
+                                    int64_t q_heads, int64_t kv_heads, int64_t max_len,
+                                    int64_t head_dim, float scale, void* out, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/*
  * Decode-time SwiGLU MLP input side: y[b, i] = bf16(silu(g) * u) with
  * g = bf16(x[b] . w_gate[i]), u = bf16(x[b] . w_up[i]) (fp32 accumulation;
  * bitwise equal to two ml_gemv_bf16 calls and ml_swiglu_forward), for

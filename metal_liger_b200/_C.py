@@ -94,6 +94,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemv_multi_bf16": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                                    c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int,
                                    c_void_p]),
+    "ml_decode_attention_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64, c_int64]),
+    "ml_decode_attention_bf16": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                         c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
+                                         ctypes.c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
     "ml_gemv_swiglu_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                     c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "ml_lm_head_argmax": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,

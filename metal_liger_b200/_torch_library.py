@@ -808,7 +808,38 @@ def gemv_multi_cuda(x: Tensor, weights: list[Tensor], biases: list[Tensor | None
     return [o.reshape(*x.shape[:-1], o.shape[1]) for o in outs]
 
 
+def decode_attention_cuda(q: Tensor, k_cache: Tensor, v_cache: Tensor, pos: Tensor,
+                          len_offset: int, scale: float):
+    """One decode step of attention: q [B, Hq, 1, D] against the first
+    ``pos + len_offset`` positions (pos: an int64 device tensor) of the static
+    caches k/v [B, Hkv, L, D]; returns [B, 1, Hq, D] bf16."""
+    _C.require_cuda("decode_attention", q, k_cache, v_cache, pos)
+    if q.dtype != torch.bfloat16 or k_cache.dtype != torch.bfloat16 or \
+            v_cache.dtype != torch.bfloat16:
+        raise RuntimeError("decode_attention: bf16 q and caches")
+    if q.dim() != 4 or q.shape[2] != 1 or k_cache.dim() != 4 or k_cache.shape != v_cache.shape:
+        raise RuntimeError(f"decode_attention: q {tuple(q.shape)} must be [B, Hq, 1, D] and the "
+                           f"caches equal [B, Hkv, L, D]")
+    B, Hq, _, D = q.shape
+    Bk, Hkv, L, Dk = k_cache.shape
+    if Bk != B or Dk != D or pos.dtype != torch.int64:
+        raise RuntimeError("decode_attention: batch / head_dim mismatch or non-int64 position")
+    if q.stride(3) != 1:
+        q = q.contiguous()
+    k_cache, v_cache = _contig(k_cache), _contig(v_cache)
+    out = torch.empty((B, 1, Hq, D), dtype=torch.bfloat16, device=q.device)
+    lib = _C.load()
+    nbytes = int(lib.ml_decode_attention_workspace_bytes(B, Hq, L, D))
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    _C.call("ml_decode_attention_bf16", _C.ptr(q), q.stride(0), q.stride(1), _C.ptr(k_cache),
+            _C.ptr(v_cache), _C.ptr(pos), int(len_offset), B, Hq, Hkv, L, D, float(scale),
+            _C.ptr(out), _C.ptr(ws), nbytes, _C.stream_of(q))
+    return out
+
+
 _SCHEMAS = {
+    "decode_attention": "decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, "
+                        "int len_offset, float scale) -> Tensor",
     "gemv_multi": "gemv_multi(Tensor x, Tensor[] weights, Tensor?[] biases) -> Tensor[]",
     "gemv_swiglu": "gemv_swiglu(Tensor x, Tensor w_gate, Tensor w_up) -> Tensor",
     "gemv": "gemv(Tensor x, Tensor weight, Tensor? bias) -> Tensor",
@@ -854,6 +885,7 @@ _SCHEMAS = {
 }
 
 _CUDA_IMPLS = {
+    "decode_attention": decode_attention_cuda,
     "gemv_multi": gemv_multi_cuda,
     "gemv_swiglu": gemv_swiglu_cuda,
     "gemv": gemv_cuda,
@@ -978,7 +1010,12 @@ def _fake_impls():
         return [torch.empty((*x.shape[:-1], w.shape[0]), dtype=x.dtype, device=x.device)
                 for w in weights]
 
+    def decode_attention_fake(q, k_cache, v_cache, pos, len_offset, scale):
+        B, Hq, _, D = q.shape
+        return torch.empty((B, 1, Hq, D), dtype=q.dtype, device=q.device)
+
     return {
+        "decode_attention": decode_attention_fake,
         "gemv_multi": gemv_multi_fake,
         "gemv_swiglu": gemv_swiglu_fake,
         "gemv": gemv_fake,

@@ -1,0 +1,316 @@
+// Decode-step attention for the static-KV generator: one query token per
+// sequence against the first `len` positions of the static KV cache, with
+// grouped-query heads read in place (no repeat_kv copies) and the length read
+// from device memory (the captured decode step advances it), so the step
+// needs no mask.  Split-K over the keys ("flash decoding"): each warp takes
+// 32 positions of one (sequence, kv head) for all G query heads of that group
+// and writes their partials (max, sum-exp, unnormalised output); a second
+// kernel merges the partials in order.
+//
+// Math: o = sum_j softmax_j(scale * q.k_j) v_j with fp32 scores, exponents
+// and accumulation over bf16 q, K, V — the computation of the reference's
+// attention on one query row (transformers' SDPA path).
+#include "common.cuh"
+
+#include <cmath>
+
+namespace ml {
+namespace {
+
+constexpr int kWarps = 4;      // warps per CTA
+constexpr int kChunk = 32;     // key positions per warp (one per lane): one partial
+constexpr int kMaxGroup = 16;  // query heads per kv head
+constexpr int kMaxDim = 256;   // head dimension, a multiple of 32
+constexpr int kMaxGD = 32;     // G * D / 32: output registers per lane
+
+struct DecodeArgs {
+  const __nv_bfloat16* q;  // [B, Hq, 1, D] at strides (sq_b, sq_h), D contiguous
+  const __nv_bfloat16* k;  // [B, Hkv, L, D] contiguous
+  const __nv_bfloat16* v;
+  const int64_t* pos;      // device: valid keys = *pos + len_offset
+  int64_t len_offset;
+  int64_t sq_b, sq_h;
+  int B, Hq, Hkv, L, D;
+  float scale;
+  float* part_m;           // [nchunk][B * Hq]
+  float* part_l;           // [nchunk][B * Hq]
+  float* part_o;           // [nchunk][B * Hq][D]
+  __nv_bfloat16* out;      // [B, 1, Hq, D]
+};
+
+// One warp = one partial over 32 key positions (a position per lane) for
+// every query head of one (sequence, kv head): the lane loads its whole K row
+// (all 16-byte loads issued before use) and forms the G scores; per head the
+// warp takes max / sum-exp with shuffles; then P.V walks the 32 positions
+// with the V row read coalesced (a lane owns DPL = D/32 output dimensions of
+// every head) and the probabilities broadcast by shuffle.  G and DPL are
+// template parameters so every per-lane array stays in registers.
+template <int G, int DPL>
+__global__ void __launch_bounds__(32 * kWarps)
+decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
+  constexpr int D = 32 * DPL;
+  constexpr int NCH = D / 8;            // 16-byte chunks of a K row
+  constexpr bool kPrefetchV = DPL <= 4;  // V fragments of all 32 positions in registers
+  __shared__ float qs[G * D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int c = blockIdx.x * kWarps + warp;  // partial index
+  const int nslot = (a.L + kChunk - 1) / kChunk;
+  const int64_t j0 = (int64_t)c * kChunk;
+  const int64_t kv_base = ((int64_t)b * a.Hkv + kvh) * a.L * D;
+  // K row and V fragments first: their addresses depend only on this warp's
+  // slot, not on the filled length, so all loads of the step overlap.
+  const int64_t j = j0 + lane;
+  const bool in_cache = c < nslot && j < a.L;
+  uint4 kv[NCH <= 16 ? NCH : 16];
+  if (in_cache) {
+    const uint4* krow = reinterpret_cast<const uint4*>(a.k + kv_base + j * D);
+#pragma unroll
+    for (int u = 0; u < (NCH <= 16 ? NCH : 16); ++u) kv[u] = krow[u];
+  }
+  __nv_bfloat162 vfrag[kPrefetchV ? kChunk : 1][DPL / 2];
+  if constexpr (kPrefetchV) {
+    if (c < nslot) {
+      const __nv_bfloat16* vbase = a.v + kv_base + j0 * D + lane * DPL;
+#pragma unroll
+      for (int kk = 0; kk < kChunk; ++kk)
+        if (j0 + kk < a.L) {
+#pragma unroll
+          for (int e = 0; e < DPL / 2; ++e)
+            vfrag[kk][e] = *reinterpret_cast<const __nv_bfloat162*>(vbase + (int64_t)kk * D + 2 * e);
+        }
+    }
+  }
+  const int64_t n = min((int64_t)a.L, *a.pos + a.len_offset);
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i - g * D;
+    qs[i] = __bfloat162float(a.q[(int64_t)b * a.sq_b + (int64_t)(kvh * G + g) * a.sq_h + d]);
+  }
+  __syncthreads();
+  if (c >= nslot) return;  // warps past the last partial slot
+  const int64_t stride = (int64_t)a.B * a.Hq;
+  const int64_t slot0 = (int64_t)c * stride + (int64_t)b * a.Hq + kvh * G;
+  if (j0 >= n) {  // past the filled positions: empty partials
+    if (lane < G) {
+      a.part_m[slot0 + lane] = -INFINITY;
+      a.part_l[slot0 + lane] = 0.f;
+    }
+    return;
+  }
+  const bool valid = j < n;
+  float s[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) s[g] = 0.f;
+  if (valid) {
+    const uint4* krow = reinterpret_cast<const uint4*>(a.k + kv_base + j * D);
+#pragma unroll
+    for (int h0 = 0; h0 < NCH; h0 += 16) {
+      constexpr int U = NCH < 16 ? NCH : 16;
+      if (h0 > 0) {  // second half of a 256-wide row
+#pragma unroll
+        for (int u = 0; u < U; ++u) kv[u] = krow[h0 + u];
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv[u]);
+        const int d0 = (h0 + u) * 8;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 kf = __bfloat1622float2(k2[e]);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            s[g] = fmaf(qs[g * D + d0 + 2 * e], kf.x, s[g]);
+            s[g] = fmaf(qs[g * D + d0 + 2 * e + 1], kf.y, s[g]);
+          }
+        }
+      }
+    }
+  }
+  float p[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float sc = valid ? s[g] * a.scale : -INFINITY;
+    const float m = warp_max(sc);
+    p[g] = valid ? __expf(sc - m) : 0.f;
+    const float l = warp_sum(p[g]);
+    if (lane == 0) {
+      a.part_m[slot0 + g] = m;
+      a.part_l[slot0 + g] = l;
+    }
+  }
+  float o[G][DPL];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) o[g][e] = 0.f;
+  const int cnt = (int)min((int64_t)kChunk, n - j0);
+  const __nv_bfloat16* vbase = a.v + kv_base + j0 * D + lane * DPL;
+#pragma unroll
+  for (int kk = 0; kk < kChunk; ++kk) {
+    if (kk < cnt) {
+      float vf[DPL];
+#pragma unroll
+      for (int e = 0; e < DPL / 2; ++e) {
+        const float2 f = kPrefetchV
+            ? __bfloat1622float2(vfrag[kPrefetchV ? kk : 0][e])
+            : __bfloat1622float2(
+                  *reinterpret_cast<const __nv_bfloat162*>(vbase + (int64_t)kk * D + 2 * e));
+        vf[2 * e] = f.x;
+        vf[2 * e + 1] = f.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pk = __shfl_sync(0xffffffffu, p[g], kk);
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[g][e] = fmaf(pk, vf[e], o[g][e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float* po = a.part_o + (slot0 + g) * D + lane * DPL;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) po[e] = o[g][e];
+  }
+}
+
+// out[b, 0, h, :] = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c over the
+// partials that hold keys (l_c > 0).  A warp per (b, h): lane c reads
+// partial c's (m, l) (32 partials per pass), one warp max and one warp sum
+// give M and the denominator, then each lane adds its D/32 output dimensions
+// of every partial with the weights broadcast by shuffle (the partials'
+// loads are independent, so they overlap).  Fixed order: deterministic.
+template <int DPL>
+__global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__ DecodeArgs a,
+                                                         int nchunk) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= (int64_t)a.B * a.Hq) return;
+  const int64_t stride = (int64_t)a.B * a.Hq;
+  float M = -INFINITY;
+  for (int c0 = 0; c0 < nchunk; c0 += 32) {
+    const int c = c0 + lane;
+    if (c < nchunk && a.part_l[c * stride + row] > 0.f)
+      M = fmaxf(M, a.part_m[c * stride + row]);
+  }
+  M = warp_max(M);
+  float L = 0.f;
+  float o[DPL];
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) o[e] = 0.f;
+  for (int c0 = 0; c0 < nchunk; c0 += 32) {
+    const int c = c0 + lane;
+    float w = 0.f, wl = 0.f;
+    if (c < nchunk) {
+      const float l = a.part_l[c * stride + row];
+      if (l > 0.f) {
+        w = __expf(a.part_m[c * stride + row] - M);
+        wl = w * l;
+      }
+    }
+    L += warp_sum(wl);
+    const int cn = min(32, nchunk - c0);
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      if (k >= cn) break;
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+      if (wk > 0.f) {
+        const float* po = a.part_o + ((int64_t)(c0 + k) * stride + row) * a.D + lane * DPL;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) o[e] = fmaf(wk, po[e], o[e]);
+      }
+    }
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const int b = (int)(row / a.Hq), h = (int)(row % a.Hq);
+  __nv_bfloat16* dst = a.out + ((int64_t)b * a.Hq + h) * a.D + lane * DPL;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) dst[e] = __float2bfloat16_rn(o[e] * inv);
+}
+
+}  // namespace
+}  // namespace ml
+
+using namespace ml;
+
+extern "C" size_t ml_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads,
+                                                      int64_t max_len, int64_t head_dim) {
+  if (batch <= 0 || q_heads <= 0 || max_len <= 0 || head_dim <= 0) return 0;
+  const int64_t nchunk = (max_len + kChunk - 1) / kChunk;
+  return (size_t)nchunk * batch * q_heads * (2 + head_dim) * sizeof(float);
+}
+
+extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_h,
+                                        const void* k_cache, const void* v_cache,
+                                        const int64_t* pos, int64_t len_offset, int64_t batch,
+                                        int64_t q_heads, int64_t kv_heads, int64_t max_len,
+                                        int64_t head_dim, float scale, void* out, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
+  ML_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && max_len > 0,
+               "decode_attention: bad sizes");
+  ML_CHECK_ARG(q_heads % kv_heads == 0 && q_heads / kv_heads <= kMaxGroup,
+               "decode_attention: %lld query heads per kv head (at most %d)",
+               (long long)(q_heads / std::max<int64_t>(kv_heads, 1)), kMaxGroup);
+  ML_CHECK_ARG(head_dim % 32 == 0 && head_dim <= kMaxDim,
+               "decode_attention: head_dim %lld must be a multiple of 32 up to %d",
+               (long long)head_dim, kMaxDim);
+  ML_CHECK_ARG((q_heads / kv_heads) * head_dim <= 32 * kMaxGD,
+               "decode_attention: query heads per kv head x head_dim above %d", 32 * kMaxGD);
+  ML_CHECK_ARG(q && k_cache && v_cache && pos && out, "decode_attention: null pointer");
+  ML_CHECK_ARG(aligned16(k_cache) && aligned16(v_cache),
+               "decode_attention: KV buffers must be 16-byte aligned");
+  ML_CHECK_ARG(batch * kv_heads <= 65535 && max_len < ((int64_t)1 << 31),
+               "decode_attention: too many sequences x kv heads");
+  ML_CHECK_ARG(workspace && workspace_bytes >= ml_decode_attention_workspace_bytes(
+                                                   batch, q_heads, max_len, head_dim),
+               "decode_attention: workspace too small");
+  DecodeArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v = static_cast<const __nv_bfloat16*>(v_cache);
+  a.pos = pos;
+  a.len_offset = len_offset;
+  a.sq_b = sq_b;
+  a.sq_h = sq_h;
+  a.B = (int)batch;
+  a.Hq = (int)q_heads;
+  a.Hkv = (int)kv_heads;
+  a.L = (int)max_len;
+  a.D = (int)head_dim;
+  a.scale = scale;
+  const int nchunk = (int)((max_len + kChunk - 1) / kChunk);
+  a.part_m = static_cast<float*>(workspace);
+  a.part_l = a.part_m + (int64_t)nchunk * batch * q_heads;
+  a.part_o = a.part_l + (int64_t)nchunk * batch * q_heads;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = (int)(q_heads / kv_heads);
+  const dim3 grid((nchunk + kWarps - 1) / kWarps, (unsigned)(batch * kv_heads));
+  const int dpl = (int)(head_dim / 32);
+#define ML_DA_CASE(G_, DPL_)                                               \
+  if (G == G_ && dpl == DPL_) {                                            \
+    decode_attn_chunk<G_, DPL_><<<grid, 32 * kWarps, 0, st>>>(a);          \
+    launched = true;                                                       \
+  }
+  bool launched = false;
+  ML_DA_CASE(1, 2) ML_DA_CASE(1, 4) ML_DA_CASE(1, 8)
+  ML_DA_CASE(2, 2) ML_DA_CASE(2, 4) ML_DA_CASE(2, 8)
+  ML_DA_CASE(4, 2) ML_DA_CASE(4, 4) ML_DA_CASE(4, 8)
+  ML_DA_CASE(8, 2) ML_DA_CASE(8, 4)
+  ML_DA_CASE(16, 2)
+#undef ML_DA_CASE
+  if (!launched) {
+    set_error("decode_attention: %d query heads per kv head with head_dim %lld is not built "
+              "(G in {1, 2, 4, 8, 16}, head_dim in {64, 128, 256}, G * head_dim <= 1024)",
+              G, (long long)head_dim);
+    return ML_ERR_INVALID_ARG;
+  }
+  ML_CHECK_LAUNCH("decode_attention(chunk)");
+  const int64_t warps = batch * q_heads;
+  const unsigned mgrid = (unsigned)((warps * 32 + 255) / 256);
+  if (dpl == 2) decode_attn_merge<2><<<mgrid, 256, 0, st>>>(a, nchunk);
+  else if (dpl == 4) decode_attn_merge<4><<<mgrid, 256, 0, st>>>(a, nchunk);
+  else decode_attn_merge<8><<<mgrid, 256, 0, st>>>(a, nchunk);
+  ML_CHECK_LAUNCH("decode_attention(merge)");
+  return ML_OK;
+}

@@ -154,24 +154,77 @@ class MetalLigerStaticCache(Cache):
         return self.max_seq_len
 
 
-class _DecodeLinears:
-    """While active, the bf16 CUDA ``nn.Linear`` layers of ``module`` run
-    calls with at most two activation rows (one decode token per sequence)
-    through ``metal_liger::gemv``, one HBM pass over the weight; the q, k
-    and v projections of an attention block share one ``gemv_multi`` launch
-    and the fused SwiGLU MLPs take gate, up and the activation in one
-    ``metal_liger::gemv_swiglu`` launch; every other call keeps the module's
-    own forward.  Restores the forwards on exit."""
+# Decode-step attention: registered with transformers' attention interface
+# under this name and selected on the decoder's config while the decode step
+# is captured.  It reads the number of filled positions from the device-side
+# position the captured step advances (_DECODE_POS), so the attention needs
+# neither a mask nor repeat_kv copies; any other call (prefill, several
+# query tokens, other dtypes) goes to transformers' SDPA path unchanged.
+_DECODE_ATTN = "metal_liger_decode"
+_DECODE_POS: list = [None]
 
-    def __init__(self, module: nn.Module):
+
+def _decode_attention_forward(module, query, key, value, attention_mask, dropout=0.0,
+                              scaling=None, **kwargs):
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    pos = _DECODE_POS[0]
+    D = query.shape[-1]
+    G = query.shape[1] // key.shape[1] if key.dim() == 4 and key.shape[1] else 0
+    if (pos is None or query.shape[2] != 1 or query.dtype != torch.bfloat16
+            or key.dtype != torch.bfloat16 or key.shape != value.shape
+            or query.shape[1] != G * key.shape[1] or G not in (1, 2, 4, 8, 16)
+            or D not in (64, 128, 256) or G * D > 1024):
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
+                                      scaling=scaling, **kwargs)
+    scale = float(scaling) if scaling is not None else query.shape[-1] ** -0.5
+    out = torch.ops.metal_liger.decode_attention(query, key, value, pos, 1, scale)
+    return out, None
+
+
+def _register_decode_attention() -> bool:
+    try:
+        from transformers import AttentionInterface
+    except ImportError:  # pragma: no cover - transformers is part of the image
+        return False
+    AttentionInterface.register(_DECODE_ATTN, _decode_attention_forward)
+    return True
+
+
+_register_decode_attention()
+
+
+class _DecodeKernels:
+    """While the decode step is captured: the decoder's SDPA attention becomes
+    the decode-step attention kernel (``pos`` = the step's device position),
+    and (``gemv``, batch <= 2) the bf16 CUDA ``nn.Linear`` layers run calls
+    with at most two activation rows through ``metal_liger::gemv``, one HBM
+    pass over the weight; the q, k and v projections of an attention block
+    share one ``gemv_multi`` launch and the fused SwiGLU MLPs take gate, up
+    and the activation in one ``metal_liger::gemv_swiglu`` launch; every
+    other call keeps the module's own forward.  All restored on exit."""
+
+    def __init__(self, module: nn.Module, pos: Optional[Tensor] = None, gemv: bool = True):
         self.module = module
+        self.pos = pos
+        self.gemv = gemv
         self.patched = []
+        self.attn_prev = None
 
     def __enter__(self):
         from metal_liger_b200 import _torch_library  # noqa: F401  (registers the ops)
 
+        cfg = getattr(self.module, "config", None)
+        if self.pos is not None and cfg is not None and \
+                getattr(cfg, "_attn_implementation", None) == "sdpa":
+            self.attn_prev = cfg._attn_implementation
+            cfg._attn_implementation = _DECODE_ATTN
+            _DECODE_POS[0] = self.pos
+
         from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU
 
+        if not self.gemv:
+            return self
         # q, k and v of an attention block in one launch: the q_proj call
         # computes all three and leaves k and v for the k_proj / v_proj calls
         # on the same activation tensor.
@@ -200,6 +253,10 @@ class _DecodeLinears:
         for mod in self.patched:
             del mod.forward
         self.patched = []
+        if self.attn_prev is not None:
+            self.module.config._attn_implementation = self.attn_prev
+            self.attn_prev = None
+        _DECODE_POS[0] = None
         return False
 
 
@@ -349,7 +406,10 @@ class MetalLigerGenerator:
         cache, tok, pos, mask, out = st["cache"], st["tok"], st["pos"], st["mask"], st["out"]
         B = tok.shape[0]
         mask.index_fill_(3, pos, True)
-        extra = {"position_ids": pos.view(1, 1, 1).expand(3, B, 1)} if self._mrope else {}
+        # positions from the device scalar (a view), never the host count a
+        # decoder would otherwise read at capture time
+        extra = {"position_ids": (pos.view(1, 1, 1).expand(3, B, 1) if self._mrope
+                                  else pos.view(1, 1).expand(B, 1))}
         h = self.decoder(input_ids=tok, attention_mask=mask, past_key_values=cache,
                          use_cache=True, return_dict=True, **extra).last_hidden_state[:, -1, :]
         tok.copy_(self._greedy(h).view(B, 1))
@@ -395,8 +455,8 @@ class MetalLigerGenerator:
         replayed; on CUDA the decoder's bf16 linear layers take the
         HBM-streaming GEMV while the step is built (batch <= 2)."""
         B = st.ids.shape[0]
-        if capture and B <= 2 and st.graph is None:
-            with _DecodeLinears(self.decoder):
+        if capture and st.graph is None:
+            with _DecodeKernels(self.decoder, st.pos, gemv=B <= 2):
                 return self._decode_static_inner(st, n, steps, eos_token_id, capture)
         return self._decode_static_inner(st, n, steps, eos_token_id, capture)
 

@@ -122,6 +122,59 @@ def test_static_decode_steps_match_reference_loop(eos):
     assert torch.equal(got, ref)
 
 
+def _qwen3_text_model(seed=0):
+    """A plain (non multimodal-RoPE) decoder: transformers' Qwen3ForCausalLM."""
+    from transformers.models.qwen3.configuration_qwen3 import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3ForCausalLM
+
+    cfg = Qwen3Config(hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=32, vocab_size=300,
+                      rms_norm_eps=1e-6, tie_word_embeddings=False)
+    cfg._attn_implementation = "sdpa"
+    torch.manual_seed(seed)
+    m = Qwen3ForCausalLM(cfg).to(torch.bfloat16)
+    with torch.no_grad():
+        m.lm_head.weight.normal_(0, 0.5)
+    return m.eval()
+
+
+def test_static_decode_on_a_plain_decoder():
+    """A decoder with 1-D RoPE positions: the static step passes [B, 1]
+    positions from the device scalar; tokens equal the reference loop's."""
+    m = _qwen3_text_model()
+    ids = torch.randint(0, 300, (2, 5), generator=torch.Generator().manual_seed(21))
+    ref = OG.generate(m, ids, max_new_tokens=10)
+    g = _TorchHeadGenerator.make(m)
+    assert not g._mrope
+    assert torch.equal(g.generate(ids, max_new_tokens=10, cuda_graph=True), ref)
+    assert torch.equal(g.generate(ids, max_new_tokens=10, cuda_graph=False), ref)
+
+
+def test_decode_attention_falls_back_outside_the_captured_step():
+    """The registered decode attention is transformers' SDPA whenever no decode
+    position is set (prefill, eager calls) or the shapes are not one query
+    token per sequence."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+
+    from metal_liger_b200 import generation as G
+
+    class _Attn(torch.nn.Module):
+        num_key_value_groups = 2
+        is_causal = True
+
+    mod = _Attn()
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(1, 4, 3, 32, generator=gen)
+    k = torch.randn(1, 2, 3, 32, generator=gen)
+    v = torch.randn(1, 2, 3, 32, generator=gen)
+    assert G._DECODE_POS[0] is None
+    a, _ = G._decode_attention_forward(mod, q, k, v, None, scaling=0.2)
+    b, _ = sdpa_attention_forward(mod, q, k, v, None, scaling=0.2)
+    torch.testing.assert_close(a, b)
+    from transformers import AttentionInterface
+    assert AttentionInterface._global_mapping[G._DECODE_ATTN] is G._decode_attention_forward
+
+
 def test_sampling_rule_matches_reference():
     """temperature != 1 samples; temperature 1 with top_p 1 is greedy, as in
     the reference (generation.py:118-123)."""

@@ -321,3 +321,43 @@ def test_gemv_multi_equals_separate_gemvs(rows):
         assert [tuple(o.shape) for o in outs] == [(rows, 1, w.shape[0]) for w in ws]
         for o, w, b in zip(outs, ws, biases):
             assert torch.equal(o, ops.gemv(x, w, b))
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L,D,n", [(1, 32, 8, 192, 128, 150), (2, 4, 2, 300, 64, 300),
+                                            (1, 8, 8, 64, 128, 1), (3, 8, 2, 260, 256, 129),
+                                            (2, 16, 1, 100, 64, 77), (2, 8, 2, 1024, 128, 777)])
+def test_decode_attention_against_fp32_reference(B, Hq, Hkv, L, D, n):
+    """Decode-step attention over the first n = pos + 1 cache positions (read
+    from device memory), grouped-query heads in place, against fp32 softmax
+    attention over the same positions."""
+    g = torch.Generator(device=DEV).manual_seed(B * L + n)
+    q = torch.randn(B, 1, Hq, D, generator=g, device=DEV).bfloat16().transpose(1, 2)
+    k = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    v = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    pos = torch.tensor([n - 1], dtype=torch.int64, device=DEV)
+    scale = D ** -0.5
+    out = torch.ops.metal_liger.decode_attention(q, k, v, pos, 1, scale)
+    assert out.shape == (B, 1, Hq, D) and out.dtype == torch.bfloat16
+    G = Hq // Hkv
+    kk = k[:, :, :n].float().repeat_interleave(G, dim=1)
+    vv = v[:, :, :n].float().repeat_interleave(G, dim=1)
+    att = torch.softmax((q.float() @ kk.transpose(-1, -2)) * scale, dim=-1)
+    ref = (att @ vv).transpose(1, 2)
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=1e-2)
+    pos.fill_(n - 2 if n > 1 else 0)                      # the length follows the device value
+    out2 = torch.ops.metal_liger.decode_attention(q, k, v, pos, 1, scale)
+    m = max(n - 1, 1)
+    att2 = torch.softmax((q.float() @ kk[:, :, :m].transpose(-1, -2)) * scale, dim=-1)
+    torch.testing.assert_close(out2.float(), (att2 @ vv[:, :, :m]).transpose(1, 2), rtol=2e-2,
+                               atol=1e-2)
+
+
+
+def test_decode_attention_rejects_unsupported_groups():
+    """Query heads per kv head x head_dim above 1024 is refused (the generator
+    then keeps transformers' attention)."""
+    q = torch.randn(1, 16, 1, 256, device=DEV).bfloat16()
+    k = torch.randn(1, 1, 64, 256, device=DEV).bfloat16()
+    pos = torch.zeros(1, dtype=torch.int64, device=DEV)
+    with pytest.raises(RuntimeError, match="above 1024"):
+        torch.ops.metal_liger.decode_attention(q, k, k, pos, 1, 0.0625)
