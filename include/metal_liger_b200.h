@@ -478,6 +478,23 @@ ML_API int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_h,
                                     size_t workspace_bytes, void* stream);
 
 /*
+ * Decode-step q/k preparation for Qwen3-style attention (no reference
+ * counterpart; it replaces, for the single new token, the per-head q_norm /
+ * k_norm RMSNorms, RoPE and the two cache writes): q [B, q_heads * D] and
+ * k [B, kv_heads * D] rows get RMSNorm with weights wq / wk (eps_q / eps_k;
+ * y = bf16((x * rrms) * w)) and RoPE with the model's cos / sin ([B, D] at
+ * batch stride cs_b, dtype cs_dtype; rotate-half, fp32, one rounding); q goes
+ * to q_out [B, q_heads, D], k to k_cache [B, kv_heads, max_len, D] at position
+ * *pos (device) and v [B, kv_heads * D] unchanged to v_cache at *pos.
+ * head_dim is 64, 128 or 256; q, k, v, caches and q_out bf16.
+ */
+ML_API int ml_decode_qk_norm_rope_bf16(
+    const void* q, const void* k, const void* v, const void* wq, const void* wk, int w_dtype,
+    float eps_q, float eps_k, const void* cos, const void* sin, int cs_dtype, int64_t cs_b,
+    int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t max_len, int64_t head_dim,
+    void* q_out, void* k_cache, void* v_cache, const int64_t* pos, void* stream);
+
+/*
  * Decode-time SwiGLU MLP input side: y[b, i] = bf16(silu(g) * u) with
  * g = bf16(x[b] . w_gate[i]), u = bf16(x[b] . w_up[i]) (fp32 accumulation;
  * bitwise equal to two ml_gemv_bf16 calls and ml_swiglu_forward), for

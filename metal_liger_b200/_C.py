@@ -98,6 +98,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_decode_attention_bf16": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                          c_int64, c_int64, c_int64, c_int64, c_int64, c_int64,
                                          ctypes.c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "ml_decode_qk_norm_rope_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_int, ctypes.c_float, ctypes.c_float, c_void_p,
+                                            c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
+                                            c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                            c_void_p, c_void_p]),
     "ml_gemv_swiglu_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                     c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "ml_lm_head_argmax": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,

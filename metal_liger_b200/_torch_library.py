@@ -837,7 +837,43 @@ def decode_attention_cuda(q: Tensor, k_cache: Tensor, v_cache: Tensor, pos: Tens
     return out
 
 
+def decode_qk_norm_rope_cuda(q: Tensor, k: Tensor, v: Tensor, wq: Tensor, wk: Tensor,
+                             eps_q: float, eps_k: float, cos: Tensor, sin: Tensor,
+                             k_cache: Tensor, v_cache: Tensor, pos: Tensor):
+    """Decode step, one new token per sequence: per-head RMSNorm + RoPE of q
+    ([B, 1, Hq*D]) and k, k and v written into the caches [B, Hkv, L, D] at
+    the device position ``pos``; returns q as [B, Hq, 1, D] bf16."""
+    _C.require_cuda("decode_qk_norm_rope", q, k, v, wq, wk, cos, sin, k_cache, v_cache, pos)
+    B, Hkv, L, D = k_cache.shape
+    if any(t.dtype != torch.bfloat16 for t in (q, k, v, k_cache, v_cache)):
+        raise RuntimeError("decode_qk_norm_rope: bf16 q, k, v and caches")
+    if q.numel() % (B * D) or k.numel() != B * Hkv * D or v.numel() != B * Hkv * D:
+        raise RuntimeError("decode_qk_norm_rope: q/k/v sizes do not match the caches")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("decode_qk_norm_rope: contiguous caches of equal shape")
+    if pos.dtype != torch.int64 or wq.numel() != D or wk.numel() != D:
+        raise RuntimeError("decode_qk_norm_rope: int64 position and [D] norm weights")
+    Hq = q.numel() // (B * D)
+    q, k, v = _contig(q), _contig(k), _contig(v)
+    cos2 = _contig(cos.reshape(B, -1))
+    sin2 = _contig(sin.reshape(B, -1))
+    if cos2.shape[1] != D or sin2.shape != cos2.shape:
+        raise RuntimeError("decode_qk_norm_rope: cos/sin must be [B, (1,) D]")
+    wq, wk = _contig(wq), _contig(wk)
+    if wk.dtype != wq.dtype:
+        wk = wk.to(wq.dtype)
+    q_out = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16, device=q.device)
+    _C.call("ml_decode_qk_norm_rope_bf16", _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(wq),
+            _C.ptr(wk), _C.dtype_code(wq), float(eps_q), float(eps_k), _C.ptr(cos2),
+            _C.ptr(sin2), _C.dtype_code(cos2), D, B, Hq, Hkv, L, D, _C.ptr(q_out),
+            _C.ptr(k_cache), _C.ptr(v_cache), _C.ptr(pos), _C.stream_of(q))
+    return q_out
+
+
 _SCHEMAS = {
+    "decode_qk_norm_rope": "decode_qk_norm_rope(Tensor q, Tensor k, Tensor v, Tensor wq, "
+                           "Tensor wk, float eps_q, float eps_k, Tensor cos, Tensor sin, "
+                           "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor pos) -> Tensor",
     "decode_attention": "decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, "
                         "int len_offset, float scale) -> Tensor",
     "gemv_multi": "gemv_multi(Tensor x, Tensor[] weights, Tensor?[] biases) -> Tensor[]",
@@ -885,6 +921,7 @@ _SCHEMAS = {
 }
 
 _CUDA_IMPLS = {
+    "decode_qk_norm_rope": decode_qk_norm_rope_cuda,
     "decode_attention": decode_attention_cuda,
     "gemv_multi": gemv_multi_cuda,
     "gemv_swiglu": gemv_swiglu_cuda,
@@ -1014,7 +1051,12 @@ def _fake_impls():
         B, Hq, _, D = q.shape
         return torch.empty((B, 1, Hq, D), dtype=q.dtype, device=q.device)
 
+    def decode_qk_fake(q, k, v, wq, wk, eps_q, eps_k, cos, sin, k_cache, v_cache, pos):
+        B, Hkv, L, D = k_cache.shape
+        return torch.empty((B, q.numel() // (B * D), 1, D), dtype=q.dtype, device=q.device)
+
     return {
+        "decode_qk_norm_rope": decode_qk_fake,
         "decode_attention": decode_attention_fake,
         "gemv_multi": gemv_multi_fake,
         "gemv_swiglu": gemv_swiglu_fake,

@@ -228,10 +228,137 @@ __global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__
   for (int e = 0; e < DPL; ++e) dst[e] = __float2bfloat16_rn(o[e] * inv);
 }
 
+// Decode-step q/k preparation for Qwen3-style attention, one warp per head
+// row of the single new token: q and k rows get the per-head RMSNorm
+// (y = bf16((x * rrms) * w), the fused RMSNorm's rounding) and then RoPE from
+// the model's own cos/sin (y1 = a1*c1 - a2*s1, y2 = a2*c2 + a1*s2 in fp32,
+// rounded once: the fused RoPE's arithmetic, partner half by shuffle); q goes
+// to q_out [B, Hq, D], k to the K cache and the v row unchanged to the V
+// cache, both at position *pos.  Replaces the two per-head norms, RoPE and
+// the two cache writes of a decode step (five launches) with one.
+struct QkPrep {
+  const __nv_bfloat16* q;  // [B, Hq * D]
+  const __nv_bfloat16* k;  // [B, Hkv * D]
+  const __nv_bfloat16* v;  // [B, Hkv * D]
+  const void* wq;
+  const void* wk;
+  int w_dtype;
+  float eps_q, eps_k;
+  const void* cos;         // [B, (1,) D] at batch stride cs_b
+  const void* sin;
+  int cs_dtype;
+  int64_t cs_b;
+  __nv_bfloat16* q_out;    // [B, Hq, D]
+  __nv_bfloat16* k_cache;  // [B, Hkv, L, D]
+  __nv_bfloat16* v_cache;
+  const int64_t* pos;
+  int B, Hq, Hkv, L;
+};
+
+template <int EPL>
+__global__ void __launch_bounds__(256) decode_qk_prep(const __grid_constant__ QkPrep a) {
+  constexpr int D = 32 * EPL;
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int per_b = a.Hq + 2 * a.Hkv;
+  if (row >= (int64_t)a.B * per_b) return;
+  const int b = (int)(row / per_b);
+  const int r = (int)(row % per_b);
+  const int64_t p = *a.pos;
+  if (p < 0 || p >= a.L) return;  // outside the cache: nothing to write
+  const int d0 = lane * EPL;
+  if (r >= a.Hq + a.Hkv) {  // v row: copy into the cache
+    const int h = r - a.Hq - a.Hkv;
+    const __nv_bfloat16* src = a.v + ((int64_t)b * a.Hkv + h) * D + d0;
+    __nv_bfloat16* dst = a.v_cache + (((int64_t)b * a.Hkv + h) * a.L + p) * D + d0;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) dst[e] = src[e];
+    return;
+  }
+  const bool is_q = r < a.Hq;
+  const int h = is_q ? r : r - a.Hq;
+  const __nv_bfloat16* src = is_q ? a.q + ((int64_t)b * a.Hq + h) * D + d0
+                                  : a.k + ((int64_t)b * a.Hkv + h) * D + d0;
+  const void* w = is_q ? a.wq : a.wk;
+  float x[EPL];
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    x[e] = __bfloat162float(src[e]);
+    ss = fmaf(x[e], x[e], ss);
+  }
+  ss = warp_sum(ss);
+  const float rr = rsqrtf(ss * (1.f / (float)D) + (is_q ? a.eps_q : a.eps_k));
+  float y[EPL], yp[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e)
+    y[e] = __bfloat162float(__float2bfloat16_rn((x[e] * rr) * load_as_f32(w, d0 + e, a.w_dtype)));
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) yp[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+  const bool first_half = lane < 16;
+  float o[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    const int d = d0 + e;
+    const float c = load_as_f32(a.cos, (int64_t)b * a.cs_b + d, a.cs_dtype);
+    const float sn = load_as_f32(a.sin, (int64_t)b * a.cs_b + d, a.cs_dtype);
+    // first half: a1 = y, a2 = partner; second half: a2 = y, a1 = partner
+    o[e] = first_half ? y[e] * c - yp[e] * sn : y[e] * c + yp[e] * sn;
+  }
+  __nv_bfloat16* dst = is_q ? a.q_out + ((int64_t)b * a.Hq + h) * D + d0
+                            : a.k_cache + (((int64_t)b * a.Hkv + h) * a.L + p) * D + d0;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(o[e]);
+}
+
 }  // namespace
 }  // namespace ml
 
 using namespace ml;
+
+extern "C" int ml_decode_qk_norm_rope_bf16(
+    const void* q, const void* k, const void* v, const void* wq, const void* wk, int w_dtype,
+    float eps_q, float eps_k, const void* cos, const void* sin, int cs_dtype, int64_t cs_b,
+    int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t max_len, int64_t head_dim,
+    void* q_out, void* k_cache, void* v_cache, const int64_t* pos, void* stream) {
+  ML_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && max_len > 0,
+               "decode_qk_norm_rope: bad sizes");
+  ML_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
+               "decode_qk_norm_rope: head_dim %lld not in {64, 128, 256}", (long long)head_dim);
+  ML_CHECK_ARG(q && k && v && wq && wk && cos && sin && q_out && k_cache && v_cache && pos,
+               "decode_qk_norm_rope: null pointer");
+  ML_CHECK_ARG((w_dtype >= 0 && w_dtype <= 2) && (cs_dtype >= 0 && cs_dtype <= 2),
+               "decode_qk_norm_rope: bad dtype codes");
+  QkPrep a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k = static_cast<const __nv_bfloat16*>(k);
+  a.v = static_cast<const __nv_bfloat16*>(v);
+  a.wq = wq;
+  a.wk = wk;
+  a.w_dtype = w_dtype;
+  a.eps_q = eps_q;
+  a.eps_k = eps_k;
+  a.cos = cos;
+  a.sin = sin;
+  a.cs_dtype = cs_dtype;
+  a.cs_b = cs_b;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.pos = pos;
+  a.B = (int)batch;
+  a.Hq = (int)q_heads;
+  a.Hkv = (int)kv_heads;
+  a.L = (int)max_len;
+  const int64_t rows = batch * (q_heads + 2 * kv_heads);
+  const unsigned grid = (unsigned)((rows * 32 + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (head_dim == 64) decode_qk_prep<2><<<grid, 256, 0, st>>>(a);
+  else if (head_dim == 128) decode_qk_prep<4><<<grid, 256, 0, st>>>(a);
+  else decode_qk_prep<8><<<grid, 256, 0, st>>>(a);
+  ML_CHECK_LAUNCH("decode_qk_norm_rope");
+  return ML_OK;
+}
 
 extern "C" size_t ml_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads,
                                                       int64_t max_len, int64_t head_dim) {

@@ -196,18 +196,22 @@ _register_decode_attention()
 
 class _DecodeKernels:
     """While the decode step is captured: the decoder's SDPA attention becomes
-    the decode-step attention kernel (``pos`` = the step's device position),
-    and (``gemv``, batch <= 2) the bf16 CUDA ``nn.Linear`` layers run calls
+    the decode-step attention kernel (``pos`` = the step's device position);
+    with ``gemv`` (batch <= 2) fully patched Qwen3-style attention blocks run
+    their decode step as q/k/v GEMV, fused norm + RoPE + cache write,
+    attention and o_proj, and the bf16 CUDA ``nn.Linear`` layers run calls
     with at most two activation rows through ``metal_liger::gemv``, one HBM
     pass over the weight; the q, k and v projections of an attention block
     share one ``gemv_multi`` launch and the fused SwiGLU MLPs take gate, up
     and the activation in one ``metal_liger::gemv_swiglu`` launch; every
     other call keeps the module's own forward.  All restored on exit."""
 
-    def __init__(self, module: nn.Module, pos: Optional[Tensor] = None, gemv: bool = True):
+    def __init__(self, module: nn.Module, pos: Optional[Tensor] = None, gemv: bool = True,
+                 cache: Optional["MetalLigerStaticCache"] = None):
         self.module = module
         self.pos = pos
         self.gemv = gemv
+        self.cache = cache
         self.patched = []
         self.attn_prev = None
 
@@ -225,6 +229,14 @@ class _DecodeKernels:
 
         if not self.gemv:
             return self
+        # Fully patched Qwen3-style attention blocks: the whole decode step of
+        # the block in four launches (q/k/v GEMV, norm + RoPE + cache write,
+        # attention chunks + merge) and o_proj.
+        if self.pos is not None and self.cache is not None:
+            for mod in self.module.modules():
+                if _decode_block_ok(mod, self.cache) and "forward" not in mod.__dict__:
+                    mod.forward = _decode_block_forward(mod, self.cache, self.pos)
+                    self.patched.append(mod)
         # q, k and v of an attention block in one launch: the q_proj call
         # computes all three and leaves k and v for the k_proj / v_proj calls
         # on the same activation tensor.
@@ -258,6 +270,63 @@ class _DecodeKernels:
             self.attn_prev = None
         _DECODE_POS[0] = None
         return False
+
+
+def _decode_block_ok(attn, cache) -> bool:
+    """Attention blocks whose decode step the fused path reproduces: q/k/v/o
+    plain bf16 linears, q_norm / k_norm this library's RMSNorm, RoPE rebound
+    to this library's kernel (so the arithmetic is the model's own eager
+    path's), and head shapes the decode kernels take."""
+    import sys
+
+    from metal_liger_b200.ops.fused_rms_norm import MetalLigerRMSNorm
+    from metal_liger_b200.patch import _fused_rotary_pos_emb
+
+    projs = [getattr(attn, n, None) for n in ("q_proj", "k_proj", "v_proj", "o_proj")]
+    if not all(_gemv_ok(p) and "forward" not in p.__dict__ for p in projs):
+        return False
+    qn, kn = getattr(attn, "q_norm", None), getattr(attn, "k_norm", None)
+    if type(qn) is not MetalLigerRMSNorm or type(kn) is not MetalLigerRMSNorm:
+        return False
+    mod = sys.modules.get(type(attn).__module__)
+    if mod is None or getattr(mod, "apply_rotary_pos_emb", None) is not _fused_rotary_pos_emb:
+        return False
+    D = getattr(attn, "head_dim", None)
+    layer = getattr(attn, "layer_idx", None)
+    if D not in (64, 128, 256) or layer is None or layer >= cache.num_layers:
+        return False
+    if cache.head_dim != D or attn.q_proj.out_features % D or attn.k_proj.out_features != \
+            cache.num_kv_heads * D or attn.v_proj.out_features != cache.num_kv_heads * D:
+        return False
+    G = attn.q_proj.out_features // D // cache.num_kv_heads
+    return (G * cache.num_kv_heads * D == attn.q_proj.out_features and G in (1, 2, 4, 8, 16)
+            and G * D <= 1024)
+
+
+def _decode_block_forward(attn, cache, pos: Tensor):
+    orig = type(attn).forward
+    layer = attn.layer_idx
+    D = attn.head_dim
+    projs = [attn.q_proj, attn.k_proj, attn.v_proj]
+    kc, vc = cache.key_cache[layer], cache.value_cache[layer]
+
+    def forward(hidden_states, position_embeddings=None, attention_mask=None,
+                past_key_values=None, **kwargs):
+        B, S = hidden_states.shape[0], hidden_states.shape[1]
+        if (S != 1 or B > 2 or hidden_states.dtype != torch.bfloat16 or position_embeddings is None
+                or past_key_values is not cache):
+            return orig(attn, hidden_states, position_embeddings, attention_mask,
+                        past_key_values, **kwargs)
+        ops = torch.ops.metal_liger
+        q, k, v = ops.gemv_multi(hidden_states, [p.weight for p in projs], [p.bias for p in projs])
+        cos, sin = position_embeddings
+        q4 = ops.decode_qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
+                                     float(attn.q_norm.eps), float(attn.k_norm.eps), cos, sin,
+                                     kc, vc, pos)
+        out = ops.decode_attention(q4, kc, vc, pos, 1, float(attn.scaling))
+        return attn.o_proj(out.reshape(B, S, -1)), None
+
+    return forward
 
 
 def _gemv_ok(mod) -> bool:
@@ -456,7 +525,7 @@ class MetalLigerGenerator:
         HBM-streaming GEMV while the step is built (batch <= 2)."""
         B = st.ids.shape[0]
         if capture and st.graph is None:
-            with _DecodeKernels(self.decoder, st.pos, gemv=B <= 2):
+            with _DecodeKernels(self.decoder, st.pos, gemv=B <= 2, cache=st.cache):
                 return self._decode_static_inner(st, n, steps, eos_token_id, capture)
         return self._decode_static_inner(st, n, steps, eos_token_id, capture)
 

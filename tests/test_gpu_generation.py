@@ -361,3 +361,40 @@ def test_decode_attention_rejects_unsupported_groups():
     pos = torch.zeros(1, dtype=torch.int64, device=DEV)
     with pytest.raises(RuntimeError, match="above 1024"):
         torch.ops.metal_liger.decode_attention(q, k, k, pos, 1, 0.0625)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D", [(1, 32, 8, 128), (2, 4, 2, 64), (1, 8, 4, 256)])
+def test_decode_qk_norm_rope_against_the_unfused_ops(B, Hq, Hkv, D):
+    """One new token: per-head RMSNorm (this library's) + RoPE (this library's,
+    with the model's cos/sin) of q and k, k/v written into the caches at the
+    device position; the fused kernel against the separate ops at bf16
+    rounding (one ulp), the untouched cache positions unchanged."""
+    from metal_liger_b200.ops.fused_rope import apply_fused_rotary
+
+    g = torch.Generator(device=DEV).manual_seed(B * Hq + D)
+    L, p = 40, 17
+    q = torch.randn(B, 1, Hq * D, generator=g, device=DEV).bfloat16()
+    k = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    v = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    wq = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    wk = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    ang = torch.rand(B, 1, D // 2, generator=g, device=DEV) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16()
+    kc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    vc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    kc0, vc0 = kc.clone(), vc.clone()
+    pos = torch.tensor([p], dtype=torch.int64, device=DEV)
+    ops = torch.ops.metal_liger
+    q4 = ops.decode_qk_norm_rope(q, k, v, wq, wk, 1e-6, 1e-5, cos, sin, kc, vc, pos)
+    assert q4.shape == (B, Hq, 1, D)
+    qn = ops.rms_norm_forward(q.view(B, 1, Hq, D), wq, 1e-6, "")[0].transpose(1, 2)
+    kn = ops.rms_norm_forward(k.view(B, 1, Hkv, D), wk, 1e-5, "")[0].transpose(1, 2)
+    qr, kr = apply_fused_rotary(qn, kn, cos.unsqueeze(1), sin.unsqueeze(1))
+    ulp = 2.0 ** -7
+    assert torch.allclose(q4.float(), qr.float(), rtol=ulp, atol=ulp)
+    assert torch.allclose(kc[:, :, p].float(), kr[:, :, 0].float(), rtol=ulp, atol=ulp)
+    assert torch.equal(vc[:, :, p], v.view(B, Hkv, D))
+    keep = torch.ones(L, dtype=torch.bool)
+    keep[p] = False
+    assert torch.equal(kc[:, :, keep], kc0[:, :, keep]) and torch.equal(vc[:, :, keep], vc0[:, :, keep])
