@@ -1,6 +1,7 @@
 """Test helpers for the vocabulary-parallel FLCE: oracle-based shard phases (CPU)
 and a multi-process runner.  Test infrastructure only."""
 
+import io
 import os
 import socket
 import traceback
@@ -69,6 +70,8 @@ def run_ranks(fn, world, port, backend, timeout_s, *args):
     results = {}
     for _ in range(world):
         rank, res = q.get(timeout=120)
+        if isinstance(res, bytes):
+            res = torch.load(io.BytesIO(res), weights_only=False)
         results[rank] = res
     for p in procs:
         p.join(timeout=60)
@@ -92,7 +95,11 @@ def _entry(fn, rank, world, port, backend, timeout_s, q, args):
         dist.init_process_group(backend, rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=timeout_s), **kw)
         res = fn(rank, world, *args)
-        q.put((rank, res))
+        # results travel as serialised bytes: tensors put on the queue would be
+        # shared through file descriptors that vanish when this process exits
+        buf = io.BytesIO()
+        torch.save(res, buf)
+        q.put((rank, buf.getvalue()))
         dist.destroy_process_group()
     except Exception:  # report, never hang the parent
         q.put((rank, "ERROR: " + traceback.format_exc()))
