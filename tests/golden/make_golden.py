@@ -171,9 +171,12 @@ def case_lora_mlp(mod, seed, x_shape, inter, r, s, dtype):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("METAL_LIGER_REF", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("METAL_LIGER_REF"),
+                    help="directory of the reference package (or METAL_LIGER_REF)")
     ap.add_argument("--out", default=str(HERE))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference (or METAL_LIGER_REF): the reference package's directory")
     rms, swi, rope, flce, lora = import_reference(Path(args.reference))
     torch.set_num_threads(max(1, min(8, os.cpu_count() or 1)))
     cases = {
