@@ -508,6 +508,39 @@ ML_API int ml_gemv_swiglu_bf16(const void* x, int64_t ld_x, const void* w_gate, 
                                int64_t inter, void* y, int64_t ld_y, void* stream);
 
 /*
+ * The decoder layer's decode step fused around the GEMVs (no reference
+ * counterpart; the reference's decode runs the layer's modules one by one,
+ * generation.py:109-115, through transformers' decoder layer: input norm,
+ * attention, residual add, post-attention norm, MLP, residual add).
+ *
+ * ml_gemv_residual_bf16: y[b, n] = bf16(bf16(x[b] . weight[n] (+ bias[n])) +
+ * residual[b, n]) — ml_gemv_bf16 followed by the bf16 residual add, bit for
+ * bit; residual [batch, N] bf16 at pitch ld_r (NULL: plain bf16 GEMV), not
+ * overlapping y; y bf16.
+ *
+ * ml_gemv_rmsnorm_multi_bf16 / ml_gemv_rmsnorm_swiglu_bf16: ml_gemv_multi_bf16
+ * / ml_gemv_swiglu_bf16 of the RMSNorm'd activations bf16((x * rrms) * w),
+ * norm_weight [K] bf16 (16-byte aligned), bitwise equal to
+ * ml_rms_norm_forward (bf16 x and weight, 16-byte aligned rows) followed by
+ * the GEMV; K a multiple of 8 up to 16,384 (the RMSNorm kernel's vector row
+ * layouts).
+ */
+ML_API int ml_gemv_residual_bf16(const void* x, int64_t ld_x, const void* weight, int64_t ld_w,
+                                 const void* bias, int bias_dtype, const void* residual,
+                                 int64_t ld_r, int64_t batch, int64_t K, int64_t N, void* y,
+                                 int64_t ld_y, void* stream);
+ML_API int ml_gemv_rmsnorm_multi_bf16(const void* x, int64_t ld_x, const void* norm_weight,
+                                      float eps, int nmat, const void* const* weight,
+                                      const int64_t* ld_w, const int64_t* n,
+                                      const void* const* bias, int bias_dtype, int64_t batch,
+                                      int64_t K, void* const* y, const int64_t* ld_y,
+                                      int y_dtype, void* stream);
+ML_API int ml_gemv_rmsnorm_swiglu_bf16(const void* x, int64_t ld_x, const void* norm_weight,
+                                       float eps, const void* w_gate, int64_t ld_g,
+                                       const void* w_up, int64_t ld_u, int64_t batch, int64_t K,
+                                       int64_t inter, void* y, int64_t ld_y, void* stream);
+
+/*
  * Self-test of the bounded device-side waits (no reference counterpart):
  * enqueues on `stream` a one-warp kernel whose mbarrier wait can never
  * complete, bounded to limit_us (1,000 - 1,000,000 us); the wait gives up and

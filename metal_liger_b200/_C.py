@@ -105,6 +105,15 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                             c_void_p, c_void_p]),
     "ml_gemv_swiglu_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                     c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
+    "ml_gemv_residual_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int,
+                                      c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                      c_int64, c_void_p]),
+    "ml_gemv_rmsnorm_multi_bf16": (c_int, [c_void_p, c_int64, c_void_p, ctypes.c_float, c_int,
+                                           c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64,
+                                           c_int64, c_void_p, c_void_p, c_int, c_void_p]),
+    "ml_gemv_rmsnorm_swiglu_bf16": (c_int, [c_void_p, c_int64, c_void_p, ctypes.c_float,
+                                            c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                                            c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "ml_lm_head_argmax": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,
                                   c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p,
                                   c_size_t, c_void_p]),

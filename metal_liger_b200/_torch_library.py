@@ -715,97 +715,166 @@ def lm_head_argmax_cuda(hidden: Tensor, weight: Tensor, bias: Tensor | None, log
     return index, value
 
 
-def gemv_cuda(x: Tensor, weight: Tensor, bias: Tensor | None):
-    """Decode-time linear layer for 1-2 activation rows: x [..., K] bf16 with
-    at most 2 rows, weight [N, K] bf16 -> [..., N] bf16 (fp32 accumulation,
-    one HBM pass over the weight)."""
-    _C.require_cuda("gemv", x, weight, bias)
-    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
-        raise RuntimeError("gemv: x and weight must be bfloat16")
-    K = x.shape[-1]
-    if weight.dim() != 2 or weight.shape[1] != K:
-        raise RuntimeError(f"gemv: weight {tuple(weight.shape)} does not match x {tuple(x.shape)}")
+def _gemv_rows(name: str, x: Tensor, K: int) -> tuple[int, Tensor]:
     rows = x.numel() // K if K else 0
     if rows > 2:
-        raise RuntimeError(f"gemv: {rows} rows; the GEMV path takes at most 2")
+        raise RuntimeError(f"{name}: {rows} rows; the GEMV path takes at most 2")
     x2 = x.reshape(rows, K)
     if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
         x2 = x2.contiguous()
+    return rows, x2
+
+
+def _norm_weight(name: str, norm_weight: Tensor, K: int) -> Tensor:
+    if norm_weight.dtype != torch.bfloat16 or norm_weight.shape != (K,):
+        raise RuntimeError(f"{name}: the norm weight must be bf16 [{K}]")
+    norm_weight = norm_weight.contiguous()
+    if norm_weight.data_ptr() % 16:
+        norm_weight = norm_weight.clone()
+    return norm_weight
+
+
+def _gemv(name: str, x: Tensor, weight: Tensor, bias: Tensor | None,
+          residual: Tensor | None = None) -> Tensor:
+    _C.require_cuda(name, x, weight, bias, residual)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x and weight must be bfloat16")
+    K = x.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != K:
+        raise RuntimeError(f"{name}: weight {tuple(weight.shape)} does not match x "
+                           f"{tuple(x.shape)}")
+    rows, x2 = _gemv_rows(name, x, K)
     weight = _contig(weight)
     if bias is not None:
         bias = _contig(bias)
     N = weight.shape[0]
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or residual.numel() != rows * N or \
+                residual.shape[-1] != N:
+            raise RuntimeError(f"{name}: residual {tuple(residual.shape)} is not bf16 "
+                               f"[..., {N}] with {rows} rows")
+        residual = residual.reshape(rows, N).contiguous()
     y = torch.empty((rows, N), dtype=torch.bfloat16, device=x.device)
     if rows:
-        _C.call("ml_gemv_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K, _C.ptr(weight),
-                weight.stride(0), _C.ptr(bias), _C.dtype_code(bias) if bias is not None else 0,
-                rows, K, N, _C.ptr(y), _C.dtype_code(torch.bfloat16), N, _C.stream_of(x))
+        ld_x = x2.stride(0) if rows > 1 else K
+        bdt = _C.dtype_code(bias) if bias is not None else 0
+        if residual is None:
+            _C.call("ml_gemv_bf16", _C.ptr(x2), ld_x, _C.ptr(weight), weight.stride(0),
+                    _C.ptr(bias), bdt, rows, K, N, _C.ptr(y), _C.dtype_code(torch.bfloat16), N,
+                    _C.stream_of(x))
+        else:
+            _C.call("ml_gemv_residual_bf16", _C.ptr(x2), ld_x, _C.ptr(weight), weight.stride(0),
+                    _C.ptr(bias), bdt, _C.ptr(residual), N, rows, K, N, _C.ptr(y), N,
+                    _C.stream_of(x))
     return y.reshape(*x.shape[:-1], N)
+
+
+def gemv_cuda(x: Tensor, weight: Tensor, bias: Tensor | None):
+    """Decode-time linear layer for 1-2 activation rows: x [..., K] bf16 with
+    at most 2 rows, weight [N, K] bf16 -> [..., N] bf16 (fp32 accumulation,
+    one HBM pass over the weight)."""
+    return _gemv("gemv", x, weight, bias)
+
+
+def gemv_residual_cuda(x: Tensor, weight: Tensor, bias: Tensor | None, residual: Tensor):
+    """residual + gemv(x, weight, bias) in one launch, bit for bit the two
+    ops (the decoder layer's `residual + o_proj(...)` / `+ down_proj(...)`)."""
+    return _gemv("gemv_residual", x, weight, bias, residual)
+
+
+def _gemv_swiglu(name: str, x: Tensor, norm_weight: Tensor | None, eps: float, w_gate: Tensor,
+                 w_up: Tensor) -> Tensor:
+    _C.require_cuda(name, x, w_gate, w_up, norm_weight)
+    if x.dtype != torch.bfloat16 or w_gate.dtype != torch.bfloat16 or w_up.dtype != torch.bfloat16:
+        raise RuntimeError(f"{name}: x and the weights must be bfloat16")
+    K = x.shape[-1]
+    if w_gate.shape != w_up.shape or w_gate.dim() != 2 or w_gate.shape[1] != K:
+        raise RuntimeError(f"{name}: weights {tuple(w_gate.shape)} / {tuple(w_up.shape)} "
+                           f"do not match x {tuple(x.shape)}")
+    rows, x2 = _gemv_rows(name, x, K)
+    if norm_weight is not None:
+        norm_weight = _norm_weight(name, norm_weight, K)
+    w_gate, w_up = _contig(w_gate), _contig(w_up)
+    inter = w_gate.shape[0]
+    y = torch.empty((rows, inter), dtype=torch.bfloat16, device=x.device)
+    if rows:
+        ld_x = x2.stride(0) if rows > 1 else K
+        if norm_weight is None:
+            _C.call("ml_gemv_swiglu_bf16", _C.ptr(x2), ld_x, _C.ptr(w_gate), w_gate.stride(0),
+                    _C.ptr(w_up), w_up.stride(0), rows, K, inter, _C.ptr(y), inter,
+                    _C.stream_of(x))
+        else:
+            _C.call("ml_gemv_rmsnorm_swiglu_bf16", _C.ptr(x2), ld_x, _C.ptr(norm_weight),
+                    float(eps), _C.ptr(w_gate), w_gate.stride(0), _C.ptr(w_up), w_up.stride(0),
+                    rows, K, inter, _C.ptr(y), inter, _C.stream_of(x))
+    return y.reshape(*x.shape[:-1], inter)
 
 
 def gemv_swiglu_cuda(x: Tensor, w_gate: Tensor, w_up: Tensor):
     """Decode-time SwiGLU input side for 1-2 rows: silu(x W_g^T) * (x W_u^T),
     bf16, equal bit for bit to gemv, gemv and swiglu_forward."""
-    _C.require_cuda("gemv_swiglu", x, w_gate, w_up)
-    if x.dtype != torch.bfloat16 or w_gate.dtype != torch.bfloat16 or w_up.dtype != torch.bfloat16:
-        raise RuntimeError("gemv_swiglu: x and the weights must be bfloat16")
-    K = x.shape[-1]
-    if w_gate.shape != w_up.shape or w_gate.dim() != 2 or w_gate.shape[1] != K:
-        raise RuntimeError(f"gemv_swiglu: weights {tuple(w_gate.shape)} / {tuple(w_up.shape)} "
-                           f"do not match x {tuple(x.shape)}")
-    rows = x.numel() // K if K else 0
-    if rows > 2:
-        raise RuntimeError(f"gemv_swiglu: {rows} rows; the GEMV path takes at most 2")
-    x2 = x.reshape(rows, K)
-    if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
-        x2 = x2.contiguous()
-    w_gate, w_up = _contig(w_gate), _contig(w_up)
-    inter = w_gate.shape[0]
-    y = torch.empty((rows, inter), dtype=torch.bfloat16, device=x.device)
-    if rows:
-        _C.call("ml_gemv_swiglu_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K,
-                _C.ptr(w_gate), w_gate.stride(0), _C.ptr(w_up), w_up.stride(0), rows, K, inter,
-                _C.ptr(y), inter, _C.stream_of(x))
-    return y.reshape(*x.shape[:-1], inter)
+    return _gemv_swiglu("gemv_swiglu", x, None, 0.0, w_gate, w_up)
 
 
-def gemv_multi_cuda(x: Tensor, weights: list[Tensor], biases: list[Tensor | None]):
-    """Several decode-time projections of the same 1-2 activation rows in one
-    launch (q, k and v): [x W_i^T (+ b_i)] as bf16 tensors [..., N_i]."""
+def gemv_rmsnorm_swiglu_cuda(x: Tensor, norm_weight: Tensor, eps: float, w_gate: Tensor,
+                             w_up: Tensor):
+    """gemv_swiglu of rms_norm_forward(x, norm_weight, eps) in one launch, bit
+    for bit the two ops (the decoder layer's post-attention norm and MLP
+    input side)."""
+    return _gemv_swiglu("gemv_rmsnorm_swiglu", x, norm_weight, eps, w_gate, w_up)
+
+
+def _gemv_multi(name: str, x: Tensor, norm_weight: Tensor | None, eps: float,
+                weights: list[Tensor], biases: list[Tensor | None]):
     import ctypes
 
-    _C.require_cuda("gemv_multi", x, *weights, *[b for b in biases if b is not None])
+    _C.require_cuda(name, x, *weights, *[b for b in biases if b is not None], norm_weight)
     if not 1 <= len(weights) <= 4 or (biases and len(biases) != len(weights)):
-        raise RuntimeError("gemv_multi: 1-4 weights, and one bias entry per weight if any")
+        raise RuntimeError(f"{name}: 1-4 weights, and one bias entry per weight if any")
     K = x.shape[-1]
     if x.dtype != torch.bfloat16 or any(w.dtype != torch.bfloat16 or w.dim() != 2 or
                                         w.shape[1] != K for w in weights):
-        raise RuntimeError("gemv_multi: bf16 x [..., K] and bf16 weights [N_i, K]")
-    rows = x.numel() // K if K else 0
-    if rows > 2:
-        raise RuntimeError(f"gemv_multi: {rows} rows; the GEMV path takes at most 2")
-    x2 = x.reshape(rows, K)
-    if x2.stride(-1) != 1 or (rows > 1 and x2.stride(0) % 8) or x2.data_ptr() % 16:
-        x2 = x2.contiguous()
+        raise RuntimeError(f"{name}: bf16 x [..., K] and bf16 weights [N_i, K]")
+    rows, x2 = _gemv_rows(name, x, K)
+    if norm_weight is not None:
+        norm_weight = _norm_weight(name, norm_weight, K)
     weights = [_contig(w) for w in weights]
     biases = [None if b is None else _contig(b) for b in (biases or [None] * len(weights))]
     bdt = {b.dtype for b in biases if b is not None}
     if len(bdt) > 1:
-        raise RuntimeError("gemv_multi: biases of different dtypes")
+        raise RuntimeError(f"{name}: biases of different dtypes")
     outs = [torch.empty((rows, w.shape[0]), dtype=torch.bfloat16, device=x.device)
             for w in weights]
     if rows:
         m = len(weights)
         P = ctypes.c_void_p * m
         I64 = ctypes.c_int64 * m
-        _C.call("ml_gemv_multi_bf16", _C.ptr(x2), x2.stride(0) if rows > 1 else K, m,
-                P(*[w.data_ptr() for w in weights]), I64(*[w.stride(0) for w in weights]),
+        mats = (m, P(*[w.data_ptr() for w in weights]), I64(*[w.stride(0) for w in weights]),
                 I64(*[w.shape[0] for w in weights]),
                 P(*[0 if b is None else b.data_ptr() for b in biases]) if bdt else None,
                 _C.dtype_code(bdt.pop()) if bdt else 0, rows, K,
                 P(*[o.data_ptr() for o in outs]), I64(*[o.shape[1] for o in outs]),
-                _C.dtype_code(torch.bfloat16), _C.stream_of(x))
+                _C.dtype_code(torch.bfloat16))
+        ld_x = x2.stride(0) if rows > 1 else K
+        if norm_weight is None:
+            _C.call("ml_gemv_multi_bf16", _C.ptr(x2), ld_x, *mats, _C.stream_of(x))
+        else:
+            _C.call("ml_gemv_rmsnorm_multi_bf16", _C.ptr(x2), ld_x, _C.ptr(norm_weight),
+                    float(eps), *mats, _C.stream_of(x))
     return [o.reshape(*x.shape[:-1], o.shape[1]) for o in outs]
+
+
+def gemv_multi_cuda(x: Tensor, weights: list[Tensor], biases: list[Tensor | None]):
+    """Several decode-time projections of the same 1-2 activation rows in one
+    launch (q, k and v): [x W_i^T (+ b_i)] as bf16 tensors [..., N_i]."""
+    return _gemv_multi("gemv_multi", x, None, 0.0, weights, biases)
+
+
+def gemv_rmsnorm_multi_cuda(x: Tensor, norm_weight: Tensor, eps: float, weights: list[Tensor],
+                            biases: list[Tensor | None]):
+    """gemv_multi of rms_norm_forward(x, norm_weight, eps) in one launch, bit
+    for bit the two ops (the decoder layer's input norm and q/k/v)."""
+    return _gemv_multi("gemv_rmsnorm_multi", x, norm_weight, eps, weights, biases)
 
 
 def decode_attention_cuda(q: Tensor, k_cache: Tensor, v_cache: Tensor, pos: Tensor,
@@ -879,6 +948,12 @@ _SCHEMAS = {
     "gemv_multi": "gemv_multi(Tensor x, Tensor[] weights, Tensor?[] biases) -> Tensor[]",
     "gemv_swiglu": "gemv_swiglu(Tensor x, Tensor w_gate, Tensor w_up) -> Tensor",
     "gemv": "gemv(Tensor x, Tensor weight, Tensor? bias) -> Tensor",
+    "gemv_residual": "gemv_residual(Tensor x, Tensor weight, Tensor? bias, Tensor residual) "
+                     "-> Tensor",
+    "gemv_rmsnorm_multi": "gemv_rmsnorm_multi(Tensor x, Tensor norm_weight, float eps, "
+                          "Tensor[] weights, Tensor?[] biases) -> Tensor[]",
+    "gemv_rmsnorm_swiglu": "gemv_rmsnorm_swiglu(Tensor x, Tensor norm_weight, float eps, "
+                           "Tensor w_gate, Tensor w_up) -> Tensor",
     "lm_head_argmax": "lm_head_argmax(Tensor hidden, Tensor weight, Tensor? bias, "
                       "int logit_dtype) -> (Tensor, Tensor)",
     "rms_norm_forward": "rms_norm_forward(Tensor x, Tensor weight, float eps, str kernel_dir) "
@@ -926,6 +1001,9 @@ _CUDA_IMPLS = {
     "gemv_multi": gemv_multi_cuda,
     "gemv_swiglu": gemv_swiglu_cuda,
     "gemv": gemv_cuda,
+    "gemv_residual": gemv_residual_cuda,
+    "gemv_rmsnorm_multi": gemv_rmsnorm_multi_cuda,
+    "gemv_rmsnorm_swiglu": gemv_rmsnorm_swiglu_cuda,
     "lm_head_argmax": lm_head_argmax_cuda,
     "rms_norm_forward": rms_norm_forward_cuda,
     "rms_norm_backward": rms_norm_backward_cuda,
@@ -1047,6 +1125,16 @@ def _fake_impls():
         return [torch.empty((*x.shape[:-1], w.shape[0]), dtype=x.dtype, device=x.device)
                 for w in weights]
 
+    def gemv_residual_fake(x, weight, bias, residual):
+        return torch.empty((*x.shape[:-1], weight.shape[0]), dtype=x.dtype, device=x.device)
+
+    def gemv_rmsnorm_multi_fake(x, norm_weight, eps, weights, biases):
+        return [torch.empty((*x.shape[:-1], w.shape[0]), dtype=x.dtype, device=x.device)
+                for w in weights]
+
+    def gemv_rmsnorm_swiglu_fake(x, norm_weight, eps, w_gate, w_up):
+        return torch.empty((*x.shape[:-1], w_gate.shape[0]), dtype=x.dtype, device=x.device)
+
     def decode_attention_fake(q, k_cache, v_cache, pos, len_offset, scale):
         B, Hq, _, D = q.shape
         return torch.empty((B, 1, Hq, D), dtype=q.dtype, device=q.device)
@@ -1061,6 +1149,9 @@ def _fake_impls():
         "gemv_multi": gemv_multi_fake,
         "gemv_swiglu": gemv_swiglu_fake,
         "gemv": gemv_fake,
+        "gemv_residual": gemv_residual_fake,
+        "gemv_rmsnorm_multi": gemv_rmsnorm_multi_fake,
+        "gemv_rmsnorm_swiglu": gemv_rmsnorm_swiglu_fake,
         "lm_head_argmax": lm_argmax,
         "lora_qkv_forward": lqkv_fwd,
         "lora_qkv_backward": lqkv_bwd,

@@ -64,6 +64,98 @@ __device__ __forceinline__ void row_dot(const uint4* __restrict__ wrow, const ui
   }
 }
 
+// RMSNorm of the staged activations in place, the decoder's input /
+// post-attention norm fused into the projection that consumes it:
+// hs[b] = bf16((x * r) * w) with r = rsqrt(mean(x^2) + eps), computed the
+// way the RMSNorm forward kernel (rms_norm.cu, rms_fwd_vec / rms_fwd_ring)
+// computes a row laid out as `tpr` threads of `nv` 16-byte vectors — thread
+// t squares vectors t, t + tpr, ... in element order with fmaf, the row
+// group sums by shuffles (tpr < 32) or by warp butterflies and then the
+// warps' partials in warp order — so the fused product equals RMSNorm
+// followed by the GEMV bit for bit.  Needs tpr <= blockDim.x.  Ends with
+// __syncthreads().
+template <int NB>
+__device__ __forceinline__ void rmsnorm_rows(uint4* hs, int64_t nchunk,
+                                             const __nv_bfloat16* __restrict__ nw, float eps,
+                                             int tpr, int nv) {
+  __shared__ float red[32];
+  __shared__ float tot_s;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float inv_h = 1.f / (float)(nchunk * 8);
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const uint4* row = hs + b * nchunk;
+    float ss = 0.f;
+    if (t < tpr) {
+      for (int i = 0; i < nv; ++i) {
+        const int64_t v = (int64_t)i * tpr + t;
+        if (v < nchunk) {
+          const uint4 c = row[v];
+          const __nv_bfloat162* e = reinterpret_cast<const __nv_bfloat162*>(&c);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(e[j]);
+            ss = fmaf(f.x, f.x, ss);
+            ss = fmaf(f.y, f.y, ss);
+          }
+        }
+      }
+    }
+    if (tpr < 32) {
+      for (int o = tpr >> 1; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if (t == 0) tot_s = ss;
+    } else {
+      ss = warp_sum(ss);
+      if (lane == 0 && warp < (tpr >> 5)) red[warp] = ss;
+    }
+    __syncthreads();
+    float tot;
+    if (tpr < 32) {
+      tot = tot_s;
+    } else {
+      tot = 0.f;
+      for (int i = 0; i < (tpr >> 5); ++i) tot += red[i];  // warp order, as the norm kernel
+    }
+    const float r = rsqrtf(fmaf(tot, inv_h, eps));
+    for (int64_t c = t; c < nchunk; c += blockDim.x) {
+      uint4 xv = hs[b * nchunk + c];
+      const uint4 wv = *reinterpret_cast<const uint4*>(nw + c * 8);
+      __nv_bfloat162* xe = reinterpret_cast<__nv_bfloat162*>(&xv);
+      const __nv_bfloat162* we = reinterpret_cast<const __nv_bfloat162*>(&wv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fx = __bfloat1622float2(xe[j]);
+        const float2 fw = __bfloat1622float2(we[j]);
+        xe[j] = __floats2bfloat162_rn((fx.x * r) * fw.x, (fx.y * r) * fw.y);
+      }
+      hs[b * nchunk + c] = xv;
+    }
+    __syncthreads();  // red / tot_s reused by the next row; hs complete
+  }
+}
+
+// Host: the RMSNorm forward kernel's row layout for a bf16 row of K
+// elements (rms_norm.cu, pick_cfg with backward = false): `nv` 16-byte
+// vectors on each of `tpr` threads.  False when that kernel takes its scalar
+// path for such a row (then there is nothing to mirror).
+inline bool rms_row_layout(int64_t K, int* tpr, int* nv) {
+  if (K % 8 != 0) return false;
+  const int64_t nvec = K / 8;
+  int v = 1;
+  if (nvec > 256)
+    while ((nvec + v - 1) / v > 256 && v < 8) v *= 2;
+  const int64_t per = (nvec + v - 1) / v;
+  int64_t t;
+  if (per <= 4) t = 4;
+  else if (per <= 8) t = 8;
+  else if (per <= 16) t = 16;
+  else t = (per + 31) / 32 * 32;
+  if (t > (v == 1 ? 512 : 256)) return false;
+  *tpr = (int)t;
+  *nv = v;
+  return true;
+}
+
 // Host: whether a call can take the GEMV kernels (16-byte rows, shared
 // memory for the activations).
 inline bool eligible(int64_t rows, int64_t K, int64_t ld_x, int64_t ld_w, const void* x,

@@ -182,7 +182,7 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
     const float tot = group_sum2(ss, 0.f, red, buf, tpr).x;
     buf ^= 1;
     if (active) {
-      const float r = rsqrtf(tot * inv_h + eps);
+      const float r = rsqrtf(fmaf(tot, inv_h, eps));
       if (t == 0 && rrms != nullptr) rrms[row] = r;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
@@ -270,7 +270,7 @@ rms_fwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict_
     const float tot = group_sum2(ss, 0.f, red, buf, tpr).x;
     buf ^= 1;
     if (row < rows) {
-      const float r = rsqrtf(tot * inv_h + eps);
+      const float r = rsqrtf(fmaf(tot, inv_h, eps));
       if (t == 0 && rrms != nullptr) rrms[row] = r;
       if (has_col) {
         Vec16<TX> o;
@@ -374,7 +374,7 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
     const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
     buf ^= 1;
     if (active) {
-      const float r = rrms != nullptr ? rv : rsqrtf(sums.x * inv_h + eps);
+      const float r = rrms != nullptr ? rv : rsqrtf(fmaf(sums.x, inv_h, eps));
       const float c = (sums.y * inv_h) * (r * r * r);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
@@ -494,7 +494,7 @@ rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __
     const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
     buf ^= 1;
     if (active) {
-      const float r = rrms != nullptr ? ringr[slot * tpr + t] : rsqrtf(sums.x * inv_h + eps);
+      const float r = rrms != nullptr ? ringr[slot * tpr + t] : rsqrtf(fmaf(sums.x, inv_h, eps));
       const float c = (sums.y * inv_h) * (r * r * r);
       Vec16<TX> o;
 #pragma unroll

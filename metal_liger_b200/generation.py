@@ -229,9 +229,18 @@ class _DecodeKernels:
 
         if not self.gemv:
             return self
-        # Fully patched Qwen3-style attention blocks: the whole decode step of
-        # the block in four launches (q/k/v GEMV, norm + RoPE + cache write,
-        # attention chunks + merge) and o_proj.
+        # Fully patched Qwen3-style decoder layers: the layer's decode step in
+        # seven launches (input norm + q/k/v GEMV, q/k norm + RoPE + cache
+        # write, attention chunks + merge, o GEMV + residual, post-attention
+        # norm + gate/up/SwiGLU GEMV, down GEMV + residual).
+        if self.pos is not None and self.cache is not None:
+            for mod in self.module.modules():
+                if _decode_layer_ok(mod, self.cache) and "forward" not in mod.__dict__:
+                    mod.forward = _decode_layer_forward(mod, self.cache, self.pos)
+                    self.patched.append(mod)
+        # Fully patched Qwen3-style attention blocks (of layers not patched
+        # whole): the decode step of the block in four launches (q/k/v GEMV,
+        # norm + RoPE + cache write, attention chunks + merge) and o_proj.
         if self.pos is not None and self.cache is not None:
             for mod in self.module.modules():
                 if _decode_block_ok(mod, self.cache) and "forward" not in mod.__dict__:
@@ -325,6 +334,73 @@ def _decode_block_forward(attn, cache, pos: Tensor):
                                      kc, vc, pos)
         out = ops.decode_attention(q4, kc, vc, pos, 1, float(attn.scaling))
         return attn.o_proj(out.reshape(B, S, -1)), None
+
+    return forward
+
+
+# Decoder layers whose forward is, for one decode token, exactly: residual =
+# h; h = input_layernorm(h); h = self_attn(h); h = residual + h; residual =
+# h; h = post_attention_layernorm(h); h = mlp(h); h = residual + h
+# (transformers' Qwen3 / Qwen3-VL text decoder layers).
+_FUSED_LAYER_TYPES = ("Qwen3DecoderLayer", "Qwen3VLTextDecoderLayer")
+
+
+def _decode_layer_ok(layer, cache) -> bool:
+    """Decoder layers whose whole decode step the fused path reproduces bit
+    for bit: a known layer type, this library's RMSNorms (bf16 weights, a
+    vector row layout: hidden a multiple of 8 up to 16,384), an attention
+    block `_decode_block_ok` takes and this library's SwiGLU MLP on plain
+    bias-free bf16 linears."""
+    from metal_liger_b200.ops.fused_rms_norm import MetalLigerRMSNorm
+    from metal_liger_b200.ops.fused_swiglu import MetalLigerSwiGLU
+
+    if type(layer).__name__ not in _FUSED_LAYER_TYPES:
+        return False
+    attn, mlp = getattr(layer, "self_attn", None), getattr(layer, "mlp", None)
+    norms = [getattr(layer, "input_layernorm", None),
+             getattr(layer, "post_attention_layernorm", None)]
+    if attn is None or "forward" in attn.__dict__ or not _decode_block_ok(attn, cache):
+        return False
+    H = attn.q_proj.in_features
+    if H % 8 or H > 16384:
+        return False
+    for n in norms:
+        if (type(n) is not MetalLigerRMSNorm or "forward" in n.__dict__
+                or n.weight.dtype != torch.bfloat16 or tuple(n.weight.shape) != (H,)):
+            return False
+    if type(mlp) is not MetalLigerSwiGLU or "forward" in mlp.__dict__:
+        return False
+    lin = [mlp.gate_proj, mlp.up_proj, mlp.down_proj]
+    return (all(_gemv_ok(p) and "forward" not in p.__dict__ and p.bias is None for p in lin)
+            and mlp.gate_proj.in_features == H and mlp.down_proj.out_features == H)
+
+
+def _decode_layer_forward(layer, cache, pos: Tensor):
+    orig = type(layer).forward
+    attn, mlp = layer.self_attn, layer.mlp
+    ln1, ln2 = layer.input_layernorm, layer.post_attention_layernorm
+    projs = [attn.q_proj, attn.k_proj, attn.v_proj]
+    kc, vc = cache.key_cache[attn.layer_idx], cache.value_cache[attn.layer_idx]
+
+    def forward(hidden_states, *args, **kwargs):
+        pe = kwargs.get("position_embeddings")
+        B, S = hidden_states.shape[0], hidden_states.shape[1]
+        if (args or S != 1 or B > 2 or hidden_states.dtype != torch.bfloat16 or pe is None
+                or kwargs.get("past_key_values") is not cache):
+            return orig(layer, hidden_states, *args, **kwargs)
+        ops = torch.ops.metal_liger
+        q, k, v = ops.gemv_rmsnorm_multi(hidden_states, ln1.weight, float(ln1.eps),
+                                         [p.weight for p in projs], [p.bias for p in projs])
+        cos, sin = pe
+        q4 = ops.decode_qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
+                                     float(attn.q_norm.eps), float(attn.k_norm.eps), cos, sin,
+                                     kc, vc, pos)
+        out = ops.decode_attention(q4, kc, vc, pos, 1, float(attn.scaling))
+        h = ops.gemv_residual(out.reshape(B, S, -1), attn.o_proj.weight, attn.o_proj.bias,
+                              hidden_states)
+        act = ops.gemv_rmsnorm_swiglu(h, ln2.weight, float(ln2.eps), mlp.gate_proj.weight,
+                                      mlp.up_proj.weight)
+        return ops.gemv_residual(act, mlp.down_proj.weight, None, h)
 
     return forward
 

@@ -398,3 +398,105 @@ def test_decode_qk_norm_rope_against_the_unfused_ops(B, Hq, Hkv, D):
     keep = torch.ones(L, dtype=torch.bool)
     keep[p] = False
     assert torch.equal(kc[:, :, keep], kc0[:, :, keep]) and torch.equal(vc[:, :, keep], vc0[:, :, keep])
+
+
+@pytest.mark.parametrize("rows,K,N", [(1, 4096, 4096), (2, 12288, 4096), (1, 1024, 1000)])
+def test_gemv_residual_equals_gemv_then_add(rows, K, N):
+    """The o / down projection with the decoder's residual add in its
+    epilogue: gemv followed by the bf16 add, bit for bit, with and without a
+    bias."""
+    g = torch.Generator(device=DEV).manual_seed(rows * 7 + K + N)
+    x = torch.randn(rows, 1, K, generator=g, device=DEV).bfloat16()
+    w = (torch.randn(N, K, generator=g, device=DEV) * 0.02).bfloat16()
+    b = torch.randn(N, generator=g, device=DEV).bfloat16()
+    res = torch.randn(rows, 1, N, generator=g, device=DEV).bfloat16()
+    ops = torch.ops.metal_liger
+    for bias in (None, b):
+        y = ops.gemv_residual(x, w, bias, res)
+        assert y.shape == (rows, 1, N)
+        assert torch.equal(y, res + ops.gemv(x, w, bias))
+
+
+@pytest.mark.parametrize("K", [4096, 2048, 8192, 16384, 1000, 256, 128, 64])
+@pytest.mark.parametrize("rows", [1, 2])
+def test_gemv_rmsnorm_multi_equals_norm_then_gemv_multi(rows, K):
+    """The decoder's input RMSNorm fused into the q/k/v GEMV's activation
+    staging: equal bit for bit to this library's RMSNorm kernel followed by
+    gemv_multi, for every RMSNorm row layout (two to eight vectors per thread
+    on 256 threads, one per thread, sub-warp rows)."""
+    g = torch.Generator(device=DEV).manual_seed(rows * 31 + K)
+    x = (torch.randn(rows, 1, K, generator=g, device=DEV) * 3).bfloat16()
+    nw = (1 + 0.1 * torch.randn(K, generator=g, device=DEV)).bfloat16()
+    ws = [(torch.randn(n, K, generator=g, device=DEV) * 0.03).bfloat16() for n in (256, 64, 64)]
+    bs = [torch.randn(w.shape[0], generator=g, device=DEV).bfloat16() for w in ws]
+    ops = torch.ops.metal_liger
+    xn = ops.rms_norm_forward(x, nw, 1e-6, "")[0]
+    for biases in ([None, None, None], bs):
+        fused = ops.gemv_rmsnorm_multi(x, nw, 1e-6, ws, biases)
+        for f, u in zip(fused, ops.gemv_multi(xn, ws, biases)):
+            assert torch.equal(f, u)
+
+
+@pytest.mark.parametrize("rows,K,I", [(1, 4096, 12288), (2, 2048, 1000), (1, 128, 96)])
+def test_gemv_rmsnorm_swiglu_equals_norm_then_gemv_swiglu(rows, K, I):
+    """The post-attention RMSNorm fused into the gate/up/SwiGLU GEMV: equal
+    bit for bit to the RMSNorm kernel followed by gemv_swiglu."""
+    g = torch.Generator(device=DEV).manual_seed(rows + K * 3 + I)
+    x = (torch.randn(rows, 1, K, generator=g, device=DEV) * 2).bfloat16()
+    nw = (1 + 0.1 * torch.randn(K, generator=g, device=DEV)).bfloat16()
+    wg = (torch.randn(I, K, generator=g, device=DEV) * 0.05).bfloat16()
+    wu = (torch.randn(I, K, generator=g, device=DEV) * 0.05).bfloat16()
+    ops = torch.ops.metal_liger
+    fused = ops.gemv_rmsnorm_swiglu(x, nw, 1e-5, wg, wu)
+    unfused = ops.gemv_swiglu(ops.rms_norm_forward(x, nw, 1e-5, "")[0], wg, wu)
+    assert torch.equal(fused, unfused)
+
+
+def test_fused_rmsnorm_gemv_rejects_bad_operands():
+    ops = torch.ops.metal_liger
+    x = torch.randn(1, 1, 256, device=DEV).bfloat16()
+    w = torch.randn(64, 256, device=DEV).bfloat16()
+    with pytest.raises(RuntimeError, match="norm weight"):
+        ops.gemv_rmsnorm_swiglu(x, torch.ones(256, device=DEV), 1e-6, w, w)  # fp32
+    with pytest.raises(RuntimeError, match="norm weight"):
+        ops.gemv_rmsnorm_multi(x, torch.ones(128, device=DEV).bfloat16(), 1e-6, [w], [None])
+    with pytest.raises(RuntimeError, match="residual"):
+        ops.gemv_residual(x, w, None, torch.randn(1, 1, 65, device=DEV).bfloat16())
+
+
+def test_fused_decoder_layers_equal_the_unfused_decode_path(monkeypatch):
+    """The CUDA-graph decode with whole decoder layers fused (the norms in the
+    q/k/v and gate/up GEMVs, the residual adds in the o and down GEMVs)
+    produces exactly the tokens of the decode path with the layers unfused
+    (RMSNorm kernels, the attention block patch, GEMVs and torch residual
+    adds): every fused op equals its unfused composition bit for bit."""
+    from metal_liger_b200 import apply_metal_liger_to_qwen3vl, generation
+    from metal_liger_b200.generation import MetalLigerGenerator
+    from metal_liger_b200.patch import restore_attention_rope
+
+    m = _model(seed=9, layers=3)
+    apply_metal_liger_to_qwen3vl(m, fuse_lora=False, fuse_qk_norm=True,
+                                 fuse_rope_in_attention=True)
+    calls = []
+    real = generation._decode_layer_forward
+
+    def counting(layer, cache, pos):
+        fwd = real(layer, cache, pos)
+
+        def wrapped(*a, **k):
+            calls.append(1)
+            return fwd(*a, **k)
+        return wrapped
+
+    try:
+        for p in m.parameters():
+            p.requires_grad_(False)
+        ids = torch.randint(0, 1000, (2, 5), generator=torch.Generator().manual_seed(21)).to(DEV)
+        monkeypatch.setattr(generation, "_decode_layer_forward", counting)
+        fused = MetalLigerGenerator(m).generate(ids, max_new_tokens=20)
+        assert calls, "the fused decoder-layer path did not run"
+        monkeypatch.setattr(generation, "_FUSED_LAYER_TYPES", ())
+        unfused = MetalLigerGenerator(m).generate(ids, max_new_tokens=20)
+        assert torch.equal(fused, unfused)
+    finally:
+        restore_attention_rope(m)
