@@ -5,7 +5,9 @@
 // needs no mask.  Split-K over the keys ("flash decoding"): each warp takes
 // 32 positions of one (sequence, kv head) for all G query heads of that group
 // and writes their partials (max, sum-exp, unnormalised output); a second
-// kernel merges the partials in order.
+// kernel merges the partials in order.  Caches of up to 256 positions run as
+// one launch: a CTA per (sequence, kv head) keeps all its partials in shared
+// memory and merges them itself, bitwise the two-kernel result.
 //
 // Math: o = sum_j softmax_j(scale * q.k_j) v_j with fp32 scores, exponents
 // and accumulation over bf16 q, K, V — the computation of the reference's
@@ -45,16 +47,20 @@ struct DecodeArgs {
 // with the V row read coalesced (a lane owns DPL = D/32 output dimensions of
 // every head) and the probabilities broadcast by shuffle.  G and DPL are
 // template parameters so every per-lane array stays in registers.
+//
+// The partial of slot c goes to pm / pl [c * stride + row0 + g] and po
+// [(c * stride + row0 + g) * D + d]: the global workspace (two-kernel path)
+// or this CTA's shared memory (single-launch path).  Every thread of the CTA
+// must call this (it loads q into `qs` behind a __syncthreads).
 template <int G, int DPL>
-__global__ void __launch_bounds__(32 * kWarps)
-decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
+__device__ __forceinline__ void attn_partial(const DecodeArgs& a, int c, float* qs, float* pm,
+                                             float* pl, float* po, int64_t stride,
+                                             int64_t row0) {
   constexpr int D = 32 * DPL;
   constexpr int NCH = D / 8;            // 16-byte chunks of a K row
   constexpr bool kPrefetchV = DPL <= 4;  // V fragments of all 32 positions in registers
-  __shared__ float qs[G * D];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31;
   const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
-  const int c = blockIdx.x * kWarps + warp;  // partial index
   const int nslot = (a.L + kChunk - 1) / kChunk;
   const int64_t j0 = (int64_t)c * kChunk;
   const int64_t kv_base = ((int64_t)b * a.Hkv + kvh) * a.L * D;
@@ -88,12 +94,11 @@ decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
   }
   __syncthreads();
   if (c >= nslot) return;  // warps past the last partial slot
-  const int64_t stride = (int64_t)a.B * a.Hq;
-  const int64_t slot0 = (int64_t)c * stride + (int64_t)b * a.Hq + kvh * G;
+  const int64_t slot0 = (int64_t)c * stride + row0;
   if (j0 >= n) {  // past the filled positions: empty partials
     if (lane < G) {
-      a.part_m[slot0 + lane] = -INFINITY;
-      a.part_l[slot0 + lane] = 0.f;
+      pm[slot0 + lane] = -INFINITY;
+      pl[slot0 + lane] = 0.f;
     }
     return;
   }
@@ -134,8 +139,8 @@ decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
     p[g] = valid ? __expf(sc - m) : 0.f;
     const float l = warp_sum(p[g]);
     if (lane == 0) {
-      a.part_m[slot0 + g] = m;
-      a.part_l[slot0 + g] = l;
+      pm[slot0 + g] = m;
+      pl[slot0 + g] = l;
     }
   }
   float o[G][DPL];
@@ -168,10 +173,20 @@ decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
   }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    float* po = a.part_o + (slot0 + g) * D + lane * DPL;
+    float* dst = po + (slot0 + g) * D + lane * DPL;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) po[e] = o[g][e];
+    for (int e = 0; e < DPL; ++e) dst[e] = o[g][e];
   }
+}
+
+template <int G, int DPL>
+__global__ void __launch_bounds__(32 * kWarps)
+decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
+  __shared__ float qs[G * 32 * DPL];
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int c = blockIdx.x * kWarps + (threadIdx.x >> 5);  // partial index
+  attn_partial<G, DPL>(a, c, qs, a.part_m, a.part_l, a.part_o, (int64_t)a.B * a.Hq,
+                       (int64_t)b * a.Hq + kvh * G);
 }
 
 // out[b, 0, h, :] = sum_c e^(m_c - M) o_c / sum_c e^(m_c - M) l_c over the
@@ -180,18 +195,18 @@ decode_attn_chunk(const __grid_constant__ DecodeArgs a) {
 // give M and the denominator, then each lane adds its D/32 output dimensions
 // of every partial with the weights broadcast by shuffle (the partials'
 // loads are independent, so they overlap).  Fixed order: deterministic.
+// merge_row merges the partials of one row held at pm / pl / po (layout of
+// attn_partial) into dst[lane * DPL ...]; one warp.
 template <int DPL>
-__global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__ DecodeArgs a,
-                                                         int nchunk) {
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+__device__ __forceinline__ void merge_row(const float* pm, const float* pl, const float* po,
+                                          int64_t stride, int64_t row, int nchunk, int D,
+                                          __nv_bfloat16* dst) {
   const int lane = threadIdx.x & 31;
-  if (row >= (int64_t)a.B * a.Hq) return;
-  const int64_t stride = (int64_t)a.B * a.Hq;
   float M = -INFINITY;
   for (int c0 = 0; c0 < nchunk; c0 += 32) {
     const int c = c0 + lane;
-    if (c < nchunk && a.part_l[c * stride + row] > 0.f)
-      M = fmaxf(M, a.part_m[c * stride + row]);
+    if (c < nchunk && pl[c * stride + row] > 0.f)
+      M = fmaxf(M, pm[c * stride + row]);
   }
   M = warp_max(M);
   float L = 0.f;
@@ -202,9 +217,9 @@ __global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__
     const int c = c0 + lane;
     float w = 0.f, wl = 0.f;
     if (c < nchunk) {
-      const float l = a.part_l[c * stride + row];
+      const float l = pl[c * stride + row];
       if (l > 0.f) {
-        w = __expf(a.part_m[c * stride + row] - M);
+        w = __expf(pm[c * stride + row] - M);
         wl = w * l;
       }
     }
@@ -215,17 +230,52 @@ __global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__
       if (k >= cn) break;
       const float wk = __shfl_sync(0xffffffffu, w, k);
       if (wk > 0.f) {
-        const float* po = a.part_o + ((int64_t)(c0 + k) * stride + row) * a.D + lane * DPL;
+        const float* src = po + ((int64_t)(c0 + k) * stride + row) * D + lane * DPL;
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) o[e] = fmaf(wk, po[e], o[e]);
+        for (int e = 0; e < DPL; ++e) o[e] = fmaf(wk, src[e], o[e]);
       }
     }
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  const int b = (int)(row / a.Hq), h = (int)(row % a.Hq);
-  __nv_bfloat16* dst = a.out + ((int64_t)b * a.Hq + h) * a.D + lane * DPL;
+  dst += lane * DPL;
 #pragma unroll
   for (int e = 0; e < DPL; ++e) dst[e] = __float2bfloat16_rn(o[e] * inv);
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(256) decode_attn_merge(const __grid_constant__ DecodeArgs a,
+                                                         int nchunk) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (row >= (int64_t)a.B * a.Hq) return;
+  // rows are b * Hq + h, the layout of out [B, 1, Hq, D]
+  merge_row<DPL>(a.part_m, a.part_l, a.part_o, (int64_t)a.B * a.Hq, row, nchunk, a.D,
+                 a.out + row * a.D);
+}
+
+// Single launch for caches of up to kFusedSlots * 32 positions: one CTA per
+// (sequence, kv head) holds every slot's partial in shared memory (a warp per
+// slot, attn_partial) and its warps merge them (merge_row, a warp per query
+// head of the group) — the two-kernel path's arithmetic in its order, so
+// the output is bitwise the same, without the workspace round trip and the
+// second launch.
+constexpr int kFusedSlots = 8;
+
+template <int G, int DPL>
+__global__ void __launch_bounds__(32 * kFusedSlots)
+decode_attn_single(const __grid_constant__ DecodeArgs a) {
+  constexpr int D = 32 * DPL;
+  __shared__ float qs[G * D];
+  __shared__ float sm_m[kFusedSlots * G], sm_l[kFusedSlots * G];
+  __shared__ float sm_o[kFusedSlots * G * D];
+  const int warp = threadIdx.x >> 5;
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  attn_partial<G, DPL>(a, warp, qs, sm_m, sm_l, sm_o, G, 0);
+  __syncthreads();
+  const int nslot = (a.L + kChunk - 1) / kChunk;  // <= kFusedSlots (host check)
+  for (int g = warp; g < G; g += kFusedSlots) {
+    const int64_t h = (int64_t)kvh * G + g;
+    merge_row<DPL>(sm_m, sm_l, sm_o, G, g, nslot, D, a.out + ((int64_t)b * a.Hq + h) * D);
+  }
 }
 
 // Decode-step q/k preparation for Qwen3-style attention, one warp per head
@@ -416,10 +466,15 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
   const int dpl = (int)(head_dim / 32);
 #define ML_DA_CASE(G_, DPL_)                                               \
   if (G == G_ && dpl == DPL_) {                                            \
-    decode_attn_chunk<G_, DPL_><<<grid, 32 * kWarps, 0, st>>>(a);          \
+    if (single)                                                            \
+      decode_attn_single<G_, DPL_>                                         \
+          <<<dim3(1, (unsigned)(batch * kv_heads)), 32 * kFusedSlots, 0, st>>>(a); \
+    else                                                                   \
+      decode_attn_chunk<G_, DPL_><<<grid, 32 * kWarps, 0, st>>>(a);        \
     launched = true;                                                       \
   }
   bool launched = false;
+  const bool single = nchunk <= kFusedSlots;
   ML_DA_CASE(1, 2) ML_DA_CASE(1, 4) ML_DA_CASE(1, 8)
   ML_DA_CASE(2, 2) ML_DA_CASE(2, 4) ML_DA_CASE(2, 8)
   ML_DA_CASE(4, 2) ML_DA_CASE(4, 4) ML_DA_CASE(4, 8)
@@ -433,6 +488,7 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
     return ML_ERR_INVALID_ARG;
   }
   ML_CHECK_LAUNCH("decode_attention(chunk)");
+  if (single) return ML_OK;
   const int64_t warps = batch * q_heads;
   const unsigned mgrid = (unsigned)((warps * 32 + 255) / 256);
   if (dpl == 2) decode_attn_merge<2><<<mgrid, 256, 0, st>>>(a, nchunk);

@@ -230,8 +230,9 @@ class _DecodeKernels:
         if not self.gemv:
             return self
         # Fully patched Qwen3-style decoder layers: the layer's decode step in
-        # seven launches (input norm + q/k/v GEMV, q/k norm + RoPE + cache
-        # write, attention chunks + merge, o GEMV + residual, post-attention
+        # six launches (input norm + q/k/v GEMV, q/k norm + RoPE + cache
+        # write, attention (chunks + merge beyond 256 cache positions), o
+        # GEMV + residual, post-attention
         # norm + gate/up/SwiGLU GEMV, down GEMV + residual).
         if self.pos is not None and self.cache is not None:
             for mod in self.module.modules():

@@ -500,3 +500,24 @@ def test_fused_decoder_layers_equal_the_unfused_decode_path(monkeypatch):
         assert torch.equal(fused, unfused)
     finally:
         restore_attention_rope(m)
+
+
+@pytest.mark.parametrize("G,D", [(4, 128), (16, 64), (1, 256), (2, 256)])
+def test_decode_attention_single_launch_equals_split_merge(G, D):
+    """Caches of up to 256 positions take the single-launch kernel (every
+    slot's partial and their merge in one CTA's shared memory), longer ones
+    the chunk and merge kernels.  Over the same filled positions both give
+    the same output bit for bit (same partials, merged in the same order)."""
+    B, Hkv, n = 2, 2, 200
+    Hq = G * Hkv
+    g = torch.Generator(device=DEV).manual_seed(G * 1000 + D)
+    q = torch.randn(B, Hq, 1, D, generator=g, device=DEV).bfloat16()
+    k_long = torch.randn(B, Hkv, 320, D, generator=g, device=DEV).bfloat16()
+    v_long = torch.randn(B, Hkv, 320, D, generator=g, device=DEV).bfloat16()
+    k_short = k_long[:, :, :256].contiguous()
+    v_short = v_long[:, :, :256].contiguous()
+    pos = torch.tensor([n - 1], dtype=torch.int64, device=DEV)
+    ops = torch.ops.metal_liger
+    single = ops.decode_attention(q, k_short, v_short, pos, 1, D ** -0.5)
+    split = ops.decode_attention(q, k_long, v_long, pos, 1, D ** -0.5)
+    assert torch.equal(single, split)
