@@ -495,6 +495,22 @@ ML_API int ml_decode_qk_norm_rope_bf16(
     void* q_out, void* k_cache, void* v_cache, const int64_t* pos, void* stream);
 
 /*
+ * ml_decode_qk_norm_rope_bf16 followed by ml_decode_attention_bf16 (len_offset
+ * 1: the new token's position is attended to) in one launch, bit for bit the
+ * two calls, for caches of at most 256 positions (max_len <= 256) and the
+ * head shapes ml_decode_attention_bf16 builds; q stays on chip (no q_out), k
+ * and v go to the caches at *pos, out [B, 1, q_heads, head_dim] bf16.  No
+ * workspace.  No reference counterpart (the reference's decode runs the
+ * block's norms, RoPE, cache update and attention module by module,
+ * generation.py:109-115).
+ */
+ML_API int ml_decode_qk_attention_bf16(
+    const void* q, const void* k, const void* v, const void* wq, const void* wk, int w_dtype,
+    float eps_q, float eps_k, const void* cos, const void* sin, int cs_dtype, int64_t cs_b,
+    int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t max_len, int64_t head_dim,
+    void* k_cache, void* v_cache, const int64_t* pos, float scale, void* out, void* stream);
+
+/*
  * Decode-time SwiGLU MLP input side: y[b, i] = bf16(silu(g) * u) with
  * g = bf16(x[b] . w_gate[i]), u = bf16(x[b] . w_up[i]) (fp32 accumulation;
  * bitwise equal to two ml_gemv_bf16 calls and ml_swiglu_forward), for

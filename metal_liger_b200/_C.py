@@ -103,6 +103,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                             c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
                                             c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                                             c_void_p, c_void_p]),
+    "ml_decode_qk_attention_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                            c_int, ctypes.c_float, ctypes.c_float, c_void_p,
+                                            c_void_p, c_int, c_int64, c_int64, c_int64, c_int64,
+                                            c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                            ctypes.c_float, c_void_p, c_void_p]),
     "ml_gemv_swiglu_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                     c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "ml_gemv_residual_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int,

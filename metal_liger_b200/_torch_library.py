@@ -939,10 +939,47 @@ def decode_qk_norm_rope_cuda(q: Tensor, k: Tensor, v: Tensor, wq: Tensor, wk: Te
     return q_out
 
 
+def decode_qk_attention_cuda(q: Tensor, k: Tensor, v: Tensor, wq: Tensor, wk: Tensor,
+                             eps_q: float, eps_k: float, cos: Tensor, sin: Tensor,
+                             k_cache: Tensor, v_cache: Tensor, pos: Tensor, scale: float):
+    """decode_qk_norm_rope followed by decode_attention(..., len_offset=1) in
+    one launch, bit for bit the two ops, for caches of at most 256 positions;
+    returns [B, 1, Hq, D] bf16."""
+    _C.require_cuda("decode_qk_attention", q, k, v, wq, wk, cos, sin, k_cache, v_cache, pos)
+    B, Hkv, L, D = k_cache.shape
+    if any(t.dtype != torch.bfloat16 for t in (q, k, v, k_cache, v_cache)):
+        raise RuntimeError("decode_qk_attention: bf16 q, k, v and caches")
+    if q.numel() % (B * D) or k.numel() != B * Hkv * D or v.numel() != B * Hkv * D:
+        raise RuntimeError("decode_qk_attention: q/k/v sizes do not match the caches")
+    if v_cache.shape != k_cache.shape or not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("decode_qk_attention: contiguous caches of equal shape")
+    if pos.dtype != torch.int64 or wq.numel() != D or wk.numel() != D:
+        raise RuntimeError("decode_qk_attention: int64 position and [D] norm weights")
+    Hq = q.numel() // (B * D)
+    q, k, v = _contig(q), _contig(k), _contig(v)
+    cos2 = _contig(cos.reshape(B, -1))
+    sin2 = _contig(sin.reshape(B, -1))
+    if cos2.shape[1] != D or sin2.shape != cos2.shape:
+        raise RuntimeError("decode_qk_attention: cos/sin must be [B, (1,) D]")
+    wq, wk = _contig(wq), _contig(wk)
+    if wk.dtype != wq.dtype:
+        wk = wk.to(wq.dtype)
+    out = torch.empty((B, 1, Hq, D), dtype=torch.bfloat16, device=q.device)
+    _C.call("ml_decode_qk_attention_bf16", _C.ptr(q), _C.ptr(k), _C.ptr(v), _C.ptr(wq),
+            _C.ptr(wk), _C.dtype_code(wq), float(eps_q), float(eps_k), _C.ptr(cos2),
+            _C.ptr(sin2), _C.dtype_code(cos2), D, B, Hq, Hkv, L, D, _C.ptr(k_cache),
+            _C.ptr(v_cache), _C.ptr(pos), float(scale), _C.ptr(out), _C.stream_of(q))
+    return out
+
+
 _SCHEMAS = {
     "decode_qk_norm_rope": "decode_qk_norm_rope(Tensor q, Tensor k, Tensor v, Tensor wq, "
                            "Tensor wk, float eps_q, float eps_k, Tensor cos, Tensor sin, "
                            "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor pos) -> Tensor",
+    "decode_qk_attention": "decode_qk_attention(Tensor q, Tensor k, Tensor v, Tensor wq, "
+                           "Tensor wk, float eps_q, float eps_k, Tensor cos, Tensor sin, "
+                           "Tensor(a!) k_cache, Tensor(b!) v_cache, Tensor pos, float scale) "
+                           "-> Tensor",
     "decode_attention": "decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor pos, "
                         "int len_offset, float scale) -> Tensor",
     "gemv_multi": "gemv_multi(Tensor x, Tensor[] weights, Tensor?[] biases) -> Tensor[]",
@@ -1001,6 +1038,7 @@ _CUDA_IMPLS = {
     "gemv_multi": gemv_multi_cuda,
     "gemv_swiglu": gemv_swiglu_cuda,
     "gemv": gemv_cuda,
+    "decode_qk_attention": decode_qk_attention_cuda,
     "gemv_residual": gemv_residual_cuda,
     "gemv_rmsnorm_multi": gemv_rmsnorm_multi_cuda,
     "gemv_rmsnorm_swiglu": gemv_rmsnorm_swiglu_cuda,
@@ -1135,6 +1173,11 @@ def _fake_impls():
     def gemv_rmsnorm_swiglu_fake(x, norm_weight, eps, w_gate, w_up):
         return torch.empty((*x.shape[:-1], w_gate.shape[0]), dtype=x.dtype, device=x.device)
 
+    def decode_qk_attention_fake(q, k, v, wq, wk, eps_q, eps_k, cos, sin, k_cache, v_cache, pos,
+                                 scale):
+        B, Hkv, L, D = k_cache.shape
+        return torch.empty((B, 1, q.numel() // (B * D), D), dtype=q.dtype, device=q.device)
+
     def decode_attention_fake(q, k_cache, v_cache, pos, len_offset, scale):
         B, Hq, _, D = q.shape
         return torch.empty((B, 1, Hq, D), dtype=q.dtype, device=q.device)
@@ -1149,6 +1192,7 @@ def _fake_impls():
         "gemv_multi": gemv_multi_fake,
         "gemv_swiglu": gemv_swiglu_fake,
         "gemv": gemv_fake,
+        "decode_qk_attention": decode_qk_attention_fake,
         "gemv_residual": gemv_residual_fake,
         "gemv_rmsnorm_multi": gemv_rmsnorm_multi_fake,
         "gemv_rmsnorm_swiglu": gemv_rmsnorm_swiglu_fake,

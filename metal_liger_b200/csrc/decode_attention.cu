@@ -7,7 +7,9 @@
 // and writes their partials (max, sum-exp, unnormalised output); a second
 // kernel merges the partials in order.  Caches of up to 256 positions run as
 // one launch: a CTA per (sequence, kv head) keeps all its partials in shared
-// memory and merges them itself, bitwise the two-kernel result.
+// memory and merges them itself, bitwise the two-kernel result; inside the
+// generator's fused decoder layers that CTA also prepares its q, k and v rows
+// first (decode_qk_attn_single), one launch for prep and attention.
 //
 // Math: o = sum_j softmax_j(scale * q.k_j) v_j with fp32 scores, exponents
 // and accumulation over bf16 q, K, V — the computation of the reference's
@@ -52,7 +54,7 @@ struct DecodeArgs {
 // [(c * stride + row0 + g) * D + d]: the global workspace (two-kernel path)
 // or this CTA's shared memory (single-launch path).  Every thread of the CTA
 // must call this (it loads q into `qs` behind a __syncthreads).
-template <int G, int DPL>
+template <int G, int DPL, bool kQReady = false>
 __device__ __forceinline__ void attn_partial(const DecodeArgs& a, int c, float* qs, float* pm,
                                              float* pl, float* po, int64_t stride,
                                              int64_t row0) {
@@ -88,9 +90,11 @@ __device__ __forceinline__ void attn_partial(const DecodeArgs& a, int c, float* 
     }
   }
   const int64_t n = min((int64_t)a.L, *a.pos + a.len_offset);
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int g = i / D, d = i - g * D;
-    qs[i] = __bfloat162float(a.q[(int64_t)b * a.sq_b + (int64_t)(kvh * G + g) * a.sq_h + d]);
+  if (!kQReady) {  // else the caller has filled qs (and synchronised)
+    for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+      const int g = i / D, d = i - g * D;
+      qs[i] = __bfloat162float(a.q[(int64_t)b * a.sq_b + (int64_t)(kvh * G + g) * a.sq_h + d]);
+    }
   }
   __syncthreads();
   if (c >= nslot) return;  // warps past the last partial slot
@@ -305,17 +309,15 @@ struct QkPrep {
   int B, Hq, Hkv, L;
 };
 
+// Row r of sequence b (q rows 0..Hq-1, k rows, v rows), one warp, for a
+// position p inside the cache.  A q row goes to q_out, or, with q_f32, to
+// q_f32[0, D) as the bf16-rounded values in fp32 (what a kernel loading
+// q_out would see).
 template <int EPL>
-__global__ void __launch_bounds__(256) decode_qk_prep(const __grid_constant__ QkPrep a) {
+__device__ __forceinline__ void prep_row(const QkPrep& a, int b, int r, int64_t p,
+                                         float* q_f32) {
   constexpr int D = 32 * EPL;
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int per_b = a.Hq + 2 * a.Hkv;
-  if (row >= (int64_t)a.B * per_b) return;
-  const int b = (int)(row / per_b);
-  const int r = (int)(row % per_b);
-  const int64_t p = *a.pos;
-  if (p < 0 || p >= a.L) return;  // outside the cache: nothing to write
   const int d0 = lane * EPL;
   if (r >= a.Hq + a.Hkv) {  // v row: copy into the cache
     const int h = r - a.Hq - a.Hkv;
@@ -355,10 +357,58 @@ __global__ void __launch_bounds__(256) decode_qk_prep(const __grid_constant__ Qk
     // first half: a1 = y, a2 = partner; second half: a2 = y, a1 = partner
     o[e] = first_half ? y[e] * c - yp[e] * sn : y[e] * c + yp[e] * sn;
   }
+  if (is_q && q_f32 != nullptr) {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) q_f32[d0 + e] = __bfloat162float(__float2bfloat16_rn(o[e]));
+    return;
+  }
   __nv_bfloat16* dst = is_q ? a.q_out + ((int64_t)b * a.Hq + h) * D + d0
                             : a.k_cache + (((int64_t)b * a.Hkv + h) * a.L + p) * D + d0;
 #pragma unroll
   for (int e = 0; e < EPL; ++e) dst[e] = __float2bfloat16_rn(o[e]);
+}
+
+template <int EPL>
+__global__ void __launch_bounds__(256) decode_qk_prep(const __grid_constant__ QkPrep a) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int per_b = a.Hq + 2 * a.Hkv;
+  if (row >= (int64_t)a.B * per_b) return;
+  const int64_t p = *a.pos;
+  if (p < 0 || p >= a.L) return;  // outside the cache: nothing to write
+  prep_row<EPL>(a, (int)(row / per_b), (int)(row % per_b), p, nullptr);
+}
+
+// q/k preparation and the single-launch attention in one kernel, a CTA per
+// (sequence, kv head): its warps first prepare the group's G q rows (into
+// shared memory, as the bf16 values q_out would hold), the k row and the v
+// row (into the caches at *pos); after a barrier, which makes the new cache
+// row visible to the whole CTA, the slot warps and the merge run as in
+// decode_attn_single.  Bitwise decode_qk_prep followed by the attention.
+template <int G, int DPL>
+__global__ void __launch_bounds__(32 * kFusedSlots)
+decode_qk_attn_single(const __grid_constant__ QkPrep qp, const __grid_constant__ DecodeArgs a) {
+  constexpr int D = 32 * DPL;
+  __shared__ float qs[G * D];
+  __shared__ float sm_m[kFusedSlots * G], sm_l[kFusedSlots * G];
+  __shared__ float sm_o[kFusedSlots * G * D];
+  const int warp = threadIdx.x >> 5;
+  const int b = blockIdx.y / a.Hkv, kvh = blockIdx.y % a.Hkv;
+  const int64_t p = *qp.pos;
+  const bool in_cache = p >= 0 && p < qp.L;
+  for (int r = warp; r < G + 2; r += kFusedSlots) {
+    if (r < G)
+      prep_row<DPL>(qp, b, kvh * G + r, p, qs + r * D);
+    else if (in_cache)  // the k row, then the v row, of this kv head
+      prep_row<DPL>(qp, b, r == G ? qp.Hq + kvh : qp.Hq + qp.Hkv + kvh, p, nullptr);
+  }
+  __syncthreads();
+  attn_partial<G, DPL, true>(a, warp, qs, sm_m, sm_l, sm_o, G, 0);
+  __syncthreads();
+  const int nslot = (a.L + kChunk - 1) / kChunk;  // <= kFusedSlots (host check)
+  for (int g = warp; g < G; g += kFusedSlots) {
+    const int64_t h = (int64_t)kvh * G + g;
+    merge_row<DPL>(sm_m, sm_l, sm_o, G, g, nslot, D, a.out + ((int64_t)b * a.Hq + h) * D);
+  }
 }
 
 }  // namespace
@@ -495,5 +545,88 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
   else if (dpl == 4) decode_attn_merge<4><<<mgrid, 256, 0, st>>>(a, nchunk);
   else decode_attn_merge<8><<<mgrid, 256, 0, st>>>(a, nchunk);
   ML_CHECK_LAUNCH("decode_attention(merge)");
+  return ML_OK;
+}
+
+extern "C" int ml_decode_qk_attention_bf16(
+    const void* q, const void* k, const void* v, const void* wq, const void* wk, int w_dtype,
+    float eps_q, float eps_k, const void* cos, const void* sin, int cs_dtype, int64_t cs_b,
+    int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t max_len, int64_t head_dim,
+    void* k_cache, void* v_cache, const int64_t* pos, float scale, void* out, void* stream) {
+  ML_CHECK_ARG(batch > 0 && q_heads > 0 && kv_heads > 0 && max_len > 0,
+               "decode_qk_attention: bad sizes");
+  ML_CHECK_ARG(head_dim == 64 || head_dim == 128 || head_dim == 256,
+               "decode_qk_attention: head_dim %lld not in {64, 128, 256}", (long long)head_dim);
+  ML_CHECK_ARG(q && k && v && wq && wk && cos && sin && k_cache && v_cache && pos && out,
+               "decode_qk_attention: null pointer");
+  ML_CHECK_ARG((w_dtype >= 0 && w_dtype <= 2) && (cs_dtype >= 0 && cs_dtype <= 2),
+               "decode_qk_attention: bad dtype codes");
+  ML_CHECK_ARG(q_heads % kv_heads == 0, "decode_qk_attention: %lld query heads for %lld kv heads",
+               (long long)q_heads, (long long)kv_heads);
+  ML_CHECK_ARG((max_len + kChunk - 1) / kChunk <= kFusedSlots,
+               "decode_qk_attention: a cache of %lld positions (at most %d; longer caches take "
+               "ml_decode_qk_norm_rope_bf16 and ml_decode_attention_bf16)",
+               (long long)max_len, kChunk * kFusedSlots);
+  ML_CHECK_ARG(aligned16(k_cache) && aligned16(v_cache),
+               "decode_qk_attention: KV buffers must be 16-byte aligned");
+  ML_CHECK_ARG(batch * kv_heads <= 65535, "decode_qk_attention: too many sequences x kv heads");
+  QkPrep qp;
+  qp.q = static_cast<const __nv_bfloat16*>(q);
+  qp.k = static_cast<const __nv_bfloat16*>(k);
+  qp.v = static_cast<const __nv_bfloat16*>(v);
+  qp.wq = wq;
+  qp.wk = wk;
+  qp.w_dtype = w_dtype;
+  qp.eps_q = eps_q;
+  qp.eps_k = eps_k;
+  qp.cos = cos;
+  qp.sin = sin;
+  qp.cs_dtype = cs_dtype;
+  qp.cs_b = cs_b;
+  qp.q_out = nullptr;  // q stays in shared memory
+  qp.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  qp.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  qp.pos = pos;
+  qp.B = (int)batch;
+  qp.Hq = (int)q_heads;
+  qp.Hkv = (int)kv_heads;
+  qp.L = (int)max_len;
+  DecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.q = nullptr;  // taken from shared memory
+  a.k = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v = static_cast<const __nv_bfloat16*>(v_cache);
+  a.pos = pos;
+  a.len_offset = 1;  // the new token's position is attended to
+  a.B = (int)batch;
+  a.Hq = (int)q_heads;
+  a.Hkv = (int)kv_heads;
+  a.L = (int)max_len;
+  a.D = (int)head_dim;
+  a.scale = scale;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  const int G = (int)(q_heads / kv_heads);
+  const int dpl = (int)(head_dim / 32);
+  const dim3 grid(1, (unsigned)(batch * kv_heads));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bool launched = false;
+#define ML_QA_CASE(G_, DPL_)                                                           \
+  if (G == G_ && dpl == DPL_) {                                                        \
+    decode_qk_attn_single<G_, DPL_><<<grid, 32 * kFusedSlots, 0, st>>>(qp, a);         \
+    launched = true;                                                                   \
+  }
+  ML_QA_CASE(1, 2) ML_QA_CASE(1, 4) ML_QA_CASE(1, 8)
+  ML_QA_CASE(2, 2) ML_QA_CASE(2, 4) ML_QA_CASE(2, 8)
+  ML_QA_CASE(4, 2) ML_QA_CASE(4, 4) ML_QA_CASE(4, 8)
+  ML_QA_CASE(8, 2) ML_QA_CASE(8, 4)
+  ML_QA_CASE(16, 2)
+#undef ML_QA_CASE
+  if (!launched) {
+    set_error("decode_qk_attention: %d query heads per kv head with head_dim %lld is not built "
+              "(G in {1, 2, 4, 8, 16}, head_dim in {64, 128, 256}, G * head_dim <= 1024)",
+              G, (long long)head_dim);
+    return ML_ERR_INVALID_ARG;
+  }
+  ML_CHECK_LAUNCH("decode_qk_attention");
   return ML_OK;
 }

@@ -230,10 +230,10 @@ class _DecodeKernels:
         if not self.gemv:
             return self
         # Fully patched Qwen3-style decoder layers: the layer's decode step in
-        # six launches (input norm + q/k/v GEMV, q/k norm + RoPE + cache
-        # write, attention (chunks + merge beyond 256 cache positions), o
-        # GEMV + residual, post-attention
-        # norm + gate/up/SwiGLU GEMV, down GEMV + residual).
+        # five launches up to 256 cache positions (input norm + q/k/v GEMV;
+        # q/k norm + RoPE + cache write + attention; o GEMV + residual;
+        # post-attention norm + gate/up/SwiGLU GEMV; down GEMV + residual),
+        # the attention's q/k prep a launch of its own beyond that.
         if self.pos is not None and self.cache is not None:
             for mod in self.module.modules():
                 if _decode_layer_ok(mod, self.cache) and "forward" not in mod.__dict__:
@@ -393,10 +393,15 @@ def _decode_layer_forward(layer, cache, pos: Tensor):
         q, k, v = ops.gemv_rmsnorm_multi(hidden_states, ln1.weight, float(ln1.eps),
                                          [p.weight for p in projs], [p.bias for p in projs])
         cos, sin = pe
-        q4 = ops.decode_qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
-                                     float(attn.q_norm.eps), float(attn.k_norm.eps), cos, sin,
-                                     kc, vc, pos)
-        out = ops.decode_attention(q4, kc, vc, pos, 1, float(attn.scaling))
+        if kc.shape[2] <= 256:  # q/k prep and attention in one launch
+            out = ops.decode_qk_attention(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
+                                          float(attn.q_norm.eps), float(attn.k_norm.eps), cos,
+                                          sin, kc, vc, pos, float(attn.scaling))
+        else:
+            q4 = ops.decode_qk_norm_rope(q, k, v, attn.q_norm.weight, attn.k_norm.weight,
+                                         float(attn.q_norm.eps), float(attn.k_norm.eps), cos,
+                                         sin, kc, vc, pos)
+            out = ops.decode_attention(q4, kc, vc, pos, 1, float(attn.scaling))
         h = ops.gemv_residual(out.reshape(B, S, -1), attn.o_proj.weight, attn.o_proj.bias,
                               hidden_states)
         act = ops.gemv_rmsnorm_swiglu(h, ln2.weight, float(ln2.eps), mlp.gate_proj.weight,

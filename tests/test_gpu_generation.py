@@ -521,3 +521,45 @@ def test_decode_attention_single_launch_equals_split_merge(G, D):
     single = ops.decode_attention(q, k_short, v_short, pos, 1, D ** -0.5)
     split = ops.decode_attention(q, k_long, v_long, pos, 1, D ** -0.5)
     assert torch.equal(single, split)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,D,L,p", [(1, 32, 8, 128, 192, 150), (2, 4, 2, 64, 256, 255),
+                                            (1, 16, 1, 64, 100, 0), (2, 8, 4, 256, 64, 40),
+                                            (3, 8, 1, 128, 200, 77)])
+def test_decode_qk_attention_equals_prep_then_attention(B, Hq, Hkv, D, L, p):
+    """q/k norm + RoPE + cache write and the attention in one launch: the
+    output and both caches bit for bit those of decode_qk_norm_rope followed
+    by decode_attention."""
+    g = torch.Generator(device=DEV).manual_seed(B * Hq + D + L + p)
+    q = torch.randn(B, 1, Hq * D, generator=g, device=DEV).bfloat16()
+    k = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    v = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    wq = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    wk = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    ang = torch.rand(B, 1, D // 2, generator=g, device=DEV) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16()
+    kc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    vc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    kc2, vc2 = kc.clone(), vc.clone()
+    pos = torch.tensor([p], dtype=torch.int64, device=DEV)
+    ops = torch.ops.metal_liger
+    fused = ops.decode_qk_attention(q, k, v, wq, wk, 1e-6, 1e-5, cos, sin, kc, vc, pos,
+                                    D ** -0.5)
+    q4 = ops.decode_qk_norm_rope(q, k, v, wq, wk, 1e-6, 1e-5, cos, sin, kc2, vc2, pos)
+    ref = ops.decode_attention(q4, kc2, vc2, pos, 1, D ** -0.5)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(fused, ref)
+
+
+def test_decode_qk_attention_rejects_long_caches():
+    ops = torch.ops.metal_liger
+    B, Hkv, D = 1, 2, 64
+    kc = torch.zeros(B, Hkv, 257, D, device=DEV).bfloat16()
+    x = torch.zeros(B, 1, 4 * D, device=DEV).bfloat16()
+    kv = torch.zeros(B, 1, Hkv * D, device=DEV).bfloat16()
+    w = torch.ones(D, device=DEV).bfloat16()
+    cs = torch.ones(B, 1, D, device=DEV).bfloat16()
+    pos = torch.zeros(1, dtype=torch.int64, device=DEV)
+    with pytest.raises(RuntimeError, match="at most 256"):
+        ops.decode_qk_attention(x, kv, kv, w, w, 1e-6, 1e-6, cs, cs, kc, kc.clone(), pos, 0.125)
