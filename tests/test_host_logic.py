@@ -35,7 +35,37 @@ def test_fake_shapes_on_meta():
     assert out.dtype == torch.float32  # torch promotion of x*cos, as in the reference
 
 
+def test_fused_decode_op_fakes_on_meta():
+    """The decoder-layer decode ops (fused norm / residual GEMVs, q/k prep +
+    attention) propagate shapes on the meta device, as graph tracers need."""
+    ops = torch.ops.metal_liger
+    m = dict(device="meta", dtype=torch.bfloat16)
+    x = torch.empty(2, 1, 64, **m)
+    nw = torch.empty(64, **m)
+    w1, w2 = torch.empty(48, 64, **m), torch.empty(16, 64, **m)
+    assert ops.gemv_residual(x, w1, None, torch.empty(2, 1, 48, **m)).shape == (2, 1, 48)
+    outs = ops.gemv_rmsnorm_multi(x, nw, 1e-6, [w1, w2], [None, None])
+    assert [tuple(o.shape) for o in outs] == [(2, 1, 48), (2, 1, 16)]
+    assert ops.gemv_rmsnorm_swiglu(x, nw, 1e-6, w1, w1).shape == (2, 1, 48)
+    kc = torch.empty(2, 2, 40, 32, **m)
+    q, kv = torch.empty(2, 1, 4 * 32, **m), torch.empty(2, 1, 2 * 32, **m)
+    cs = torch.empty(2, 1, 32, **m)
+    w = torch.empty(32, **m)
+    pos = torch.empty(1, device="meta", dtype=torch.int64)
+    out = ops.decode_qk_attention(q, kv, kv, w, w, 1e-6, 1e-6, cs, cs, kc, kc, pos, 0.2)
+    assert out.shape == (2, 1, 4, 32)
+
+
 @pytest.mark.parametrize("call", [
+    lambda: torch.ops.metal_liger.gemv_residual(
+        torch.randn(1, 64).bfloat16(), torch.randn(8, 64).bfloat16(), None,
+        torch.randn(1, 8).bfloat16()),
+    lambda: torch.ops.metal_liger.gemv_rmsnorm_swiglu(
+        torch.randn(1, 64).bfloat16(), torch.ones(64).bfloat16(), 1e-6,
+        torch.randn(8, 64).bfloat16(), torch.randn(8, 64).bfloat16()),
+    lambda: torch.ops.metal_liger.gemv_rmsnorm_multi(
+        torch.randn(1, 64).bfloat16(), torch.ones(64).bfloat16(), 1e-6,
+        [torch.randn(8, 64).bfloat16()], [None]),
     lambda: torch.ops.metal_liger.rms_norm_forward(torch.randn(2, 8), torch.ones(8), 1e-6, ""),
     lambda: torch.ops.metal_liger.swiglu_forward(torch.randn(8), torch.randn(8), ""),
     lambda: ml.ops.fused_swiglu.fused_swiglu(torch.randn(8), torch.randn(8)),
