@@ -859,9 +859,12 @@ class Generate:
     tokens for one sequence, greedy.  Decode is HBM-bound on the weights
     (16.4 GB per token); the roofline line is this library's kernel on that
     path, the fused lm_head argmax (one pass over the 1.24 GB lm_head per
-    token).  The decoder's projections and attention are transformers
-    modules (cuBLAS / SDPA, library kernels).  Decoding replays a CUDA graph
-    of one self-advancing decode step per token (the generator's default)."""
+    token).  Decoding replays a CUDA graph of one self-advancing decode step
+    per token (the generator's default) in which every decoder layer runs as
+    five of this library's launches (input norm + q/k/v GEMV; q/k norm,
+    RoPE, cache write and attention; o GEMV + residual; post-attention norm
+    + gate/up/SwiGLU GEMV; down GEMV + residual); the prefill runs the
+    patched modules (cuBLAS projections, SDPA attention)."""
 
     name = "generate"
     bound = "hbm"
