@@ -2,23 +2,31 @@
 """Benchmark of the fused-op hot path on B200 (one JSON line on rank 0).
 
 Metric: fwd+bwd tokens/s per fused op at Qwen3-VL shapes, with
-the fraction of the HBM / tensor-core roofline.  The default workload is
-BASELINE configs[1] — SwiGLU (gate/up [8,2048,6144] bf16) plus RoPE (q
-[8,16,2048,128], k [8,8,2048,128] bf16, positions 0..2047, theta 5e6, cos/sin
-recomputed in-kernel), forward + backward — one "step" = one fwd+bwd pass of
-both ops over the 16,384 tokens.  Other configs are selectable with
-``--workload`` (they are parity-test cases; the default line is configs[1]):
-rmsnorm, flce (configs[2]; vocabulary-parallel under torchrun),
-lora, c5_step (configs[4], the Qwen3-VL-8B LoRA training step)
-and generate (greedy decoding with the static-KV generator on the Qwen3-VL-8B
-text decoder; its metric is generated tokens/s).
+the fraction of the HBM / tensor-core roofline, on 1-8 GPUs.  The line's own
+workload (``value``) is BASELINE configs[1] — SwiGLU (gate/up [8,2048,6144]
+bf16) plus RoPE (q [8,16,2048,128], k [8,8,2048,128] bf16, positions
+0..2047, theta 5e6, cos/sin recomputed in-kernel), forward + backward — one
+"step" = one fwd+bwd pass of both ops over the 16,384 tokens.  The default run
+also measures every other fused op at its BASELINE config, each with its own
+roofline, e2e, launch count, peak memory and (N=1) CPU baseline, under
+``workloads``: rmsnorm (configs[0]), flce (configs[2]), lora (configs[3]) and
+c5_step (configs[4], the Qwen3-VL-8B LoRA training step; data-parallel with
+the NCCL gradient all-reduce at N > 1).  Under ``flce_vp`` it reports the
+FLCE at N GPUs: vocabulary-parallel (lm_head rows sharded, NCCL all-reduce of
+the per-token statistics and of the partial dX), strong scaling, with its
+speed-up over the single-GPU op timed on the same GPUs in the same run and a
+parity check of every rank's shard against the single-GPU result.
+``--workload NAME`` runs one workload alone as the line (also ``generate``:
+greedy decoding with the static-KV generator; its metric is generated
+tokens/s).
 
   value    device-timed tokens/s, inputs resident in HBM, CUDA events on the
            launching stream, max over ranks (weak scaling: every rank runs
            the full per-GPU workload, no collective on the data path);
   e2e      the same metric through the public autograd API with HOST
            (pinned) buffers: per step H2D of all inputs and D2H of all
-           outputs inside the timed region;
+           outputs inside the timed region (row-wise ops: the batch rows
+           pipelined over H2D / compute / D2H streams);
   roofline the dominant kernel's algorithmic bytes (or FLOPs) per launch over
            its event-timed average duration, against MEASURED_PEAKS.json;
   cpu_baseline  the CPU oracle (a restatement of the reference's torch ops)
@@ -174,6 +182,49 @@ def plain(name, fn, *args):
     return fn(*args)
 
 
+class CopyPipeline:
+    """Host<->device copies overlapped with compute for an end-to-end step.
+
+    The step's token rows are split into chunks; chunk i's inputs go up on an
+    H2D stream, its compute runs on a compute stream once they have arrived,
+    and its outputs come back on a D2H stream once computed, so the H2D of
+    chunk i+1, the compute of chunk i and the D2H of chunk i-1 run together
+    (PCIe is full duplex).  Device input buffers are reused across steps: the
+    H2D of a chunk waits until the previous step's compute of that chunk has
+    finished reading it.  The caller's stream waits for all three streams at
+    the end, so events recorded on it bracket the whole step."""
+
+    def __init__(self, device, nchunks):
+        self.nchunks = nchunks
+        self.h2d = torch.cuda.Stream(device)
+        self.comp = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.freed = [None] * nchunks
+
+    def run(self, load, compute, store):
+        main = torch.cuda.current_stream()
+        start = main.record_event()
+        for s in (self.h2d, self.comp, self.d2h):
+            s.wait_event(start)
+        for i in range(self.nchunks):
+            with torch.cuda.stream(self.h2d):
+                if self.freed[i] is not None:
+                    self.h2d.wait_event(self.freed[i])
+                load(i)
+                arrived = self.h2d.record_event()
+            with torch.cuda.stream(self.comp):
+                self.comp.wait_event(arrived)
+                outs = compute(i)
+                done = self.comp.record_event()
+                self.freed[i] = done
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(done)
+                for t in store(i, outs):
+                    t.record_stream(self.d2h)
+        for s in (self.h2d, self.comp, self.d2h):
+            main.wait_stream(s)
+
+
 # ---------------------------------------------------------------------------
 # workloads
 # ---------------------------------------------------------------------------
@@ -182,8 +233,10 @@ class SwigluRope:
     """SwiGLU + RoPE fwd+bwd, bf16, Qwen3-VL-2B layer shape."""
 
     name = "swiglu_rope"
+    short = "configs[1] SwiGLU [8,2048,6144] + RoPE q[8,16,2048,128] k[8,8,2048,128] bf16"
     bound = "hbm"
     dtype = "bf16"
+    e2e_pipelined = True
     B, S, I = 8, 2048, 6144
     HQ, HK, D = 16, 8, 128
     THETA = 5e6
@@ -258,27 +311,41 @@ class SwigluRope:
                     for k, v in outs_shapes.items()}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+        # one chunk per batch row: every tensor splits along dim 0
         return {"host": host, "dev": dev, "host_out": host_out, "pos": t["pos"],
-                "inv_freq": t["inv_freq"], "h2d": h2d, "d2h": d2h}
+                "inv_freq": t["inv_freq"], "h2d": h2d, "d2h": d2h,
+                "pipe": CopyPipeline(device, self.B)}
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_swiglu import fused_swiglu
         from metal_liger_b200.ops.fused_rope import apply_fused_rotary_from_positions
 
         d, h, ho = s["dev"], s["host"], s["host_out"]
-        for k in d:
-            d[k].copy_(h[k], non_blocking=True)
-        gate = d["gate"].detach().requires_grad_(True)
-        up = d["up"].detach().requires_grad_(True)
-        out = fused_swiglu(gate, up)
-        out.backward(d["dout"])
-        q = d["q"].detach().requires_grad_(True)
-        k = d["k"].detach().requires_grad_(True)
-        qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"], inv_freq=s["inv_freq"])
-        torch.autograd.backward([qr, kr], [d["dq"], d["dk"]])
-        for name, src in (("out", out), ("dgate", gate.grad), ("dup", up.grad), ("q_rot", qr),
-                          ("k_rot", kr), ("dq_in", q.grad), ("dk_in", k.grad)):
-            ho[name].copy_(src.detach(), non_blocking=True)
+
+        def load(i):
+            for k in d:
+                d[k][i].copy_(h[k][i], non_blocking=True)
+
+        def compute(i):
+            gate = d["gate"][i:i + 1].detach().requires_grad_(True)
+            up = d["up"][i:i + 1].detach().requires_grad_(True)
+            out = fused_swiglu(gate, up)
+            out.backward(d["dout"][i:i + 1])
+            q = d["q"][i:i + 1].detach().requires_grad_(True)
+            k = d["k"][i:i + 1].detach().requires_grad_(True)
+            qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"][i:i + 1],
+                                                       inv_freq=s["inv_freq"])
+            torch.autograd.backward([qr, kr], [d["dq"][i:i + 1], d["dk"][i:i + 1]])
+            return {"out": out.detach(), "dgate": gate.grad, "dup": up.grad,
+                    "q_rot": qr.detach(), "k_rot": kr.detach(), "dq_in": q.grad,
+                    "dk_in": k.grad}
+
+        def store(i, outs):
+            for name, src in outs.items():
+                ho[name][i:i + 1].copy_(src, non_blocking=True)
+            return outs.values()
+
+        s["pipe"].run(load, compute, store)
 
     # ---- CPU oracle on a bounded sample ----
     def cpu_inputs(self, tokens, seed=5):
@@ -311,8 +378,10 @@ class RmsNorm:
     """RMSNorm fwd+bwd fp32, x [8,1024,2048]."""
 
     name = "rmsnorm"
+    short = "configs[0] RMSNorm fp32 x[8,1024,2048]"
     bound = "hbm"
     dtype = "f32"
+    e2e_pipelined = True
     B, S, H = 8, 1024, 2048
     dominant = "rms_norm_backward"
 
@@ -362,21 +431,41 @@ class RmsNorm:
                     "dw": torch.empty_like(host["w"]).pin_memory()}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
-        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h}
+        return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h,
+                "pipe": CopyPipeline(device, self.B)}
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_rms_norm import _FusedRMSNormFunction
 
         d, h, ho = s["dev"], s["host"], s["host_out"]
-        for k in d:
-            d[k].copy_(h[k], non_blocking=True)
-        x = d["x"].detach().requires_grad_(True)
+        nb = self.B
+        # the weight is one leaf for the whole step: its gradient accumulates
+        # over the chunks (autograd adds), as over the batch rows of one call
         w = d["w"].detach().requires_grad_(True)
-        y = _FusedRMSNormFunction.apply(x, w, 1e-6)
-        y.backward(d["dy"])
-        ho["y"].copy_(y.detach(), non_blocking=True)
-        ho["dx"].copy_(x.grad, non_blocking=True)
-        ho["dw"].copy_(w.grad, non_blocking=True)
+
+        def load(i):
+            if i == 0:
+                d["w"].copy_(h["w"], non_blocking=True)
+            d["x"][i].copy_(h["x"][i], non_blocking=True)
+            d["dy"][i].copy_(h["dy"][i], non_blocking=True)
+
+        def compute(i):
+            x = d["x"][i:i + 1].detach().requires_grad_(True)
+            y = _FusedRMSNormFunction.apply(x, w, 1e-6)
+            y.backward(d["dy"][i:i + 1])
+            outs = {"y": y.detach(), "dx": x.grad}
+            if i == nb - 1:
+                outs["dw"] = w.grad
+            return outs
+
+        def store(i, outs):
+            ho["y"][i:i + 1].copy_(outs["y"], non_blocking=True)
+            ho["dx"][i:i + 1].copy_(outs["dx"], non_blocking=True)
+            if "dw" in outs:
+                ho["dw"].copy_(outs["dw"], non_blocking=True)
+            return outs.values()
+
+        s["pipe"].run(load, compute, store)
 
     def cpu_inputs(self, tokens, seed=6):
         g = torch.Generator().manual_seed(seed)
@@ -400,10 +489,12 @@ class Flce:
     N, H, V, CHUNK = 16384, 2048, 151936, 8192
     dominant = "flce_forward"
 
-    def __init__(self):
+    short = "configs[2] FLCE bf16 h[16384,2048] W[151936,2048] chunk 8192"
+
+    def __init__(self, world=None, rank=None):
         self.tokens = self.N
-        self.world = int(os.environ.get("WORLD_SIZE", "1"))
-        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1")) if world is None else world
+        self.rank = int(os.environ.get("RANK", "0")) if rank is None else rank
         # vocabulary shard of this rank (the whole vocabulary on one GPU)
         base, rem = divmod(self.V, self.world)
         self.v_local = base + (1 if self.rank < rem else 0)
@@ -512,8 +603,10 @@ class Lora:
     """fused LoRA QKV + MLP fwd+bwd, bf16, X [8,2048,4096], r=16, alpha=32."""
 
     name = "lora"
+    short = "configs[3] LoRA QKV+MLP bf16 X[8,2048,4096] r16"
     bound = "tensor"
     dtype = "bf16"
+    e2e_pipelined = True
     T, H, I, R, S = 8 * 2048, 4096, 12288, 16, 2.0
     QO, KVO = 4096, 1024
     dominant = "lora_mlp_backward"
@@ -595,31 +688,53 @@ class Lora:
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
         return {"host": host, "dev": dev, "host_out": host_out, "params": params, "h2d": h2d,
-                "d2h": d2h}
+                "d2h": d2h, "pipe": CopyPipeline(device, self.E2E_CHUNKS)}
+
+    E2E_CHUNKS = 4  # 4096 token rows per chunk
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_lora import _LoRA_MLP, _LoRA_QKV
 
         d, h, ho, P = s["dev"], s["host"], s["host_out"], s["params"]
-        for k in d:
-            d[k].copy_(h[k], non_blocking=True)
+        nc = s["pipe"].nchunks
+        rows = self.T // nc
+        # one set of adapter leaves per step: their gradients accumulate over
+        # the chunks (autograd adds), as over the token rows of one call
         leaves = {}
         for k in ("q", "k", "v", "g", "u", "d"):
             w, a, b = P[k]
             leaves[k] = (w, a.detach().requires_grad_(True), b.detach().requires_grad_(True),
                          self.S)
-        x = d["x"].detach().requires_grad_(True)
-        Q, K, V = _LoRA_QKV.apply(x, *leaves["q"], *leaves["k"], *leaves["v"])
-        torch.autograd.backward([Q, K, V], [d["dq"], d["dk"], d["dv"]])
-        x2 = d["x"].detach().requires_grad_(True)
-        out = _LoRA_MLP.apply(x2, *leaves["g"], *leaves["u"], *leaves["d"])
-        out.backward(d["dy"])
-        for name, src in (("Q", Q), ("K", K), ("V", V), ("out", out), ("dx_qkv", x.grad),
-                          ("dx_mlp", x2.grad)):
-            ho[name].copy_(src.detach(), non_blocking=True)
-        for i, k in enumerate(("q", "k", "v", "g", "u", "d")):
-            ho[f"dA{i}"].copy_(leaves[k][1].grad.float(), non_blocking=True)
-            ho[f"dB{i}"].copy_(leaves[k][2].grad.float(), non_blocking=True)
+
+        def load(i):
+            sl = slice(i * rows, (i + 1) * rows)
+            for k in d:
+                d[k][sl].copy_(h[k][sl], non_blocking=True)
+
+        def compute(i):
+            sl = slice(i * rows, (i + 1) * rows)
+            x = d["x"][sl].detach().requires_grad_(True)
+            Q, K, V = _LoRA_QKV.apply(x, *leaves["q"], *leaves["k"], *leaves["v"])
+            torch.autograd.backward([Q, K, V], [d["dq"][sl], d["dk"][sl], d["dv"][sl]])
+            x2 = d["x"][sl].detach().requires_grad_(True)
+            out = _LoRA_MLP.apply(x2, *leaves["g"], *leaves["u"], *leaves["d"])
+            out.backward(d["dy"][sl])
+            outs = {"Q": Q.detach(), "K": K.detach(), "V": V.detach(), "out": out.detach(),
+                    "dx_qkv": x.grad, "dx_mlp": x2.grad}
+            if i == nc - 1:
+                for j, k in enumerate(("q", "k", "v", "g", "u", "d")):
+                    outs[f"dA{j}"] = leaves[k][1].grad.float()
+                    outs[f"dB{j}"] = leaves[k][2].grad.float()
+            return outs
+
+        def store(i, outs):
+            sl = slice(i * rows, (i + 1) * rows)
+            for name, src in outs.items():
+                dst = ho[name] if name.startswith("d") and name[1] in "AB" else ho[name][sl]
+                dst.copy_(src, non_blocking=True)
+            return outs.values()
+
+        s["pipe"].run(load, compute, store)
 
     def cpu_inputs(self, tokens, seed=8):
         g = torch.Generator().manual_seed(seed)
@@ -659,6 +774,7 @@ class FullStep:
     """
 
     name = "c5_step"
+    short = "configs[4] Qwen3-VL-8B text LoRA step, 36 layers, seq 4096 per GPU"
     bound = "tensor"
     dtype = "bf16"
     L, H, NH, NKV, D, I, V = 36, 4096, 32, 8, 128, 12288, 151936
@@ -761,14 +877,9 @@ class FullStep:
         loss = MetalLigerFusedLinearCrossEntropy(m.lm_head)(h, labels)
         loss.backward()
         if self.world > 1:
-            import torch.distributed as dist
+            from metal_liger_b200.data_parallel import all_reduce_gradients
 
-            grads = [p.grad for p in self.params]
-            flat = torch._utils._flatten_dense_tensors(grads)
-            dist.all_reduce(flat)
-            flat.div_(self.world)
-            for gd, red in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
-                gd.copy_(red)
+            all_reduce_gradients(self.params)
         self.opt.step()
         self.opt.zero_grad(set_to_none=True)
         return loss.detach()
@@ -867,6 +978,7 @@ class Generate:
     patched modules (cuBLAS projections, SDPA attention)."""
 
     name = "generate"
+    short = "static-KV greedy generate, Qwen3-VL-8B text, prompt 128 + 64 tokens"
     bound = "hbm"
     dtype = "bf16"
     L, H, NH, NKV, D, I, V = 36, 4096, 32, 8, 128, 12288, 151936
@@ -1177,7 +1289,7 @@ def run_reference_arm(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    budget = float(os.environ.get("BENCH_CPU_BUDGET_S", "60"))
+    budget = float(os.environ.get("BENCH_CPU_BUDGET_S", "90"))
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     per_step_budget = budget / max(1, args.steps + args.warmup)
@@ -1218,53 +1330,81 @@ def run_reference_arm(args, wl):
     return 0
 
 
-def run_gpu_arm(args, wl):
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if not torch.cuda.is_available():
-        print(json.dumps({"error": "no CUDA device"}), flush=True)
-        return 1
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
+def _sig(x, n=5):
+    """x rounded to n significant digits (keeps the JSON line short)."""
+    if isinstance(x, float) and math.isfinite(x) and x != 0.0:
+        return float(f"{x:.{n}g}")
+    return x
 
-        import torch.distributed as dist_mod
 
-        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=device)
-        dist = dist_mod
+def _rounded(o, n=5):
+    if isinstance(o, dict):
+        return {k: _rounded(v, n) for k, v in o.items()}
+    if isinstance(o, (list, tuple)):
+        return [_rounded(v, n) for v in o]
+    return _sig(o, n)
 
-    import metal_liger_b200  # noqa: F401  (registers ops, loads the library on first call)
-    from metal_liger_b200 import _C
 
-    _C.load()
-    peaks, peaks_kind = load_peaks()
+class Ctx:
+    """Rank, device, process group and peaks shared by every measurement."""
 
-    t = wl.make_inputs(device)
+    def __init__(self, args):
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.device = torch.device("cuda", self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist_mod
+
+            dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                        device_id=self.device)
+            self.dist = dist_mod
+        self.peaks, self.peaks_kind = load_peaks()
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def reduce(self, x, op="max"):
+        """x reduced over ranks (MAX or MIN) with one NCCL all-reduce."""
+        if not self.dist:
+            return x
+        t = torch.tensor([float(x)], device=self.device, dtype=torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX if op == "max" else
+                             self.dist.ReduceOp.MIN)
+        return t.item()
+
+    def close(self):
+        if self.dist:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def timed_steps(ctx, wl, t, steps, warmup, spin_us):
+    """W untimed steps, then K steps each bracketed by its own pair of CUDA
+    events on the launching stream.  Before a step's first event the stream
+    gets the workload's untimed prelude (the L2 flush) and a short GPU spin,
+    so the host has queued the whole step before the GPU reaches it.
+    Returns (sum of the K spans in ms, max over ranks; per-kernel average ms
+    on this rank; clock summary sampled during the K steps)."""
     prelude = getattr(wl, "prelude", None)
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         if prelude:
             prelude(t)
         wl.step(t)
     torch.cuda.synchronize()
-
-    # ---- timed region ----
-    # Each step is bracketed by its own pair of events.  Before a step's first
-    # event the stream gets the workload's untimed prelude (the L2 flush) and
-    # a short GPU spin, so the host has queued the whole step before the GPU
-    # reaches it: the spans then hold device time only, not host launch
-    # latency, for the short HBM-bound kernels as for the long ones.
     timer = KernelTimer()
     spans = []
-    spin_cycles = int(args.spin_us * 2000)  # ~2 GHz SM clock
-    if dist:
-        dist.barrier()
+    spin_cycles = int(spin_us * 2000)  # ~2 GHz SM clock
+    ctx.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        for _ in range(args.steps):
+    with ClockSampler(ctx.local) as clk:
+        for _ in range(steps):
             if prelude:
                 prelude(t)
             if spin_cycles:
@@ -1276,144 +1416,336 @@ def run_gpu_arm(args, wl):
             e_ev.record()
             spans.append((s_ev, e_ev))
         torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    elapsed_ms = sum(a.elapsed_time(b) for a, b in spans)
-    if dist:
-        el = torch.tensor([elapsed_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(el, op=dist.ReduceOp.MAX)
-        elapsed_ms = el.item()
-    kernel_ms = timer.averages_ms()
-    per_step_launches = count_our_launches(wl, t, table=args.kernel_table and rank == 0)
-    if per_step_launches is None:
-        per_step_launches = wl.launches_per_step
-    # weak scaling: every rank processes wl.tokens; strong: the job processes wl.tokens
-    job_tokens = wl.tokens * (world if getattr(wl, "scaling", "weak") == "weak" else 1)
-    value = job_tokens * args.steps / (elapsed_ms / 1e3)
+    ctx.barrier()
+    elapsed = ctx.reduce(sum(a.elapsed_time(b) for a, b in spans))
+    return elapsed, timer.averages_ms(), clk.summary()
 
-    # ---- end to end through the public API with host buffers ----
-    del t
-    torch.cuda.empty_cache()
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    s = wl.e2e_setup(device)
+
+def peak_extra_bytes(wl, t):
+    """Device memory one step allocates beyond what is resident before it
+    (workspaces, temporaries and the step's outputs), from the caching
+    allocator's peak counter on an extra, untimed step."""
+    prelude = getattr(wl, "prelude", None)
+    if prelude:
+        prelude(t)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    wl.step(t)
+    torch.cuda.synchronize()
+    return int(torch.cuda.max_memory_allocated() - base)
+
+
+def e2e_measure(ctx, wl, steps):
+    s = wl.e2e_setup(ctx.device)
     for _ in range(2):
         wl.e2e_step(s)
     torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
+    ctx.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(e2e_steps):
+    for _ in range(steps):
         wl.e2e_step(s)
     e1.record()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if dist:
-        el = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(el, op=dist.ReduceOp.MAX)
-        e2e_ms = el.item()
-    e2e_value = job_tokens * e2e_steps / (e2e_ms / 1e3)
+    ms = ctx.reduce(e0.elapsed_time(e1))
     h2d, d2h = s["h2d"], s["d2h"]
     del s
     torch.cuda.empty_cache()
+    return ms, h2d, d2h
 
-    # ---- roofline of the dominant kernel ----
+
+def roofline(ctx, wl, kernel_ms, burst):
+    """The dominant kernel's roofline entry and the per-kernel fractions."""
+    peaks = ctx.peaks
     dom = wl.dominant
     dom_ms = kernel_ms.get(dom)
     if wl.bound == "hbm":
         peak = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
         achieved = wl.bytes[dom] / (dom_ms / 1e3) / 1e9
         unit = "GB/s"
+        which = ""
     else:
         # The tensor-bound kernels run inside multi-millisecond steps repeated for
         # the whole timed region, i.e. under the 1 kW power cap: the sustained
         # cuBLAS figure is the matching denominator (--burst selects the other).
-        key = "bf16_tflops" if args.burst else "bf16_tflops_sustained"
+        key = "bf16_tflops" if burst else "bf16_tflops_sustained"
         peak = float(peaks.get(key, FALLBACK_PEAKS[key]))
         achieved = wl.flops[dom] / (dom_ms / 1e3) / 1e12
         unit = "TFLOP/s"
-    traffic = load_traffic(wl.name, dom)
+        which = ", burst" if burst else ", sustained"
+    src = "MEASURED_PEAKS.json" if ctx.peaks_kind == "measured" else "profiling-recipe fallback"
+    roof = {"kernel": dom, "bound": wl.bound, "achieved": achieved, "peak": peak,
+            "peak_source": f"{ctx.peaks_kind} ({src}{which})", "unit": unit,
+            "frac": achieved / peak, "traffic": load_traffic(wl.name, dom)}
     per_kernel = {}
     for k, ms in kernel_ms.items():
-        entry = {"avg_ms": ms}
+        entry = {"ms": ms}
         if wl.bound == "hbm" and k in wl.bytes:
             gbs = wl.bytes[k] / (ms / 1e3) / 1e9
-            entry.update({"algorithmic_bytes": wl.bytes[k], "GB/s": gbs,
-                          "frac_of_measured_hbm": gbs / float(peaks.get("hbm_gbs", 1))})
+            entry.update({"GB/s": gbs, "frac": gbs / float(peaks.get("hbm_gbs", 1))})
         if getattr(wl, "flops", None) and k in wl.flops:
             tf = wl.flops[k] / (ms / 1e3) / 1e12
-            entry.update({"algorithmic_flops": wl.flops[k], "TFLOP/s": tf,
-                          "frac_of_measured_bf16_burst": tf / float(peaks.get("bf16_tflops", 1)),
-                          "frac_of_measured_bf16_sustained":
-                              tf / float(peaks.get("bf16_tflops_sustained", 1))})
+            key = "bf16_tflops" if burst else "bf16_tflops_sustained"
+            entry.update({"TFLOP/s": tf, "frac": tf / float(peaks.get(key, 1))})
         per_kernel[k] = entry
+    return roof, per_kernel
 
+
+def cpu_baseline(wl, budget_s):
+    v, tok, st, cores = cpu_measure(wl, budget_s=budget_s)
+    sample = (f"{tok} of {wl.tokens} tokens x {st} steps through the CPU oracle "
+              f"(torch fp32 restatement of the reference ops), {cores} threads")
+    if getattr(wl, "cpu_extrapolated", False):
+        v *= wl.cpu_scale()
+        sample = (f"{tok} tokens x {st} steps of {wl.cpu_desc} on {cores} threads; "
+                  f"tokens/s extrapolated to {wl.L} layers by the FLOP ratio "
+                  f"{wl.cpu_scale():.4f}")
+    return {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+
+
+def measure_workload(ctx, wl, steps, warmup, e2e_steps, cpu_budget, table=False, keep=False):
+    """Device-timed value, roofline, launch count, peak memory, e2e and (rank 0
+    at N=1) the CPU baseline of one workload.  With `keep`, the resident
+    inputs are returned in the result under "inputs" instead of freed."""
+    args = ctx.args
+    t = wl.make_inputs(ctx.device)
+    elapsed_ms, kernel_ms, clocks = timed_steps(ctx, wl, t, steps, warmup, args.spin_us)
+    launches = count_our_launches(wl, t, table=table and ctx.rank == 0)
+    if launches is None:
+        launches = wl.launches_per_step
+    peak = peak_extra_bytes(wl, t)
     extra = None
-    if rank == 0 and hasattr(wl, "extra_measurements"):
-        extra = wl.extra_measurements(device)
+    if ctx.rank == 0 and hasattr(wl, "extra_measurements"):
+        extra = wl.extra_measurements(ctx.device)
+    inputs = t if keep else None
+    del t
+    torch.cuda.empty_cache()
+    # weak scaling: every rank processes wl.tokens; strong: the job processes wl.tokens
+    job_tokens = wl.tokens * (ctx.world if getattr(wl, "scaling", "weak") == "weak" else 1)
+    e2e_steps = max(1, min(steps, e2e_steps))
+    e2e_ms, h2d, d2h = e2e_measure(ctx, wl, e2e_steps)
+    roof, per_kernel = roofline(ctx, wl, kernel_ms, args.burst)
+    cpu = None
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(wl, cpu_budget)
+    return {
+        "value": job_tokens * steps / (elapsed_ms / 1e3),
+        "ms_per_step": elapsed_ms / steps,
+        "roofline": roof, "per_kernel": per_kernel, "clocks": clocks,
+        "gpu_launches": launches * steps if launches is not None else None,
+        "peak_extra_bytes": peak,
+        "e2e": {"value": job_tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "cpu_baseline": cpu, "extra": extra, "inputs": inputs,
+    }
 
-    line = None
-    if rank == 0:
-        cpu = None
-        if world == 1 and not args.no_cpu:
-            v, tok, st, cores = cpu_measure(wl, budget_s=args.cpu_budget)
-            sample = (f"{tok} of {wl.tokens} tokens x {st} steps through the CPU oracle "
-                      f"(torch fp32 restatement of the reference ops), {cores} threads")
-            if getattr(wl, "cpu_extrapolated", False):
-                v *= wl.cpu_scale()
-                sample = (f"{tok} tokens x {st} steps of {wl.cpu_desc} on {cores} threads; "
-                          f"tokens/s extrapolated to {wl.L} layers by the FLOP ratio "
-                          f"{wl.cpu_scale():.4f}")
-            cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
-                   "sample": sample}
+
+def compact_entry(wl, r, steps):
+    """One workload of the default run's `workloads` object."""
+    roof = dict(r["roofline"])
+    roof.pop("peak_source", None)
+    e = {"config": wl.short, "value": r["value"], "unit": "tokens/s",
+         "ms_per_step": r["ms_per_step"], "steps": steps,
+         "scaling": getattr(wl, "scaling", "weak"), "roofline": roof,
+         "kernel_frac": {k: v.get("frac") for k, v in r["per_kernel"].items()},
+         "e2e": {k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+         "gpu_launches": r["gpu_launches"], "peak_extra_bytes": r["peak_extra_bytes"],
+         "clocks": {"sm_mhz": r["clocks"].get("sm_mhz"), "reasons": r["clocks"].get("reasons")}}
+    if r["cpu_baseline"]:
+        c = r["cpu_baseline"]
+        e["cpu_baseline"] = {"value": c["value"], "cores": c["cores"], "kind": c["kind"],
+                             "sample": c["sample"]}
+    return e
+
+
+def _frob(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp(min=1e-30)).item()
+
+
+def _bf16_close(a, b):
+    """Element-wise bf16 contract with the absolute term scaled to the
+    tensor's largest magnitude (the FLCE gradients carry a 1/n_valid factor,
+    so a fixed 1e-2 would pass anything): |a - b| <= 2e-2 |b| + 1e-2 max|b|."""
+    a, b = a.float(), b.float()
+    bad = (a - b).abs() > 2e-2 * b.abs() + 1e-2 * b.abs().max()
+    return int(bad.sum().item())
+
+
+def measure_flce_vp(ctx, steps, warmup, vp):
+    """The vocabulary-parallel FLCE at N ranks (already timed in `vp`, with
+    its inputs kept) against the single-GPU FLCE on the same seeded inputs:
+    every rank times the single-GPU op on its own GPU (no collectives) for the
+    speed-up, and checks its own vocabulary shard of the parallel result
+    against the single-GPU result (loss, dX, dW rows, exact ignore count)."""
+    from metal_liger_b200 import _C
+
+    ops = torch.ops.metal_liger
+    t = vp["inputs"]
+    single = Flce(world=1, rank=0)
+    full = single.make_inputs(ctx.device)  # the same seeded tensors, whole vocabulary
+    ms1, _, _ = timed_steps(ctx, single, full, steps, warmup, ctx.args.spin_us)
+
+    # parity: one step of each on the same inputs
+    vpw = Flce()
+    loss_v, dx_v, dw_v = vpw._vp(t)
+    gh_v, gw_v = ops.flce_backward(t["go"], dx_v, dw_v, 1, 1)
+    loss_1, dx_1, dw_1 = ops.flce_forward(full["h"], full["w"], full["lab"], None, -100,
+                                          single.CHUNK, True, True)
+    gh_1, gw_1 = ops.flce_backward(full["go"], dx_1, dw_1, 1, 1)
+    off, vl = t["off"], t["w"].shape[0]
+    rows_1 = gw_1[off:off + vl]
+    cnt = torch.empty(2, dtype=torch.float32, device=ctx.device)
+    _C.call("ml_flce_count_valid", t["lab"].data_ptr(), t["lab"].numel(), -100,
+            cnt.data_ptr(), _C.stream_of(t["lab"]))
+    torch.cuda.synchronize()
+    n_valid = int((t["lab"] != -100).sum().item())
+    errs = {
+        "loss_rel": abs(loss_v.item() - loss_1.item()) / max(abs(loss_1.item()), 1e-30),
+        "dx_frob": _frob(gh_v, gh_1), "dw_frob": _frob(gw_v, rows_1),
+        "dx_bad": _bf16_close(gh_v, gh_1), "dw_bad": _bf16_close(gw_v, rows_1),
+    }
+    ok = (errs["loss_rel"] <= 1e-4 and errs["dx_frob"] <= 1e-2 and errs["dw_frob"] <= 1e-2
+          and errs["dx_bad"] == 0 and errs["dw_bad"] == 0 and int(cnt[0].item()) == n_valid)
+    all_ok = ctx.reduce(1.0 if ok else 0.0, "min") == 1.0
+    worst = {k: ctx.reduce(v) for k, v in errs.items()}
+    del full, dx_1, dw_1, gh_1, gw_1, rows_1, gh_v, gw_v, dx_v, dw_v
+    torch.cuda.empty_cache()
+
+    # where the step's time goes: one profiled step (CUPTI) on every rank
+    timeline = vp_timeline(vpw, t)
+    tok = single.tokens
+    out = {"n_gpus": ctx.world, "scaling": "strong", "tokens_per_step": tok,
+           "tokens_per_s": tok * steps / (vp["ms_per_step"] * steps / 1e3),
+           "ms_per_step": vp["ms_per_step"], "one_gpu_ms_per_step": ms1 / steps,
+           "speedup_vs_1": (ms1 / steps) / vp["ms_per_step"],
+           "parity": all_ok,
+           "parity_vs": "single-GPU FLCE on the same seeded inputs, every rank's shard: loss "
+                        "1e-4 rel, dX/dW |d| <= 2e-2|ref| + 1e-2 max|ref| and 1e-2 Frobenius, "
+                        "ignore count exact",
+           "worst_errors": worst, "n_valid": n_valid, "timeline_rank0": timeline,
+           "roofline": {k: vp["roofline"][k] for k in ("kernel", "achieved", "peak", "unit",
+                                                       "frac")},
+           "clocks": {"sm_mhz": vp["clocks"].get("sm_mhz"),
+                      "reasons": vp["clocks"].get("reasons")}}
+    return out
+
+
+def vp_timeline(wl, t):
+    """Device time of one vocabulary-parallel step split into NCCL kernels and
+    this library's kernels (CUPTI), with the step's event-timed span."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            wl.step(t)
+            e.record()
+            torch.cuda.synchronize()
+        nccl = ours = other = 0.0
+        for ev in prof.events():
+            if getattr(ev, "device_type", None) != torch.autograd.DeviceType.CUDA:
+                continue
+            tr = getattr(ev, "time_range", None)
+            us = (tr.end - tr.start) if tr is not None else 0.0
+            name = ev.name or ""
+            if "nccl" in name.lower():
+                nccl += us
+            elif _OUR_KERNEL is not None and _OUR_KERNEL.search(name):
+                ours += us
+            else:
+                other += us
+        return {"span_ms": s.elapsed_time(e), "nccl_kernel_ms": nccl / 1e3,
+                "library_kernel_ms": ours / 1e3, "other_kernel_ms": other / 1e3}
+    except Exception as exc:  # the timeline is diagnostic only
+        return {"error": str(exc)[:120]}
+
+
+SUITE_N1 = ("rmsnorm", "flce", "lora", "c5_step")
+SUITE_NN = ("rmsnorm", "lora", "c5_step")  # flce runs as flce_vp at N > 1
+
+
+def run_gpu_arm(args, wl):
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}), flush=True)
+        return 1
+    ctx = Ctx(args)
+    import metal_liger_b200  # noqa: F401  (registers ops, loads the library on first call)
+    from metal_liger_b200 import _C
+
+    _C.load()
+    suite = args.workload is None and not args.headline_only
+    r = measure_workload(ctx, wl, args.steps, args.warmup, args.e2e_steps, args.cpu_budget,
+                         table=args.kernel_table)
+
+    workloads, flce_vp = {}, None
+    if suite:
+        for name in (SUITE_N1 if ctx.world == 1 else SUITE_NN):
+            sub = WORKLOADS[name]()
+            res = measure_workload(ctx, sub, args.steps, args.warmup, args.e2e_steps,
+                                   args.cpu_budget_sub)
+            workloads[name] = compact_entry(sub, res, args.steps)
+            if ctx.world == 1 and name == "flce":
+                flce_vp = {"n_gpus": 1, "scaling": "strong", "tokens_per_step": sub.tokens,
+                           "tokens_per_s": res["value"], "ms_per_step": res["ms_per_step"],
+                           "one_gpu_ms_per_step": res["ms_per_step"], "speedup_vs_1": 1.0,
+                           "parity": None,
+                           "parity_vs": "one GPU holds the whole vocabulary: no shards"}
+            del sub, res
+            torch.cuda.empty_cache()
+        if ctx.world > 1:
+            fl = Flce()
+            vp = measure_workload(ctx, fl, args.steps, args.warmup, args.e2e_steps, 0.0,
+                                  keep=True)
+            flce_vp = measure_flce_vp(ctx, args.steps, args.warmup, vp)
+            del fl, vp
+            torch.cuda.empty_cache()
+
+    if ctx.rank == 0:
         line = {
             "metric": getattr(wl, "metric", METRIC),
-            "value": value,
+            "value": r["value"],
             "unit": "tokens/s",
-            "n_gpus": world,
+            "n_gpus": ctx.world,
             "steps": args.steps,
             "warmup": args.warmup,
-            "ms_per_step": elapsed_ms / args.steps,
+            "ms_per_step": r["ms_per_step"],
             "higher_is_better": True,
             "scaling": getattr(wl, "scaling", "weak"),
             "vs_baseline": None,
             "dtype": wl.dtype,
             "data": "synthetic (seeded normal inputs of the BASELINE shapes)",
             "config": {**wl.config(),
-                       "timed_region": "sum over the K steps of per-step CUDA-event spans on "
-                                       "the launching stream (max over ranks); the L2 flush "
-                                       "(where the inputs fit in L2) and a "
-                                       f"{args.spin_us:g} us GPU spin before each step are "
+                       "timed_region": "sum of per-step CUDA-event spans on the launching "
+                                       "stream, max over ranks; L2 flush and a "
+                                       f"{args.spin_us:g} us GPU spin before each step, "
                                        "outside the spans"},
-            "roofline": {
-                "kernel": dom,
-                "bound": wl.bound,
-                "achieved": achieved,
-                "peak": peak,
-                "peak_source": (f"{peaks_kind} "
-                                f"({'MEASURED_PEAKS.json' if peaks_kind == 'measured' else 'profiling-recipe fallback'}"
-                                f"{'' if wl.bound == 'hbm' else (', burst' if args.burst else ', sustained')})"),
-                "unit": unit,
-                "frac": achieved / peak,
-                "traffic": traffic,
-            },
-            "per_kernel": per_kernel,
-            "cpu_baseline": cpu,
-            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                    "api": getattr(wl, "e2e_api", "public autograd Functions (metal_liger_b200.ops.*), pinned "
-                                   "host buffers, H2D inputs + D2H all outputs per step")},
-            "gpu_launches": (per_step_launches * args.steps
-                             if per_step_launches is not None else None),
-            "clocks": clk.summary(),
+            "roofline": r["roofline"],
+            "per_kernel": {k: {kk: vv for kk, vv in v.items() if kk in ("ms", "frac")}
+                           for k, v in r["per_kernel"].items()},
+            "cpu_baseline": r["cpu_baseline"],
+            "e2e": {**r["e2e"],
+                    "api": getattr(wl, "e2e_api", "public autograd Functions, pinned host "
+                                   "buffers, H2D of inputs + D2H of all outputs every step"
+                                   + (", batch rows pipelined over 3 streams"
+                                      if getattr(wl, "e2e_pipelined", False) else ""))},
+            "gpu_launches": r["gpu_launches"],
+            "peak_extra_bytes": r["peak_extra_bytes"],
+            "clocks": r["clocks"],
         }
-        if extra:
-            line.update(extra)
-        print(json.dumps(line), flush=True)
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+        if r["extra"]:
+            line.update(r["extra"])
+        if workloads:
+            line["workloads"] = workloads
+        if flce_vp is not None:
+            line["flce_vp"] = flce_vp
+        print(json.dumps(_rounded(line)), flush=True)
+    ctx.close()
     return 0
 
 
@@ -1421,24 +1753,30 @@ def main(argv=None):
     _register_optional_workloads()
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu_rope")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=None,
+                    help="run this workload alone as the line (default: swiglu_rope as the "
+                         "line plus every other op under 'workloads' and 'flce_vp')")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="default workload without the other ops")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--kernel-table", action="store_true",
                     help="print one extra step's per-kernel device times (CUPTI) to stderr")
     ap.add_argument("--spin-us", type=float, default=200.0,
                     help="untimed GPU spin before each timed step (host run-ahead); 0 = off")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
-                    help="seconds of CPU-oracle work for cpu_baseline")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurement")
+                    help="seconds of CPU-oracle work for the line's cpu_baseline")
+    ap.add_argument("--cpu-budget-sub", type=float, default=6.0,
+                    help="seconds of CPU-oracle work for each entry of 'workloads'")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurements")
     ap.add_argument("--burst", action="store_true",
                     help="use the burst (not sustained) bf16 peak for tensor-bound rooflines")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload or "swiglu_rope"]()
     if args.impl == "reference":
         return run_reference_arm(args, wl)
     return run_gpu_arm(args, wl)

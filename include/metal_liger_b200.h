@@ -466,7 +466,9 @@ ML_API int ml_gemv_multi_bf16(const void* x, int64_t ld_x, int nmat, const void*
  * element strides (sq_b, sq_h), head_dim contiguous; k_cache / v_cache
  * [B, kv_heads, max_len, head_dim] contiguous bf16; out [B, 1, q_heads,
  * head_dim] bf16; head_dim a multiple of 32 up to 256; fp32 scores and
- * accumulation; workspace >= ml_decode_attention_workspace_bytes.
+ * accumulation; workspace >= ml_decode_attention_workspace_bytes, which is 0
+ * for caches of at most 256 positions (one launch, the partials in shared
+ * memory: workspace may then be NULL).
  */
 ML_API size_t ml_decode_attention_workspace_bytes(int64_t batch, int64_t q_heads,
                                                   int64_t max_len, int64_t head_dim);

@@ -898,8 +898,9 @@ def decode_attention_cuda(q: Tensor, k_cache: Tensor, v_cache: Tensor, pos: Tens
     k_cache, v_cache = _contig(k_cache), _contig(v_cache)
     out = torch.empty((B, 1, Hq, D), dtype=torch.bfloat16, device=q.device)
     lib = _C.load()
+    # caches of up to 8 chunks run as one launch that needs no workspace
     nbytes = int(lib.ml_decode_attention_workspace_bytes(B, Hq, L, D))
-    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=q.device)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device) if nbytes else None
     _C.call("ml_decode_attention_bf16", _C.ptr(q), q.stride(0), q.stride(1), _C.ptr(k_cache),
             _C.ptr(v_cache), _C.ptr(pos), int(len_offset), B, Hq, Hkv, L, D, float(scale),
             _C.ptr(out), _C.ptr(ws), nbytes, _C.stream_of(q))

@@ -58,6 +58,39 @@ inline bool aligned16(const void* p) {
   return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }
 
+// RMSNorm row split, shared by the RMSNorm kernels (rms_norm.cu) and the
+// decode GEMVs that replay the norm on their staged activations (gemv.cu),
+// which must match it bit for bit: a row of `nvec` 16-byte vectors goes to
+// `tpr` threads holding `nv` vectors each.  One vector per thread while
+// nvec <= one_vec_limit, else the fewest of 2/4/8 that keep a row within
+// kRmsMaxThreads threads; sub-warp groups of 4/8/16 threads for short rows,
+// whole warps above.  False when no vector layout fits (scalar path).
+constexpr int kRmsMaxThreads = 256;  // vector path: per-thread registers hold 2 rows (prefetch)
+
+// Rows up to this many vectors take one vector per thread.  Measured on B200
+// (bf16 [16384, 4096]): the forward is faster with two vectors per thread on
+// 256 threads (4.4 vs 2.8 TB/s), the backward with one on 512 threads and
+// the ring kernel (2.9 vs 2.6 TB/s).
+constexpr int64_t rms_one_vec_limit(int elem_bytes, bool backward) {
+  return (elem_bytes == 2 && backward) ? 512 : 256;
+}
+
+inline bool rms_row_split(int64_t nvec, int64_t one_vec_limit, int* nv_out, int* tpr_out) {
+  int nv = 1;
+  if (nvec > one_vec_limit)
+    while ((nvec + nv - 1) / nv > kRmsMaxThreads && nv < 8) nv *= 2;
+  const int64_t per = (nvec + nv - 1) / nv;
+  int64_t tpr;
+  if (per <= 4) tpr = 4;
+  else if (per <= 8) tpr = 8;
+  else if (per <= 16) tpr = 16;
+  else tpr = (per + 31) / 32 * 32;
+  if (tpr > (nv == 1 ? 512 : kRmsMaxThreads)) return false;
+  *nv_out = nv;
+  *tpr_out = (int)tpr;
+  return true;
+}
+
 // ---------------------------------------------------------------------------
 // Element access (device): load/store one element of a runtime dtype as fp32.
 // ---------------------------------------------------------------------------

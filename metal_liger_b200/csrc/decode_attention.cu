@@ -309,8 +309,9 @@ struct QkPrep {
   int B, Hq, Hkv, L;
 };
 
-// Row r of sequence b (q rows 0..Hq-1, k rows, v rows), one warp, for a
-// position p inside the cache.  A q row goes to q_out, or, with q_f32, to
+// Row r of sequence b (q rows 0..Hq-1, k rows, v rows), one warp; k and v
+// rows index the caches at p, so they need p inside [0, L).  A q row (whose
+// cos/sin are per sequence, not per cache slot) goes to q_out, or, with q_f32, to
 // q_f32[0, D) as the bf16-rounded values in fp32 (what a kernel loading
 // q_out would see).
 template <int EPL>
@@ -374,8 +375,11 @@ __global__ void __launch_bounds__(256) decode_qk_prep(const __grid_constant__ Qk
   const int per_b = a.Hq + 2 * a.Hkv;
   if (row >= (int64_t)a.B * per_b) return;
   const int64_t p = *a.pos;
-  if (p < 0 || p >= a.L) return;  // outside the cache: nothing to write
-  prep_row<EPL>(a, (int)(row / per_b), (int)(row % per_b), p, nullptr);
+  const int r = (int)(row % per_b);
+  // A q row is prepared for any position (as decode_qk_attn_single does);
+  // the k and v rows are written only at a position inside the cache.
+  if (r >= a.Hq && (p < 0 || p >= a.L)) return;
+  prep_row<EPL>(a, (int)(row / per_b), r, p, nullptr);
 }
 
 // q/k preparation and the single-launch attention in one kernel, a CTA per
@@ -464,6 +468,7 @@ extern "C" size_t ml_decode_attention_workspace_bytes(int64_t batch, int64_t q_h
                                                       int64_t max_len, int64_t head_dim) {
   if (batch <= 0 || q_heads <= 0 || max_len <= 0 || head_dim <= 0) return 0;
   const int64_t nchunk = (max_len + kChunk - 1) / kChunk;
+  if (nchunk <= kFusedSlots) return 0;  // one launch, partials in shared memory
   return (size_t)nchunk * batch * q_heads * (2 + head_dim) * sizeof(float);
 }
 
@@ -488,8 +493,10 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
                "decode_attention: KV buffers must be 16-byte aligned");
   ML_CHECK_ARG(batch * kv_heads <= 65535 && max_len < ((int64_t)1 << 31),
                "decode_attention: too many sequences x kv heads");
-  ML_CHECK_ARG(workspace && workspace_bytes >= ml_decode_attention_workspace_bytes(
-                                                   batch, q_heads, max_len, head_dim),
+  const int nchunk = (int)((max_len + kChunk - 1) / kChunk);
+  const bool single = nchunk <= kFusedSlots;
+  ML_CHECK_ARG(single || (workspace && workspace_bytes >= ml_decode_attention_workspace_bytes(
+                                                              batch, q_heads, max_len, head_dim)),
                "decode_attention: workspace too small");
   DecodeArgs a;
   a.q = static_cast<const __nv_bfloat16*>(q);
@@ -505,10 +512,9 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
   a.L = (int)max_len;
   a.D = (int)head_dim;
   a.scale = scale;
-  const int nchunk = (int)((max_len + kChunk - 1) / kChunk);
-  a.part_m = static_cast<float*>(workspace);
-  a.part_l = a.part_m + (int64_t)nchunk * batch * q_heads;
-  a.part_o = a.part_l + (int64_t)nchunk * batch * q_heads;
+  a.part_m = single ? nullptr : static_cast<float*>(workspace);
+  a.part_l = single ? nullptr : a.part_m + (int64_t)nchunk * batch * q_heads;
+  a.part_o = single ? nullptr : a.part_l + (int64_t)nchunk * batch * q_heads;
   a.out = static_cast<__nv_bfloat16*>(out);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int G = (int)(q_heads / kv_heads);
@@ -524,7 +530,6 @@ extern "C" int ml_decode_attention_bf16(const void* q, int64_t sq_b, int64_t sq_
     launched = true;                                                       \
   }
   bool launched = false;
-  const bool single = nchunk <= kFusedSlots;
   ML_DA_CASE(1, 2) ML_DA_CASE(1, 4) ML_DA_CASE(1, 8)
   ML_DA_CASE(2, 2) ML_DA_CASE(2, 4) ML_DA_CASE(2, 8)
   ML_DA_CASE(4, 2) ML_DA_CASE(4, 4) ML_DA_CASE(4, 8)

@@ -135,25 +135,13 @@ __device__ __forceinline__ void rmsnorm_rows(uint4* hs, int64_t nchunk,
 }
 
 // Host: the RMSNorm forward kernel's row layout for a bf16 row of K
-// elements (rms_norm.cu, pick_cfg with backward = false): `nv` 16-byte
-// vectors on each of `tpr` threads.  False when that kernel takes its scalar
-// path for such a row (then there is nothing to mirror).
+// elements (the same rms_row_split call as rms_norm.cu's pick_cfg with
+// backward = false): `nv` 16-byte vectors on each of `tpr` threads.  False
+// when that kernel takes its scalar path for such a row (then there is
+// nothing to mirror).
 inline bool rms_row_layout(int64_t K, int* tpr, int* nv) {
   if (K % 8 != 0) return false;
-  const int64_t nvec = K / 8;
-  int v = 1;
-  if (nvec > 256)
-    while ((nvec + v - 1) / v > 256 && v < 8) v *= 2;
-  const int64_t per = (nvec + v - 1) / v;
-  int64_t t;
-  if (per <= 4) t = 4;
-  else if (per <= 8) t = 8;
-  else if (per <= 16) t = 16;
-  else t = (per + 31) / 32 * 32;
-  if (t > (v == 1 ? 512 : 256)) return false;
-  *tpr = (int)t;
-  *nv = v;
-  return true;
+  return rms_row_split(K / 8, rms_one_vec_limit(2, /*backward=*/false), nv, tpr);
 }
 
 // Host: whether a call can take the GEMV kernels (16-byte rows, shared

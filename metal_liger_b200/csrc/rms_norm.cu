@@ -20,7 +20,7 @@
 namespace ml {
 namespace {
 
-constexpr int kMaxThreads = 256;  // vector path: per-thread registers hold 2 rows (prefetch)
+constexpr int kMaxThreads = kRmsMaxThreads;
 
 // Backward CTA size: when a thread's share of two rows (current + prefetch)
 // fits in ~80 registers the CTA holds three 256-thread row groups and runs one
@@ -62,22 +62,10 @@ RowCfg pick_cfg(int64_t hidden, const void* a, const void* b, const void* c, con
   if (hidden % VEC != 0 || !aligned16(a) || !aligned16(b) || !aligned16(c) || !aligned16(d))
     return cfg;
   const int64_t nvec = hidden / VEC;
-  int nv = 1;
-  // Measured on B200 (bf16 [16384, 4096]): the forward is faster with two
-  // vectors per thread on 256 threads (4.4 vs 2.8 TB/s), the backward with
-  // one on 512 threads and the ring kernel (2.9 vs 2.6 TB/s).
-  const int64_t one_vec_limit = (sizeof(TX) == 2 && backward) ? 512 : 256;
-  if (nvec > one_vec_limit)
-    while ((nvec + nv - 1) / nv > kMaxThreads && nv < 8) nv *= 2;
-  const int64_t per = (nvec + nv - 1) / nv;
-  int64_t tpr;
-  if (per <= 4) tpr = 4;
-  else if (per <= 8) tpr = 8;
-  else if (per <= 16) tpr = 16;
-  else tpr = (per + 31) / 32 * 32;
-  if (tpr > (nv == 1 ? 512 : kMaxThreads)) return cfg;
+  int nv, tpr;
+  if (!rms_row_split(nvec, rms_one_vec_limit((int)sizeof(TX), backward), &nv, &tpr)) return cfg;
   cfg.nv = nv;
-  cfg.tpr = static_cast<int>(tpr);
+  cfg.tpr = tpr;
   const int max_groups = tpr < 32 ? 32 : 8;  // named barriers are only needed for tpr >= 32
   const int cta_threads = (!backward && nv == 2) ? fwd_max_threads(nv) : kMaxThreads;
   cfg.groups = std::max(1, std::min<int>(max_groups, cta_threads / cfg.tpr));

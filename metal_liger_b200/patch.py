@@ -11,17 +11,26 @@ behaviour (reference patch.py:181-240):
 * every MLP with a ``gate_proj`` is wrapped in ``MetalLigerSwiGLU``;
 * PEFT LoRA projections are routed through the fused LoRA Functions by
   ``patch_fused_lora`` (which never touches ``_modules``);
-* ``fuse_rope`` / ``fuse_cross_entropy`` only log that the fused functions are
-  available (``apply_fused_rotary*``, ``MetalLigerFusedLinearCrossEntropy``),
-  exactly as the reference does.
+* ``fuse_rope`` only logs that the fused functions are available
+  (``apply_fused_rotary*``), as the reference does;
+* ``fuse_cross_entropy`` (the reference only logs it) routes the causal-LM
+  loss through ``MetalLigerFusedLinearCrossEntropy``: in training mode, when
+  ``labels`` are given, the model's forward runs with its ``lm_head`` shadowed
+  by a capture of the hidden states, and the loss over HF's shifted labels
+  (``ignore_index=-100``) comes from the fused op, so the ``[B*S, V]`` logits
+  are never formed (the output's ``logits`` is None).
 
 Layers are located through the same PEFT / VL nesting paths the reference
 tries (patch.py:27-89).
 """
 
+import inspect
 import logging
+import types
 
+import torch
 import torch.nn as nn
+import torch.nn.functional as F
 
 from metal_liger_b200.generation import patch_generator
 from metal_liger_b200.ops.fused_lora import patch_fused_lora
@@ -185,6 +194,124 @@ def restore_attention_rope(model: nn.Module) -> int:
     return done
 
 
+# Owners of the lm_head whose forward takes ``labels``: a PEFT wrapper's HF
+# model, a DDP-style ``module``, or the model itself (deepest first, since
+# PEFT wrappers forward unknown attributes to the model they wrap).
+_LM_PATHS = (("base_model", "model"), ("module",), ())
+
+
+def _find_causal_lm(model: nn.Module):
+    for path in _LM_PATHS:
+        obj = _walk(model, path) if path else model
+        head = getattr(obj, "lm_head", None) if obj is not None else None
+        if not isinstance(head, nn.Linear) or hasattr(head, "lora_A"):
+            continue
+        fwd = obj.__dict__.get("_metal_liger_original_forward", obj.forward)
+        try:
+            params = inspect.signature(fwd).parameters
+        except (TypeError, ValueError):
+            continue
+        if "labels" in params:
+            return obj
+    return None
+
+
+class _HiddenCapture(nn.Module):
+    """Stands in for the lm_head during one forward: keeps the hidden states
+    it is given and returns an empty [..., 0] tensor in place of the logits."""
+
+    def __init__(self):
+        super().__init__()
+        self.hidden = None
+
+    def forward(self, hidden_states):
+        self.hidden = hidden_states
+        return hidden_states.new_empty(*hidden_states.shape[:-1], 0)
+
+
+def causal_lm_loss(hidden, lm_head, labels=None, shift_labels=None, num_items_in_batch=None,
+                   ignore_index=-100, chunk_size=8192):
+    """HF's causal-LM loss (transformers ``ForCausalLMLoss``: labels shifted by
+    one, the last position ignored; a mean over the non-ignored tokens, or a
+    sum divided by ``num_items_in_batch`` when that is given) computed by the
+    fused linear cross-entropy from the final hidden states."""
+    from metal_liger_b200.ops.fused_linear_cross_entropy import MetalLigerFusedLinearCrossEntropy
+
+    if shift_labels is None:
+        shift_labels = F.pad(labels, (0, 1), value=ignore_index)[..., 1:]
+    shift_labels = shift_labels.reshape(-1).to(hidden.device)
+    loss = MetalLigerFusedLinearCrossEntropy(lm_head, ignore_index=ignore_index,
+                                             chunk_size=chunk_size)(
+        hidden.reshape(-1, hidden.shape[-1]), shift_labels)
+    if num_items_in_batch is not None:
+        n_valid = (shift_labels != ignore_index).sum().to(loss.dtype)
+        if torch.is_tensor(num_items_in_batch):
+            num_items_in_batch = num_items_in_batch.to(loss.device)
+        loss = loss * n_valid / num_items_in_batch
+    return loss
+
+
+def _fused_ce_forward(self, *args, **kwargs):
+    """The causal LM's forward with the loss from the fused linear
+    cross-entropy (training mode with labels); otherwise the original."""
+    orig = self.__dict__["_metal_liger_original_forward"]
+    if args:  # positional arguments by the original forward's parameter names
+        sig = inspect.signature(orig)
+        named = {}
+        for name, val in sig.bind_partial(*args, **kwargs).arguments.items():
+            kind = sig.parameters[name].kind
+            if kind is inspect.Parameter.VAR_POSITIONAL:
+                return orig(*args, **kwargs)
+            if kind is inspect.Parameter.VAR_KEYWORD:
+                named.update(val)
+            else:
+                named[name] = val
+        kwargs = named
+    labels = kwargs.get("labels")
+    shift_labels = kwargs.get("shift_labels")
+    keep = kwargs.get("logits_to_keep", 0)
+    if (not self.training or (labels is None and shift_labels is None)
+            or not (isinstance(keep, int) and keep == 0)):
+        return orig(**kwargs)
+    kwargs = dict(kwargs)
+    kwargs["labels"] = None
+    kwargs.pop("shift_labels", None)
+    capture = _HiddenCapture()
+    object.__setattr__(self, "lm_head", capture)  # shadows _modules["lm_head"]
+    try:
+        out = orig(**kwargs)
+    finally:
+        self.__dict__.pop("lm_head", None)
+    if capture.hidden is None:
+        raise RuntimeError("fuse_cross_entropy: the model's forward did not call its lm_head")
+    loss = causal_lm_loss(capture.hidden, self.lm_head, labels, shift_labels,
+                          kwargs.get("num_items_in_batch"))
+    if isinstance(out, tuple):
+        return (loss,) + tuple(out[1:])
+    fields = {k: v for k, v in out.items() if k not in ("loss", "logits")}
+    return type(out)(loss=loss, **fields)
+
+
+def _patch_cross_entropy(model: nn.Module) -> int:
+    lm = _find_causal_lm(model)
+    if lm is None:
+        return 0
+    if "_metal_liger_original_forward" not in lm.__dict__:
+        lm.__dict__["_metal_liger_original_forward"] = lm.forward
+        lm.forward = types.MethodType(_fused_ce_forward, lm)
+    return 1
+
+
+def restore_cross_entropy(model: nn.Module) -> int:
+    """Undo ``fuse_cross_entropy``: the causal LM's original forward again."""
+    lm = _find_causal_lm(model)
+    if lm is None or "_metal_liger_original_forward" not in lm.__dict__:
+        return 0
+    lm.__dict__.pop("forward", None)
+    lm.__dict__.pop("_metal_liger_original_forward")
+    return 1
+
+
 def apply_metal_liger_to_qwen3vl(
     model: nn.Module,
     fuse_rms_norm: bool = True,
@@ -230,8 +357,13 @@ def apply_metal_liger_to_qwen3vl(
                     "apply_fused_rotary_from_positions()")
         stats["rope"] = "available"
     if fuse_cross_entropy:
-        logger.info("MetalLiger: fused CE — use MetalLigerFusedLinearCrossEntropy in the trainer")
-        stats["cross_entropy"] = "available"
+        stats["cross_entropy"] = _patch_cross_entropy(model)
+        if stats["cross_entropy"]:
+            logger.info("MetalLiger: causal-LM loss routed through the fused linear "
+                        "cross-entropy (training mode with labels)")
+        else:
+            logger.warning("MetalLiger: no lm_head with a labels-taking forward found; use "
+                           "MetalLigerFusedLinearCrossEntropy in the trainer")
     total = sum(v for v in stats.values() if isinstance(v, int))
     logger.info("MetalLiger: %d total layers patched. Details: %s", total, stats)
     return model

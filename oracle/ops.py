@@ -129,8 +129,8 @@ def flce_forward(hidden, weight, labels, bias=None, ignore_index=-100, chunk_siz
     h = _up(hidden, dtype)
     w = _up(weight, dtype)
     n, v = h.shape[0], w.shape[0]
-    run_max = torch.full((n,), float("-inf"), dtype=dtype)
-    run_sum = torch.zeros(n, dtype=dtype)
+    run_max = torch.full((n,), float("-inf"), dtype=dtype, device=h.device)
+    run_sum = torch.zeros(n, dtype=dtype, device=h.device)
     for start in range(0, v, chunk_size):
         end = min(start + chunk_size, v)
         logits = h @ w[start:end].t()
@@ -165,6 +165,7 @@ def flce_backward(hidden, weight, labels, lse, mask, grad_output=1.0, bias=None,
     n, v = h.shape[0], w.shape[0]
     num_valid = torch.clamp(mask.to(dtype).sum(), min=1.0)
     go = grad_output if torch.is_tensor(grad_output) else torch.tensor(grad_output)
+    go = go.to(h.device)
     scale = go.to(dtype) / num_valid
     fmask = mask.to(dtype)[:, None]
     dx = torch.zeros_like(h)
@@ -175,7 +176,7 @@ def flce_backward(hidden, weight, labels, lse, mask, grad_output=1.0, bias=None,
         if bias is not None:
             logits = logits + _up(bias[start:end], dtype)
         p = torch.exp(logits - lse.to(dtype)[:, None])
-        cls = torch.arange(start, end, dtype=labels.dtype)[None, :]
+        cls = torch.arange(start, end, dtype=labels.dtype, device=labels.device)[None, :]
         p = torch.where(labels[:, None] == cls, p - 1.0, p)
         p = p * fmask * scale
         dx += p @ w[start:end]

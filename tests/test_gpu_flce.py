@@ -116,29 +116,15 @@ def test_ignore_bookkeeping_exact():
     assert abs(loss.item() - rl.item()) <= 1e-4 * abs(rl.item())
 
 
-def _gpu_reference(hid, w, lab, chunk=4096):
-    """fp32 torch reference on the GPU (chunked over tokens), same math as the oracle."""
+def _gpu_reference(hid, w, lab):
+    """The pinned oracle (oracle.ops.flce_forward / flce_backward, the
+    reference's vocab-chunked algorithm in fp32) evaluated on the GPU's
+    tensors, TF32 off.  Returns (loss, dX, dW) in fp32."""
+    torch.backends.cuda.matmul.allow_tf32 = False
     hf, wf = hid.float(), w.float()
-    n = hf.shape[0]
-    mask = lab != -100
-    nvalid = mask.sum().clamp(min=1).float()
-    loss = torch.zeros((), device=DEV)
-    dx = torch.zeros_like(hf)
-    dw = torch.zeros_like(wf)
-    for r0 in range(0, n, chunk):
-        logits = hf[r0:r0 + chunk] @ wf.t()
-        lse = torch.logsumexp(logits, dim=-1)
-        m = mask[r0:r0 + chunk]
-        safe = torch.where(m, lab[r0:r0 + chunk], 0)
-        tgt = logits.gather(1, safe[:, None]).squeeze(1)
-        loss += ((lse - tgt) * m).sum()
-        p = torch.exp(logits - lse[:, None])
-        p[torch.arange(p.shape[0], device=DEV), safe] -= 1.0
-        p *= (m.float() / nvalid)[:, None]
-        dx[r0:r0 + chunk] = p @ wf
-        dw += p.t() @ hf[r0:r0 + chunk]
-        del logits, p
-    return loss / nvalid, dx, dw
+    loss, lse, mask = O.flce_forward(hf, wf, lab, None, -100, 8192)
+    dx, dw = O.flce_backward(hf, wf, lab, lse, mask, 1.0, None, 8192)
+    return loss, dx, dw
 
 
 def test_baseline_config_c3_full_size():
@@ -158,6 +144,10 @@ def test_baseline_config_c3_full_size():
         diff = (got.float() - ref).abs()
         bad = diff > 1e-2 + 2e-2 * ref.abs()
         assert not bad.any(), f"{what}: {int(bad.sum())} elements out of tolerance"
+        # the gradients carry 1/n_valid, so also hold the absolute term to
+        # 1e-2 of the tensor's largest magnitude rather than 1e-2 outright
+        bad = diff > 1e-2 * ref.abs().max() + 2e-2 * ref.abs()
+        assert not bad.any(), f"{what}: {int(bad.sum())} elements out of the scaled tolerance"
         rel = (got.float() - ref).norm() / ref.norm()
         assert rel.item() < 2e-2, f"{what}: relative Frobenius error {rel.item():.3e}"
     # size-independent property: each valid row of P sums to zero, so the

@@ -563,3 +563,40 @@ def test_decode_qk_attention_rejects_long_caches():
     pos = torch.zeros(1, dtype=torch.int64, device=DEV)
     with pytest.raises(RuntimeError, match="at most 256"):
         ops.decode_qk_attention(x, kv, kv, w, w, 1e-6, 1e-6, cs, cs, kc, kc.clone(), pos, 0.125)
+
+
+@pytest.mark.parametrize("p", [40, 41, -1])
+def test_decode_prep_outside_the_cache_writes_q_only(p):
+    """A device position outside [0, L): both forms still prepare q (norm +
+    RoPE) and leave both caches untouched, and the one-launch attention stays
+    bit for bit the prep kernel followed by the attention."""
+    from metal_liger_b200.ops.fused_rope import apply_fused_rotary
+
+    B, Hq, Hkv, D, L = 2, 8, 2, 64, 40
+    g = torch.Generator(device=DEV).manual_seed(71 + p)
+    q = torch.randn(B, 1, Hq * D, generator=g, device=DEV).bfloat16()
+    k = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    v = torch.randn(B, 1, Hkv * D, generator=g, device=DEV).bfloat16()
+    wq = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    wk = (1 + 0.1 * torch.randn(D, generator=g, device=DEV)).bfloat16()
+    ang = torch.rand(B, 1, D // 2, generator=g, device=DEV) * 6.0
+    cos = torch.cat([ang.cos(), ang.cos()], -1).bfloat16()
+    sin = torch.cat([ang.sin(), ang.sin()], -1).bfloat16()
+    kc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    vc = torch.randn(B, Hkv, L, D, generator=g, device=DEV).bfloat16()
+    kc0, vc0 = kc.clone(), vc.clone()
+    kc2, vc2 = kc.clone(), vc.clone()
+    pos = torch.tensor([p], dtype=torch.int64, device=DEV)
+    ops = torch.ops.metal_liger
+    q4 = ops.decode_qk_norm_rope(q, k, v, wq, wk, 1e-6, 1e-5, cos, sin, kc2, vc2, pos)
+    assert torch.equal(kc2, kc0) and torch.equal(vc2, vc0)
+    qn = ops.rms_norm_forward(q.view(B, 1, Hq, D), wq, 1e-6, "")[0].transpose(1, 2)
+    kn = ops.rms_norm_forward(k.view(B, 1, Hkv, D), wk, 1e-5, "")[0].transpose(1, 2)
+    qr, _ = apply_fused_rotary(qn, kn, cos.unsqueeze(1), sin.unsqueeze(1))
+    ulp = 2.0 ** -7
+    assert torch.allclose(q4.float(), qr.float(), rtol=ulp, atol=ulp)
+    if p >= 0:  # the attention reads min(p + 1, L) positions
+        fused = ops.decode_qk_attention(q, k, v, wq, wk, 1e-6, 1e-5, cos, sin, kc, vc, pos,
+                                        D ** -0.5)
+        assert torch.equal(kc, kc0) and torch.equal(vc, vc0)
+        assert torch.equal(fused, ops.decode_attention(q4, kc2, vc2, pos, 1, D ** -0.5))
