@@ -381,6 +381,20 @@ ML_API int ml_lora_linear_backward(const void* x, const void* u, int64_t tokens,
                                    void* const* da, void* const* db, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/*
+ * Process-wide choice for the MLP entry points below: 1 (default) applies the
+ * SwiGLU inside the GEMMs — the forward's gate and up projections run as one
+ * GEMM whose epilogue also writes h = silu(gate) * up, and the backward's dH
+ * GEMM writes d_gate / d_up directly (dH is never stored); 0 runs the
+ * projections and the SwiGLU as separate passes.  Results are bitwise the
+ * same; the backward workspace is smaller with 1 (no dH buffer), so query
+ * ml_lora_mlp_workspace_bytes after setting it.  The previous setting is
+ * stored to *previous when non-NULL.  A tuning and test knob with no
+ * reference counterpart (the reference computes the SwiGLU between its
+ * matmuls, ops/fused_lora.py:195-197, :235-244).
+ */
+ML_API int ml_lora_set_mlp_swiglu_fusion(int enable, int* previous);
+
 /* Workspace bytes for the MLP entry points (backward = 0 or 1). */
 ML_API size_t ml_lora_mlp_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
                                           int backward);

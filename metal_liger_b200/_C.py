@@ -87,6 +87,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemm_bf16": (c_int, [c_int64, c_int64, ctypes.POINTER(GemmSegment), c_int, c_void_p, c_int,
                              c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "ml_gemm_set_cta_pair": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "ml_lora_set_mlp_swiglu_fusion": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_selftest_bounded_wait": (c_int, [c_int64, c_void_p]),
     "ml_lm_head_argmax_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ml_gemv_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,
@@ -253,6 +254,18 @@ def gemm_cta_pair(mode: int):
         yield
     finally:
         call("ml_gemm_set_cta_pair", prev.value, None)
+
+
+@contextlib.contextmanager
+def lora_mlp_swiglu_fusion(enable: bool):
+    """Run the LoRA MLP with the SwiGLU inside its GEMMs (True, the default)
+    or as separate elementwise passes (False) for the duration of a block."""
+    prev = ctypes.c_int(1)
+    call("ml_lora_set_mlp_swiglu_fusion", 1 if enable else 0, ctypes.byref(prev))
+    try:
+        yield
+    finally:
+        call("ml_lora_set_mlp_swiglu_fusion", prev.value, None)
 
 
 def exported_symbols() -> list[str]:

@@ -155,6 +155,26 @@ __device__ __forceinline__ void st_vec_stream(T* p, const Vec16<T>& v) {
   __stcs(reinterpret_cast<int4*>(p), *reinterpret_cast<const int4*>(&v));
 }
 
+// SwiGLU arithmetic (reference ops/fused_swiglu.py:26-50, fp32), shared by
+// the elementwise kernels (swiglu.cu) and the GEMM epilogues that apply it to
+// a fresh accumulator tile (gemm.cuh), so both round identically.
+// sigmoid(g) = 1 / (1 + e^-g) with the SFU exponential and reciprocal (2 ulp
+// each); the quotient tends to exactly 0 for large negative g.
+__device__ __forceinline__ float swiglu_sigmoid(float g) {
+  return __fdividef(1.f, 1.f + __expf(-g));
+}
+// h = silu(g) * u
+__device__ __forceinline__ float swiglu_fwd(float g, float u) {
+  const float s = swiglu_sigmoid(g);
+  return (g * s) * u;
+}
+// d_gate = d u s (1 + g (1 - s)),  d_up = d silu(g)
+__device__ __forceinline__ void swiglu_bwd(float g, float u, float d, float& dg, float& du) {
+  const float s = swiglu_sigmoid(g);
+  du = d * (g * s);
+  dg = d * u * s * (1.f + g * (1.f - s));
+}
+
 // Runs a setup step (a kernel attribute, an occupancy query) once per CUDA
 // device — the current one — and returns its cached result: kernel
 // attributes belong to the device context they were set in.

@@ -4,6 +4,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <initializer_list>
 #include <mutex>
 
 namespace ml {
@@ -220,6 +221,17 @@ int launch(const Problem& pr, cudaStream_t st) {
     set_error("gemm: the FLCE epilogue needs 256-wide tiles");
     return ML_ERR_INVALID_ARG;
   }
+  if ((pr.b_split || pr.epi == EPI_SWIGLU) &&
+      (!pr.b_split || pr.epi != EPI_SWIGLU || bn != 256 || pr.b_mn)) {
+    set_error("gemm: the SwiGLU epilogue takes split K-major B operands on 256-wide tiles");
+    return ML_ERR_INVALID_ARG;
+  }
+  if ((pr.epi == EPI_SWIGLU && (pr.D == nullptr || pr.D2 == nullptr || pr.D3 == nullptr)) ||
+      (pr.epi == EPI_DSWIGLU && (pr.D == nullptr || pr.D2 == nullptr || pr.aux1 == nullptr ||
+                                 pr.aux2 == nullptr))) {
+    set_error("gemm: SwiGLU epilogue with a null output or input");
+    return ML_ERR_INVALID_ARG;
+  }
   Params prm;
   memset(&prm, 0, sizeof(prm));
   int kb_total = 0;
@@ -236,12 +248,19 @@ int launch(const Problem& pr, cudaStream_t st) {
     else
       rc = make_map(&prm.tma_a[s], g.a.ptr, pr.M, g.K, g.a.ld, BK, "gemm A (M-major)");
     if (rc) return rc;
-    // B: logical [N, K]; each CTA of a pair loads 128 of the tile's 256 rows
-    if (!pr.b_mn)
+    // B: logical [N, K]; each CTA of a pair loads 128 of the tile's 256 rows.
+    // Split B: two [N, K] matrices, half a tile's rows from each.
+    if (pr.b_split) {
+      rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, bn / 2, "gemm B (split, first)");
+      if (rc) return rc;
+      rc = make_map(&prm.tma_b2[s], g.b2.ptr, g.K, pr.N, g.b2.ld, bn / 2,
+                    "gemm B (split, second)");
+    } else if (!pr.b_mn) {
       rc = make_map(&prm.tma_b[s], g.b.ptr, g.K, pr.N, g.b.ld, pair ? bn / 2 : bn,
                     "gemm B (K-major)");
-    else
+    } else {
       rc = make_map(&prm.tma_b[s], g.b.ptr, pr.N, g.K, g.b.ld, BK, "gemm B (N-major)");
+    }
     if (rc) return rc;
     prm.seg_kb[s] = (int)((g.K + BK - 1) / BK);
     kb_total += prm.seg_kb[s];
@@ -250,7 +269,9 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.M = (int)pr.M;
   prm.N = (int)pr.N;
   prm.m_tiles = (int)((pr.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
-  prm.n_tiles = (int)((pr.N + bn - 1) / bn);
+  const int tile_n = pr.b_split ? bn / 2 : bn;  // columns of N per tile
+  prm.n_tiles = (int)((pr.N + tile_n - 1) / tile_n);
+  prm.b_split = pr.b_split ? 1 : 0;
   int splits = std::max(1, std::min(pr.splits, kb_total));
   const int kb_per = (kb_total + splits - 1) / splits;
   splits = (kb_total + kb_per - 1) / kb_per;
@@ -288,8 +309,16 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.ldd = pr.ldd;
   prm.alpha = pr.alpha;
   prm.beta = pr.beta;
-  const int elt = (pr.epi == EPI_STORE && !pr.d_f32) || pr.epi == EPI_FLCE ? 2 : 4;
+  const bool bf16_out = (pr.epi == EPI_STORE && !pr.d_f32) || pr.epi == EPI_FLCE ||
+                        pr.epi == EPI_SWIGLU || pr.epi == EPI_DSWIGLU;
+  const int elt = bf16_out ? 2 : 4;
   prm.vec_ok = aligned16(pr.D) && ((pr.ldd * elt) % 16 == 0);
+  for (const void* q : std::initializer_list<const void*>{pr.D2, pr.D3, pr.aux1, pr.aux2})
+    if (q != nullptr && !aligned16(q)) prm.vec_ok = 0;
+  prm.D2 = pr.D2;
+  prm.D3 = pr.D3;
+  prm.aux1 = pr.aux1;
+  prm.aux2 = pr.aux2;
   prm.labels = pr.labels;
   prm.label_base = pr.label_base;
   prm.ignore_index = pr.ignore_index;

@@ -40,6 +40,9 @@ enum Epi : int {
   EPI_FLCE = 2,         // fused linear-cross-entropy logits epilogue (BN = 256)
   EPI_ARGMAX = 3,       // greedy decoding head: per tile, the row's largest logit (rounded
                         // to the logit dtype) and the first column holding it
+  EPI_SWIGLU = 4,       // split-B gate|up tile (BN = 256): gate, up and h = silu(gate) * up
+                        // stored (bf16) from one accumulator
+  EPI_DSWIGLU = 5,      // dH tile: d_gate, d_up of SwiGLU from dH and the stored gate / up
 };
 
 // Wait sites recorded in the device error word.
@@ -49,6 +52,11 @@ enum Site : int { SITE_PROD_EMPTY = 1, SITE_MMA_TEMPTY = 2, SITE_MMA_FULL = 3, S
 struct alignas(64) Params {
   CUtensorMap tma_a[kMaxSeg];
   CUtensorMap tma_b[kMaxSeg];
+  // b_split: the B tile's columns [0, BN/2) come from tma_b and [BN/2, BN)
+  // from tma_b2, both at rows [nt BN/2, nt BN/2 + BN/2) of their matrices
+  // (K-major B only) — two weights whose matching rows share one tile.
+  CUtensorMap tma_b2[kMaxSeg];
+  int b_split;
   int seg_kb[kMaxSeg];     // k-blocks (of BK) per segment
   int nseg;
   int M, N;
@@ -76,6 +84,12 @@ struct alignas(64) Params {
   // EPI_ARGMAX (also uses part_m, vocab, bias)
   int* part_i;             // [n_tiles][M] first column of the tile's row maximum
   int logit_dtype;         // ML_DTYPE_* the logits are rounded to before comparing
+  // EPI_SWIGLU: D = gate, D2 = up, D3 = h.  EPI_DSWIGLU: D = d_gate, D2 = d_up,
+  // aux1 = gate, aux2 = up (inputs).  All bf16 [M, N] at pitch ldd.
+  void* D2;
+  void* D3;
+  const void* aux1;
+  const void* aux2;
   int* err;                // device error word (bounded-wait timeouts)
 };
 
@@ -214,6 +228,139 @@ __device__ __forceinline__ bool argmax_better(float a, int ca, float b, int cb) 
   return ca < cb;
 }
 
+// 8 bf16 from 8 floats (round to nearest even), as one 16-byte word.
+__device__ __forceinline__ uint4 pack8_bf16(const float* v) {
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  return o;
+}
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void unpack8_bf16(const uint4& w, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 f = __bfloat1622float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+// EPI_SWIGLU, one 256-wide split-B tile: accumulator columns [0, 128) are
+// gate and [128, 256) up for intermediate columns [128 nt, 128 nt + 128).
+// gate and up are rounded to bf16 as the unfused projections store them, and
+// h is computed from those stored values exactly as the SwiGLU kernel does.
+__device__ __forceinline__ void swiglu_tile(const Params& p, uint32_t taddr, int64_t row,
+                                            bool row_ok, int nt) {
+  constexpr int HALF = 128;
+  const int col_base = nt * HALF;
+  __nv_bfloat16* dg = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
+  __nv_bfloat16* du = static_cast<__nv_bfloat16*>(p.D2) + row * p.ldd;
+  __nv_bfloat16* dh = static_cast<__nv_bfloat16*>(p.D3) + row * p.ldd;
+#pragma unroll 1
+  for (int c = 0; c < HALF / 32; ++c) {
+    float g[32], u[32];
+    sm100::tmem_ld_32x32b_x32(taddr + c * 32, g);
+    sm100::tmem_ld_32x32b_x32(taddr + HALF + c * 32, u);
+    const int col0 = col_base + c * 32;
+    if (!row_ok || col0 >= p.N) continue;
+    float h[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      g[j] = bf16r(g[j] * p.alpha);
+      u[j] = bf16r(u[j] * p.alpha);
+      h[j] = swiglu_fwd(g[j], u[j]);
+    }
+    if (p.vec_ok && col0 + 32 <= p.N) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        *reinterpret_cast<uint4*>(dg + col0 + j) = pack8_bf16(g + j);
+        *reinterpret_cast<uint4*>(du + col0 + j) = pack8_bf16(u + j);
+        *reinterpret_cast<uint4*>(dh + col0 + j) = pack8_bf16(h + j);
+      }
+    } else {
+      for (int j = 0; j < 32 && col0 + j < p.N; ++j) {
+        dg[col0 + j] = __float2bfloat16_rn(g[j]);
+        du[col0 + j] = __float2bfloat16_rn(u[j]);
+        dh[col0 + j] = __float2bfloat16_rn(h[j]);
+      }
+    }
+  }
+}
+
+// EPI_DSWIGLU: the accumulator is dH; dH is rounded to bf16 (as the unfused
+// path stores it) and the SwiGLU backward is applied with the stored gate /
+// up, written as d_gate (D) and d_up (D2): dH never reaches memory.  The
+// gate / up words of the next 32 columns are loaded before the current ones
+// are used, so one chunk of loads is always in flight behind the math.
+template <int BN>
+__device__ __forceinline__ void dswiglu_tile(const Params& p, uint32_t taddr, int64_t row,
+                                             bool row_ok, int nt) {
+  const int col_base = nt * BN;
+  const __nv_bfloat16* gin = static_cast<const __nv_bfloat16*>(p.aux1) + row * p.ldd;
+  const __nv_bfloat16* uin = static_cast<const __nv_bfloat16*>(p.aux2) + row * p.ldd;
+  __nv_bfloat16* dgo = static_cast<__nv_bfloat16*>(p.D) + row * p.ldd;
+  __nv_bfloat16* duo = static_cast<__nv_bfloat16*>(p.D2) + row * p.ldd;
+  auto full_chunk = [&](int c) { return row_ok && p.vec_ok && col_base + c * 32 + 32 <= p.N; };
+  uint4 gw[4], uw[4];
+  if (full_chunk(0)) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      gw[q] = *reinterpret_cast<const uint4*>(gin + col_base + q * 8);
+      uw[q] = *reinterpret_cast<const uint4*>(uin + col_base + q * 8);
+    }
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float v[32];
+    sm100::tmem_ld_32x32b_x32(taddr + c * 32, v);
+    const int col0 = col_base + c * 32;
+    uint4 gn[4], un[4];
+    const bool next = c + 1 < BN / 32 && full_chunk(c + 1);
+    if (next) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        gn[q] = *reinterpret_cast<const uint4*>(gin + col0 + 32 + q * 8);
+        un[q] = *reinterpret_cast<const uint4*>(uin + col0 + 32 + q * 8);
+      }
+    }
+    if (full_chunk(c)) {
+      float g[32], u[32], dg[32], du[32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        unpack8_bf16(gw[q], g + 8 * q);
+        unpack8_bf16(uw[q], u + 8 * q);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) swiglu_bwd(g[j], u[j], bf16r(v[j] * p.alpha), dg[j], du[j]);
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        *reinterpret_cast<uint4*>(dgo + col0 + j) = pack8_bf16(dg + j);
+        *reinterpret_cast<uint4*>(duo + col0 + j) = pack8_bf16(du + j);
+      }
+    } else if (row_ok) {
+      for (int j = 0; j < 32 && col0 + j < p.N; ++j) {
+        float dg, du;
+        swiglu_bwd(__bfloat162float(gin[col0 + j]), __bfloat162float(uin[col0 + j]),
+                   bf16r(v[j] * p.alpha), dg, du);
+        dgo[col0 + j] = __float2bfloat16_rn(dg);
+        duo[col0 + j] = __float2bfloat16_rn(du);
+      }
+    }
+    if (next) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        gw[q] = gn[q];
+        uw[q] = un[q];
+      }
+    }
+  }
+}
+
 // Drains one accumulator tile (this thread's TMEM lane = output row `row`,
 // BN fp32 columns starting at `taddr`) through the selected epilogue.
 template <int BN>
@@ -305,6 +452,10 @@ __device__ __forceinline__ void epilogue_tile(const Params& p, uint32_t taddr, i
       p.part_m[(int64_t)nt * p.M + row] = best;
       p.part_i[(int64_t)nt * p.M + row] = best_col;
     }
+  } else if (p.epi == EPI_SWIGLU) {
+    if constexpr (BN == 256) swiglu_tile(p, taddr, row, row_ok, nt);
+  } else if (p.epi == EPI_DSWIGLU) {
+    dswiglu_tile<BN>(p, taddr, row, row_ok, nt);
   } else {
     float* partial_base = nullptr;
     if (p.epi == EPI_PARTIAL) partial_base = static_cast<float*>(p.D) + (int64_t)sp * p.split_stride;
@@ -402,7 +553,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             sm100::tma_load_2d(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, mt * BM + 64, kx);
           }
           if constexpr (!B_MN) {
-            sm100::tma_load_2d(b_dst, &p.tma_b[seg], bar, kx, nt * BN);
+            if (p.b_split) {
+              sm100::tma_load_2d(b_dst, &p.tma_b[seg], bar, kx, nt * (BN / 2));
+              sm100::tma_load_2d(b_dst + (BN / 2) * BK * 2, &p.tma_b2[seg], bar, kx,
+                                 nt * (BN / 2));
+            } else {
+              sm100::tma_load_2d(b_dst, &p.tma_b[seg], bar, kx, nt * BN);
+            }
           } else {
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
@@ -628,7 +785,11 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
             sm100::tma_load_2d_pair(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, m0 + 64, kx);
           }
           if constexpr (!B_MN) {
-            sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, kx, n0);
+            if (p.b_split)  // this CTA's half of the tile: the first or the second matrix
+              sm100::tma_load_2d_pair(b_dst, rank ? &p.tma_b2[seg] : &p.tma_b[seg], bar, kx,
+                                      nt * BH);
+            else
+              sm100::tma_load_2d_pair(b_dst, &p.tma_b[seg], bar, kx, n0);
           } else {
 #pragma unroll
             for (int c = 0; c < BH / 64; ++c)
@@ -751,6 +912,7 @@ struct Mat {
 //   b_mn = false: B stored as [N, K];                true: stored as [K, N].
 struct Seg {
   Mat a, b;
+  Mat b2;  // Problem::b_split: the matrix of the second half of every B tile
   int64_t K = 0;
 };
 
@@ -783,6 +945,14 @@ struct Problem {
   // EPI_ARGMAX
   int* part_i = nullptr;
   int logit_dtype = 0;
+  // b_split (K-major B, 256-wide tiles): N is the width of each of the two
+  // B matrices; tile n holds their rows [128 n, 128 n + 128) side by side
+  bool b_split = false;
+  // EPI_SWIGLU / EPI_DSWIGLU outputs and inputs (see Params)
+  void* D2 = nullptr;
+  void* D3 = nullptr;
+  const void* aux1 = nullptr;
+  const void* aux2 = nullptr;
 };
 
 // Builds tensor maps, picks the tile width and launches.  Returns ML_OK or an

@@ -19,6 +19,7 @@
 #include "gemm.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <initializer_list>
 #include <vector>
 
@@ -33,6 +34,10 @@ namespace {
 
 constexpr int kSlot = 64;  // padded rank width shared by the adapters of one call
 using bf16 = __nv_bfloat16;
+
+// SwiGLU inside the MLP's GEMMs (1, the default) or as separate elementwise
+// passes (0): process-wide, read once per call (ml_lora_set_mlp_swiglu_fusion).
+std::atomic<int> g_mlp_swiglu_fused{1};
 
 inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
@@ -455,10 +460,23 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
 }
 
 // ------------------------------- MLP --------------------------------------
+// With the SwiGLU fused into the GEMMs (the default):
+//  * forward: ONE GEMM produces gate, up and h.  Its 256-wide tiles take B
+//    rows [128 n, 128 n + 128) of [Wg | s_g Bg] for the first half and of
+//    [Wu | s_u Bu] for the second (two tensor maps, no weight copy), so the
+//    accumulator holds gate and up of the same 128 intermediate columns and
+//    the epilogue writes gate, up (saved for the backward) and
+//    h = silu(gate) * up from the bf16-rounded values — the separate SwiGLU
+//    pass, which re-read gate and up, is gone;
+//  * backward: the dH GEMM's epilogue applies the SwiGLU backward with the
+//    saved gate / up and writes d_gate / d_up — dH never reaches memory.
+// Both round exactly where the unfused path stores bf16 tensors, so their
+// outputs are bitwise those of the unfused kernels.
 // pj[0] = gate (I x H), pj[1] = up (I x H), pj[2] = down (H x I).
 int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
                 const ml_lora_proj* pj, bf16* gate, bf16* up, bf16* h, bf16* out, bf16* u1,
                 bf16* u2, Arena& ar, cudaStream_t st) {
+  const bool fused = g_mlp_swiglu_fused.load(std::memory_order_relaxed) != 0;
   bf16* acat = ar.take<bf16>((size_t)kSlot * H);   // rows [0,r) = Ag, [r,2r) = Au
   bf16* bgp = ar.take<bf16>((size_t)I * kSlot);     // cols [0,r) = s_g Bg
   bf16* bup = ar.take<bf16>((size_t)I * kSlot);     // cols [r,2r) = s_u Bu
@@ -478,13 +496,33 @@ int mlp_forward(const bf16* x, int64_t T, int64_t H, int64_t I, int64_t r,
   LORA_TRY(as.launch(st));
   // U1 = X [Ag; Au]^T
   LORA_TRY(rank_proj(T, {seg(x, H, acat, H, H)}, u1, rpart, rpf, st));
-  // gate / up = [X | U1] [W | s B]^T
-  LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[0].w, H, H), seg(u1, kSlot, bgp, kSlot, kSlot)}, false,
-                     false, gate, I, st));
-  LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[1].w, H, H), seg(u1, kSlot, bup, kSlot, kSlot)}, false,
-                     false, up, I, st));
-  // h = silu(gate) * up (fp32 math)
-  LORA_TRY(ml_swiglu_forward(gate, up, h, T * I, ML_DTYPE_BF16, st));
+  if (fused) {
+    // gate | up = [X | U1] [W | s B]^T of both projections, h in the epilogue
+    gemm::Problem p;
+    p.M = T;
+    p.N = I;
+    p.nseg = 2;
+    p.seg[0] = seg(x, H, pj[0].w, H, H);
+    p.seg[0].b2 = {pj[1].w, I, H, H};
+    p.seg[1] = seg(u1, kSlot, bgp, kSlot, kSlot);
+    p.seg[1].b2 = {bup, I, kSlot, kSlot};
+    p.b_split = true;
+    p.bn = 256;
+    p.epi = gemm::EPI_SWIGLU;
+    p.D = gate;
+    p.D2 = up;
+    p.D3 = h;
+    p.ldd = I;
+    LORA_TRY(gemm::launch(p, st));
+  } else {
+    // gate / up = [X | U1] [W | s B]^T
+    LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[0].w, H, H), seg(u1, kSlot, bgp, kSlot, kSlot)},
+                       false, false, gate, I, st));
+    LORA_TRY(gemm_bf16(T, I, {seg(x, H, pj[1].w, H, H), seg(u1, kSlot, bup, kSlot, kSlot)},
+                       false, false, up, I, st));
+    // h = silu(gate) * up (fp32 math)
+    LORA_TRY(ml_swiglu_forward(gate, up, h, T * I, ML_DTYPE_BF16, st));
+  }
   // U2 = h Ad^T ; out = [h | U2] [Wd | s Bd]^T
   LORA_TRY(rank_proj(T, {seg(h, I, ad, I, I)}, u2, rpart, rpf, st));
   LORA_TRY(gemm_bf16(T, H, {seg(h, I, pj[2].w, I, I), seg(u2, kSlot, bdp, kSlot, kSlot)}, false,
@@ -496,6 +534,7 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                  const bf16* u2, int64_t T, int64_t H, int64_t I, int64_t r,
                  const ml_lora_proj* pj, const bf16* dy, bf16* dx, void* const* da,
                  void* const* db, Arena& ar, cudaStream_t st) {
+  const bool fused = g_mlp_swiglu_fused.load(std::memory_order_relaxed) != 0;
   bf16* bdT = ar.take<bf16>((size_t)kSlot * H);     // rows [0,r) = Bd^T
   bf16* ads = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = s_d Ad
   bf16* bgT = ar.take<bf16>((size_t)kSlot * I);     // rows [0,r) = Bg^T
@@ -503,7 +542,7 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   bf16* acs = ar.take<bf16>((size_t)kSlot * H);     // rows [0,r) = s_g Ag, [r,2r) = s_u Au
   bf16* Gd = ar.take<bf16>((size_t)T * kSlot);
   bf16* Ggu = ar.take<bf16>((size_t)T * kSlot);
-  bf16* dH = ar.take<bf16>((size_t)T * I);
+  bf16* dH = fused ? nullptr : ar.take<bf16>((size_t)T * I);
   bf16* dgate = ar.take<bf16>((size_t)T * I);
   bf16* dup = ar.take<bf16>((size_t)T * I);
   float* dAT_d = ar.take<float>((size_t)I * kSlot);   // h^T G_d
@@ -526,13 +565,31 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   LORA_TRY(as.launch(st));
   // G_d = dY Bd ; dH = dY Wd + G_d (s_d Ad)      (Wd stored [H, I]: N-major)
   LORA_TRY(rank_proj(T, {seg(dy, H, bdT, H, H)}, Gd, part, pf, st));
-  LORA_TRY(gemm_bf16(T, I, {seg(dy, H, pj[2].w, I, H), seg(Gd, kSlot, ads, I, kSlot)}, false,
-                     true, dH, I, st));
+  if (fused) {
+    // d_gate, d_up from the dH accumulator and the saved gate / up
+    gemm::Problem p;
+    p.M = T;
+    p.N = I;
+    p.nseg = 2;
+    p.seg[0] = seg(dy, H, pj[2].w, I, H);
+    p.seg[1] = seg(Gd, kSlot, ads, I, kSlot);
+    p.b_mn = true;
+    p.epi = gemm::EPI_DSWIGLU;
+    p.D = dgate;
+    p.D2 = dup;
+    p.aux1 = gate;
+    p.aux2 = up;
+    p.ldd = I;
+    LORA_TRY(gemm::launch(p, st));
+  } else {
+    LORA_TRY(gemm_bf16(T, I, {seg(dy, H, pj[2].w, I, H), seg(Gd, kSlot, ads, I, kSlot)}, false,
+                       true, dH, I, st));
+  }
   // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
   LORA_TRY(gemm_skinny_f32(I, seg(h, I, Gd, kSlot, T), dAT_d, part, pf * 4, st));
   LORA_TRY(gemm_skinny_f32(H, seg(dy, H, u2, kSlot, T), dBt_d, part, pf * 4, st));
-  // SwiGLU backward (sigmoid recomputed)
-  LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
+  // SwiGLU backward (sigmoid recomputed), unless the dH GEMM applied it
+  if (!fused) LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
   // G_gu = [d_gate Bg | d_up Bu]
   LORA_TRY(rank_proj(T, {seg(dgate, I, bgT, I, I), seg(dup, I, buT, I, I)}, Ggu, part, pf, st));
   // dX = d_gate Wg + d_up Wu + G_gu (s A)        (Wg/Wu stored [I, H]: N-major)
@@ -689,6 +746,13 @@ extern "C" int ml_lora_qkv_backward(const void* x, const void* u, int64_t tokens
   ML_CHECK_ARG(proj[0].out_features == inter && proj[1].out_features == inter &&               \
                    proj[2].out_features == hidden,                                             \
                what ": projection shapes do not match hidden/intermediate");
+
+extern "C" int ml_lora_set_mlp_swiglu_fusion(int enable, int* previous) {
+  ML_CHECK_ARG(enable == 0 || enable == 1, "lora_set_mlp_swiglu_fusion: enable must be 0 or 1");
+  const int old = lora::g_mlp_swiglu_fused.exchange(enable);
+  if (previous) *previous = old;
+  return ML_OK;
+}
 
 extern "C" size_t ml_lora_mlp_workspace_bytes(int64_t tokens, int64_t hidden, int64_t inter,
                                               int backward) {

@@ -17,10 +17,6 @@
 namespace ml {
 namespace {
 
-// 1 / (1 + e^-g) with the SFU exponential and reciprocal (2 ulp each); the
-// quotient tends to exactly 0 for large negative g.
-__device__ __forceinline__ float sigmoidf_(float g) { return __fdividef(1.f, 1.f + __expf(-g)); }
-
 template <typename T, int UNROLL>
 __global__ void __launch_bounds__(256)
 swiglu_fwd_kernel(const T* __restrict__ gate, const T* __restrict__ up, T* __restrict__ out,
@@ -49,9 +45,7 @@ swiglu_fwd_kernel(const T* __restrict__ gate, const T* __restrict__ up, T* __res
           Vec16<T> o;
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
-            const float gf = to_f32(g[k].v[j]);
-            const float s = sigmoidf_(gf);
-            o.v[j] = from_f32<T>((gf * s) * to_f32(u[k].v[j]));
+            o.v[j] = from_f32<T>(swiglu_fwd(to_f32(g[k].v[j]), to_f32(u[k].v[j])));
           }
           st_vec_stream(out + v * VEC, o);
         }
@@ -60,9 +54,7 @@ swiglu_fwd_kernel(const T* __restrict__ gate, const T* __restrict__ up, T* __res
     done = nvec * VEC;
   }
   for (int64_t i = done + tid; i < n; i += nthreads) {
-    const float gf = to_f32(gate[i]);
-    const float s = sigmoidf_(gf);
-    out[i] = from_f32<T>((gf * s) * to_f32(up[i]));
+    out[i] = from_f32<T>(swiglu_fwd(to_f32(gate[i]), to_f32(up[i])));
   }
 }
 
@@ -95,13 +87,10 @@ swiglu_bwd_kernel(const T* __restrict__ gate, const T* __restrict__ up,
           Vec16<T> og, ou;
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
-            const float gf = to_f32(g[k].v[j]);
-            const float uf = to_f32(u[k].v[j]);
-            const float df = to_f32(d[k].v[j]);
-            const float s = sigmoidf_(gf);
-            const float silu = gf * s;
-            ou.v[j] = from_f32<T>(df * silu);
-            og.v[j] = from_f32<T>(df * uf * s * (1.f + gf * (1.f - s)));
+            float dg, du;
+            swiglu_bwd(to_f32(g[k].v[j]), to_f32(u[k].v[j]), to_f32(d[k].v[j]), dg, du);
+            ou.v[j] = from_f32<T>(du);
+            og.v[j] = from_f32<T>(dg);
           }
           st_vec_stream(dgate + v * VEC, og);
           st_vec_stream(dup + v * VEC, ou);
@@ -111,12 +100,10 @@ swiglu_bwd_kernel(const T* __restrict__ gate, const T* __restrict__ up,
     done = nvec * VEC;
   }
   for (int64_t i = done + tid; i < n; i += nthreads) {
-    const float gf = to_f32(gate[i]);
-    const float uf = to_f32(up[i]);
-    const float df = to_f32(dout[i]);
-    const float s = sigmoidf_(gf);
-    dup[i] = from_f32<T>(df * (gf * s));
-    dgate[i] = from_f32<T>(df * uf * s * (1.f + gf * (1.f - s)));
+    float dg, du;
+    swiglu_bwd(to_f32(gate[i]), to_f32(up[i]), to_f32(dout[i]), dg, du);
+    dup[i] = from_f32<T>(du);
+    dgate[i] = from_f32<T>(dg);
   }
 }
 

@@ -199,7 +199,10 @@ def patch_fused_lora(model: nn.Module, fuse_o_proj: bool = False) -> int:
     on the instance.  ``state_dict`` keys and values are unchanged.  Returns
     the number of patched modules.
     """
-    base = model.base_model.model if hasattr(model, "base_model") else model
+    # A PEFT wrapper's HF model (reference ops/fused_lora.py:344).  A plain HF
+    # PreTrainedModel also has ``base_model`` (its inner backbone, without a
+    # ``.model``): search it from the model itself then.
+    base = getattr(getattr(model, "base_model", None), "model", None) or model
     layers = _find_layers_list(base)
     if layers is None:
         logger.warning("MetalLiger fused LoRA: could not find transformer layers")

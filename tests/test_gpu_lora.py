@@ -352,3 +352,38 @@ def test_c4_adapter_grads_against_pure_fp32():
     for name, (ours, ref) in report.items():
         assert ours["frob"] <= 1.25 * ref["frob"] + 1e-3, (name, ours, ref)
         assert ours["max_over_rms"] <= 1.5 * ref["max_over_rms"] + 1e-2, (name, ours, ref)
+
+
+@pytest.mark.parametrize("T,H,I,r", [(300, 256, 768, 16), (2048, 512, 1000, 16), (64, 128, 256, 8),
+                                     (50, 104, 200, 8)])
+def test_mlp_swiglu_in_gemm_epilogues_is_bitwise_the_unfused_path(T, H, I, r, pair_mode):
+    """The MLP with the SwiGLU inside its GEMMs (the forward's gate|up GEMM
+    writing gate, up and h; the backward's dH GEMM writing d_gate / d_up)
+    against the separate passes: every output of the forward (out, gate, up,
+    h) and the backward (dX, all six adapter gradients) bit for bit, on the
+    1-SM and CTA-pair kernels, intermediate sizes not a multiple of the
+    128-column half tile included."""
+    from metal_liger_b200 import _C
+
+    gen = torch.Generator(device=DEV).manual_seed(T + H + I)
+    x = torch.randn(T, H, generator=gen, device=DEV).bfloat16()
+    g = _proj(gen, I, H, r, 2.0, dev=DEV)
+    u = _proj(gen, I, H, r, 1.5, dev=DEV)
+    d = _proj(gen, H, I, r, 0.5, dev=DEV)
+    dy = torch.randn(T, H, generator=gen, device=DEV).bfloat16()
+    mlp = (*g[:3], *u[:3], *d[:3])
+    sc = [g[3], u[3], d[3]]
+    ops = torch.ops.metal_liger
+    res = {}
+    for fused in (True, False):
+        with _C.lora_mlp_swiglu_fusion(fused):
+            fwd = ops.lora_mlp_forward(x, *mlp, sc)
+            bwd = ops.lora_mlp_backward(x, *fwd[1:], *mlp, sc, dy)
+            torch.cuda.synchronize()
+        res[fused] = (list(fwd[:4]), list(bwd))
+    for what, a_list, b_list in (("forward", res[True][0], res[False][0]),
+                                 ("backward", res[True][1], res[False][1])):
+        assert len(a_list) == len(b_list)
+        for i, (a, b) in enumerate(zip(a_list, b_list)):
+            assert a.shape == b.shape and a.dtype == b.dtype, (what, i)
+            assert torch.equal(a, b), f"{what} output {i}: max |diff| {(a.float() - b.float()).abs().max().item()}"
