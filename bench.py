@@ -157,12 +157,16 @@ class ClockSampler:
 
 
 class KernelTimer:
-    """CUDA-event brackets around named launches on the current stream."""
+    """CUDA-event brackets around named launches on the current stream
+    (`before`, if given, runs on the stream ahead of each bracket)."""
 
-    def __init__(self):
+    def __init__(self, before=None):
         self.marks = []
+        self.before = before
 
     def __call__(self, name, fn, *args):
+        if self.before is not None:
+            self.before()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
@@ -514,7 +518,7 @@ class Flce:
                f"all-reduce of row max / sum-exp / target logit and of partial dX)")
         return {"workload": "flce_bf16 (BASELINE configs[2]): hidden [16384,2048] ~N(0,1), "
                             "lm_head W [151936,2048] ~N(0,0.02), 10% labels = -100, token "
-                            "chunk 8192, mean over non-ignored; loss + dX + dW",
+                            f"chunk {self.CHUNK}, mean over non-ignored; loss + dX + dW",
                 "tokens_per_step": self.N, "hidden": self.H, "vocab": self.V,
                 "vocab_per_rank": self.v_local, "chunk_tokens": self.CHUNK,
                 "parallelism": par, "l2": "inputs larger than L2 (W 622 MB)"}
@@ -777,6 +781,7 @@ class FullStep:
     short = "configs[4] Qwen3-VL-8B text LoRA step, 36 layers, seq 4096 per GPU"
     bound = "tensor"
     dtype = "bf16"
+    single_bracket = True  # one timed bracket, the whole training step
     L, H, NH, NKV, D, I, V = 36, 4096, 32, 8, 128, 12288, 151936
     R, ALPHA, SEQ, THETA = 16, 32.0, 4096, 5e6
     dominant = "train_step"
@@ -1385,20 +1390,29 @@ class Ctx:
             self.dist.destroy_process_group()
 
 
-def timed_steps(ctx, wl, t, steps, warmup, spin_us):
-    """W untimed steps, then K steps each bracketed by its own pair of CUDA
-    events on the launching stream.  Before a step's first event the stream
-    gets the workload's untimed prelude (the L2 flush) and a short GPU spin,
-    so the host has queued the whole step before the GPU reaches it.
-    Returns (sum of the K spans in ms, max over ranks; per-kernel average ms
-    on this rank; clock summary sampled during the K steps)."""
+def timed_steps(ctx, wl, t, steps, warmup, spin_us, per_kernel=True):
+    """W untimed steps, then the K timed steps: each step bracketed by one
+    pair of CUDA events on the launching stream, with nothing between its
+    launches.  Before a step's first event the stream gets the workload's
+    untimed prelude (the L2 flush) and a short GPU spin, so the host has
+    queued the whole step before the GPU reaches it.
+
+    Then, for the per-kernel breakdown, K more steps with a pair of events
+    around every launch (events between back-to-back launches add a few
+    microseconds of launch gap each, which is why the step value comes from
+    the first K); and for HBM-bound workloads each launch once more alone,
+    after an L2 flush whose lines are then clean (the kernel's own bandwidth,
+    without the write-back of the previous kernel's output).
+
+    Returns (sum of the K step spans in ms, max over ranks; per-kernel
+    average ms inside steps; per-kernel average ms alone; clock summary
+    sampled during the K timed steps)."""
     prelude = getattr(wl, "prelude", None)
     for _ in range(warmup):
         if prelude:
             prelude(t)
         wl.step(t)
     torch.cuda.synchronize()
-    timer = KernelTimer()
     spans = []
     spin_cycles = int(spin_us * 2000)  # ~2 GHz SM clock
     ctx.barrier()
@@ -1412,13 +1426,50 @@ def timed_steps(ctx, wl, t, steps, warmup, spin_us):
             s_ev = torch.cuda.Event(enable_timing=True)
             e_ev = torch.cuda.Event(enable_timing=True)
             s_ev.record()
-            wl.step(t, timer)
+            wl.step(t)
             e_ev.record()
             spans.append((s_ev, e_ev))
         torch.cuda.synchronize()
     ctx.barrier()
     elapsed = ctx.reduce(sum(a.elapsed_time(b) for a, b in spans))
-    return elapsed, timer.averages_ms(), clk.summary()
+    name = getattr(wl, "dominant", "step")
+    in_step = {name: elapsed / steps}
+    alone = {}
+    if per_kernel and not getattr(wl, "single_bracket", False):
+        timer = KernelTimer()
+        for _ in range(steps):
+            if prelude:
+                prelude(t)
+            if spin_cycles:
+                torch.cuda._sleep(spin_cycles)
+            wl.step(t, timer)
+        torch.cuda.synchronize()
+        in_step = timer.averages_ms()
+        if wl.bound == "hbm":
+            flush = L2Flush(ctx.device)
+            timer = KernelTimer(before=flush)
+            for _ in range(steps):
+                wl.step(t, timer)
+            torch.cuda.synchronize()
+            alone = timer.averages_ms()
+    ctx.barrier()
+    return elapsed, in_step, alone, clk.summary()
+
+
+class L2Flush:
+    """Evicts L2 (126 MB) so the next kernel reads from HBM and finds no
+    dirty lines to write back: writes a 256 MB buffer, then reads another
+    256 MB; a short spin follows so the next launch is queued in time."""
+
+    def __init__(self, device):
+        n = 256 * 1024 * 1024 // 4
+        self.wr = torch.empty(n, dtype=torch.float32, device=device)
+        self.rd = torch.zeros(n, dtype=torch.float32, device=device)
+
+    def __call__(self):
+        self.wr.fill_(0.0)
+        self.rd.amax()
+        torch.cuda._sleep(100000)
 
 
 def peak_extra_bytes(wl, t):
@@ -1456,8 +1507,10 @@ def e2e_measure(ctx, wl, steps):
     return ms, h2d, d2h
 
 
-def roofline(ctx, wl, kernel_ms, burst):
-    """The dominant kernel's roofline entry and the per-kernel fractions."""
+def roofline(ctx, wl, kernel_ms, burst, alone_ms=None, step_ms=None):
+    """The dominant kernel's roofline entry and the per-kernel fractions
+    (inside the step, and alone after a clean L2 flush where measured); the
+    entry also carries the whole step's algorithmic work over its time."""
     peaks = ctx.peaks
     dom = wl.dominant
     dom_ms = kernel_ms.get(dom)
@@ -1479,12 +1532,21 @@ def roofline(ctx, wl, kernel_ms, burst):
     roof = {"kernel": dom, "bound": wl.bound, "achieved": achieved, "peak": peak,
             "peak_source": f"{ctx.peaks_kind} ({src}{which})", "unit": unit,
             "frac": achieved / peak, "traffic": load_traffic(wl.name, dom)}
+    work = wl.bytes if wl.bound == "hbm" else getattr(wl, "flops", {})
+    if step_ms and work:
+        per_s = sum(work.values()) / (step_ms / 1e3) / (1e9 if wl.bound == "hbm" else 1e12)
+        roof["step"] = {"achieved": per_s, "frac": per_s / peak,
+                        "what": "all kernels' algorithmic work over the step time"}
+    alone_ms = alone_ms or {}
     per_kernel = {}
     for k, ms in kernel_ms.items():
         entry = {"ms": ms}
         if wl.bound == "hbm" and k in wl.bytes:
             gbs = wl.bytes[k] / (ms / 1e3) / 1e9
             entry.update({"GB/s": gbs, "frac": gbs / float(peaks.get("hbm_gbs", 1))})
+            if k in alone_ms:
+                entry["frac_alone"] = (wl.bytes[k] / (alone_ms[k] / 1e3) / 1e9
+                                       / float(peaks.get("hbm_gbs", 1)))
         if getattr(wl, "flops", None) and k in wl.flops:
             tf = wl.flops[k] / (ms / 1e3) / 1e12
             key = "bf16_tflops" if burst else "bf16_tflops_sustained"
@@ -1511,7 +1573,8 @@ def measure_workload(ctx, wl, steps, warmup, e2e_steps, cpu_budget, table=False,
     inputs are returned in the result under "inputs" instead of freed."""
     args = ctx.args
     t = wl.make_inputs(ctx.device)
-    elapsed_ms, kernel_ms, clocks = timed_steps(ctx, wl, t, steps, warmup, args.spin_us)
+    elapsed_ms, kernel_ms, alone_ms, clocks = timed_steps(ctx, wl, t, steps, warmup,
+                                                          args.spin_us)
     launches = count_our_launches(wl, t, table=table and ctx.rank == 0)
     if launches is None:
         launches = wl.launches_per_step
@@ -1526,7 +1589,7 @@ def measure_workload(ctx, wl, steps, warmup, e2e_steps, cpu_budget, table=False,
     job_tokens = wl.tokens * (ctx.world if getattr(wl, "scaling", "weak") == "weak" else 1)
     e2e_steps = max(1, min(steps, e2e_steps))
     e2e_ms, h2d, d2h = e2e_measure(ctx, wl, e2e_steps)
-    roof, per_kernel = roofline(ctx, wl, kernel_ms, args.burst)
+    roof, per_kernel = roofline(ctx, wl, kernel_ms, args.burst, alone_ms, elapsed_ms / steps)
     cpu = None
     if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu:
         cpu = cpu_baseline(wl, cpu_budget)
@@ -1546,10 +1609,15 @@ def compact_entry(wl, r, steps):
     """One workload of the default run's `workloads` object."""
     roof = dict(r["roofline"])
     roof.pop("peak_source", None)
+    if "step" in roof:
+        roof["step"] = {k: v for k, v in roof["step"].items() if k != "what"}
     e = {"config": wl.short, "value": r["value"], "unit": "tokens/s",
          "ms_per_step": r["ms_per_step"], "steps": steps,
          "scaling": getattr(wl, "scaling", "weak"), "roofline": roof,
          "kernel_frac": {k: v.get("frac") for k, v in r["per_kernel"].items()},
+         **({"kernel_frac_alone": {k: v["frac_alone"] for k, v in r["per_kernel"].items()
+                                   if "frac_alone" in v}}
+            if any("frac_alone" in v for v in r["per_kernel"].values()) else {}),
          "e2e": {k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step", "d2h_bytes_per_step")},
          "gpu_launches": r["gpu_launches"], "peak_extra_bytes": r["peak_extra_bytes"],
          "clocks": {"sm_mhz": r["clocks"].get("sm_mhz"), "reasons": r["clocks"].get("reasons")}}
@@ -1586,7 +1654,8 @@ def measure_flce_vp(ctx, steps, warmup, vp):
     t = vp["inputs"]
     single = Flce(world=1, rank=0)
     full = single.make_inputs(ctx.device)  # the same seeded tensors, whole vocabulary
-    ms1, _, _ = timed_steps(ctx, single, full, steps, warmup, ctx.args.spin_us)
+    ms1, _, _, _ = timed_steps(ctx, single, full, steps, warmup, ctx.args.spin_us,
+                               per_kernel=False)
 
     # parity: one step of each on the same inputs
     vpw = Flce()
@@ -1721,12 +1790,16 @@ def run_gpu_arm(args, wl):
             "dtype": wl.dtype,
             "data": "synthetic (seeded normal inputs of the BASELINE shapes)",
             "config": {**wl.config(),
-                       "timed_region": "sum of per-step CUDA-event spans on the launching "
-                                       "stream, max over ranks; L2 flush and a "
+                       "timed_region": "sum of K per-step CUDA-event spans on the launching "
+                                       "stream (no events between a step's launches), max "
+                                       "over ranks; L2 flush and a "
                                        f"{args.spin_us:g} us GPU spin before each step, "
-                                       "outside the spans"},
+                                       "outside the spans; per_kernel from K more steps with "
+                                       "events around every launch, frac_alone from each "
+                                       "launch alone after a clean L2 flush"},
             "roofline": r["roofline"],
-            "per_kernel": {k: {kk: vv for kk, vv in v.items() if kk in ("ms", "frac")}
+            "per_kernel": {k: {kk: vv for kk, vv in v.items() if kk in ("ms", "frac",
+                                                                         "frac_alone")}
                            for k, v in r["per_kernel"].items()},
             "cpu_baseline": r["cpu_baseline"],
             "e2e": {**r["e2e"],
@@ -1773,7 +1846,12 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurements")
     ap.add_argument("--burst", action="store_true",
                     help="use the burst (not sustained) bf16 peak for tensor-bound rooflines")
+    ap.add_argument("--flce-chunk", type=int, default=None,
+                    help="FLCE token-chunk length (default: BASELINE's 8192; smaller chunks "
+                         "bound the exponentials buffer, chunk x vocab bf16)")
     args = ap.parse_args(argv)
+    if args.flce_chunk:
+        Flce.CHUNK = int(args.flce_chunk)
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
     wl = WORKLOADS[args.workload or "swiglu_rope"]()

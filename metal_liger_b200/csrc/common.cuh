@@ -8,6 +8,7 @@
 #pragma once
 
 #include <mutex>
+#include <utility>
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -173,6 +174,35 @@ __device__ __forceinline__ void swiglu_bwd(float g, float u, float d, float& dg,
   const float s = swiglu_sigmoid(g);
   du = d * (g * s);
   dg = d * u * s * (1.f + g * (1.f - s));
+}
+
+// Programmatic dependent launch (PDL).  A kernel launched with launch_pdl
+// may be scheduled while the previous kernel on the stream is still
+// draining; it must call pdl_wait() before its first access to global
+// memory that an earlier kernel may have written (the wait returns once the
+// previous grid has completed and its writes are visible).  pdl_release()
+// lets the next programmatic dependent start launching: every CTA calls it
+// once, right after its own pdl_wait(), so the next kernel's CTAs fill the SMs
+// as this grid's CTAs retire.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kernel, std::forward<Args>(args)...);
 }
 
 // Runs a setup step (a kernel attribute, an occupancy query) once per CUDA

@@ -126,6 +126,8 @@ __device__ __forceinline__ void load_raw(const T* p, Raw<N, T>& r) {
 template <typename Tin, typename Tout, int VEC, bool TABLE>
 __global__ void __launch_bounds__(kThreads) rope_kernel(const RopeArgs a, int64_t units_per_cta,
                                                         int npos) {
+  pdl_wait();  // a programmatic dependent: inputs may come from the previous kernel
+  pdl_release();
   const int64_t D = a.head_dim;
   const int64_t half = D >> 1;
   const int tph = (int)(half / VEC);           // threads per row
@@ -257,18 +259,12 @@ int launch(const RopeArgs& a, bool vec_ok, cudaStream_t st) {
   int64_t per_cta = units / hblocks >= 2 * slots ? hblocks : 1;
   while (per_cta > 1 && (units + per_cta - 1) / per_cta < 2 * slots) per_cta /= 2;
   int64_t ctas = (units + per_cta - 1) / per_cta;
-  if (table) {
-    if (vec_ok)
-      rope_kernel<Tin, Tout, V, true><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
-    else
-      rope_kernel<Tin, Tout, 1, true><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
-  } else {
-    if (vec_ok)
-      rope_kernel<Tin, Tout, V, false><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
-    else
-      rope_kernel<Tin, Tout, 1, false><<<(unsigned)ctas, threads, 0, st>>>(a, per_cta, npos);
-  }
-  ML_CHECK_LAUNCH("rope");
+  // Launched as a programmatic dependent (PDL): the CTAs are scheduled while
+  // the previous kernel drains and wait for it before their first load.
+  auto k = table ? (vec_ok ? rope_kernel<Tin, Tout, V, true> : rope_kernel<Tin, Tout, 1, true>)
+                 : (vec_ok ? rope_kernel<Tin, Tout, V, false> : rope_kernel<Tin, Tout, 1, false>);
+  ML_CHECK_CUDA(launch_pdl(k, dim3((unsigned)ctas), dim3(threads), 0, st, a, per_cta, npos),
+                "rope launch");
   return ML_OK;
 }
 

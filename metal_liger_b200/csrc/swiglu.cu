@@ -8,7 +8,9 @@
 //
 // Launch shape: grid-stride over 16-byte vectors (8 bf16 / 4 fp32 per
 // thread per step), grid = SM count x resident CTAs; streaming loads/stores
-// because every byte is touched exactly once.  A scalar tail handles n not a
+// because every byte is touched exactly once.  Launched as programmatic
+// dependents (PDL): the CTAs are scheduled while the previous kernel drains
+// and wait for it before their first load.  A scalar tail handles n not a
 // multiple of the vector width or unaligned pointers.
 #include "common.cuh"
 
@@ -24,6 +26,8 @@ swiglu_fwd_kernel(const T* __restrict__ gate, const T* __restrict__ up, T* __res
   constexpr int VEC = 16 / sizeof(T);
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();  // launched as a programmatic dependent: inputs may come from the previous kernel
+  pdl_release();
   int64_t done = 0;
   if (vec_ok) {
     const int64_t nvec = n / VEC;
@@ -66,6 +70,8 @@ swiglu_bwd_kernel(const T* __restrict__ gate, const T* __restrict__ up,
   constexpr int VEC = 16 / sizeof(T);
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_release();
   int64_t done = 0;
   if (vec_ok) {
     const int64_t nvec = n / VEC;
@@ -126,9 +132,9 @@ int launch_fwd(const void* gate, const void* up, void* out, int64_t n, cudaStrea
   const bool vec_ok = aligned16(gate) && aligned16(up) && aligned16(out);
   auto k = swiglu_fwd_kernel<T, kUnroll>;
   const int grid = elementwise_grid(k, n, VEC * kUnroll);
-  k<<<grid, 256, 0, st>>>(static_cast<const T*>(gate), static_cast<const T*>(up),
-                          static_cast<T*>(out), n, vec_ok);
-  ML_CHECK_LAUNCH("swiglu_forward");
+  ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(256), 0, st, static_cast<const T*>(gate),
+                           static_cast<const T*>(up), static_cast<T*>(out), n, vec_ok),
+                "swiglu_forward launch");
   return ML_OK;
 }
 
@@ -140,10 +146,10 @@ int launch_bwd(const void* gate, const void* up, const void* dout, void* dgate, 
                       aligned16(dup);
   auto k = swiglu_bwd_kernel<T, kUnroll>;
   const int grid = elementwise_grid(k, n, VEC * kUnroll);
-  k<<<grid, 256, 0, st>>>(static_cast<const T*>(gate), static_cast<const T*>(up),
-                          static_cast<const T*>(dout), static_cast<T*>(dgate),
-                          static_cast<T*>(dup), n, vec_ok);
-  ML_CHECK_LAUNCH("swiglu_backward");
+  ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(256), 0, st, static_cast<const T*>(gate),
+                           static_cast<const T*>(up), static_cast<const T*>(dout),
+                           static_cast<T*>(dgate), static_cast<T*>(dup), n, vec_ok),
+                "swiglu_backward launch");
   return ML_OK;
 }
 
