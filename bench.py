@@ -315,10 +315,25 @@ class SwigluRope:
                     for k, v in outs_shapes.items()}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
-        # one chunk per batch row: every tensor splits along dim 0
         return {"host": host, "dev": dev, "host_out": host_out, "pos": t["pos"],
                 "inv_freq": t["inv_freq"], "h2d": h2d, "d2h": d2h,
-                "pipe": CopyPipeline(device, self.B)}
+                "pipe": CopyPipeline(device, self.B * self.E2E_SPLIT)}
+
+    # Chunks per batch row in the e2e pipeline.  Every chunk stays contiguous:
+    # SwiGLU rows split along the sequence, RoPE rows along the heads (all
+    # positions of the batch row in every chunk).
+    E2E_SPLIT = 2
+
+    def _e2e_views(self, i):
+        sp = self.E2E_SPLIT
+        b, part = divmod(i, sp)
+        rows, hq, hk = self.S // sp, self.HQ // sp, self.HK // sp
+        sw = (b, slice(part * rows, (part + 1) * rows))
+        rq = (b, slice(part * hq, (part + 1) * hq))
+        rk = (b, slice(part * hk, (part + 1) * hk))
+        return {"gate": sw, "up": sw, "dout": sw, "q": rq, "dq": rq, "k": rk, "dk": rk,
+                "out": sw, "dgate": sw, "dup": sw, "q_rot": rq, "dq_in": rq,
+                "k_rot": rk, "dk_in": rk}, b
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_swiglu import fused_swiglu
@@ -327,26 +342,30 @@ class SwigluRope:
         d, h, ho = s["dev"], s["host"], s["host_out"]
 
         def load(i):
+            v, _ = self._e2e_views(i)
             for k in d:
-                d[k][i].copy_(h[k][i], non_blocking=True)
+                d[k][v[k]].copy_(h[k][v[k]], non_blocking=True)
 
         def compute(i):
-            gate = d["gate"][i:i + 1].detach().requires_grad_(True)
-            up = d["up"][i:i + 1].detach().requires_grad_(True)
+            v, b = self._e2e_views(i)
+            gate = d["gate"][v["gate"]].unsqueeze(0).detach().requires_grad_(True)
+            up = d["up"][v["up"]].unsqueeze(0).detach().requires_grad_(True)
             out = fused_swiglu(gate, up)
-            out.backward(d["dout"][i:i + 1])
-            q = d["q"][i:i + 1].detach().requires_grad_(True)
-            k = d["k"][i:i + 1].detach().requires_grad_(True)
-            qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"][i:i + 1],
+            out.backward(d["dout"][v["dout"]].unsqueeze(0))
+            q = d["q"][v["q"]].unsqueeze(0).detach().requires_grad_(True)
+            k = d["k"][v["k"]].unsqueeze(0).detach().requires_grad_(True)
+            qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"][b:b + 1],
                                                        inv_freq=s["inv_freq"])
-            torch.autograd.backward([qr, kr], [d["dq"][i:i + 1], d["dk"][i:i + 1]])
+            torch.autograd.backward([qr, kr], [d["dq"][v["dq"]].unsqueeze(0),
+                                               d["dk"][v["dk"]].unsqueeze(0)])
             return {"out": out.detach(), "dgate": gate.grad, "dup": up.grad,
                     "q_rot": qr.detach(), "k_rot": kr.detach(), "dq_in": q.grad,
                     "dk_in": k.grad}
 
         def store(i, outs):
+            v, _ = self._e2e_views(i)
             for name, src in outs.items():
-                ho[name][i:i + 1].copy_(src, non_blocking=True)
+                ho[name][v[name]].copy_(src[0], non_blocking=True)
             return outs.values()
 
         s["pipe"].run(load, compute, store)
@@ -1846,12 +1865,24 @@ def main(argv=None):
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline measurements")
     ap.add_argument("--burst", action="store_true",
                     help="use the burst (not sustained) bf16 peak for tensor-bound rooflines")
+    ap.add_argument("--lora-swiglu-fusion", type=int, choices=[0, 1], default=None,
+                    help="LoRA MLP: SwiGLU inside the GEMMs (1, the library default) or as "
+                         "separate elementwise passes (0)")
+    ap.add_argument("--lora-tokens", type=int, default=None,
+                    help="token rows of the lora workload (default: BASELINE's 16,384); a "
+                         "smaller case for profiler captures")
     ap.add_argument("--flce-chunk", type=int, default=None,
                     help="FLCE token-chunk length (default: BASELINE's 8192; smaller chunks "
                          "bound the exponentials buffer, chunk x vocab bf16)")
     args = ap.parse_args(argv)
     if args.flce_chunk:
         Flce.CHUNK = int(args.flce_chunk)
+    if args.lora_tokens:
+        Lora.T = int(args.lora_tokens)
+    if args.lora_swiglu_fusion is not None and args.impl != "reference":
+        from metal_liger_b200 import _C
+
+        _C.call("ml_lora_set_mlp_swiglu_fusion", int(args.lora_swiglu_fusion), None)
     if args.warmup < 3:
         args.warmup = 3  # timing rule: at least 3 warm-up steps
     wl = WORKLOADS[args.workload or "swiglu_rope"]()
