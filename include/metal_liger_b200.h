@@ -224,6 +224,17 @@ ML_API int ml_gemm_bf16(int64_t m, int64_t n, const ml_gemm_segment* segs, int n
  */
 ML_API int ml_gemm_set_cta_pair(int mode, int* previous);
 
+/*
+ * Process-wide number of SMs (0-128) every GEMM of this library leaves free
+ * while it is set: the persistent GEMM grid then stops short of the whole
+ * GPU, so a kernel on another stream (an NCCL collective the GEMM is meant
+ * to overlap) can be scheduled next to it instead of after it.  Read at
+ * launch time; 0 (the default) uses every SM.  The previous value is stored
+ * to *previous when non-NULL.  No reference counterpart (the reference is
+ * single-device).
+ */
+ML_API int ml_gemm_set_reserved_sms(int n, int* previous);
+
 /* ------------------------------------------------------------------------
  * Fused linear cross-entropy
  * ------------------------------------------------------------------------ */

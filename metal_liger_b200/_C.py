@@ -88,6 +88,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                              c_int64, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "ml_gemm_set_cta_pair": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_lora_set_mlp_swiglu_fusion": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "ml_gemm_set_reserved_sms": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_selftest_bounded_wait": (c_int, [c_int64, c_void_p]),
     "ml_lm_head_argmax_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ml_gemv_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,
@@ -254,6 +255,18 @@ def gemm_cta_pair(mode: int):
         yield
     finally:
         call("ml_gemm_set_cta_pair", prev.value, None)
+
+
+@contextlib.contextmanager
+def gemm_reserved_sms(n: int):
+    """Leave `n` SMs free of this library's GEMMs for the duration of a block
+    (for kernels on other streams that should overlap them)."""
+    prev = ctypes.c_int(0)
+    call("ml_gemm_set_reserved_sms", int(n), ctypes.byref(prev))
+    try:
+        yield
+    finally:
+        call("ml_gemm_set_reserved_sms", prev.value, None)
 
 
 @contextlib.contextmanager

@@ -100,6 +100,10 @@ int launch_t(const Params& prm, int grid, cudaStream_t st) {
 }
 
 std::atomic<int> g_pair_mode{-1};
+// SMs every GEMM leaves free (ml_gemm_set_reserved_sms): its persistent grid
+// then stops short of the whole GPU, so a kernel on another stream — an
+// NCCL collective overlapping the GEMM — finds SMs to run on.
+std::atomic<int> g_reserved_sms{0};
 
 template <int BN, bool A_MN, bool B_MN>
 int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t st) {
@@ -337,8 +341,14 @@ int launch(const Problem& pr, cudaStream_t st) {
     set_error("gemm: problem too large");
     return ML_ERR_INVALID_ARG;
   }
-  if (pair) return launch_pair(prm, bn, pr.a_mn, pr.b_mn, units, pr.max_ctas, st);
-  int grid = (int)std::min<int64_t>(units, pr.max_ctas > 0 ? pr.max_ctas : num_sms());
+  int max_ctas = pr.max_ctas;
+  const int reserved = g_reserved_sms.load(std::memory_order_relaxed);
+  if (reserved > 0) {
+    const int avail = std::max(2, num_sms() - reserved);
+    max_ctas = max_ctas > 0 ? std::min(max_ctas, avail) : avail;
+  }
+  if (pair) return launch_pair(prm, bn, pr.a_mn, pr.b_mn, units, max_ctas, st);
+  int grid = (int)std::min<int64_t>(units, max_ctas > 0 ? max_ctas : num_sms());
   grid = std::max(grid, 1);
   switch (bn) {
     case 64: return launch_bn<64>(prm, pr.a_mn, pr.b_mn, grid, st);
@@ -527,6 +537,13 @@ extern "C" size_t ml_gemm_bf16_workspace_bytes(int64_t m, int64_t n, int64_t k_t
   if (m <= 0 || n <= 0 || k_total <= 0) return 0;
   const int s = choose_splits(m, n, k_total, gemm::pick_bn(n));
   return s > 1 ? (size_t)s * (size_t)m * (size_t)n * sizeof(float) : 0;
+}
+
+extern "C" int ml_gemm_set_reserved_sms(int n, int* previous) {
+  ML_CHECK_ARG(n >= 0 && n <= 128, "gemm_set_reserved_sms: n must be in [0, 128]");
+  const int old = gemm::g_reserved_sms.exchange(n);
+  if (previous) *previous = old;
+  return ML_OK;
 }
 
 extern "C" int ml_gemm_set_cta_pair(int mode, int* previous) {

@@ -138,6 +138,53 @@ class CudaShardPhases:
                 _C.stream_of(hidden))
 
 
+# How the vocabulary-parallel FLCE runs its collectives (process-wide):
+# * VP_STATS_EXCHANGE: "allreduce" merges the per-row statistics with two
+#   all-reduces (MAX of the maxima, then SUM of the rescaled sums and target
+#   logits); "allgather" gathers every rank's (max, sum, target) in one
+#   collective and merges them locally in rank order.
+# * VP_OVERLAP_SMS: SMs the GEMMs leave free while a chunk's asynchronous dX
+#   all-reduce may be in flight, so the collective's kernels run beside the
+#   dW GEMM instead of after it (0: the GEMMs take every SM).
+VP_STATS_EXCHANGE = "allreduce"
+VP_OVERLAP_SMS = 0
+
+
+def _merge_stats(m, s, t, group, phases):
+    """Global (max, sum exp(logit - max), target logit) per row from every
+    rank's shard statistics."""
+    import torch.distributed as dist
+
+    if VP_STATS_EXCHANGE == "allgather":
+        world = dist.get_world_size(group)
+        mine = torch.stack([m, s, t])
+        if dist.get_backend(group) == "nccl":
+            every = torch.empty((world,) + tuple(mine.shape), dtype=mine.dtype,
+                                device=mine.device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+        else:
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine, group=group)
+            every = torch.stack(parts)
+        mg = every[:, 0].amax(dim=0)
+        sg = (every[:, 1] * torch.exp(every[:, 0] - mg)).sum(dim=0)
+        return mg, sg, every[:, 2].sum(dim=0)
+    mg = m.clone()
+    dist.all_reduce(mg, op=dist.ReduceOp.MAX, group=group)
+    st = torch.stack([s * torch.exp(m - mg), t])
+    dist.all_reduce(st, op=dist.ReduceOp.SUM, group=group)
+    return mg, st[0], st[1]
+
+
+def _leave_sms_for_collectives(phases, pending):
+    import contextlib
+
+    if VP_OVERLAP_SMS <= 0 or not pending or not isinstance(phases, CudaShardPhases):
+        return contextlib.nullcontext()
+    from metal_liger_b200 import _C
+    return _C.gemm_reserved_sms(VP_OVERLAP_SMS)
+
+
 def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=None,
                         ignore_index=-100, chunk_size=8192, group=None, phases=None,
                         need_dx=True, need_dw=True):
@@ -184,15 +231,13 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
     for r0 in range(0, n, chunk):
         r1 = min(n, r0 + chunk)
         hc, lc = hidden[r0:r1], labels[r0:r1]
-        m, s, t, state = phases.stats(hc, weight_shard, bias_shard, lc, vocab_offset,
-                                      ignore_index)
-        mg = m.clone()
-        dist.all_reduce(mg, op=dist.ReduceOp.MAX, group=group)
-        st = torch.stack([s * torch.exp(m - mg), t])
-        dist.all_reduce(st, op=dist.ReduceOp.SUM, group=group)
-        lse = mg + torch.log(st[0])
+        with _leave_sms_for_collectives(phases, pending):
+            m, s, t, state = phases.stats(hc, weight_shard, bias_shard, lc, vocab_offset,
+                                          ignore_index)
+        mg, sg, tg = _merge_stats(m, s, t, group, phases)
+        lse = mg + torch.log(sg)
         mask = (lc != ignore_index).to(torch.float32)
-        row_loss[r0:r1] = (lse - st[1]) * mask
+        row_loss[r0:r1] = (lse - tg) * mask
         # dX first, so its all-reduce runs while this chunk's dW GEMM does
         phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index, lse.contiguous(),
                      cnt[1:2], dx[r0:r1] if need_dx else None, None, r0 > 0)
@@ -200,7 +245,8 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
             pending.append(dist.all_reduce(dx[r0:r1], op=dist.ReduceOp.SUM, group=group,
                                            async_op=True))
         if need_dw:
-            phases.grads_dw(state, hc, weight_shard, dw, r0 > 0)
+            with _leave_sms_for_collectives(phases, pending):
+                phases.grads_dw(state, hc, weight_shard, dw, r0 > 0)
     for work in pending:
         work.wait()
     loss = row_loss.sum() * cnt[1]

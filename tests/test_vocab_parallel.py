@@ -23,9 +23,11 @@ def _problem():
     return hid, w, lab
 
 
-def _rank_fn(rank, world, chunk):
+def _rank_fn(rank, world, chunk, exchange="allreduce"):
+    import metal_liger_b200.ops.fused_linear_cross_entropy as F
     from metal_liger_b200.ops.fused_linear_cross_entropy import shard_lm_head, \
         vocab_parallel_flce
+    F.VP_STATS_EXCHANGE = exchange
     hid, w, lab = _problem()
     ws, off = shard_lm_head(w, rank, world)
     loss, dx, dw = vocab_parallel_flce(hid, ws, lab, off, chunk_size=chunk,
@@ -33,9 +35,12 @@ def _rank_fn(rank, world, chunk):
     return {"loss": loss, "dx": dx, "dw": dw, "off": off}
 
 
+@pytest.mark.parametrize("exchange", ["allreduce", "allgather"])
 @pytest.mark.parametrize("chunk", [16, 4096])
-def test_gloo_two_ranks_match_single_process_oracle(chunk):
-    res = run_ranks(_rank_fn, 2, free_port(), "gloo", 30, chunk)
+def test_gloo_two_ranks_match_single_process_oracle(chunk, exchange):
+    """Both ways of merging the per-row statistics (two all-reduces, or one
+    all-gather merged in rank order) give the single-process result."""
+    res = run_ranks(_rank_fn, 2, free_port(), "gloo", 30, chunk, exchange)
     for r in (0, 1):
         assert not isinstance(res[r], str), res[r]
     hid, w, lab = _problem()
