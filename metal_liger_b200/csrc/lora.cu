@@ -119,13 +119,18 @@ __global__ void __launch_bounds__(256) assemble_k(const __grid_constant__ Assemb
 }
 
 // Scatter of the fp32 [n, 64] skinny-GEMM results into the per-adapter
-// gradients, several adapters per launch:
-//   trans = 0 (dB): dst[i * cols + j] = scale * src[i * 64 + off + j]   dst [rows, cols = r]
-//   trans = 1 (dA): dst[i * cols + j] = scale * src[j * 64 + off + i]   dst [rows = r, cols]
+// gradients, several adapters per launch.  The results arrive as the
+// split-K GEMM's `splits` partial slabs (split_stride floats apart), summed
+// here in slab order — the sum a separate reduction kernel would form, so
+// none is launched:
+//   trans = 0 (dB): dst[i * cols + j] = scale * sum_s src[s][i * 64 + off + j]   dst [rows, cols = r]
+//   trans = 1 (dA): dst[i * cols + j] = scale * sum_s src[s][j * 64 + off + i]   dst [rows = r, cols]
 struct UnpackJob {
   void* dst;         // in the adapter parameter's dtype (dt)
   const float* src;
   int64_t rows, cols, off;
+  int64_t split_stride;
+  int splits;
   float scale;
   int trans;
   int dt;
@@ -148,9 +153,10 @@ __global__ void unpack_k(const __grid_constant__ Unpacks u) {
     const UnpackJob& jb = u.j[k];
     const int64_t local = e - u.start[k];
     const int64_t i = local / jb.cols, j = local - (local / jb.cols) * jb.cols;
-    store_from_f32(jb.dst, local, jb.dt,
-                   jb.scale * (jb.trans ? jb.src[j * kSlot + jb.off + i]
-                                        : jb.src[i * kSlot + jb.off + j]));
+    const int64_t at = jb.trans ? j * kSlot + jb.off + i : i * kSlot + jb.off + j;
+    float acc = 0.f;
+    for (int sp = 0; sp < jb.splits; ++sp) acc += jb.src[sp * jb.split_stride + at];
+    store_from_f32(jb.dst, local, jb.dt, jb.scale * acc);
   }
 }
 
@@ -230,9 +236,17 @@ struct Assembler {
   }
 };
 
+// The split-K partial slabs of one skinny product (summed by unpack_k).
+struct Partials {
+  const float* ptr = nullptr;
+  int splits = 1;
+  int64_t split_stride = 0;
+};
+
 struct Unpacker {
   Unpacks u{};
-  int add(void* dst, int dt, const float* src, int64_t rows, int64_t cols, int64_t off,
+  // `p` holds `p.splits` partial slabs of `p.split_stride` floats each.
+  int add(void* dst, int dt, const Partials& p, int64_t rows, int64_t cols, int64_t off,
           float scale, bool trans) {
     if (u.n >= kMaxUnpack) {
       set_error("lora: too many gradient scatters in one launch");
@@ -240,7 +254,9 @@ struct Unpacker {
     }
     UnpackJob& j = u.j[u.n];
     j.dst = dst;
-    j.src = src;
+    j.src = p.ptr;
+    j.splits = p.splits;
+    j.split_stride = p.split_stride;
     j.rows = rows;
     j.cols = cols;
     j.off = off;
@@ -302,9 +318,15 @@ int gemm_bf16(int64_t M, int64_t N, const std::vector<gemm::Seg>& segs, bool a_m
   return gemm_bf16(M, N, segs.data(), segs.size(), a_mn, b_mn, D, ldd, st);
 }
 
-// out[M, 64] fp32 = A^T-style skinny product over the token dimension, split-K.
-int gemm_skinny_f32(int64_t M, const gemm::Seg& s, float* out, float* partial,
-                    size_t partial_bytes, cudaStream_t st) {
+size_t skinny_partial_floats(int64_t M, int64_t K) {
+  return (size_t)gemm::auto_splits(M, kSlot, K) * (size_t)M * kSlot;
+}
+
+// A^T-style skinny product over the token dimension ([M, 64] fp32), left as
+// the split-K GEMM's partial slabs in `partial` (skinny_partial_floats(M, K)
+// floats) for unpack_k to sum: no reduction launch.
+int gemm_skinny_partials(int64_t M, const gemm::Seg& s, float* partial, Partials* out,
+                         cudaStream_t st) {
   gemm::Problem p;
   p.M = M;
   p.N = kSlot;
@@ -312,12 +334,15 @@ int gemm_skinny_f32(int64_t M, const gemm::Seg& s, float* out, float* partial,
   p.seg[0] = s;
   p.a_mn = true;
   p.b_mn = true;
-  const int splits = gemm::auto_splits(M, kSlot, s.K);
-  return gemm::launch_splitk(p, splits, out, kSlot, partial, partial_bytes, st);
-}
-
-size_t skinny_partial_floats(int64_t M, int64_t K) {
-  return (size_t)gemm::auto_splits(M, kSlot, K) * (size_t)M * kSlot;
+  p.epi = gemm::EPI_PARTIAL;
+  p.splits = gemm::auto_splits(M, kSlot, s.K);
+  p.D = partial;
+  p.ldd = kSlot;
+  p.split_stride = M * kSlot;
+  out->ptr = partial;
+  out->splits = p.splits;
+  out->split_stride = M * kSlot;
+  return gemm::launch(p, st);
 }
 
 // out[T, 64] bf16 = sum of segments: the rank projections (U = X A^T,
@@ -409,13 +434,11 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   for (int i = 0; i < np; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
   bf16* acat_s = ar.take<bf16>((size_t)kSlot * H);
   bf16* G = ar.take<bf16>((size_t)T * kSlot);
-  float* dAT = ar.take<float>((size_t)H * kSlot);
-  float* dBt[3] = {};
-  size_t pf = std::max(skinny_partial_floats(H, T), skinny_partial_floats(T, osum));
-  for (int i = 0; i < np; ++i) {
-    dBt[i] = ar.take<float>((size_t)pj[i].out_features * kSlot);
-    pf = std::max(pf, skinny_partial_floats(pj[i].out_features, T));
-  }
+  // split-K partial slabs of dA (X^T G) and of each dB (dY_i^T U), summed by unpack_k
+  float* dAp = ar.take<float>(skinny_partial_floats(H, T));
+  float* dBp[3] = {};
+  for (int i = 0; i < np; ++i) dBp[i] = ar.take<float>(skinny_partial_floats(pj[i].out_features, T));
+  const size_t pf = skinny_partial_floats(T, osum);
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
   // bt_i = B_i^T in rows [i r, (i + 1) r); acat_s = [s_0 A_0; s_1 A_1; ...]
@@ -445,15 +468,16 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   // dX = sum_i dY_i W_i + G (s A)   — one accumulator, W read in place (N-major)
   LORA_TRY(gemm_bf16(T, H, xsegs, false, true, dx, H, st));
   // dA_i = s_i (X^T G)[:, slot_i]^T ;  dB_i = s_i dY_i^T U[:, slot_i]
-  LORA_TRY(gemm_skinny_f32(H, seg(x, H, G, kSlot, T), dAT, part, pf * 4, st));
+  Partials pA, pB[3];
+  LORA_TRY(gemm_skinny_partials(H, seg(x, H, G, kSlot, T), dAp, &pA, st));
   for (int i = 0; i < np; ++i) {
     const int64_t o = pj[i].out_features;
-    LORA_TRY(gemm_skinny_f32(o, seg(dy[i], o, u, kSlot, T), dBt[i], part, pf * 4, st));
+    LORA_TRY(gemm_skinny_partials(o, seg(dy[i], o, u, kSlot, T), dBp[i], &pB[i], st));
   }
   Unpacker un;
   for (int i = 0; i < np; ++i) {
-    LORA_TRY(un.add(da[i], pj[i].a_dtype, dAT, r, H, i * r, pj[i].scaling, true));
-    LORA_TRY(un.add(db[i], pj[i].b_dtype, dBt[i], pj[i].out_features, r, i * r, pj[i].scaling,
+    LORA_TRY(un.add(da[i], pj[i].a_dtype, pA, r, H, i * r, pj[i].scaling, true));
+    LORA_TRY(un.add(db[i], pj[i].b_dtype, pB[i], pj[i].out_features, r, i * r, pj[i].scaling,
                     false));
   }
   return un.launch(st);
@@ -545,13 +569,13 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   bf16* dH = fused ? nullptr : ar.take<bf16>((size_t)T * I);
   bf16* dgate = ar.take<bf16>((size_t)T * I);
   bf16* dup = ar.take<bf16>((size_t)T * I);
-  float* dAT_d = ar.take<float>((size_t)I * kSlot);   // h^T G_d
-  float* dAT_gu = ar.take<float>((size_t)H * kSlot);  // X^T G_gu
-  float* dBt_d = ar.take<float>((size_t)H * kSlot);   // dY^T U2
-  float* dBt_g = ar.take<float>((size_t)I * kSlot);   // d_gate^T U1
-  float* dBt_u = ar.take<float>((size_t)I * kSlot);   // d_up^T U1
-  const size_t pf = std::max({skinny_partial_floats(H, T), skinny_partial_floats(I, T),
-                              skinny_partial_floats(T, H), skinny_partial_floats(T, 2 * I)});
+  // split-K partial slabs of the adapter-gradient products, summed by unpack_k
+  float* dAp_d = ar.take<float>(skinny_partial_floats(I, T));   // h^T G_d
+  float* dAp_gu = ar.take<float>(skinny_partial_floats(H, T));  // X^T G_gu
+  float* dBp_d = ar.take<float>(skinny_partial_floats(H, T));   // dY^T U2
+  float* dBp_g = ar.take<float>(skinny_partial_floats(I, T));   // d_gate^T U1
+  float* dBp_u = ar.take<float>(skinny_partial_floats(I, T));   // d_up^T U1
+  const size_t pf = std::max(skinny_partial_floats(T, H), skinny_partial_floats(T, 2 * I));
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
   Assembler as;
@@ -586,8 +610,9 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                        true, dH, I, st));
   }
   // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
-  LORA_TRY(gemm_skinny_f32(I, seg(h, I, Gd, kSlot, T), dAT_d, part, pf * 4, st));
-  LORA_TRY(gemm_skinny_f32(H, seg(dy, H, u2, kSlot, T), dBt_d, part, pf * 4, st));
+  Partials pAd, pBd, pAgu, pBg, pBu;
+  LORA_TRY(gemm_skinny_partials(I, seg(h, I, Gd, kSlot, T), dAp_d, &pAd, st));
+  LORA_TRY(gemm_skinny_partials(H, seg(dy, H, u2, kSlot, T), dBp_d, &pBd, st));
   // SwiGLU backward (sigmoid recomputed), unless the dH GEMM applied it
   if (!fused) LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
   // G_gu = [d_gate Bg | d_up Bu]
@@ -598,16 +623,16 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                       seg(Ggu, kSlot, acs, H, kSlot)},
                      false, true, dx, H, st));
   // gate/up adapter grads
-  LORA_TRY(gemm_skinny_f32(H, seg(x, H, Ggu, kSlot, T), dAT_gu, part, pf * 4, st));
-  LORA_TRY(gemm_skinny_f32(I, seg(dgate, I, u1, kSlot, T), dBt_g, part, pf * 4, st));
-  LORA_TRY(gemm_skinny_f32(I, seg(dup, I, u1, kSlot, T), dBt_u, part, pf * 4, st));
+  LORA_TRY(gemm_skinny_partials(H, seg(x, H, Ggu, kSlot, T), dAp_gu, &pAgu, st));
+  LORA_TRY(gemm_skinny_partials(I, seg(dgate, I, u1, kSlot, T), dBp_g, &pBg, st));
+  LORA_TRY(gemm_skinny_partials(I, seg(dup, I, u1, kSlot, T), dBp_u, &pBu, st));
   Unpacker un;
-  LORA_TRY(un.add(da[2], pj[2].a_dtype, dAT_d, r, I, 0, pj[2].scaling, true));
-  LORA_TRY(un.add(db[2], pj[2].b_dtype, dBt_d, H, r, 0, pj[2].scaling, false));
-  LORA_TRY(un.add(da[0], pj[0].a_dtype, dAT_gu, r, H, 0, pj[0].scaling, true));
-  LORA_TRY(un.add(da[1], pj[1].a_dtype, dAT_gu, r, H, r, pj[1].scaling, true));
-  LORA_TRY(un.add(db[0], pj[0].b_dtype, dBt_g, I, r, 0, pj[0].scaling, false));
-  LORA_TRY(un.add(db[1], pj[1].b_dtype, dBt_u, I, r, r, pj[1].scaling, false));
+  LORA_TRY(un.add(da[2], pj[2].a_dtype, pAd, r, I, 0, pj[2].scaling, true));
+  LORA_TRY(un.add(db[2], pj[2].b_dtype, pBd, H, r, 0, pj[2].scaling, false));
+  LORA_TRY(un.add(da[0], pj[0].a_dtype, pAgu, r, H, 0, pj[0].scaling, true));
+  LORA_TRY(un.add(da[1], pj[1].a_dtype, pAgu, r, H, r, pj[1].scaling, true));
+  LORA_TRY(un.add(db[0], pj[0].b_dtype, pBg, I, r, 0, pj[0].scaling, false));
+  LORA_TRY(un.add(db[1], pj[1].b_dtype, pBu, I, r, r, pj[1].scaling, false));
   return un.launch(st);
 }
 
