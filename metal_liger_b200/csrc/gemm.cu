@@ -213,7 +213,28 @@ int launch(const Problem& pr, cudaStream_t st) {
               pr.nseg);
     return ML_ERR_INVALID_ARG;
   }
-  const int mode = pr.pair >= 0 ? pr.pair : g_pair_mode.load(std::memory_order_relaxed);
+  const bool grouped = pr.m_groups > 1;
+  if (grouped) {
+    if (pr.m_groups > kMaxSeg || pr.nseg != pr.m_groups || pr.b_split ||
+        (pr.epi != EPI_PARTIAL && pr.epi != EPI_STORE)) {
+      set_error("gemm: grouped GEMM needs 2..%d groups, one segment each, a store or "
+                "partial epilogue", kMaxSeg);
+      return ML_ERR_INVALID_ARG;
+    }
+    int64_t total = 0;
+    for (int g = 0; g < pr.m_groups; ++g) {
+      if (pr.grp_m[g] <= 0 || pr.seg[g].K != pr.seg[0].K) {
+        set_error("gemm: grouped GEMM needs rows in every group and one K for all");
+        return ML_ERR_INVALID_ARG;
+      }
+      total += pr.grp_m[g];
+    }
+    if (total != pr.M) {
+      set_error("gemm: grouped GEMM rows do not add up to M");
+      return ML_ERR_INVALID_ARG;
+    }
+  }
+  const int mode = grouped ? 0 : (pr.pair >= 0 ? pr.pair : g_pair_mode.load(std::memory_order_relaxed));
   const TileChoice tc = choose_tile(pr, mode);
   const int bn = tc.bn;
   const bool pair = tc.pair;
@@ -246,11 +267,12 @@ int launch(const Problem& pr, cudaStream_t st) {
       return ML_ERR_INVALID_ARG;
     }
     int rc;
-    // A: logical [M, K]
+    // A: logical [M, K] (a grouped GEMM's group s: its own grp_m[s] rows)
+    const int64_t am = grouped ? pr.grp_m[s] : pr.M;
     if (!pr.a_mn)
-      rc = make_map(&prm.tma_a[s], g.a.ptr, g.K, pr.M, g.a.ld, BM, "gemm A (K-major)");
+      rc = make_map(&prm.tma_a[s], g.a.ptr, g.K, am, g.a.ld, BM, "gemm A (K-major)");
     else
-      rc = make_map(&prm.tma_a[s], g.a.ptr, pr.M, g.K, g.a.ld, BK, "gemm A (M-major)");
+      rc = make_map(&prm.tma_a[s], g.a.ptr, am, g.K, g.a.ld, BK, "gemm A (M-major)");
     if (rc) return rc;
     // B: logical [N, K]; each CTA of a pair loads 128 of the tile's 256 rows.
     // Split B: two [N, K] matrices, half a tile's rows from each.
@@ -273,6 +295,20 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.M = (int)pr.M;
   prm.N = (int)pr.N;
   prm.m_tiles = (int)((pr.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM));
+  prm.m_groups = grouped ? pr.m_groups : 1;
+  if (grouped) {
+    kb_total = prm.seg_kb[0];  // the groups share one K range
+    int mt = 0, row = 0;
+    for (int g = 0; g < pr.m_groups; ++g) {
+      prm.grp_mt0[g] = mt;
+      prm.grp_row0[g] = row;
+      prm.grp_m[g] = (int)pr.grp_m[g];
+      mt += (int)((pr.grp_m[g] + BM - 1) / BM);
+      row += (int)pr.grp_m[g];
+    }
+    prm.grp_mt0[pr.m_groups] = mt;
+    prm.m_tiles = mt;
+  }
   const int tile_n = pr.b_split ? bn / 2 : bn;  // columns of N per tile
   prm.n_tiles = (int)((pr.N + tile_n - 1) / tile_n);
   prm.b_split = pr.b_split ? 1 : 0;

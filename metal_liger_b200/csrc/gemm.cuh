@@ -59,6 +59,14 @@ struct alignas(64) Params {
   int b_split;
   int seg_kb[kMaxSeg];     // k-blocks (of BK) per segment
   int nseg;
+  // m_groups > 1 (1-SM kernel only): independent products stacked along M.
+  // Group g takes m-tiles [grp_mt0[g], grp_mt0[g + 1]) with its own tensor
+  // maps tma_a[g] / tma_b[g] and the K range all groups share; its output
+  // rows start at row grp_row0[g] of D and it has grp_m[g] valid rows.
+  int m_groups;
+  int grp_mt0[kMaxSeg + 1];
+  int grp_row0[kMaxSeg];
+  int grp_m[kMaxSeg];
   int M, N;
   int m_tiles, n_tiles, splits, kb_per_split, kb_total;
   int raster;              // 0: M-tiles fastest, 1: N-tiles fastest
@@ -113,6 +121,12 @@ __device__ __forceinline__ void decode_unit(const Params& p, int unit, int& mt, 
     nt = t / p.m_tiles;
     mt = t - nt * p.m_tiles;
   }
+}
+
+__device__ __forceinline__ int group_of(const Params& p, int mt) {
+  int g = 0;
+  while (g + 1 < p.m_groups && mt >= p.grp_mt0[g + 1]) ++g;
+  return g;
 }
 
 __device__ __forceinline__ void locate_kb(const Params& p, int kb, int& seg, int& kl) {
@@ -540,17 +554,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           }
           inflight = min(inflight + 1, STAGES);
           int seg, kl;
-          locate_kb(p, kb, seg, kl);
+          int a_row = mt * BM;  // M coordinate of the A tile in its tensor
+          if (p.m_groups > 1) {
+            seg = group_of(p, mt);
+            kl = kb;
+            a_row = (mt - p.grp_mt0[seg]) * BM;
+          } else {
+            locate_kb(p, kb, seg, kl);
+          }
           const int kx = kl * BK;
           uint64_t* bar = &full[stage];
           sm100::mbar_arrive_expect_tx(bar, C::STAGE_BYTES);
           uint8_t* a_dst = sA + stage * C::A_BYTES;
           uint8_t* b_dst = sB + stage * C::B_BYTES;
           if constexpr (!A_MN) {
-            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, kx, mt * BM);
+            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, kx, a_row);
           } else {
-            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, mt * BM, kx);
-            sm100::tma_load_2d(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, mt * BM + 64, kx);
+            sm100::tma_load_2d(a_dst, &p.tma_a[seg], bar, a_row, kx);
+            sm100::tma_load_2d(a_dst + 64 * BK * 2, &p.tma_a[seg], bar, a_row + 64, kx);
           }
           if constexpr (!B_MN) {
             if (p.b_split) {
@@ -648,8 +669,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       if (!ok) break;
       sm100::tc_fence_after();
       const uint32_t taddr = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
-      const int64_t row = (int64_t)mt * BM + rloc;
-      const bool row_ok = row < p.M;
+      int64_t row = (int64_t)mt * BM + rloc;
+      bool row_ok = row < p.M;
+      if (p.m_groups > 1) {
+        const int g = group_of(p, mt);
+        const int lr = (mt - p.grp_mt0[g]) * BM + rloc;
+        row = (int64_t)p.grp_row0[g] + lr;
+        row_ok = lr < p.grp_m[g];
+      }
       epilogue_tile<BN>(p, taddr, row, row_ok, nt, sp);
       sm100::tc_fence_before();
       __syncwarp();
@@ -945,6 +972,11 @@ struct Problem {
   // EPI_ARGMAX
   int* part_i = nullptr;
   int logit_dtype = 0;
+  // m_groups > 1: seg[g] is an independent product (A of grp_m[g] rows,
+  // B, one K shared by all groups), stacked along M in D; M = sum grp_m.
+  // Runs on the 1-SM kernel.
+  int m_groups = 1;
+  int64_t grp_m[kMaxSeg] = {};
   // b_split (K-major B, 256-wide tiles): N is the width of each of the two
   // B matrices; tile n holds their rows [128 n, 128 n + 128) side by side
   bool b_split = false;

@@ -322,26 +322,50 @@ size_t skinny_partial_floats(int64_t M, int64_t K) {
   return (size_t)gemm::auto_splits(M, kSlot, K) * (size_t)M * kSlot;
 }
 
-// A^T-style skinny product over the token dimension ([M, 64] fp32), left as
-// the split-K GEMM's partial slabs in `partial` (skinny_partial_floats(M, K)
-// floats) for unpack_k to sum: no reduction launch.
-int gemm_skinny_partials(int64_t M, const gemm::Seg& s, float* partial, Partials* out,
+// One A^T-style skinny product over the token dimension: [M, 64] fp32 from
+// A (MN-major, M columns) and B (MN-major, 64 columns), K = tokens.
+struct Skinny {
+  int64_t M;
+  gemm::Seg s;
+};
+
+// Up to gemm::kMaxSeg skinny products sharing K, stacked along M in ONE
+// grouped split-K GEMM launch and left as its partial slabs in `partial`
+// (skinny_partial_floats(sum M, K) floats) for unpack_k to sum: no reduction
+// launch.  outs[g] locates product g's rows in the slabs.
+int gemm_skinny_partials(std::initializer_list<Skinny> parts, float* partial, Partials* outs,
                          cudaStream_t st) {
   gemm::Problem p;
-  p.M = M;
   p.N = kSlot;
-  p.nseg = 1;
-  p.seg[0] = s;
   p.a_mn = true;
   p.b_mn = true;
   p.epi = gemm::EPI_PARTIAL;
-  p.splits = gemm::auto_splits(M, kSlot, s.K);
+  int g = 0;
+  int64_t total = 0;
+  for (const Skinny& q : parts) {
+    if (g == gemm::kMaxSeg) {
+      set_error("lora: more than %d skinny products in one launch", gemm::kMaxSeg);
+      return ML_ERR_INVALID_ARG;
+    }
+    p.seg[g] = q.s;
+    p.grp_m[g] = q.M;
+    total += q.M;
+    ++g;
+  }
+  p.nseg = g;
+  p.m_groups = g;
+  p.M = total;
+  p.splits = gemm::auto_splits(total, kSlot, p.seg[0].K);
   p.D = partial;
   p.ldd = kSlot;
-  p.split_stride = M * kSlot;
-  out->ptr = partial;
-  out->splits = p.splits;
-  out->split_stride = M * kSlot;
+  p.split_stride = total * kSlot;
+  int64_t row = 0;
+  for (int i = 0; i < g; ++i) {
+    outs[i].ptr = partial + row * kSlot;
+    outs[i].splits = p.splits;
+    outs[i].split_stride = total * kSlot;
+    row += p.grp_m[i];
+  }
   return gemm::launch(p, st);
 }
 
@@ -434,10 +458,9 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   for (int i = 0; i < np; ++i) bt[i] = ar.take<bf16>((size_t)kSlot * pj[i].out_features);
   bf16* acat_s = ar.take<bf16>((size_t)kSlot * H);
   bf16* G = ar.take<bf16>((size_t)T * kSlot);
-  // split-K partial slabs of dA (X^T G) and of each dB (dY_i^T U), summed by unpack_k
-  float* dAp = ar.take<float>(skinny_partial_floats(H, T));
-  float* dBp[3] = {};
-  for (int i = 0; i < np; ++i) dBp[i] = ar.take<float>(skinny_partial_floats(pj[i].out_features, T));
+  // split-K partial slabs of dA (X^T G) and of every dB (dY_i^T U), one
+  // grouped launch, summed by unpack_k
+  float* dABp = ar.take<float>(skinny_partial_floats(H + osum, T));
   const size_t pf = skinny_partial_floats(T, osum);
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
@@ -468,17 +491,23 @@ int qkv_backward(const bf16* x, const bf16* u, int64_t T, int64_t H, int64_t r, 
   // dX = sum_i dY_i W_i + G (s A)   — one accumulator, W read in place (N-major)
   LORA_TRY(gemm_bf16(T, H, xsegs, false, true, dx, H, st));
   // dA_i = s_i (X^T G)[:, slot_i]^T ;  dB_i = s_i dY_i^T U[:, slot_i]
-  Partials pA, pB[3];
-  LORA_TRY(gemm_skinny_partials(H, seg(x, H, G, kSlot, T), dAp, &pA, st));
-  for (int i = 0; i < np; ++i) {
-    const int64_t o = pj[i].out_features;
-    LORA_TRY(gemm_skinny_partials(o, seg(dy[i], o, u, kSlot, T), dBp[i], &pB[i], st));
+  Partials pp[4];  // [0] = dA, [1 + i] = dB_i
+  {
+    const Skinny a{H, seg(x, H, G, kSlot, T)};
+    Skinny b[3];
+    for (int i = 0; i < np; ++i) {
+      const int64_t o = pj[i].out_features;
+      b[i] = {o, seg(dy[i], o, u, kSlot, T)};
+    }
+    if (np == 1) LORA_TRY(gemm_skinny_partials({a, b[0]}, dABp, pp, st));
+    if (np == 2) LORA_TRY(gemm_skinny_partials({a, b[0], b[1]}, dABp, pp, st));
+    if (np == 3) LORA_TRY(gemm_skinny_partials({a, b[0], b[1], b[2]}, dABp, pp, st));
   }
   Unpacker un;
   for (int i = 0; i < np; ++i) {
-    LORA_TRY(un.add(da[i], pj[i].a_dtype, pA, r, H, i * r, pj[i].scaling, true));
-    LORA_TRY(un.add(db[i], pj[i].b_dtype, pB[i], pj[i].out_features, r, i * r, pj[i].scaling,
-                    false));
+    LORA_TRY(un.add(da[i], pj[i].a_dtype, pp[0], r, H, i * r, pj[i].scaling, true));
+    LORA_TRY(un.add(db[i], pj[i].b_dtype, pp[1 + i], pj[i].out_features, r, i * r,
+                    pj[i].scaling, false));
   }
   return un.launch(st);
 }
@@ -569,12 +598,11 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
   bf16* dH = fused ? nullptr : ar.take<bf16>((size_t)T * I);
   bf16* dgate = ar.take<bf16>((size_t)T * I);
   bf16* dup = ar.take<bf16>((size_t)T * I);
-  // split-K partial slabs of the adapter-gradient products, summed by unpack_k
-  float* dAp_d = ar.take<float>(skinny_partial_floats(I, T));   // h^T G_d
-  float* dAp_gu = ar.take<float>(skinny_partial_floats(H, T));  // X^T G_gu
-  float* dBp_d = ar.take<float>(skinny_partial_floats(H, T));   // dY^T U2
-  float* dBp_g = ar.take<float>(skinny_partial_floats(I, T));   // d_gate^T U1
-  float* dBp_u = ar.take<float>(skinny_partial_floats(I, T));   // d_up^T U1
+  // split-K partial slabs of the adapter-gradient products in two grouped
+  // launches, summed by unpack_k: the down adapter's [h^T G_d; dY^T U2] and
+  // the gate/up adapters' [X^T G_gu; d_gate^T U1; d_up^T U1]
+  float* down_p = ar.take<float>(skinny_partial_floats(I + H, T));
+  float* gu_p = ar.take<float>(skinny_partial_floats(H + 2 * I, T));
   const size_t pf = std::max(skinny_partial_floats(T, H), skinny_partial_floats(T, 2 * I));
   float* part = ar.take<float>(pf);
   if (ar.dry) return ML_OK;
@@ -610,9 +638,9 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                        true, dH, I, st));
   }
   // down adapter grads: dA_d = s_d (h^T G_d)^T, dB_d = s_d dY^T U2
-  Partials pAd, pBd, pAgu, pBg, pBu;
-  LORA_TRY(gemm_skinny_partials(I, seg(h, I, Gd, kSlot, T), dAp_d, &pAd, st));
-  LORA_TRY(gemm_skinny_partials(H, seg(dy, H, u2, kSlot, T), dBp_d, &pBd, st));
+  Partials pd[2], pgu[3];  // {dA_d, dB_d}, {dA_gu, dB_g, dB_u}
+  LORA_TRY(gemm_skinny_partials({{I, seg(h, I, Gd, kSlot, T)}, {H, seg(dy, H, u2, kSlot, T)}},
+                                down_p, pd, st));
   // SwiGLU backward (sigmoid recomputed), unless the dH GEMM applied it
   if (!fused) LORA_TRY(ml_swiglu_backward(gate, up, dH, dgate, dup, T * I, ML_DTYPE_BF16, st));
   // G_gu = [d_gate Bg | d_up Bu]
@@ -623,16 +651,17 @@ int mlp_backward(const bf16* x, const bf16* gate, const bf16* up, const bf16* h,
                       seg(Ggu, kSlot, acs, H, kSlot)},
                      false, true, dx, H, st));
   // gate/up adapter grads
-  LORA_TRY(gemm_skinny_partials(H, seg(x, H, Ggu, kSlot, T), dAp_gu, &pAgu, st));
-  LORA_TRY(gemm_skinny_partials(I, seg(dgate, I, u1, kSlot, T), dBp_g, &pBg, st));
-  LORA_TRY(gemm_skinny_partials(I, seg(dup, I, u1, kSlot, T), dBp_u, &pBu, st));
+  LORA_TRY(gemm_skinny_partials({{H, seg(x, H, Ggu, kSlot, T)},
+                                 {I, seg(dgate, I, u1, kSlot, T)},
+                                 {I, seg(dup, I, u1, kSlot, T)}},
+                                gu_p, pgu, st));
   Unpacker un;
-  LORA_TRY(un.add(da[2], pj[2].a_dtype, pAd, r, I, 0, pj[2].scaling, true));
-  LORA_TRY(un.add(db[2], pj[2].b_dtype, pBd, H, r, 0, pj[2].scaling, false));
-  LORA_TRY(un.add(da[0], pj[0].a_dtype, pAgu, r, H, 0, pj[0].scaling, true));
-  LORA_TRY(un.add(da[1], pj[1].a_dtype, pAgu, r, H, r, pj[1].scaling, true));
-  LORA_TRY(un.add(db[0], pj[0].b_dtype, pBg, I, r, 0, pj[0].scaling, false));
-  LORA_TRY(un.add(db[1], pj[1].b_dtype, pBu, I, r, r, pj[1].scaling, false));
+  LORA_TRY(un.add(da[2], pj[2].a_dtype, pd[0], r, I, 0, pj[2].scaling, true));
+  LORA_TRY(un.add(db[2], pj[2].b_dtype, pd[1], H, r, 0, pj[2].scaling, false));
+  LORA_TRY(un.add(da[0], pj[0].a_dtype, pgu[0], r, H, 0, pj[0].scaling, true));
+  LORA_TRY(un.add(da[1], pj[1].a_dtype, pgu[0], r, H, r, pj[1].scaling, true));
+  LORA_TRY(un.add(db[0], pj[0].b_dtype, pgu[1], I, r, 0, pj[0].scaling, false));
+  LORA_TRY(un.add(db[1], pj[1].b_dtype, pgu[2], I, r, r, pj[1].scaling, false));
   return un.launch(st);
 }
 
