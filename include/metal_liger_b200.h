@@ -93,6 +93,17 @@ ML_API int ml_rms_norm_backward(const void* x, int x_dtype, const void* weight, 
                          int64_t rows, int64_t hidden, void* stream);
 
 /*
+ * Process-wide override of the RMSNorm backward's row layout: every row is
+ * split over threads holding nv 16-byte vectors each (1 = one vector per
+ * thread, streamed through a shared-memory ring; 2, 4, 8 = register rows),
+ * where the split fits a CTA; 0 (the default) uses the measured choice per
+ * shape.  Results are identical up to the order of the row reduction.  The
+ * previous setting is stored to *previous when non-NULL.  A tuning and test
+ * knob with no reference counterpart.
+ */
+ML_API int ml_rms_norm_set_bwd_vectors(int nv, int* previous);
+
+/*
  * Allocation-free ml_rms_norm_backward: same arguments and results, minus the
  * workspace.  It has no counterpart in the reference; it exists for callers
  * that cannot allocate device memory at call time -- hosts whose memory

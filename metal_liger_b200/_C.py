@@ -89,6 +89,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ml_gemm_set_cta_pair": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_lora_set_mlp_swiglu_fusion": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_gemm_set_reserved_sms": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "ml_rms_norm_set_bwd_vectors": (c_int, [c_int, ctypes.POINTER(c_int)]),
     "ml_selftest_bounded_wait": (c_int, [c_int64, c_void_p]),
     "ml_lm_head_argmax_workspace_bytes": (c_size_t, [c_int64, c_int64]),
     "ml_gemv_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int64,

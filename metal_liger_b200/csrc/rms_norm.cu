@@ -15,6 +15,7 @@
 #include "common.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 namespace ml {
@@ -653,6 +654,10 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
   return ML_OK;
 }
 
+// Process-wide override of the backward's vectors per thread (0 = measured
+// default; ml_rms_norm_set_bwd_vectors, a tuning and test knob).
+std::atomic<int> g_bwd_nv{0};
+
 template <typename TX, typename TW>
 int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, void* dx, void* dw,
                float eps, float* partial, size_t partial_bytes, int64_t rows, int64_t hidden,
@@ -662,6 +667,18 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
   const TX* gp = static_cast<const TX*>(dy);
   TX* dxp = static_cast<TX*>(dx);
   RowCfg cfg = pick_cfg<TX>(hidden, x, dy, dx, x, true);
+  const int force_nv = g_bwd_nv.load(std::memory_order_relaxed);
+  if (force_nv > 0 && cfg.vec) {
+    // the same row split with the vectors per thread forced (rows whose split
+    // does not fit a CTA keep the default)
+    const int64_t nvec = hidden / (16 / (int64_t)sizeof(TX));
+    const int64_t per = (nvec + force_nv - 1) / force_nv;
+    const int64_t tpr = per <= 4 ? 4 : per <= 8 ? 8 : per <= 16 ? 16 : (per + 31) / 32 * 32;
+    if (tpr <= (force_nv == 1 ? 512 : kMaxThreads)) {
+      cfg.nv = force_nv;
+      cfg.tpr = (int)tpr;
+    }
+  }
   if (cfg.vec)
     cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8,
                                       bwd_max_threads<TX>(cfg.nv) / cfg.tpr));
@@ -825,6 +842,14 @@ extern "C" int ml_rms_norm_forward(const void* x, int x_dtype, const void* weigh
 extern "C" size_t ml_rms_norm_backward_workspace_bytes(int64_t rows, int64_t hidden) {
   if (rows <= 0 || hidden <= 0) return 0;
   return (size_t)bwd_grid_upper_bound(rows) * (size_t)hidden * sizeof(float);
+}
+
+extern "C" int ml_rms_norm_set_bwd_vectors(int nv, int* previous) {
+  ML_CHECK_ARG(nv == 0 || nv == 1 || nv == 2 || nv == 4 || nv == 8,
+               "rms_norm_set_bwd_vectors: nv must be 0, 1, 2, 4 or 8");
+  const int old = g_bwd_nv.exchange(nv);
+  if (previous) *previous = old;
+  return ML_OK;
 }
 
 extern "C" int ml_rms_norm_backward(const void* x, int x_dtype, const void* weight, int w_dtype,
