@@ -46,6 +46,7 @@ def all_reduce_gradients(params: Iterable[torch.nn.Parameter], group=None,
     dist.all_reduce(flat, group=group)
     if average and world > 1:
         flat.div_(world)
-    for g, red in zip(grads, torch._utils._unflatten_dense_tensors(flat, grads)):
-        g.copy_(red)
+    # one multi-tensor copy back (a copy per parameter would be ~500 launches
+    # for a LoRA-adapted 36-layer model)
+    torch._foreach_copy_(grads, list(torch._utils._unflatten_dense_tensors(flat, grads)))
     return int(flat.numel())
