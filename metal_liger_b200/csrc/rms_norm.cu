@@ -417,43 +417,60 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   }
 }
 
-// Backward, ring-prefetch variant (NV = 1): x, dY and the saved rrms of the
-// next S - 1 rows stream into shared memory while the current row is reduced.
-// Dynamic shared memory: [groups][S][tpr] x vectors, the same for dY,
-// [groups][S][tpr] rrms words, then the [groups][hidden] dweight fold.
-template <typename TX, typename TW, int S>
-__global__ void __launch_bounds__(512)
+// Backward, ring-prefetch variant: x, dY and the saved rrms of the next
+// S - 1 rows stream into shared memory while the current row is reduced; a
+// thread owns NV 16-byte vectors of the row (vector i at columns
+// (i * tpr + t) * VEC: each vector of the row is contiguous over the
+// threads).  Dynamic shared memory: [groups][S][NV][tpr] x vectors, the
+// same for dY, [groups][S][tpr] rrms words, and the [groups][hidden]
+// dweight fold — after the ring when NV = 1, over the ring's own memory
+// (free once the last row is read) when NV > 1.  NV = 2 lets a 16-bit row of
+// 4096 run on 256 threads, so three rows are reduced at once per SM where
+// one vector per thread (512 threads per row) fits two.
+template <typename TX, typename TW, int S, int NV>
+__global__ void __launch_bounds__(NV == 1 ? 512 : 768)
 rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __restrict__ rrms,
              const TX* __restrict__ dy, TX* __restrict__ dx, float* __restrict__ partial,
              int64_t rows, int64_t hidden, float eps, int tpr, int groups) {
   constexpr int VEC = 16 / sizeof(TX);
+  constexpr bool kFoldOverRing = NV > 1;
   __shared__ float red[2][32][2];
   extern __shared__ __align__(16) uint8_t ring_raw[];
   const int g = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
   const int nthreads = tpr * groups;
-  Vec16<TX>* ringx = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)g * S * tpr;
-  Vec16<TX>* ringg = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)(groups + g) * S * tpr;
+  Vec16<TX>* ringx = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)g * S * NV * tpr;
+  Vec16<TX>* ringg = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)(groups + g) * S * NV * tpr;
   float* ringr = reinterpret_cast<float*>(reinterpret_cast<Vec16<TX>*>(ring_raw) +
-                                          (size_t)2 * groups * S * tpr) +
+                                          (size_t)2 * groups * S * NV * tpr) +
                  (size_t)g * S * tpr;
-  float* fold = reinterpret_cast<float*>(ring_raw + (size_t)2 * groups * S * tpr * 16 +
-                                         (size_t)groups * S * tpr * 4);
-  const int64_t col = (int64_t)t * VEC;
-  const bool has_col = col < hidden;
-  float wr[VEC], acc[VEC];
-  load_weight<TW, VEC>(w, col, hidden, wr);
+  float* fold = kFoldOverRing
+                    ? reinterpret_cast<float*>(ring_raw)
+                    : reinterpret_cast<float*>(ring_raw + (size_t)2 * groups * S * NV * tpr * 16 +
+                                               (size_t)groups * S * tpr * 4);
+  int64_t colv[NV];
+  bool hasv[NV];
+  float wr[NV][VEC], acc[NV][VEC];
 #pragma unroll
-  for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+  for (int i = 0; i < NV; ++i) {
+    colv[i] = (int64_t)(i * tpr + t) * VEC;
+    hasv[i] = colv[i] < hidden;
+    load_weight<TW, VEC>(w, colv[i], hidden, wr[i]);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[i][j] = 0.f;
+  }
   const int64_t row_stride = (int64_t)gridDim.x * groups;
   const int64_t niter = (rows + row_stride - 1) / row_stride;
   const float inv_h = 1.f / (float)hidden;
   const int64_t row0 = (int64_t)blockIdx.x * groups + g;
   auto issue = [&](int64_t r, int slot) {
     if (r < rows) {
-      if (has_col) {
-        cp_async16(&ringx[slot * tpr + t], x + r * hidden + col);
-        cp_async16(&ringg[slot * tpr + t], dy + r * hidden + col);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if (hasv[i]) {
+          cp_async16(&ringx[(slot * NV + i) * tpr + t], x + r * hidden + colv[i]);
+          cp_async16(&ringg[(slot * NV + i) * tpr + t], dy + r * hidden + colv[i]);
+        }
       }
       if (rrms != nullptr) cp_async4(&ringr[slot * tpr + t], rrms + r);
     }
@@ -467,17 +484,21 @@ rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __
     issue(row + (S - 1) * row_stride, (int)((it + S - 1) % S));
     cp_async_wait<S - 1>();
     const int slot = (int)(it % S);
-    const bool active = row < rows && has_col;
-    Vec16<TX> xv, gv;
+    const bool active = row < rows;
+    Vec16<TX> xv[NV], gv[NV];
     float ss = 0.f, gwx = 0.f;
     if (active) {
-      xv = ringx[slot * tpr + t];
-      gv = ringg[slot * tpr + t];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float xf = to_f32(xv.v[j]);
-        ss = fmaf(xf, xf, ss);
-        gwx = fmaf(to_f32(gv.v[j]) * wr[j], xf, gwx);
+      for (int i = 0; i < NV; ++i) {
+        if (!hasv[i]) continue;
+        xv[i] = ringx[(slot * NV + i) * tpr + t];
+        gv[i] = ringg[(slot * NV + i) * tpr + t];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = to_f32(xv[i].v[j]);
+          ss = fmaf(xf, xf, ss);
+          gwx = fmaf(to_f32(gv[i].v[j]) * wr[i][j], xf, gwx);
+        }
       }
     }
     const float2 sums = group_sum2(ss, gwx, red, buf, tpr);
@@ -485,24 +506,31 @@ rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __
     if (active) {
       const float r = rrms != nullptr ? ringr[slot * tpr + t] : rsqrtf(fmaf(sums.x, inv_h, eps));
       const float c = (sums.y * inv_h) * (r * r * r);
-      Vec16<TX> o;
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float xf = to_f32(xv.v[j]);
-        const float gf = to_f32(gv.v[j]);
-        o.v[j] = from_f32<TX>((gf * wr[j]) * r - xf * c);
-        acc[j] = fmaf(gf, xf * r, acc[j]);
+      for (int i = 0; i < NV; ++i) {
+        if (!hasv[i]) continue;
+        Vec16<TX> o;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float xf = to_f32(xv[i].v[j]);
+          const float gf = to_f32(gv[i].v[j]);
+          o.v[j] = from_f32<TX>((gf * wr[i][j]) * r - xf * c);
+          acc[i][j] = fmaf(gf, xf * r, acc[i][j]);
+        }
+        st_vec_stream(dx + row * hidden + colv[i], o);
       }
-      st_vec_stream(dx + row * hidden + col, o);
     }
   }
   cp_async_wait<0>();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (kFoldOverRing) __syncthreads();  // every group is done with the ring
   // Fold the row groups' partials (fixed order) and store one row per CTA.
-  if (has_col) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (!hasv[i]) continue;
 #pragma unroll
     for (int j = 0; j < VEC; ++j)
-      if (col + j < hidden) fold[(int64_t)g * hidden + col + j] = acc[j];
+      if (colv[i] + j < hidden) fold[(int64_t)g * hidden + colv[i] + j] = acc[i][j];
   }
   __syncthreads();
   for (int64_t c = threadIdx.x; c < hidden; c += nthreads) {
@@ -684,7 +712,34 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
                                       bwd_max_threads<TX>(cfg.nv) / cfg.tpr));
   int grid = 0;
   const int64_t max_parts = static_cast<int64_t>(partial_bytes / (sizeof(float) * (size_t)hidden));
-  if (cfg.vec && cfg.nv == 1) {
+  // 16-bit rows of 257-512 vectors (hidden 2056-4096): the ring with two
+  // vectors per thread, three row groups of 256 threads per CTA, one CTA
+  // per SM (the layout knob still selects the others).
+  const bool ring2 = cfg.vec && force_nv == 0 && sizeof(TX) == 2 && cfg.nv == 1 &&
+                     cfg.tpr > 256 && cfg.tpr <= 512;
+  if (ring2) {
+    constexpr int S = 4, NV = 2, kGroups = 3;
+    cfg.nv = NV;
+    cfg.tpr = 256;
+    cfg.groups = kGroups;
+    const size_t ring_bytes = (size_t)kGroups * S * cfg.tpr * (2 * NV * 16 + 4);
+    const size_t smem = std::max(ring_bytes, (size_t)kGroups * hidden * sizeof(float));
+    const int threads = cfg.tpr * cfg.groups;
+    auto k = rms_bwd_ring<TX, TW, S, NV>;
+    static PerDevice<cudaError_t> attr;
+    ML_CHECK_CUDA(attr.get([&] {
+                    return cudaFuncSetAttribute(
+                        (const void*)k, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+                  }),
+                  "rms_norm_backward: smem attribute");
+    const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
+    const int per_sm = std::min<int>(
+        kBwdCtasPerSm, occupancy_grid((const void*)k, threads, smem, 1 << 30) / num_sms());
+    grid = static_cast<int>(balanced_grid(
+        work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));
+    k<<<grid, threads, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps, cfg.tpr,
+                                   cfg.groups);
+  } else if (cfg.vec && cfg.nv == 1) {
     constexpr int S = 4;
     cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8, 512 / cfg.tpr));
     size_t smem = (size_t)cfg.groups * S * cfg.tpr * (2 * 16 + 4) +
@@ -695,7 +750,7 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
              (size_t)cfg.groups * hidden * sizeof(float);
     }
     const int threads = cfg.tpr * cfg.groups;
-    auto k = rms_bwd_ring<TX, TW, S>;
+    auto k = rms_bwd_ring<TX, TW, S, 1>;
     static PerDevice<cudaError_t> attr;
     ML_CHECK_CUDA(attr.get([&] {
                     return cudaFuncSetAttribute(

@@ -146,6 +146,22 @@ def test_large_square(pair_mode):
     assert_close(d, ref, dtype=torch.bfloat16, norm_rtol=5e-3, what="4096^3 D")
 
 
+@pytest.mark.parametrize("reserve", [16, 100])
+def test_reserved_sms_give_the_same_result(reserve, pair_mode):
+    """A GEMM launched while SMs are reserved for other streams
+    (ml_gemm_set_reserved_sms) runs on a smaller persistent grid and writes
+    exactly the same D; the setting is restored afterwards."""
+    m, n, k = 1024, 768, 512
+    a, b = rand(m, k, seed=21), rand(n, k, seed=22)
+    d0, _ = run_gemm([(a, b)], m, n)
+    with _C.gemm_reserved_sms(reserve):
+        d1, _ = run_gemm([(a, b)], m, n)
+    assert torch.equal(d0, d1)
+    prev = ctypes.c_int(-1)
+    _C.call("ml_gemm_set_reserved_sms", 0, ctypes.byref(prev))
+    assert prev.value == 0
+
+
 def test_bad_arguments_rejected():
     lib = _C.load()
     arr = (_C.GemmSegment * 1)()

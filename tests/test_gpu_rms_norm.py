@@ -171,3 +171,31 @@ def test_metal_liger_ext_mirror():
     assert_close(rc.cpu(), rr, rtol=1e-5, atol=1e-6, what="ext rrms")
     assert_close(dx.cpu(), rdx, rtol=1e-5, atol=1e-5, what="ext dx")
     assert_close(dw.cpu(), rdw, rtol=1e-5, atol=1e-5, what="ext dw")
+
+
+@pytest.mark.parametrize("rows,h,dtype", [(4096, 4096, torch.bfloat16), (1000, 128, torch.bfloat16),
+                                         (8192, 2048, torch.float32), (513, 1000, torch.float32)])
+def test_backward_layouts_agree(rows, h, dtype):
+    """Every row layout the backward can be forced to (ml_rms_norm_set_bwd_vectors:
+    1, 2, 4 or 8 vectors per thread, where the split fits a CTA) gives the
+    default layout's dX and dW up to the order of the row reductions."""
+    from metal_liger_b200 import _C
+
+    g = torch.Generator(device=DEV).manual_seed(rows + h)
+    x = torch.randn(rows, h, generator=g, device=DEV).to(dtype)
+    w = (1 + 0.1 * torch.randn(h, generator=g, device=DEV)).to(dtype)
+    dy = torch.randn(rows, h, generator=g, device=DEV).to(dtype)
+    ops = torch.ops.metal_liger
+    _, rr = ops.rms_norm_forward(x, w, 1e-6, "")
+    ref = ops.rms_norm_backward(x, w, dy, 1e-6, "", rr)
+    rtol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    try:
+        for nv in (1, 2, 4, 8):
+            _C.call("ml_rms_norm_set_bwd_vectors", nv, None)
+            got = ops.rms_norm_backward(x, w, dy, 1e-6, "", rr)
+            torch.cuda.synchronize()
+            for a, b in zip(got, ref):
+                assert torch.allclose(a.float(), b.float(), rtol=rtol,
+                                      atol=rtol * b.float().abs().max().item()), nv
+    finally:
+        _C.call("ml_rms_norm_set_bwd_vectors", 0, None)
