@@ -529,13 +529,14 @@ class Flce:
             self.per_rank_tokens = False
         # count, (logits GEMM, lse, transform, dX GEMM, dW GEMM, memset) per chunk, loss;
         # backward: two scale-casts
-        self.launches_per_step = 1 + 5 * (self.N // self.CHUNK) + 1 + 2
+        self.launches_per_step = 1 + 5 * (-(-self.N // self.CHUNK)) + 1 + 2
 
     def config(self):
         par = ("single GPU" if self.world == 1 else
                f"vocab-parallel over {self.world} GPUs (lm_head rows sharded; per-chunk NCCL "
                f"all-reduce of row max / sum-exp / target logit and of partial dX)")
-        return {"workload": "flce_bf16 (BASELINE configs[2]): hidden [16384,2048] ~N(0,1), "
+        base = "BASELINE configs[2]" if self.N == 16384 else "smaller than BASELINE configs[2]"
+        return {"workload": f"flce_bf16 ({base}): hidden [{self.N},2048] ~N(0,1), "
                             "lm_head W [151936,2048] ~N(0,0.02), 10% labels = -100, token "
                             f"chunk {self.CHUNK}, mean over non-ignored; loss + dX + dW",
                 "tokens_per_step": self.N, "hidden": self.H, "vocab": self.V,
@@ -1871,6 +1872,9 @@ def main(argv=None):
     ap.add_argument("--lora-tokens", type=int, default=None,
                     help="token rows of the lora workload (default: BASELINE's 16,384); a "
                          "smaller case for profiler captures")
+    ap.add_argument("--flce-tokens", type=int, default=None,
+                    help="token rows of the flce workload (default: BASELINE's 16,384); a "
+                         "smaller case for profiler captures")
     ap.add_argument("--flce-chunk", type=int, default=None,
                     help="FLCE token-chunk length (default: BASELINE's 8192; smaller chunks "
                          "bound the exponentials buffer, chunk x vocab bf16)")
@@ -1879,6 +1883,8 @@ def main(argv=None):
         Flce.CHUNK = int(args.flce_chunk)
     if args.lora_tokens:
         Lora.T = int(args.lora_tokens)
+    if args.flce_tokens:
+        Flce.N = int(args.flce_tokens)
     if args.lora_swiglu_fusion is not None and args.impl != "reference":
         from metal_liger_b200 import _C
 

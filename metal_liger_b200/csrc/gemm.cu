@@ -94,8 +94,7 @@ int launch_t(const Params& prm, int grid, cudaStream_t st) {
     set_error("gemm: cudaFuncSetAttribute failed: %s", cudaGetErrorString(attr_err));
     return ML_ERR_CUDA;
   }
-  k<<<grid, kThreads, smem, st>>>(prm);
-  ML_CHECK_LAUNCH("gemm_kernel");
+  ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(kThreads), smem, st, prm), "gemm_kernel");
   return ML_OK;
 }
 
@@ -137,8 +136,7 @@ int launch_pair_t(const Params& prm, int64_t units, int max_ctas, cudaStream_t s
   int64_t pairs = std::min<int64_t>(units, resident_pairs);
   if (max_ctas > 0) pairs = std::min<int64_t>(pairs, max_ctas / 2);
   const int grid = 2 * (int)std::max<int64_t>(pairs, 1);
-  k<<<grid, kThreads, smem, st>>>(prm);
-  ML_CHECK_LAUNCH("gemm_pair_kernel");
+  ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(kThreads), smem, st, prm), "gemm_pair_kernel");
   return ML_OK;
 }
 
@@ -401,8 +399,10 @@ namespace {
 __global__ void splitk_reduce(const float* __restrict__ part, int splits, int64_t M, int64_t N,
                               int64_t ldp, void* __restrict__ D, int64_t ldd, int d_f32,
                               float beta) {
-  // Launched as a programmatic dependent of the GEMM that wrote `part`.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Launched as a programmatic dependent of the GEMM that wrote `part`; the
+  // next programmatic dependent may start launching once this wait returns.
+  pdl_wait();
+  pdl_release();
   const int64_t total = M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {

@@ -534,6 +534,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
   sm100::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_units = p.m_tiles * p.n_tiles * p.splits;
+  // Launched as a programmatic dependent: the set-up above overlaps the
+  // previous kernel's tail; no operand, output or FLCE statistic is touched
+  // before that kernel has completed.
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------ producer ------------------------------
@@ -776,6 +780,7 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
   const int num_units = p.m_tiles * p.n_tiles * p.splits;
   const int cluster_id = blockIdx.x >> 1;
   const int nclusters = gridDim.x >> 1;
+  pdl_wait();  // programmatic dependent (see gemm_kernel)
 
   if (warp == 0) {
     // --------------------------- producer (both CTAs) ------------------------

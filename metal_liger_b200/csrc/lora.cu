@@ -91,6 +91,8 @@ struct Assembly {
 // width is a multiple of 8), written as one 16-byte store; 32-bit index math
 // (the host checks the total fits).
 __global__ void __launch_bounds__(256) assemble_k(const __grid_constant__ Assembly a) {
+  pdl_wait();  // a programmatic dependent: the pieces may come from the previous kernel
+  pdl_release();
   const int e8 = blockIdx.x * blockDim.x + threadIdx.x;  // index of an 8-element chunk
   if (e8 >= (int)(a.start[a.nops] >> 3)) return;
   const int e = e8 << 3;
@@ -145,6 +147,8 @@ struct Unpacks {
 };
 
 __global__ void unpack_k(const __grid_constant__ Unpacks u) {
+  pdl_wait();  // a programmatic dependent: the slabs come from the previous GEMM
+  pdl_release();
   const int64_t total = u.start[u.n];
   for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
        e += (int64_t)gridDim.x * blockDim.x) {
@@ -230,8 +234,9 @@ struct Assembler {
         return ML_ERR_INVALID_ARG;
       }
     const int64_t chunks = n / 8;
-    assemble_k<<<(unsigned)((chunks + 255) / 256), 256, 0, st>>>(a);
-    ML_CHECK_LAUNCH("lora: assemble rank operands");
+    ML_CHECK_CUDA(launch_pdl(assemble_k, dim3((unsigned)((chunks + 255) / 256)), dim3(256), 0,
+                             st, a),
+                  "lora: assemble rank operands");
     return ML_OK;
   }
 };
@@ -270,8 +275,8 @@ struct Unpacker {
   int launch(cudaStream_t st) {
     const int64_t n = u.start[u.n];
     if (n == 0) return ML_OK;
-    unpack_k<<<egrid(n), 256, 0, st>>>(u);
-    ML_CHECK_LAUNCH("lora: scatter adapter gradients");
+    ML_CHECK_CUDA(launch_pdl(unpack_k, dim3(egrid(n)), dim3(256), 0, st, u),
+                  "lora: scatter adapter gradients");
     return ML_OK;
   }
 };

@@ -131,6 +131,9 @@ rms_fwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__
   __shared__ float red[2][32][2];
   const int g = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
+  // launched as a programmatic dependent: x and w may come from the previous kernel
+  pdl_wait();
+  pdl_release();
   float wr[NV][VEC];
 #pragma unroll
   for (int i = 0; i < NV; ++i) load_weight<TW, VEC>(w, (int64_t)(i * tpr + t) * VEC, hidden, wr[i]);
@@ -228,6 +231,8 @@ rms_fwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict_
   Vec16<TX>* ring = reinterpret_cast<Vec16<TX>*>(ring_raw) + (size_t)g * S * tpr;
   const int64_t col = (int64_t)t * VEC;
   const bool has_col = col < hidden;
+  pdl_wait();
+  pdl_release();
   float wr[VEC];
   load_weight<TW, VEC>(w, col, hidden, wr);
   const int64_t row_stride = (int64_t)gridDim.x * groups;
@@ -279,6 +284,8 @@ __global__ void __launch_bounds__(256)
 rms_fwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, TX* __restrict__ y,
                 float* __restrict__ rrms, int64_t rows, int64_t hidden, float eps) {
   __shared__ float red[2][32][2];
+  pdl_wait();
+  pdl_release();
   int buf = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const TX* xr = x + row * hidden;
@@ -310,6 +317,9 @@ rms_bwd_vec(const TX* __restrict__ x, const TW* __restrict__ w, const float* __r
   extern __shared__ float fold[];  // [groups][hidden] when groups > 1
   const int g = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
+  // launched as a programmatic dependent: every input, and the partials the
+  // previous call's reduction reads, belong to earlier kernels until this wait
+  pdl_wait();
   float wr[NV][VEC];
   float acc[NV][VEC];
 #pragma unroll
@@ -448,6 +458,7 @@ rms_bwd_ring(const TX* __restrict__ x, const TW* __restrict__ w, const float* __
                     ? reinterpret_cast<float*>(ring_raw)
                     : reinterpret_cast<float*>(ring_raw + (size_t)2 * groups * S * NV * tpr * 16 +
                                                (size_t)groups * S * tpr * 4);
+  pdl_wait();  // programmatic dependent (see rms_bwd_vec)
   int64_t colv[NV];
   bool hasv[NV];
   float wr[NV][VEC], acc[NV][VEC];
@@ -549,6 +560,7 @@ rms_bwd_generic(const TX* __restrict__ x, const TW* __restrict__ w, const float*
   // Per-CTA dweight partial lives directly in `partial` (this CTA's row):
   // each column is owned by exactly one thread, so no races.
   float* prow = partial + (int64_t)blockIdx.x * hidden;
+  pdl_wait();  // programmatic dependent (see rms_bwd_vec)
   for (int64_t c = threadIdx.x; c < hidden; c += blockDim.x) prow[c] = 0.f;
   int buf = 0;
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -655,7 +667,9 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
                   "rms_norm_forward: smem attribute");
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
     const int grid = (int)balanced_grid(work, occupancy_grid((const void*)k, threads, smem, work));
-    k<<<grid, threads, smem, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups);
+    ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(threads), smem, st, xp, wp, yp, rrms, rows,
+                             hidden, eps, cfg.tpr, cfg.groups),
+                  "rms_norm_forward");
   } else if (cfg.vec) {
     const int threads = cfg.tpr * cfg.groups;
     const int64_t work = (rows + cfg.groups - 1) / cfg.groups;
@@ -663,7 +677,9 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
   case NV_: {                                                                              \
     auto k = rms_fwd_vec<TX, TW, NV_>;                                                     \
     int grid = (int)balanced_grid(work, occupancy_grid((const void*)k, threads, 0, work)); \
-    k<<<grid, threads, 0, st>>>(xp, wp, yp, rrms, rows, hidden, eps, cfg.tpr, cfg.groups); \
+    ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(threads), 0, st, xp, wp, yp, rrms, rows, \
+                             hidden, eps, cfg.tpr, cfg.groups),                          \
+                  "rms_norm_forward");                                                   \
     break;                                                                                 \
   }
     switch (cfg.nv) {
@@ -676,7 +692,9 @@ int launch_fwd(const void* x, const void* w, void* y, float* rrms, int64_t rows,
 #undef ML_FWD_CASE
   } else {
     int grid = static_cast<int>(std::min<int64_t>(rows, (int64_t)num_sms() * kGenericGrid));
-    rms_fwd_generic<TX, TW><<<std::max(grid, 1), 256, 0, st>>>(xp, wp, yp, rrms, rows, hidden, eps);
+    ML_CHECK_CUDA(launch_pdl(rms_fwd_generic<TX, TW>, dim3(std::max(grid, 1)), dim3(256), 0, st,
+                             xp, wp, yp, rrms, rows, hidden, eps),
+                  "rms_norm_forward");
   }
   ML_CHECK_LAUNCH("rms_norm_forward");
   return ML_OK;
@@ -737,8 +755,9 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
         kBwdCtasPerSm, occupancy_grid((const void*)k, threads, smem, 1 << 30) / num_sms());
     grid = static_cast<int>(balanced_grid(
         work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));
-    k<<<grid, threads, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps, cfg.tpr,
-                                   cfg.groups);
+    ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(threads), smem, st, xp, wp, rrms, gp, dxp,
+                             partial, rows, hidden, eps, cfg.tpr, cfg.groups),
+                  "rms_norm_backward");
   } else if (cfg.vec && cfg.nv == 1) {
     constexpr int S = 4;
     cfg.groups = std::max(1, std::min(cfg.tpr < 32 ? 32 : 8, 512 / cfg.tpr));
@@ -762,8 +781,9 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
         kBwdCtasPerSm, occupancy_grid((const void*)k, threads, smem, 1 << 30) / num_sms());
     grid = static_cast<int>(balanced_grid(
         work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));
-    k<<<grid, threads, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps, cfg.tpr,
-                                   cfg.groups);
+    ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(threads), smem, st, xp, wp, rrms, gp, dxp,
+                             partial, rows, hidden, eps, cfg.tpr, cfg.groups),
+                  "rms_norm_backward");
   } else if (cfg.vec) {
     const int threads = cfg.tpr * cfg.groups;
     size_t smem = cfg.groups > 1 ? (size_t)cfg.groups * hidden * sizeof(float) : 0;
@@ -786,8 +806,9 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
         kBwdCtasPerSm, occupancy_grid((const void*)k, threads_eff, smem, 1 << 30) / num_sms()); \
     grid = static_cast<int>(balanced_grid(                                                   \
         work, std::min<int64_t>((int64_t)num_sms() * std::max(per_sm, 1), max_parts)));      \
-    k<<<grid, threads_eff, smem, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps,    \
-                                       cfg.tpr, cfg.groups);                                 \
+    ML_CHECK_CUDA(launch_pdl(k, dim3(grid), dim3(threads_eff), smem, st, xp, wp, rrms, gp,  \
+                             dxp, partial, rows, hidden, eps, cfg.tpr, cfg.groups),          \
+                  "rms_norm_backward");                                                      \
     break;                                                                                   \
   }
     switch (cfg.nv) {
@@ -802,7 +823,9 @@ int launch_bwd(const void* x, const void* w, const float* rrms, const void* dy, 
     grid = static_cast<int>(std::min<int64_t>(
         std::min<int64_t>(rows, (int64_t)num_sms() * kGenericGrid), max_parts));
     grid = std::max(grid, 1);
-    rms_bwd_generic<TX, TW><<<grid, 256, 0, st>>>(xp, wp, rrms, gp, dxp, partial, rows, hidden, eps);
+    ML_CHECK_CUDA(launch_pdl(rms_bwd_generic<TX, TW>, dim3(grid), dim3(256), 0, st, xp, wp, rrms,
+                             gp, dxp, partial, rows, hidden, eps),
+                  "rms_norm_backward");
   }
   ML_CHECK_LAUNCH("rms_norm_backward");
   // Programmatic dependent launch: the reduction's launch overlaps the tail
