@@ -195,36 +195,64 @@ class CopyPipeline:
     chunk i+1, the compute of chunk i and the D2H of chunk i-1 run together
     (PCIe is full duplex).  Device input buffers are reused across steps: the
     H2D of a chunk waits until the previous step's compute of that chunk has
-    finished reading it.  The caller's stream waits for all three streams at
-    the end, so events recorded on it bracket the whole step."""
+    finished reading it.  Consecutive steps are not joined, so the next step's
+    uploads run while this step's last downloads drain, as behind a
+    prefetching data loader; join() makes the caller's stream wait for all
+    three streams, so events recorded on it after join() bracket every step
+    issued before it.  The host runs at most `depth` steps ahead of the
+    device (it waits for the step `depth` back before issuing another), so
+    the caching allocator recycles the outputs of finished steps instead of
+    growing, and blocking, while the host races ahead.  With `slots` > 1 the
+    caller keeps that many sets of device input buffers and uses set
+    `self.slot` in a step, so a step's uploads also overlap the previous
+    step's compute (one-chunk steps whose inputs are all needed up front)."""
 
-    def __init__(self, device, nchunks):
+    def __init__(self, device, nchunks, depth=2, slots=1):
         self.nchunks = nchunks
+        self.depth = depth
+        self.slots = slots
+        self.slot = 0
+        self.steps = 0
         self.h2d = torch.cuda.Stream(device)
         self.comp = torch.cuda.Stream(device)
         self.d2h = torch.cuda.Stream(device)
-        self.freed = [None] * nchunks
+        self.freed = [[None] * nchunks for _ in range(slots)]
+        self.issued = []  # completion events of the steps in flight
 
     def run(self, load, compute, store):
+        while len(self.issued) >= self.depth:
+            self.issued.pop(0).synchronize()
+        self.slot = self.steps % self.slots
+        self.steps += 1
+        freed = self.freed[self.slot]
         main = torch.cuda.current_stream()
         start = main.record_event()
         for s in (self.h2d, self.comp, self.d2h):
             s.wait_event(start)
         for i in range(self.nchunks):
             with torch.cuda.stream(self.h2d):
-                if self.freed[i] is not None:
-                    self.h2d.wait_event(self.freed[i])
+                # chunk 0 may also reload buffers every chunk of a step reads
+                # (a weight): it waits for the last compute that read this
+                # buffer set
+                wait = freed[self.nchunks - 1] if i == 0 else freed[i]
+                if wait is not None:
+                    self.h2d.wait_event(wait)
                 load(i)
                 arrived = self.h2d.record_event()
             with torch.cuda.stream(self.comp):
                 self.comp.wait_event(arrived)
                 outs = compute(i)
                 done = self.comp.record_event()
-                self.freed[i] = done
+                freed[i] = done
             with torch.cuda.stream(self.d2h):
                 self.d2h.wait_event(done)
                 for t in store(i, outs):
                     t.record_stream(self.d2h)
+        # the D2H stream ends after every compute and copy of this step
+        self.issued.append(self.d2h.record_event())
+
+    def join(self):
+        main = torch.cuda.current_stream()
         for s in (self.h2d, self.comp, self.d2h):
             main.wait_stream(s)
 
@@ -321,8 +349,11 @@ class SwigluRope:
 
     # Chunks per batch row in the e2e pipeline.  Every chunk stays contiguous:
     # SwiGLU rows split along the sequence, RoPE rows along the heads (all
-    # positions of the batch row in every chunk).
-    E2E_SPLIT = 2
+    # positions of the batch row in every chunk).  One chunk per batch row
+    # (8 per step) keeps the host's enqueue time per step (copies and
+    # autograd calls, ~0.5 ms per chunk) well under the ~16 ms the copies
+    # take on the host link; 16 and more chunks measured slower.
+    E2E_SPLIT = 1
 
     def _e2e_views(self, i):
         sp = self.E2E_SPLIT
@@ -351,13 +382,14 @@ class SwigluRope:
             gate = d["gate"][v["gate"]].unsqueeze(0).detach().requires_grad_(True)
             up = d["up"][v["up"]].unsqueeze(0).detach().requires_grad_(True)
             out = fused_swiglu(gate, up)
-            out.backward(d["dout"][v["dout"]].unsqueeze(0))
             q = d["q"][v["q"]].unsqueeze(0).detach().requires_grad_(True)
             k = d["k"][v["k"]].unsqueeze(0).detach().requires_grad_(True)
             qr, kr = apply_fused_rotary_from_positions(q, k, s["pos"][b:b + 1],
                                                        inv_freq=s["inv_freq"])
-            torch.autograd.backward([qr, kr], [d["dq"][v["dq"]].unsqueeze(0),
-                                               d["dk"][v["dk"]].unsqueeze(0)])
+            # one backward pass for both ops (one autograd engine call per chunk)
+            torch.autograd.backward([out, qr, kr], [d["dout"][v["dout"]].unsqueeze(0),
+                                                    d["dq"][v["dq"]].unsqueeze(0),
+                                                    d["dk"][v["dk"]].unsqueeze(0)])
             return {"out": out.detach(), "dgate": gate.grad, "dup": up.grad,
                     "q_rot": qr.detach(), "k_rot": kr.detach(), "dq_in": q.grad,
                     "dk_in": k.grad}
@@ -455,35 +487,44 @@ class RmsNorm:
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
         return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h,
-                "pipe": CopyPipeline(device, self.B)}
+                "pipe": CopyPipeline(device, self.E2E_CHUNKS)}
+
+    # Chunks of batch rows in the e2e pipeline: two keep the host's enqueue
+    # time per step (copies and autograd calls, ~0.3 ms per chunk) under the
+    # ~2.7 ms the copies take on the host link; consecutive steps overlap.
+    E2E_CHUNKS = 2
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_rms_norm import _FusedRMSNormFunction
 
         d, h, ho = s["dev"], s["host"], s["host_out"]
-        nb = self.B
+        nc = s["pipe"].nchunks
+        per = self.B // nc
         # the weight is one leaf for the whole step: its gradient accumulates
         # over the chunks (autograd adds), as over the batch rows of one call
         w = d["w"].detach().requires_grad_(True)
 
         def load(i):
+            sl = slice(i * per, (i + 1) * per)
             if i == 0:
                 d["w"].copy_(h["w"], non_blocking=True)
-            d["x"][i].copy_(h["x"][i], non_blocking=True)
-            d["dy"][i].copy_(h["dy"][i], non_blocking=True)
+            d["x"][sl].copy_(h["x"][sl], non_blocking=True)
+            d["dy"][sl].copy_(h["dy"][sl], non_blocking=True)
 
         def compute(i):
-            x = d["x"][i:i + 1].detach().requires_grad_(True)
+            sl = slice(i * per, (i + 1) * per)
+            x = d["x"][sl].detach().requires_grad_(True)
             y = _FusedRMSNormFunction.apply(x, w, 1e-6)
-            y.backward(d["dy"][i:i + 1])
+            y.backward(d["dy"][sl])
             outs = {"y": y.detach(), "dx": x.grad}
-            if i == nb - 1:
+            if i == nc - 1:
                 outs["dw"] = w.grad
             return outs
 
         def store(i, outs):
-            ho["y"][i:i + 1].copy_(outs["y"], non_blocking=True)
-            ho["dx"][i:i + 1].copy_(outs["dx"], non_blocking=True)
+            sl = slice(i * per, (i + 1) * per)
+            ho["y"][sl].copy_(outs["y"], non_blocking=True)
+            ho["dx"][sl].copy_(outs["dx"], non_blocking=True)
             if "dw" in outs:
                 ho["dw"].copy_(outs["dw"], non_blocking=True)
             return outs.values()
@@ -573,39 +614,55 @@ class Flce:
             loss, dx, dw = timer("flce_forward", self._vp, t)
         timer("flce_backward", ops.flce_backward, t["go"], dx, dw, 1, 1)
 
+    e2e_pipelined = True
+
     def e2e_setup(self, device):
         t = self.make_inputs(device, seed=79)
         host = {k: t[k].cpu().pin_memory() for k in ("h", "w", "lab")}
-        dev = {k: torch.empty_like(t[k]) for k in ("h", "w", "lab")}
+        # two device input sets: a step's uploads (the whole lm_head among
+        # them) run during the previous step's compute, its downloads during
+        # the next one's
+        dev = [{k: torch.empty_like(t[k]) for k in ("h", "w", "lab")} for _ in range(2)]
         host_out = {"loss": torch.empty((), pin_memory=True),
                     "dh": torch.empty_like(host["h"]).pin_memory(),
                     "dw": torch.empty_like(host["w"]).pin_memory()}
         h2d = sum(v.numel() * v.element_size() for v in host.values())
         d2h = sum(v.numel() * v.element_size() for v in host_out.values())
         return {"host": host, "dev": dev, "host_out": host_out, "h2d": h2d, "d2h": d2h,
-                "off": t["off"]}
+                "off": t["off"], "pipe": CopyPipeline(device, 1, slots=2)}
 
     def e2e_step(self, s):
         from metal_liger_b200.ops.fused_linear_cross_entropy import \
             _FusedLinearCrossEntropyFunction
 
-        d, h, ho = s["dev"], s["host"], s["host_out"]
-        for k in d:
-            d[k].copy_(h[k], non_blocking=True)
-        hid = d["h"].detach().requires_grad_(True)
-        w = d["w"].detach().requires_grad_(True)
-        if self.world == 1:
-            loss = _FusedLinearCrossEntropyFunction.apply(hid, w, d["lab"], None, -100,
-                                                          self.CHUNK)
-        else:
-            from metal_liger_b200.ops.fused_linear_cross_entropy import \
-                _VocabParallelFLCEFunction
-            loss = _VocabParallelFLCEFunction.apply(hid, w, d["lab"], None, s["off"], -100,
-                                                    self.CHUNK, None)
-        loss.backward()
-        ho["loss"].copy_(loss.detach(), non_blocking=True)
-        ho["dh"].copy_(hid.grad, non_blocking=True)
-        ho["dw"].copy_(w.grad, non_blocking=True)
+        h, ho, pipe = s["host"], s["host_out"], s["pipe"]
+
+        def load(i):
+            d = s["dev"][pipe.slot]
+            for k in d:
+                d[k].copy_(h[k], non_blocking=True)
+
+        def compute(i):
+            d = s["dev"][pipe.slot]
+            hid = d["h"].detach().requires_grad_(True)
+            w = d["w"].detach().requires_grad_(True)
+            if self.world == 1:
+                loss = _FusedLinearCrossEntropyFunction.apply(hid, w, d["lab"], None, -100,
+                                                              self.CHUNK)
+            else:
+                from metal_liger_b200.ops.fused_linear_cross_entropy import \
+                    _VocabParallelFLCEFunction
+                loss = _VocabParallelFLCEFunction.apply(hid, w, d["lab"], None, s["off"], -100,
+                                                        self.CHUNK, None)
+            loss.backward()
+            return {"loss": loss.detach(), "dh": hid.grad, "dw": w.grad}
+
+        def store(i, outs):
+            for name, src in outs.items():
+                ho[name].copy_(src, non_blocking=True)
+            return outs.values()
+
+        pipe.run(load, compute, store)
 
     def cpu_inputs(self, tokens, seed=7):
         g = torch.Generator().manual_seed(seed)
@@ -1507,6 +1564,57 @@ def peak_extra_bytes(wl, t):
     return int(torch.cuda.max_memory_allocated() - base)
 
 
+_LINK = {}
+
+
+def host_link_ceiling(device, nbytes=256 << 20, reps=3):
+    """Pinned host<->device copy rates of this GPU's host link, measured once
+    per process: H2D alone, D2H alone and both directions at once (GB/s,
+    best of `reps`, CUDA events).  The e2e step's copies cannot beat them."""
+    if device in _LINK:
+        return _LINK[device]
+    hs = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    hd = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    d1 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    d2 = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+
+    def best(h2d, d2h):
+        t = float("inf")
+        for _ in range(reps):
+            main = torch.cuda.current_stream(device)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(main)
+            for st, on, fn in ((up, h2d, lambda: d1.copy_(hs, non_blocking=True)),
+                               (down, d2h, lambda: hd.copy_(d2, non_blocking=True))):
+                if on:
+                    st.wait_event(a)
+                    with torch.cuda.stream(st):
+                        fn()
+                    main.wait_stream(st)
+            b.record(main)
+            b.synchronize()
+            t = min(t, a.elapsed_time(b))
+        return t / 1e3
+
+    _LINK[device] = {"h2d_gbs": nbytes / best(True, False) / 1e9,
+                     "d2h_gbs": nbytes / best(False, True) / 1e9,
+                     "duplex_gbs": 2 * nbytes / best(True, True) / 1e9}
+    del hs, hd, d1, d2
+    torch.cuda.empty_cache()
+    return _LINK[device]
+
+
+def link_roofline(link, h2d, d2h, ms_per_step):
+    """The e2e step's copy floor on the measured link and the fraction of it
+    reached: floor = the slowest of H2D alone, D2H alone and both at once."""
+    if h2d + d2h == 0:
+        return None
+    floor_s = max(h2d / (link["h2d_gbs"] * 1e9), d2h / (link["d2h_gbs"] * 1e9),
+                  (h2d + d2h) / (link["duplex_gbs"] * 1e9))
+    return {**link, "floor_ms": 1e3 * floor_s, "frac": 1e3 * floor_s / ms_per_step}
+
+
 def e2e_measure(ctx, wl, steps):
     s = wl.e2e_setup(ctx.device)
     for _ in range(2):
@@ -1518,6 +1626,8 @@ def e2e_measure(ctx, wl, steps):
     e0.record()
     for _ in range(steps):
         wl.e2e_step(s)
+    if s.get("pipe") is not None:
+        s["pipe"].join()
     e1.record()
     torch.cuda.synchronize()
     ms = ctx.reduce(e0.elapsed_time(e1))
@@ -1620,7 +1730,9 @@ def measure_workload(ctx, wl, steps, warmup, e2e_steps, cpu_budget, table=False,
         "gpu_launches": launches * steps if launches is not None else None,
         "peak_extra_bytes": peak,
         "e2e": {"value": job_tokens * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "link": link_roofline(host_link_ceiling(ctx.device), h2d, d2h,
+                                      e2e_ms / e2e_steps)},
         "cpu_baseline": cpu, "extra": extra, "inputs": inputs,
     }
 
@@ -1638,7 +1750,8 @@ def compact_entry(wl, r, steps):
          **({"kernel_frac_alone": {k: v["frac_alone"] for k, v in r["per_kernel"].items()
                                    if "frac_alone" in v}}
             if any("frac_alone" in v for v in r["per_kernel"].values()) else {}),
-         "e2e": {k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+         "e2e": {**{k: r["e2e"][k] for k in ("value", "h2d_bytes_per_step", "d2h_bytes_per_step")},
+                 **({"link_frac": r["e2e"]["link"]["frac"]} if r["e2e"].get("link") else {})},
          "gpu_launches": r["gpu_launches"], "peak_extra_bytes": r["peak_extra_bytes"],
          "clocks": {"sm_mhz": r["clocks"].get("sm_mhz"), "reasons": r["clocks"].get("reasons")}}
     if r["cpu_baseline"]:
@@ -1825,7 +1938,9 @@ def run_gpu_arm(args, wl):
             "e2e": {**r["e2e"],
                     "api": getattr(wl, "e2e_api", "public autograd Functions, pinned host "
                                    "buffers, H2D of inputs + D2H of all outputs every step"
-                                   + (", batch rows pipelined over 3 streams"
+                                   + (", copies overlapped with compute on 3 streams "
+                                      "(H2D / compute / D2H; consecutive steps overlap, the "
+                                      "host at most 2 steps ahead)"
                                       if getattr(wl, "e2e_pipelined", False) else ""))},
             "gpu_launches": r["gpu_launches"],
             "peak_extra_bytes": r["peak_extra_bytes"],
@@ -1854,7 +1969,7 @@ def main(argv=None):
                          "line plus every other op under 'workloads' and 'flce_vp')")
     ap.add_argument("--headline-only", action="store_true",
                     help="default workload without the other ops")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--kernel-table", action="store_true",
                     help="print one extra step's per-kernel device times (CUPTI) to stderr")
     ap.add_argument("--spin-us", type=float, default=200.0,
@@ -1872,6 +1987,9 @@ def main(argv=None):
     ap.add_argument("--lora-tokens", type=int, default=None,
                     help="token rows of the lora workload (default: BASELINE's 16,384); a "
                          "smaller case for profiler captures")
+    ap.add_argument("--e2e-split", type=int, default=None,
+                    help="e2e pipeline chunks per batch row of the swiglu_rope workload "
+                         "(default 1)")
     ap.add_argument("--flce-tokens", type=int, default=None,
                     help="token rows of the flce workload (default: BASELINE's 16,384); a "
                          "smaller case for profiler captures")
@@ -1885,6 +2003,10 @@ def main(argv=None):
         Lora.T = int(args.lora_tokens)
     if args.flce_tokens:
         Flce.N = int(args.flce_tokens)
+    if args.e2e_split:
+        if SwigluRope.HK % args.e2e_split or args.e2e_split < 1:
+            ap.error(f"--e2e-split must divide the {SwigluRope.HK} k heads")
+        SwigluRope.E2E_SPLIT = int(args.e2e_split)
     if args.lora_swiglu_fusion is not None and args.impl != "reference":
         from metal_liger_b200 import _C
 
