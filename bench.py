@@ -1775,6 +1775,33 @@ def _bf16_close(a, b):
     return int(bad.sum().item())
 
 
+def measure_flce_vp_p2p(ctx, args):
+    """flce_vp again with VP_DX_EXCHANGE = "p2p" (no collective in the step);
+    the compact fields, or the error every rank recorded."""
+    import metal_liger_b200.ops.fused_linear_cross_entropy as flce_ops
+
+    previous = flce_ops.VP_DX_EXCHANGE
+    flce_ops.VP_DX_EXCHANGE = "p2p"
+    try:
+        fl = Flce()
+        vp = measure_workload(ctx, fl, args.steps, args.warmup, 1, 0.0, keep=True)
+        r = measure_flce_vp(ctx, args.steps, args.warmup, vp)
+        del fl, vp
+        from metal_liger_b200 import _C
+
+        err = int(_C.load().ml_device_error(None))
+        out = {k: r[k] for k in ("tokens_per_s", "ms_per_step", "one_gpu_ms_per_step",
+                                 "speedup_vs_1", "parity", "worst_errors", "timeline_rank0")}
+        out["device_error"] = err
+    except Exception as exc:  # every rank runs the same steps; report, do not abort the line
+        out = {"error": f"{type(exc).__name__}: {exc}"[:300]}
+    finally:
+        flce_ops.VP_DX_EXCHANGE = previous
+        torch.cuda.empty_cache()
+    ctx.barrier()
+    return out
+
+
 def measure_flce_vp(ctx, steps, warmup, vp):
     """The vocabulary-parallel FLCE at N ranks (already timed in `vp`, with
     its inputs kept) against the single-GPU FLCE on the same seeded inputs:
@@ -1819,7 +1846,10 @@ def measure_flce_vp(ctx, steps, warmup, vp):
     # where the step's time goes: one profiled step (CUPTI) on every rank
     timeline = vp_timeline(vpw, t)
     tok = single.tokens
+    import metal_liger_b200.ops.fused_linear_cross_entropy as flce_ops
+
     out = {"n_gpus": ctx.world, "scaling": "strong", "tokens_per_step": tok,
+           "dx_exchange": (flce_ops.VP_DX_EXCHANGE if ctx.world > 1 else None),
            "tokens_per_s": tok * steps / (vp["ms_per_step"] * steps / 1e3),
            "ms_per_step": vp["ms_per_step"], "one_gpu_ms_per_step": ms1 / steps,
            "speedup_vs_1": (ms1 / steps) / vp["ms_per_step"],
@@ -1886,8 +1916,11 @@ def run_gpu_arm(args, wl):
                          table=args.kernel_table)
 
     workloads, flce_vp = {}, None
+    chosen = None if args.suite is None else {x for x in args.suite.split(",") if x}
     if suite:
         for name in (SUITE_N1 if ctx.world == 1 else SUITE_NN):
+            if chosen is not None and name not in chosen:
+                continue
             sub = WORKLOADS[name]()
             res = measure_workload(ctx, sub, args.steps, args.warmup, args.e2e_steps,
                                    args.cpu_budget_sub)
@@ -1900,13 +1933,17 @@ def run_gpu_arm(args, wl):
                            "parity_vs": "one GPU holds the whole vocabulary: no shards"}
             del sub, res
             torch.cuda.empty_cache()
-        if ctx.world > 1:
+        if ctx.world > 1 and (chosen is None or "flce" in chosen):
             fl = Flce()
             vp = measure_workload(ctx, fl, args.steps, args.warmup, args.e2e_steps, 0.0,
                                   keep=True)
             flce_vp = measure_flce_vp(ctx, args.steps, args.warmup, vp)
             del fl, vp
             torch.cuda.empty_cache()
+            if args.vp_dx_exchange is None:
+                # the same measurement with the collective-free exchange (peer
+                # memory from the dX GEMM's epilogue) beside the NCCL one
+                flce_vp["p2p"] = measure_flce_vp_p2p(ctx, args)
 
     if ctx.rank == 0:
         line = {
@@ -1987,6 +2024,12 @@ def main(argv=None):
     ap.add_argument("--lora-tokens", type=int, default=None,
                     help="token rows of the lora workload (default: BASELINE's 16,384); a "
                          "smaller case for profiler captures")
+    ap.add_argument("--suite", default=None,
+                    help="comma-separated subset of the default run's extra workloads "
+                         "(rmsnorm,flce,lora,c5_step; flce is flce_vp at N > 1)")
+    ap.add_argument("--vp-dx-exchange", choices=["nccl", "p2p"], default=None,
+                    help="vocabulary-parallel FLCE (N > 1): sum the partial dX with NCCL "
+                         "(default) or through peer memory from the dX GEMM's epilogue")
     ap.add_argument("--e2e-split", type=int, default=None,
                     help="e2e pipeline chunks per batch row of the swiglu_rope workload "
                          "(default 1)")
@@ -2003,6 +2046,10 @@ def main(argv=None):
         Lora.T = int(args.lora_tokens)
     if args.flce_tokens:
         Flce.N = int(args.flce_tokens)
+    if args.vp_dx_exchange:
+        import metal_liger_b200.ops.fused_linear_cross_entropy as flce_ops
+
+        flce_ops.VP_DX_EXCHANGE = args.vp_dx_exchange
     if args.e2e_split:
         if SwigluRope.HK % args.e2e_split or args.e2e_split < 1:
             ap.error(f"--e2e-split must divide the {SwigluRope.HK} k heads")

@@ -338,6 +338,71 @@ ML_API int ml_flce_shard_grads_dw(const void* hidden, int64_t rows, int64_t h, i
                                   float* dw, int dw_accumulate, void* workspace,
                                   size_t workspace_bytes, void* stream);
 
+/* --- peer memory between the node's GPUs (one process per GPU) ----------
+ * A device buffer from ml_p2p_alloc (cudaMalloc'd, zeroed) is exported as an
+ * opaque handle of ml_p2p_handle_bytes() bytes, passed to the other ranks by
+ * the caller (the process group), and mapped there with ml_p2p_import
+ * (peer access enabled on demand); ml_p2p_close unmaps, ml_p2p_free frees. */
+ML_API int ml_p2p_alloc(size_t bytes, void** out);
+ML_API int ml_p2p_free(void* ptr);
+ML_API size_t ml_p2p_handle_bytes(void);
+ML_API int ml_p2p_export(const void* base, void* handle_out);
+ML_API int ml_p2p_import(const void* handle, void** out);
+ML_API int ml_p2p_close(void* ptr);
+
+/*
+ * The vocabulary-parallel dX without a collective library: every rank keeps
+ * an exchange buffer of ml_flce_p2p_workspace_bytes(world, chunk_cap, h)
+ * bytes (ml_p2p_alloc) mapped on every other rank; `peer_ws` lists the
+ * world buffers as mapped on this GPU (own included), indexed by rank.
+ * Rank r owns the chunk's rows [r R, r R + R), R = ceil(chunk_cap / world)
+ * rounded up to a multiple of 256.  Per chunk, with an epoch that starts at
+ * 1 and grows by one per chunk, identical on every rank:
+ *   ml_flce_shard_dx_p2p  after ml_flce_shard_grads(dx = dw = NULL) on the
+ *                         same shard workspace: the shard's dX GEMM, whose
+ *                         epilogue stores each fp32 tile into its row owner's
+ *                         receive slot for this rank (plain stores into peer
+ *                         memory, overlapping the math), then an arrive flag
+ *                         on every rank;
+ *   ml_flce_p2p_reduce    waits for every rank's arrive flag, sums this
+ *                         rank's rows over the ranks in rank order and writes
+ *                         them into every rank's gather buffer, then a done
+ *                         flag on every rank;
+ *   ml_flce_p2p_finish    waits for every owner's done flag and copies the
+ *                         chunk's summed dX (rows x h fp32) to dx_out.
+ * Waits are bounded (2 s): one that gives up records ML_ERR_TIMEOUT in the
+ * device error word (ml_device_error).  Replaces the NCCL all-reduce of the
+ * shard's partial dX; the result is bit for bit independent of the ranks'
+ * timing (fixed summation order).  world <= 8, h a multiple of 8.
+ */
+ML_API size_t ml_flce_p2p_workspace_bytes(int world, int64_t chunk_cap, int64_t h);
+ML_API int ml_flce_shard_dx_p2p(const void* weight, int64_t rows, int64_t h, int64_t v_local,
+                                const void* shard_ws, size_t shard_ws_bytes, int64_t chunk_cap,
+                                int world, int rank, void* const* peer_ws, int64_t epoch,
+                                void* stream);
+ML_API int ml_flce_p2p_reduce(int64_t rows, int64_t h, int64_t chunk_cap, int world, int rank,
+                              void* const* peer_ws, int64_t epoch, void* stream);
+ML_API int ml_flce_p2p_finish(int64_t rows, int64_t h, int64_t chunk_cap, int world, int rank,
+                              void* const* peer_ws, int64_t epoch, float* dx_out, void* stream);
+
+/*
+ * The chunk's softmax statistics through the same buffers (replacing the two
+ * all-reduces of ml_flce_shard_stats' outputs), same epoch as the chunk's dX:
+ *   ml_flce_p2p_stats_put    this rank's [rows] max / sum-exp / target logit
+ *                            into its slot on every rank, then a stats flag;
+ *   ml_flce_p2p_stats_merge  waits for every rank's flag and writes, per row,
+ *                            max = max_r max_r, sum = sum_r sum_r exp(max_r -
+ *                            max), target = sum_r target_r, over the ranks in
+ *                            rank order (identical on every rank).
+ */
+ML_API int ml_flce_p2p_stats_put(const float* row_max, const float* row_sum,
+                                 const float* row_tgt, int64_t rows, int64_t h,
+                                 int64_t chunk_cap, int world, int rank, void* const* peer_ws,
+                                 int64_t epoch, void* stream);
+ML_API int ml_flce_p2p_stats_merge(int64_t rows, int64_t h, int64_t chunk_cap, int world,
+                                   int rank, void* const* peer_ws, int64_t epoch, float* out_max,
+                                   float* out_sum, float* out_tgt, void* stream);
+
 /* ------------------------------------------------------------------------
  * Fused LoRA QKV / MLP
  * ------------------------------------------------------------------------ */

@@ -142,6 +142,25 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
                                     c_int, c_void_p, c_size_t, c_void_p]),
     "ml_flce_shard_grads_dw": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
                                        c_void_p, c_size_t, c_void_p]),
+    "ml_p2p_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
+    "ml_p2p_free": (c_int, [c_void_p]),
+    "ml_p2p_handle_bytes": (c_size_t, []),
+    "ml_p2p_export": (c_int, [c_void_p, c_void_p]),
+    "ml_p2p_import": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "ml_p2p_close": (c_int, [c_void_p]),
+    "ml_flce_p2p_workspace_bytes": (c_size_t, [c_int, c_int64, c_int64]),
+    "ml_flce_shard_dx_p2p": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_size_t,
+                                     c_int64, c_int, c_int, ctypes.POINTER(c_void_p), c_int64,
+                                     c_void_p]),
+    "ml_flce_p2p_reduce": (c_int, [c_int64, c_int64, c_int64, c_int, c_int,
+                                   ctypes.POINTER(c_void_p), c_int64, c_void_p]),
+    "ml_flce_p2p_finish": (c_int, [c_int64, c_int64, c_int64, c_int, c_int,
+                                   ctypes.POINTER(c_void_p), c_int64, c_void_p, c_void_p]),
+    "ml_flce_p2p_stats_put": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                      c_int, c_int, ctypes.POINTER(c_void_p), c_int64, c_void_p]),
+    "ml_flce_p2p_stats_merge": (c_int, [c_int64, c_int64, c_int64, c_int, c_int,
+                                        ctypes.POINTER(c_void_p), c_int64, c_void_p, c_void_p,
+                                        c_void_p, c_void_p]),
     "ml_lora_qkv_workspace_bytes": (c_size_t, [c_int64, c_int64, ctypes.POINTER(LoraProj), c_int]),
     "ml_lora_qkv_forward": (c_int, [c_void_p, c_int64, c_int64, c_int64, ctypes.POINTER(LoraProj),
                                     ctypes.POINTER(c_void_p), c_void_p, c_void_p, c_size_t,

@@ -24,6 +24,7 @@
 // ml_flce_backward multiplies them by the real grad_output and casts, which
 // is exact because they are linear in it.  6*H*V FLOPs per token in total.
 #include "gemm.cuh"
+#include "p2p.cuh"
 
 #include <algorithm>
 
@@ -668,4 +669,49 @@ extern "C" int ml_flce_shard_grads_dw(const void* hidden, int64_t rows, int64_t 
       reinterpret_cast<const __nv_bfloat16*>(static_cast<uint8_t*>(workspace) + L.off_E);
   return flce::shard_dw_gemm(hidden, E, L.ldE, rows, h, v_local, dw, dw_accumulate,
                              static_cast<cudaStream_t>(stream));
+}
+
+// Vocabulary-parallel dX through peer memory: dX = P W of this rank's shard
+// (P: the transformed exponentials that ml_flce_shard_grads left in the
+// shard workspace, rows x v_local), every output tile stored by the GEMM's
+// epilogue straight into its row owner's receive slot for this rank
+// (p2p.cu); then this rank's arrive flag is raised on every rank.  Followed
+// by ml_flce_p2p_reduce and ml_flce_p2p_finish with the same epoch.
+extern "C" int ml_flce_shard_dx_p2p(const void* weight, int64_t rows, int64_t h, int64_t v_local,
+                                    const void* shard_ws, size_t shard_ws_bytes, int64_t chunk_cap,
+                                    int world, int rank, void* const* peer_ws, int64_t epoch,
+                                    void* stream) {
+  ML_CHECK_ARG(weight && shard_ws, "flce_shard_dx_p2p: null pointer");
+  ML_CHECK_ARG(rows > 0 && rows <= chunk_cap && h > 0 && h % 8 == 0 && v_local > 0 && epoch > 0,
+               "flce_shard_dx_p2p: bad sizes (rows %lld, chunk %lld, h %lld)", (long long)rows,
+               (long long)chunk_cap, (long long)h);
+  const flce::Layout L = flce::layout(rows, v_local, rows);
+  ML_CHECK_ARG(((uintptr_t)shard_ws & 255) == 0 && shard_ws_bytes >= L.total,
+               "flce_shard_dx_p2p: shard workspace must be 256-byte aligned and >= %zu bytes",
+               L.total);
+  p2p::Peers pe;
+  if (int rc = p2p::check_peers(world, rank, peer_ws, pe)) return rc;
+  const p2p::XLayout X = p2p::xlayout(world, chunk_cap, h);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const __nv_bfloat16* E =
+      reinterpret_cast<const __nv_bfloat16*>(static_cast<const uint8_t*>(shard_ws) + L.off_E);
+  gemm::Problem g;
+  g.M = rows;
+  g.N = h;
+  g.nseg = 1;
+  g.seg[0].a = {E, rows, v_local, L.ldE};
+  g.seg[0].b = {weight, v_local, h, h};
+  g.seg[0].K = v_local;
+  g.b_mn = true;
+  g.epi = gemm::EPI_STORE;
+  g.d_f32 = true;
+  g.ldd = h;
+  g.raster = 1;
+  g.peer_n = world;
+  g.peer_me = rank;
+  g.peer_rows = X.rows_per_owner;
+  for (int r = 0; r < world; ++r)
+    g.peer_dst[r] = reinterpret_cast<float*>(pe.ws[r] + X.off_recv);
+  if (int rc = gemm::launch(g, st)) return rc;
+  return p2p::launch_signal(pe, world, rank, 0, epoch, st);
 }

@@ -357,6 +357,27 @@ int launch(const Problem& pr, cudaStream_t st) {
   prm.D3 = pr.D3;
   prm.aux1 = pr.aux1;
   prm.aux2 = pr.aux2;
+  prm.peer_n = 0;
+  if (pr.peer_n > 0) {
+    if (pr.epi != EPI_STORE || !pr.d_f32 || pr.beta != 0.f || pr.peer_n > kMaxPeers ||
+        pr.peer_me < 0 || pr.peer_me >= pr.peer_n || pr.peer_rows <= 0 ||
+        pr.peer_rows * pr.peer_n < pr.M || pr.peer_rows > 0x7fffffff) {
+      set_error("gemm: bad peer-store request");
+      return ML_ERR_INVALID_ARG;
+    }
+    prm.vec_ok = (pr.ldd * 4) % 16 == 0;
+    for (int o = 0; o < pr.peer_n; ++o) {
+      if (pr.peer_dst[o] == nullptr) {
+        set_error("gemm: null peer destination %d", o);
+        return ML_ERR_INVALID_ARG;
+      }
+      if (!aligned16(pr.peer_dst[o])) prm.vec_ok = 0;
+      prm.peer_dst[o] = pr.peer_dst[o];
+    }
+    prm.peer_n = pr.peer_n;
+    prm.peer_me = pr.peer_me;
+    prm.peer_rows = (int)pr.peer_rows;
+  }
   prm.labels = pr.labels;
   prm.label_base = pr.label_base;
   prm.ignore_index = pr.ignore_index;

@@ -32,6 +32,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;       // one 128-byte swizzle row of bf16
 constexpr int kMaxSeg = 4;
+constexpr int kMaxPeers = 8;  // ranks a peer-mode store epilogue can address
 constexpr int kThreads = 192;
 
 enum Epi : int {
@@ -98,6 +99,15 @@ struct alignas(64) Params {
   void* D3;
   const void* aux1;
   const void* aux2;
+  // EPI_STORE fp32, peer mode (peer_n > 0): output row r goes to rank
+  // o = r / peer_rows, into the receive slot that rank keeps for this one:
+  // peer_dst[o] + (peer_me * peer_rows + r - o * peer_rows) * ldd — plain
+  // stores into another GPU's memory (mapped here), issued tile by tile
+  // while the GEMM runs.
+  int peer_n;
+  int peer_me;
+  int peer_rows;
+  float* peer_dst[kMaxPeers];
   int* err;                // device error word (bounded-wait timeouts)
 };
 
@@ -178,7 +188,14 @@ __device__ __forceinline__ void store_row32(const Params& p, float (&v)[32], int
     return;
   }
   if (p.d_f32) {
-    float* dst = static_cast<float*>(p.D) + row * p.ldd + col0;
+    float* dst;
+    if (p.peer_n > 0) {
+      const int o = (int)(row / p.peer_rows);
+      dst = p.peer_dst[o] + ((int64_t)p.peer_me * p.peer_rows + row - (int64_t)o * p.peer_rows) *
+                                p.ldd + col0;
+    } else {
+      dst = static_cast<float*>(p.D) + row * p.ldd + col0;
+    }
     if (p.vec_ok && col0 + 32 <= N) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
@@ -688,6 +705,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // peer mode: this thread's stores into other GPUs are visible system-wide
+    // before the grid completes
+    if (p.peer_n > 0) __threadfence_system();
   }
 
   // A programmatic dependent (e.g. the split-K reduction) may begin launching.
@@ -918,6 +938,7 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    if (p.peer_n > 0) __threadfence_system();  // peer mode (see gemm_kernel)
   }
 
   // A programmatic dependent (e.g. the split-K reduction) may begin launching.
@@ -990,6 +1011,11 @@ struct Problem {
   void* D3 = nullptr;
   const void* aux1 = nullptr;
   const void* aux2 = nullptr;
+  // EPI_STORE fp32 peer mode (see Params): D unused; peer_dst[0..peer_n)
+  int peer_n = 0;
+  int peer_me = 0;
+  int64_t peer_rows = 0;
+  float* peer_dst[kMaxPeers] = {};
 };
 
 // Builds tensor maps, picks the tile width and launches.  Returns ML_OK or an

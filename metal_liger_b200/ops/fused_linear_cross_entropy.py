@@ -148,6 +148,75 @@ class CudaShardPhases:
 #   dW GEMM instead of after it (0: the GEMMs take every SM).
 VP_STATS_EXCHANGE = "allreduce"
 VP_OVERLAP_SMS = 0
+# * VP_DX_EXCHANGE: "nccl" sums each chunk's partial dX with an asynchronous
+#   NCCL all-reduce that overlaps the chunk's dW GEMM; "p2p" exchanges it
+#   through peer memory without a collective library: the dX GEMM's epilogue
+#   stores every tile into its row owner's buffer on the owning GPU while the
+#   GEMM runs, then each owner sums its rows in rank order and writes them to
+#   every rank (ml_flce_shard_dx_p2p / ml_flce_p2p_reduce / ml_flce_p2p_finish),
+#   the owner's phase on a side stream beside the dW GEMM; the statistics go
+#   through the same buffers (ml_flce_p2p_stats_put / _merge), so the step
+#   uses no collective at all.
+VP_DX_EXCHANGE = "nccl"
+
+
+class PeerExchange:
+    """The p2p dX exchange's buffers for one (process group, device, chunk
+    capacity, hidden size): one ml_p2p_alloc buffer per rank, exported once
+    and mapped on every other rank (handles exchanged through the process
+    group), plus the side stream of the owners' phase and the epoch counter
+    every rank advances identically (one per chunk)."""
+
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, group, device, chunk_cap, h):
+        import torch.distributed as dist
+
+        key = (id(group) if group is not None else None, dist.get_rank(group), device.index,
+               int(chunk_cap), int(h))
+        ex = cls._cache.get(key)
+        if ex is None:
+            ex = cls(group, device, int(chunk_cap), int(h))
+            cls._cache[key] = ex
+        return ex
+
+    def __init__(self, group, device, chunk_cap, h):
+        import ctypes
+
+        import torch.distributed as dist
+        from metal_liger_b200 import _C
+
+        lib = _C.load()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.chunk_cap, self.h = chunk_cap, h
+        nbytes = int(lib.ml_flce_p2p_workspace_bytes(self.world, chunk_cap, h))
+        if nbytes == 0:
+            raise RuntimeError(f"vocab-parallel FLCE p2p exchange: unsupported world size "
+                               f"{self.world} (at most 8) or sizes")
+        with torch.cuda.device(device):
+            base = ctypes.c_void_p()
+            _C.call("ml_p2p_alloc", nbytes, ctypes.byref(base))
+            hb = int(lib.ml_p2p_handle_bytes())
+            handle = (ctypes.c_uint8 * hb)()
+            _C.call("ml_p2p_export", base, handle)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs, self.imported = [], []
+            for r, hnd in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(base.value)
+                    continue
+                buf = (ctypes.c_uint8 * hb).from_buffer_copy(hnd)
+                out = ctypes.c_void_p()
+                _C.call("ml_p2p_import", buf, ctypes.byref(out))
+                ptrs.append(out.value)
+                self.imported.append(out.value)
+            self.stream = torch.cuda.Stream(device)
+        self.base = base.value
+        self.table = (ctypes.c_void_p * self.world)(*ptrs)
+        self.epoch = 0
 
 
 def _merge_stats(m, s, t, group, phases):
@@ -183,6 +252,42 @@ def _leave_sms_for_collectives(phases, pending):
         return contextlib.nullcontext()
     from metal_liger_b200 import _C
     return _C.gemm_reserved_sms(VP_OVERLAP_SMS)
+
+
+def _p2p_stats(ex, m, s, t, h):
+    """The chunk's (max, sum-exp, target) merged over the ranks through peer
+    memory (rank order; the same on every rank), for epoch ex.epoch."""
+    from metal_liger_b200 import _C
+
+    rows = m.numel()
+    st = torch.cuda.current_stream(m.device).cuda_stream
+    _C.call("ml_flce_p2p_stats_put", m.data_ptr(), s.data_ptr(), t.data_ptr(), rows, h,
+            ex.chunk_cap, ex.world, ex.rank, ex.table, ex.epoch, st)
+    mg, sg, tg = torch.empty_like(m), torch.empty_like(s), torch.empty_like(t)
+    _C.call("ml_flce_p2p_stats_merge", rows, h, ex.chunk_cap, ex.world, ex.rank, ex.table,
+            ex.epoch, mg.data_ptr(), sg.data_ptr(), tg.data_ptr(), st)
+    return mg, sg, tg
+
+
+def _p2p_dx(ex, state, weight_shard, rows, h, dx_rows, previous):
+    """One chunk's dX through peer memory (epoch ex.epoch, set by the
+    chunk's statistics exchange): the dX GEMM with the peer-store epilogue on
+    the current stream (after the previous chunk's exchange, whose owners must
+    be done reading their receive slots), the owners' phase on the exchange's
+    side stream, writing the summed rows into `dx_rows`."""
+    from metal_liger_b200 import _C
+
+    main = torch.cuda.current_stream(dx_rows.device)
+    if previous is not None:
+        main.wait_event(previous)
+    _C.call("ml_flce_shard_dx_p2p", weight_shard.data_ptr(), rows, h, weight_shard.shape[0],
+            state.data_ptr(), state.numel(), ex.chunk_cap, ex.world, ex.rank, ex.table,
+            ex.epoch, main.cuda_stream)
+    ex.stream.wait_stream(main)
+    _C.call("ml_flce_p2p_reduce", rows, h, ex.chunk_cap, ex.world, ex.rank, ex.table, ex.epoch,
+            ex.stream.cuda_stream)
+    _C.call("ml_flce_p2p_finish", rows, h, ex.chunk_cap, ex.world, ex.rank, ex.table, ex.epoch,
+            dx_rows.data_ptr(), ex.stream.cuda_stream)
 
 
 def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=None,
@@ -228,27 +333,45 @@ def vocab_parallel_flce(hidden, weight_shard, labels, vocab_offset, bias_shard=N
           if need_dw else None)
     chunk = int(chunk_size) if chunk_size and chunk_size > 0 else n
     pending = []
+    ex = None
+    if (need_dx and VP_DX_EXCHANGE == "p2p" and isinstance(phases, CudaShardPhases)
+            and dist.get_backend(group) == "nccl"):
+        ex = PeerExchange.get(group, dev, chunk, h)
+    exchanged = None  # event: the previous chunk's p2p exchange is complete
     for r0 in range(0, n, chunk):
         r1 = min(n, r0 + chunk)
         hc, lc = hidden[r0:r1], labels[r0:r1]
         with _leave_sms_for_collectives(phases, pending):
             m, s, t, state = phases.stats(hc, weight_shard, bias_shard, lc, vocab_offset,
                                           ignore_index)
-        mg, sg, tg = _merge_stats(m, s, t, group, phases)
+        if ex is not None:
+            ex.epoch += 1
+            mg, sg, tg = _p2p_stats(ex, m, s, t, h)
+        else:
+            mg, sg, tg = _merge_stats(m, s, t, group, phases)
         lse = mg + torch.log(sg)
         mask = (lc != ignore_index).to(torch.float32)
         row_loss[r0:r1] = (lse - tg) * mask
-        # dX first, so its all-reduce runs while this chunk's dW GEMM does
-        phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index, lse.contiguous(),
-                     cnt[1:2], dx[r0:r1] if need_dx else None, None, r0 > 0)
-        if need_dx:
-            pending.append(dist.all_reduce(dx[r0:r1], op=dist.ReduceOp.SUM, group=group,
-                                           async_op=True))
+        if ex is not None:
+            phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index,
+                         lse.contiguous(), cnt[1:2], None, None, r0 > 0)
+            _p2p_dx(ex, state, weight_shard, r1 - r0, h, dx[r0:r1], exchanged)
+            exchanged = ex.stream.record_event()
+        else:
+            # dX first, so its all-reduce runs while this chunk's dW GEMM does
+            phases.grads(state, hc, weight_shard, lc, vocab_offset, ignore_index,
+                         lse.contiguous(), cnt[1:2], dx[r0:r1] if need_dx else None, None,
+                         r0 > 0)
+            if need_dx:
+                pending.append(dist.all_reduce(dx[r0:r1], op=dist.ReduceOp.SUM, group=group,
+                                               async_op=True))
         if need_dw:
             with _leave_sms_for_collectives(phases, pending):
                 phases.grads_dw(state, hc, weight_shard, dw, r0 > 0)
     for work in pending:
         work.wait()
+    if exchanged is not None:
+        torch.cuda.current_stream(dev).wait_event(exchanged)
     loss = row_loss.sum() * cnt[1]
     if h != h_in:
         dx = dx[:, :h_in].contiguous() if dx is not None else None

@@ -1,7 +1,11 @@
-"""Vocabulary-parallel FLCE on 2+ GPUs (NCCL) against the single-GPU FLCE.
+"""Vocabulary-parallel FLCE on 2+ GPUs against the single-GPU FLCE, with the
+partial dX summed by NCCL or through peer memory (the dX GEMM storing into
+the row owners' buffers; every rank then holds the bitwise same dX).
 
 Needs at least two CUDA devices; skipped otherwise (the 1-GPU round-end run
-skips it; the host logic is covered by tests/test_vocab_parallel.py on CPU).
+skips it; the host logic is covered by tests/test_vocab_parallel.py on CPU
+and the peer-memory exchange's kernels by tests/test_gpu_flce_p2p.py, which
+emulates the ranks on one GPU).
 """
 
 import pytest
@@ -23,9 +27,11 @@ def _problem(device):
     return hid, w, lab
 
 
-def _rank_fn(rank, world, chunk):
+def _rank_fn(rank, world, chunk, exchange="nccl"):
+    import metal_liger_b200.ops.fused_linear_cross_entropy as F
     from metal_liger_b200.ops.fused_linear_cross_entropy import (
         _VocabParallelFLCEFunction, shard_lm_head)
+    F.VP_DX_EXCHANGE = exchange
     dev = torch.device("cuda", rank)
     hid, w, lab = _problem(dev)
     ws, off = shard_lm_head(w, rank, world)
@@ -34,17 +40,24 @@ def _rank_fn(rank, world, chunk):
     loss = _VocabParallelFLCEFunction.apply(h, wsh, lab, None, off, -100, chunk, None)
     loss.backward(torch.tensor(1.5, device=dev))
     torch.cuda.synchronize()
+    from metal_liger_b200 import _C
     return {"loss": loss.item(), "dx": h.grad.float().cpu(), "dw": wsh.grad.float().cpu(),
-            "off": off}
+            "off": off, "err": int(_C.load().ml_device_error(None))}
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
 @pytest.mark.parametrize("chunk", [1024, 8192])
-def test_two_gpu_vocab_parallel_matches_single_gpu(chunk):
+def test_two_gpu_vocab_parallel_matches_single_gpu(chunk, exchange):
     from metal_liger_b200.ops.fused_linear_cross_entropy import _FusedLinearCrossEntropyFunction
     world = min(torch.cuda.device_count(), 2)
-    res = run_ranks(_rank_fn, world, free_port(), "nccl", 60, chunk)
+    res = run_ranks(_rank_fn, world, free_port(), "nccl", 60, chunk, exchange)
     for r in range(world):
         assert not isinstance(res[r], str), res[r]
+        assert res[r]["err"] == 0, hex(res[r]["err"])
+    # every rank ends with the same summed dX
+    for r in range(1, world):
+        if exchange == "p2p":
+            assert torch.equal(res[r]["dx"], res[0]["dx"])
     hid, w, lab = _problem(torch.device("cuda", 0))
     h = hid.clone().requires_grad_(True)
     wf = w.clone().requires_grad_(True)
