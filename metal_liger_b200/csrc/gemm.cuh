@@ -692,14 +692,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
           sm100::tc_fence_after();
           const uint32_t a_base = sm100::smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b_base = sm100::smem_u32(sB + stage * C::B_BYTES);
+          // one descriptor per operand and stage; each K = 16 step advances its
+          // start-address field (address / 16) by 2048 / 16 (MN-major) or
+          // 32 / 16 (K-major), which stays inside the 14-bit field
+          const uint64_t ad0 = A_MN ? sm100::sdesc_sw128(a_base, 64 * BK * 2, 1024)
+                                    : sm100::sdesc_sw128(a_base, 16, 1024);
+          const uint64_t bd0 = B_MN ? sm100::sdesc_sw128(b_base, 64 * BK * 2, 1024)
+                                    : sm100::sdesc_sw128(b_base, 16, 1024);
+          constexpr uint64_t kAStep = A_MN ? 2048 / 16 : 32 / 16;
+          constexpr uint64_t kBStep = B_MN ? 2048 / 16 : 32 / 16;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? sm100::sdesc_sw128(a_base + k * 2048, 64 * BK * 2, 1024)
-                                     : sm100::sdesc_sw128(a_base + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? sm100::sdesc_sw128(b_base + k * 2048, 64 * BK * 2, 1024)
-                                     : sm100::sdesc_sw128(b_base + k * 32, 16, 1024);
-            sm100::umma_bf16(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            sm100::umma_bf16(d_tmem, ad0 + k * kAStep, bd0 + k * kBStep, IDESC,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
           sm100::umma_commit(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -932,14 +937,19 @@ gemm_pair_kernel(const __grid_constant__ Params p) {
           sm100::tc_fence_after();
           const uint32_t a_base = sm100::smem_u32(sA + stage * C::A_BYTES);
           const uint32_t b_base = sm100::smem_u32(sB + stage * C::B_BYTES);
+          // one descriptor per operand and stage; each K = 16 step advances its
+          // start-address field (address / 16) by 2048 / 16 (MN-major) or
+          // 32 / 16 (K-major), which stays inside the 14-bit field
+          const uint64_t ad0 = A_MN ? sm100::sdesc_sw128(a_base, 64 * BK * 2, 1024)
+                                    : sm100::sdesc_sw128(a_base, 16, 1024);
+          const uint64_t bd0 = B_MN ? sm100::sdesc_sw128(b_base, 64 * BK * 2, 1024)
+                                    : sm100::sdesc_sw128(b_base, 16, 1024);
+          constexpr uint64_t kAStep = A_MN ? 2048 / 16 : 32 / 16;
+          constexpr uint64_t kBStep = B_MN ? 2048 / 16 : 32 / 16;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t ad = A_MN ? sm100::sdesc_sw128(a_base + k * 2048, 64 * BK * 2, 1024)
-                                     : sm100::sdesc_sw128(a_base + k * 32, 16, 1024);
-            const uint64_t bd = B_MN ? sm100::sdesc_sw128(b_base + k * 2048, 64 * BK * 2, 1024)
-                                     : sm100::sdesc_sw128(b_base + k * 32, 16, 1024);
-            sm100::umma_bf16_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            sm100::umma_bf16_pair(d_tmem, ad0 + k * kAStep, bd0 + k * kBStep, IDESC,
+                        (kb > kb0 || k > 0) ? 1u : 0u);
           sm100::umma_commit_pair(&empty[stage], 0x3);
           if (++stage == STAGES) {
             stage = 0;
