@@ -110,19 +110,39 @@ __global__ void __launch_bounds__(256) reduce_gather_k(const __grid_constant__ P
   const int64_t n4 = nr * h / 4;
   const size_t slot4 = (size_t)rows_per_owner * h / 4;
   const float4* recv = reinterpret_cast<const float4*>(pe.ws[me] + off_recv);
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    float4 acc = __ldcg(recv + i);
-    for (int s = 1; s < world; ++s) {
-      const float4 v = __ldcg(recv + (size_t)s * slot4 + i);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+  // kU independent vectors per thread per step: enough loads in flight for
+  // a grid that shares the SMs with the concurrent dW GEMM
+  constexpr int kU = 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < n4;
+       base += stride * kU) {
+    float4 acc[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int64_t i = base + u * stride;
+      if (i < n4) acc[u] = __ldcg(recv + i);
     }
-    const size_t at = (size_t)r0 * h / 4 + i;
-    for (int p = 0; p < world; ++p)
-      reinterpret_cast<float4*>(pe.ws[p] + off_gather)[at] = acc;
+    for (int s = 1; s < world; ++s) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < n4) {
+          const float4 v = __ldcg(recv + (size_t)s * slot4 + i);
+          acc[u].x += v.x;
+          acc[u].y += v.y;
+          acc[u].z += v.z;
+          acc[u].w += v.w;
+        }
+      }
+    }
+    for (int p = 0; p < world; ++p) {
+      float4* dst = reinterpret_cast<float4*>(pe.ws[p] + off_gather) + (size_t)r0 * h / 4;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < n4) dst[i] = acc[u];
+      }
+    }
   }
   __threadfence_system();
 }
@@ -270,7 +290,13 @@ extern "C" int ml_flce_p2p_reduce(int64_t rows, int64_t h, int64_t chunk_cap, in
   if (int rc = p2p::check_peers(world, rank, peer_ws, pe)) return rc;
   const p2p::XLayout X = p2p::xlayout(world, chunk_cap, h);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  p2p::reduce_gather_k<<<32, 256, 0, st>>>(pe, world, rank, rows, h, X.rows_per_owner,
+  // this rank's rows: a grid of up to two CTAs per SM (the owner phase runs
+  // beside the dW GEMM, whose one CTA per SM leaves room for them)
+  const int64_t r0 = (int64_t)rank * X.rows_per_owner;
+  const int64_t nr = std::max<int64_t>(0, std::min<int64_t>(rows, r0 + X.rows_per_owner) - r0);
+  const int grid = (int)std::max<int64_t>(
+      1, std::min<int64_t>((nr * h / 4 + 1023) / 1024, (int64_t)2 * num_sms()));
+  p2p::reduce_gather_k<<<grid, 256, 0, st>>>(pe, world, rank, rows, h, X.rows_per_owner,
                                            X.off_recv, X.off_gather, epoch,
                                            gemm::device_error_word());
   ML_CHECK_LAUNCH("flce_p2p_reduce");
