@@ -156,7 +156,9 @@ VP_OVERLAP_SMS = 0
 #   every rank (ml_flce_shard_dx_p2p / ml_flce_p2p_reduce / ml_flce_p2p_finish),
 #   the owner's phase on a side stream beside the dW GEMM; the statistics go
 #   through the same buffers (ml_flce_p2p_stats_put / _merge), so the step
-#   uses no collective at all.
+#   uses no collective at all.  Its waits are bounded: one that gives up (a
+#   rank that never arrives) leaves ML_ERR_TIMEOUT in the device error word,
+#   which _C.load().ml_device_error(None) reads and clears.
 VP_DX_EXCHANGE = "nccl"
 
 
